@@ -1,0 +1,229 @@
+"""CPU oracle for the NanoQuant quantized-linear path (TEST INFRASTRUCTURE ONLY).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py``
+may import this module; the product package ``nanoquant_b200`` never does.
+
+It wraps ``nq_oracle.c`` (a plain-C restatement of the reference packers and dense
+forward) through ctypes and adds the seeded input generator shared by tests and the
+benchmark.  Reference behaviour restated here:
+
+* ``pack``      -> ``src/nanoquant/kernel/utils.py:51-113``  (``pack_binary_gemv``)
+* ``unpack``    -> ``src/nanoquant/kernel/utils.py:116-183`` (``unpack_binary_gemv``)
+* ``forward``   -> ``src/nanoquant/modules/linear.py:282-291`` (``_compute_forward``)
+  evaluated in float64 on the packed planes.
+* ``dense_forward_torch`` -> the same ``_compute_forward`` as the reference's CPU path
+  runs it after ``load_compressed_model`` has unpacked every factor to dense +-1
+  tensors (``src/nanoquant/utils/load_utils.py:372-392``): two dense matmuls.
+
+Pinning: ``tests/test_oracle.py`` checks every function here against golden vectors
+that ``tests/golden/make_golden.py`` produced by importing the reference itself.
+"""
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import os
+import subprocess
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+ORDERS = {"lsb_first": 0, "half2": 1}
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_SO = os.path.join(_HERE, "_build", "libnq_oracle.so")
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compile nq_oracle.c with gcc into oracle/_build/libnq_oracle.so."""
+    src = os.path.join(_HERE, "nq_oracle.c")
+    if force or not os.path.exists(_SO) or os.path.getmtime(_SO) < os.path.getmtime(src):
+        os.makedirs(os.path.dirname(_SO), exist_ok=True)
+        subprocess.check_call(["gcc", "-O2", "-fPIC", "-shared", "-o", _SO, src])
+    return _SO
+
+
+def _load():
+    global _lib
+    if _lib is None:
+        lib = ctypes.CDLL(build())
+        lib.nqo_pack.restype = ctypes.c_long
+        lib.nqo_pack.argtypes = [ctypes.c_void_p, ctypes.c_long, ctypes.c_long, ctypes.c_int, ctypes.c_void_p]
+        lib.nqo_unpack.restype = ctypes.c_int
+        lib.nqo_unpack.argtypes = [ctypes.c_void_p, ctypes.c_long, ctypes.c_long, ctypes.c_int, ctypes.c_void_p]
+        lib.nqo_forward.restype = ctypes.c_int
+        lib.nqo_forward.argtypes = [ctypes.c_void_p, ctypes.c_long, ctypes.c_long, ctypes.c_void_p,
+                                    ctypes.c_void_p, ctypes.c_long, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_long, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                    ctypes.c_void_p]
+        _lib = lib
+    return _lib
+
+
+def _ptr(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data
+
+
+def words(cols: int) -> int:
+    return (cols + 31) // 32
+
+
+def pack(signs: np.ndarray, method: str = "lsb_first") -> np.ndarray:
+    """int8 +-1 [rows, cols] -> int32 [rows, ceil(cols/32)] (utils.py:51-113)."""
+    if signs.dtype != np.int8:
+        raise TypeError("Input tensor must be int8.")
+    if method not in ORDERS:
+        raise ValueError(f"Unsupported method: '{method}'.")
+    s = np.ascontiguousarray(signs)
+    rows, cols = s.shape
+    out = np.empty((rows, words(cols)), dtype=np.int32)
+    bad = _load().nqo_pack(_ptr(s), rows, cols, ORDERS[method], _ptr(out))
+    if bad:
+        raise ValueError(f"{bad} entries are not exactly +1 or -1")
+    return out
+
+
+def unpack(packed: np.ndarray, shape, method: str = "lsb_first") -> np.ndarray:
+    """int32 planes -> int8 +-1 (utils.py:116-183); padding bits are ignored."""
+    rows, cols = int(shape[0]), int(shape[1])
+    if packed.ndim != 2 or packed.shape != (rows, words(cols)):
+        raise ValueError(f"Unsupported packed tensor shape {packed.shape} for {shape}")
+    p = np.ascontiguousarray(packed, dtype=np.int32)
+    out = np.empty((rows, cols), dtype=np.int8)
+    if _load().nqo_unpack(_ptr(p), rows, cols, ORDERS[method], _ptr(out)) != 0:
+        raise ValueError(f"Unsupported method: '{method}'.")
+    return out
+
+
+def forward(x, s2, v_bits, rank, smid, u_bits, s1, method: str = "lsb_first", return_interm=False):
+    """float64 y = s1 * (U (smid * (V (s2 * x)))) from packed planes (linear.py:282-291).
+
+    x: float32 [batch, in]; s2: [in]; v_bits: int32 [rank, ceil(in/32)];
+    smid: [rank] or None; u_bits: int32 [out, ceil(rank/32)]; s1: [out].
+    """
+    x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    batch, in_f = x.shape
+    out_f = int(np.asarray(s1).size)
+    s2 = np.ascontiguousarray(s2, dtype=np.float32).reshape(-1)
+    s1 = np.ascontiguousarray(s1, dtype=np.float32).reshape(-1)
+    sm = None if smid is None else np.ascontiguousarray(smid, dtype=np.float32).reshape(-1)
+    vb = np.ascontiguousarray(v_bits, dtype=np.int32)
+    ub = np.ascontiguousarray(u_bits, dtype=np.int32)
+    assert vb.shape == (rank, words(in_f)) and ub.shape == (out_f, words(rank))
+    y = np.empty((batch, out_f), dtype=np.float64)
+    t = np.empty((batch, rank), dtype=np.float64) if return_interm else None
+    rc = _load().nqo_forward(_ptr(x), batch, in_f, _ptr(s2), _ptr(vb), rank, _ptr(sm), _ptr(ub),
+                             out_f, _ptr(s1), ORDERS[method], _ptr(y), _ptr(t))
+    if rc != 0:
+        raise ValueError(method)
+    return (y, t) if return_interm else y
+
+
+def dense_forward_torch(x, s2, V, smid, U, s1):
+    """The reference CPU path: _compute_forward on dense +-1 factors (linear.py:282-291)."""
+    import torch.nn.functional as F
+    y = F.linear(x * s2, V)
+    if smid is not None:
+        y = y * smid
+    y = F.linear(y, U)
+    return y * s1
+
+
+# --------------------------------------------------------------------------------------
+# Seeded synthetic inputs (same stream on every machine: splitmix64, no library RNG)
+# --------------------------------------------------------------------------------------
+_GOLD = np.uint64(0x9E3779B97F4A7C15)
+
+
+def splitmix64(seed: int, n: int, stream: int = 0) -> np.ndarray:
+    """n uint64 values of the splitmix64 sequence for (seed, stream)."""
+    with np.errstate(over="ignore"):
+        base = np.uint64((seed * 0x100000001B3 + stream * 0xC2B2AE3D27D4EB4F) & 0xFFFFFFFFFFFFFFFF)
+        z = base + (np.arange(1, n + 1, dtype=np.uint64) * _GOLD)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+
+def random_signs(seed: int, rows: int, cols: int, stream: int = 0) -> np.ndarray:
+    u = splitmix64(seed, rows * cols, stream)
+    return (1 - 2 * (u >> np.uint64(63)).astype(np.int8)).reshape(rows, cols).astype(np.int8)
+
+
+def random_normal(seed: int, n: int, stream: int = 0) -> np.ndarray:
+    """float64 N(0,1) via Box-Muller on two splitmix64 streams."""
+    u1 = ((splitmix64(seed, n, 2 * stream + 101) >> np.uint64(11)).astype(np.float64) + 1.0) * 2.0 ** -53
+    u2 = (splitmix64(seed, n, 2 * stream + 102) >> np.uint64(11)).astype(np.float64) * 2.0 ** -53
+    return np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * np.pi * u2)
+
+
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even float32 -> bfloat16 bit patterns (uint16)."""
+    b = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    rounding = ((b >> np.uint32(16)) & np.uint32(1)) + np.uint32(0x7FFF)
+    with np.errstate(over="ignore"):
+        out = ((b + rounding) >> np.uint32(16)).astype(np.uint16)
+    nan = np.isnan(np.asarray(a, dtype=np.float32))
+    out[nan] = 0x7FC0
+    return out
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << np.uint32(16)).view(np.float32)
+
+
+def round_to(a: np.ndarray, dtype: str) -> np.ndarray:
+    """Round float values to fp16/bf16 and return them as float32."""
+    if dtype == "f16":
+        return np.asarray(a, dtype=np.float32).astype(np.float16).astype(np.float32)
+    if dtype == "bf16":
+        return bf16_bits_to_f32(f32_to_bf16_bits(np.asarray(a, dtype=np.float32)))
+    if dtype == "f32":
+        return np.asarray(a, dtype=np.float32)
+    raise ValueError(dtype)
+
+
+@dataclass
+class Layer:
+    """One seeded NanoQuant layer, values already rounded to ``dtype`` (held as float32)."""
+    out_f: int
+    in_f: int
+    rank: int
+    V: np.ndarray        # int8 [rank, in]   (module layout, linear.py:99)
+    U: np.ndarray        # int8 [out, rank]  (module layout, linear.py:100)
+    s2: np.ndarray       # scale_pre  [in]
+    s1: np.ndarray       # scale_post [out]
+    smid: Optional[np.ndarray]  # scale_mid [rank] or None
+    x: np.ndarray        # [batch, in]
+    dtype: str
+
+    def packed(self, method="lsb_first"):
+        return pack(self.V, method), pack(self.U, method)
+
+    def reference(self, method="lsb_first"):
+        vb, ub = self.packed(method)
+        return forward(self.x, self.s2, vb, self.rank, self.smid, ub, self.s1, method)
+
+
+def make_layer(seed: int, out_f: int, in_f: int, rank: int, batch: int = 1, dtype: str = "f16",
+               with_mid: bool = False, s1_std: float = 0.02) -> Layer:
+    """Synthetic layer with the distributions of the benchmark configs:
+    signs i.i.d. +-1; s1 = |N(0, 0.02)|; s2 = |N(0, 1)|; smid = |N(0, 1)|; x = N(0, 1)."""
+    V = random_signs(seed, rank, in_f, stream=1)
+    U = random_signs(seed, out_f, rank, stream=2)
+    s1 = round_to(np.abs(random_normal(seed, out_f, 3)) * s1_std, dtype)
+    s2 = round_to(np.abs(random_normal(seed, in_f, 4)), dtype)
+    smid = round_to(np.abs(random_normal(seed, rank, 5)), dtype) if with_mid else None
+    x = round_to(random_normal(seed, batch * in_f, 6).reshape(batch, in_f), dtype)
+    return Layer(out_f, in_f, rank, V, U, s2, s1, smid, x, dtype)
+
+
+def rel_l2(a, b) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+def sha256(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
