@@ -1,0 +1,124 @@
+/*
+ * nq_b200.h -- C ABI of the B200 (sm_100a) NanoQuant quantized-linear kernels.
+ *
+ * A NanoQuant layer stores W ~= diag(s1) . U . V^T . diag(s2) with U (out x r) and
+ * V^T (r x in) in {-1,+1}, kept as bit-packed int32 sign planes, and computes
+ *     y = s1 * (U (smid * (V (s2 * x))))          (smid optional, length r)
+ * Naming follows the reference module (src/nanoquant/modules/linear.py:74-114):
+ *     scale_pre = s2 [in], scale_post = s1 [out], scale_mid [r],
+ *     V planes [r, ceil(in/32)], U planes [out, ceil(r/32)].
+ *
+ * Conventions shared by every entry point:
+ *   - all pointers are device pointers unless stated; nothing here allocates;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *     work is enqueued asynchronously, no entry point synchronises;
+ *   - the caller selects the device (cudaSetDevice) before calling;
+ *   - return value is an nq_status; on failure nq_last_error_message() gives a
+ *     human-readable reason (thread-local) and nothing was enqueued;
+ *   - errors detected on the device (a bounded wait that gave up, a pack input that
+ *     was not +-1) are recorded in a status word inside the caller's workspace or
+ *     counter and read back with nq_workspace_status().
+ */
+#ifndef NQ_B200_H_
+#define NQ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NQ_API __attribute__((visibility("default")))
+#else
+#define NQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    NQ_OK = 0,
+    NQ_ERR_INVALID_ARGUMENT = 1, /* null pointer, non-positive size, misaligned pointer */
+    NQ_ERR_UNSUPPORTED = 2,      /* well-formed but unsupported (dtype, bit order, shape) */
+    NQ_ERR_WORKSPACE = 3,        /* workspace missing or smaller than the query says */
+    NQ_ERR_CUDA = 4,             /* the CUDA runtime refused the launch */
+    NQ_ERR_DEVICE_TIMEOUT = 5,   /* a bounded device-side wait gave up (status word) */
+    NQ_ERR_NOT_SIGNS = 6         /* a pack input held values other than +-1 */
+} nq_status;
+
+typedef enum { NQ_DTYPE_F16 = 0, NQ_DTYPE_BF16 = 1 } nq_dtype;
+
+/* Bit order inside each 32-bit word (src/nanoquant/kernel/utils.py:98-106):
+ * LSB_FIRST: column j of a 32-column chunk -> bit j (checkpoint format);
+ * HALF2:     column j -> bit 15 - j/2 + 16*(j%2) (the decode-kernel format). */
+typedef enum { NQ_BITS_LSB_FIRST = 0, NQ_BITS_HALF2 = 1 } nq_bit_order;
+
+NQ_API int nq_abi_version(void);
+NQ_API const char *nq_status_string(int status);
+NQ_API const char *nq_last_error_message(void);
+
+/* ---------------------------------------------------------------------------------
+ * Sign packing.
+ * nq_pack_signs replaces pack_binary_gemv (src/nanoquant/kernel/utils.py:51-113):
+ * int8 +-1 [rows, cols] -> int32 [rows, ceil(cols/32)], +1 -> bit 0, -1 -> bit 1,
+ * columns padded with +1.  If `invalid_count` (device int32, may be NULL) is given,
+ * the number of inputs that are not exactly +-1 is atomically ADDED to it (the caller
+ * zeroes it); those entries are packed by their sign.
+ * nq_unpack_signs replaces unpack_binary_gemv (utils.py:116-183); padding bits ignored.
+ * nq_repack_signs has no single reference counterpart: it converts planes between bit
+ * orders on the device (the reference does unpack -> dense -> pack for this,
+ * src/nanoquant/modules/linear.py:205-206 after load_utils.py:392), clearing padding bits.
+ * ------------------------------------------------------------------------------- */
+NQ_API int nq_pack_signs(const int8_t *signs, int64_t rows, int64_t cols, int bit_order,
+                  int32_t *packed, int32_t *invalid_count, void *stream);
+NQ_API int nq_unpack_signs(const int32_t *packed, int64_t rows, int64_t cols, int bit_order,
+                    int8_t *signs, void *stream);
+NQ_API int nq_repack_signs(const int32_t *src, int64_t rows, int64_t cols, int src_order,
+                    int dst_order, int32_t *dst, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * Decode GEMV: replaces nanoquant_dyn_forward (src/nanoquant/kernel/cuda/gemv_kernel.cu:308-429,
+ * op schema src/nanoquant/kernel/pybind.cpp:85-90), fused into ONE launch per 8 rows of x.
+ *   x [batch, in], scale_pre [in], scale_mid [rank] or NULL, scale_post [out], y [batch, out]
+ *   all of `dtype`; v_bits [rank, ceil(in/32)] and u_bits [out, ceil(rank/32)] in HALF2 order.
+ * Accumulation is float32; fp16 outputs are clamped to +-64504 like the reference
+ * (src/nanoquant/kernel/cuda/cuda_utils.cuh:80-90).
+ * The workspace (>= nq_gemv_workspace_bytes) must be zero-filled once before its
+ * first use (nq_workspace_reset); every successful call leaves it reusable.  Calls
+ * that share one workspace must be ordered on one stream.
+ * ------------------------------------------------------------------------------- */
+NQ_API size_t nq_gemv_workspace_bytes(int64_t batch, int64_t rank);
+NQ_API int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features,
+            const void *scale_pre, const int32_t *v_bits, int64_t rank,
+            const void *scale_mid, const int32_t *u_bits, int64_t out_features,
+            const void *scale_post, void *y, void *workspace, size_t workspace_bytes,
+            void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * Prefill GEMM: replaces marlin_nanoquant_cuda (src/nanoquant/kernel/cuda/gemm.cpp:112-122,
+ * schema src/nanoquant/kernel/pybind.cpp:99-104) on the same HALF2 planes the GEMV uses.
+ * tcgen05 tensor-core contraction in two stages, T = (x*s2) V^T * smid then y = (T U^T) * s1.
+ * `precise` = 1 keeps T as a bf16 hi/lo pair (float32-grade intermediate); 0 rounds T
+ * once to bf16 like the reference's fp16/bf16 intermediate (gemm.cpp:119).
+ * Requires in_features % 8 == 0 and 16-byte aligned x / y.
+ * ------------------------------------------------------------------------------- */
+NQ_API size_t nq_gemm_workspace_bytes(int64_t m, int64_t rank);
+NQ_API int nq_gemm(int dtype, const void *x, int64_t m, int64_t in_features, const void *scale_pre,
+            const int32_t *v_bits, int64_t rank, const void *scale_mid, const int32_t *u_bits,
+            int64_t out_features, const void *scale_post, int precise, void *y, void *workspace,
+            size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * Workspace status word (no reference counterpart: the reference kernels have no
+ * device-side error reporting).
+ * nq_workspace_reset zero-fills a workspace (enqueued on `stream`).
+ * nq_workspace_status synchronises `stream`, then reads the status word: NQ_OK or the
+ * first device-side error (NQ_ERR_DEVICE_TIMEOUT); the word is left as it was.
+ * ------------------------------------------------------------------------------- */
+NQ_API int nq_workspace_reset(void *workspace, size_t workspace_bytes, void *stream);
+NQ_API int nq_workspace_status(const void *workspace, size_t workspace_bytes, void *stream,
+                        int *status_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NQ_B200_H_ */

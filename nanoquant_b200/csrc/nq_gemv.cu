@@ -1,0 +1,505 @@
+// Fused NanoQuant decode GEMV for sm_100a (one launch per <= 8 rows of x).
+//
+// Computes, for b < batch (<= 8):
+//   t[b, k] = smid[k] * sum_n sign(V[k, n]) * s2[n] * x[b, n]          (stage 1, k < rank)
+//   y[b, m] = clamp(s1[m] * sum_k sign(U[m, k]) * t[b, k])             (stage 2, m < out)
+// replacing the reference's two launches with a half-precision interm round trip
+// (src/nanoquant/kernel/cuda/gemv_kernel.cu:43-301, dispatched at :308-429).
+//
+// Design (one CTA per SM, cooperative launch):
+//  * At kernel start one thread issues 1-D bulk copies (TMA engine, no multicast) of
+//    this CTA's contiguous slab of V rows AND of U rows into shared memory, so every
+//    weight byte the CTA will ever need is in flight at once; U streams in while
+//    stage 1 computes and while the grid waits at the barrier.
+//  * s2 and x are staged in shared memory by plain coalesced loads (zero-padded to a
+//    multiple of 64 columns).
+//  * Both stages are tensor-core matrix-vector products with mma.sync.m16n8k16 and
+//    float32 accumulation: the A fragment (16 weight rows x 16 columns) is built in
+//    registers straight from the HALF2 sign words -- the bit pair of columns
+//    (2p, 2p+1) sits at bits (15-p, 31-p), so `(w << p) & 0x80008000` is the sign mask
+//    of one bf16/fp16 pair -- and the B fragment is the activation column(s).
+//    Stage 1 folds s2 into A (A = +-s2[n], exact in the input dtype; B = x, exact),
+//    so the products are exact and only the float32 accumulation rounds.
+//    Stage 2 uses A = +-1.0 (bf16) and B = t split into bf16 hi + lo halves (two
+//    B columns per batch row), which keeps ~16 mantissa bits of the float32 t.
+//  * Each warp owns a contiguous range of 64-column K blocks of every 16-row tile;
+//    the 8 warps' partial 16x8 tiles are reduced through shared memory.
+//  * t[b, :] goes to the (L2-resident) workspace; one bounded grid barrier separates
+//    the stages.  The barrier resets itself, so the workspace stays reusable.
+// Layers too large for the per-CTA shared-memory budget run the same kernel as two
+// ordinary launches (stage 1 then stage 2, one 16-row tile per CTA).
+#include "nq_common.cuh"
+
+namespace nq {
+namespace gemv {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxBatch = 8;
+constexpr int kStaticSmemReserve = 1024;  // static __shared__ of the kernel (grid barrier flag)
+
+enum Mode : int { kStage1 = 1, kStage2 = 2, kFused = 3 };
+
+struct Params {
+    const void *x;            // [batch, in]
+    const void *s2;           // [in]
+    const uint32_t *vbits;    // [rank, wv]
+    const void *smid;         // [rank] or null
+    const uint32_t *ubits;    // [out, wu]
+    const void *s1;           // [out]
+    void *y;                  // [batch, out]
+    float *interm;            // [batch, rank]
+    Ctrl *ctrl;
+    int batch, in_f, rank, out_f;
+    int wv, wu;               // words per V row / U row
+    int kb1, kb2;             // 64-column K blocks per stage
+    int tiles1, tiles2;       // 16-row tiles per stage
+    int mode;
+    int x_in_smem;
+    uint32_t off_red, off_s2, off_x, off_v, off_u, off_b;
+};
+
+__device__ __forceinline__ void tile_range(int tiles, int c, int G, int &b, int &e) {
+    b = (int)(((long long)tiles * c) / G);
+    e = (int)(((long long)tiles * (c + 1)) / G);
+}
+
+// Copy `n` 16-bit values into a zero-padded shared row of `npad` values.
+template <typename T>
+__device__ __forceinline__ void stage_row(T *dst, const T *src, int n, int npad) {
+    const bool vec = ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+    for (int c8 = threadIdx.x; c8 < npad / 8; c8 += kThreads) {
+        const int c = c8 * 8;
+        uint4 v;
+        if (vec && c + 8 <= n) {
+            v = __ldg(reinterpret_cast<const uint4 *>(src + c));
+        } else {
+            uint16_t h[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                h[j] = (c + j < n) ? reinterpret_cast<const uint16_t *>(src)[c + j] : uint16_t(0);
+            v = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                           h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+        }
+        reinterpret_cast<uint4 *>(dst + c)[0] = v;
+    }
+}
+
+// 16 consecutive 16-bit values from a global row with bounds checks (zero beyond n).
+template <typename T>
+__device__ __forceinline__ void load16_global(const T *row, int c, int n, uint32_t (&v)[8]) {
+    if (c + 16 <= n && (reinterpret_cast<uintptr_t>(row + c) & 15) == 0) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4 *>(row + c));
+        const uint4 b = __ldg(reinterpret_cast<const uint4 *>(row + c) + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+        const uint16_t *r = reinterpret_cast<const uint16_t *>(row);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t lo = (c + 2 * j < n) ? r[c + 2 * j] : 0u;
+            const uint32_t hi = (c + 2 * j + 1 < n) ? r[c + 2 * j + 1] : 0u;
+            v[j] = lo | (hi << 16);
+        }
+    }
+}
+
+__device__ __forceinline__ void load16_smem(const void *p, uint32_t (&v)[8]) {
+    const uint4 a = reinterpret_cast<const uint4 *>(p)[0];
+    const uint4 b = reinterpret_cast<const uint4 *>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Issue the bulk copy of rows [r0, r1) of a plane with `w` words per row into smem.
+// The 16-byte-multiple prefix goes through the TMA engine (signalled on `bar`),
+// the remaining <16 bytes are copied by plain loads (caller syncs afterwards).
+__device__ __forceinline__ void issue_slab(uint32_t *dst, const uint32_t *plane, int r0, int r1, int w,
+                                           uint64_t *bar, bool leader) {
+    const uint32_t words = (r1 > r0) ? (uint32_t)(r1 - r0) * (uint32_t)w : 0u;
+    const uint32_t bytes = words * 4u;
+    const uint32_t bulk = bytes & ~15u;
+    const uint32_t *src = plane + (size_t)r0 * w;
+    if (leader) {
+        mbar_arrive_expect_tx(bar, bulk);
+        if (bulk) bulk_g2s_pieces(dst, src, bulk, bar);
+    }
+    for (uint32_t i = bulk / 4 + threadIdx.x; i < words; i += kThreads) dst[i] = __ldg(src + i);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    using E = Elem<T>;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int G = gridDim.x, c = blockIdx.x;
+    const bool do1 = (p.mode & kStage1) != 0, do2 = (p.mode & kStage2) != 0;
+
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    float *red = reinterpret_cast<float *>(smem + p.off_red);
+    T *s2s = reinterpret_cast<T *>(smem + p.off_s2);
+    T *xs = reinterpret_cast<T *>(smem + p.off_x);
+    uint32_t *vch = reinterpret_cast<uint32_t *>(smem + p.off_v);
+    uint32_t *uch = reinterpret_cast<uint32_t *>(smem + p.off_u);
+    __nv_bfloat16 *bsm = reinterpret_cast<__nv_bfloat16 *>(smem + p.off_b);
+
+    int t1b = 0, t1e = 0, t2b = 0, t2e = 0;
+    if (do1) tile_range(p.tiles1, c, G, t1b, t1e);
+    if (do2) tile_range(p.tiles2, c, G, t2b, t2e);
+    const int r1b = 16 * t1b, r1e = min(16 * t1e, p.rank);
+    const int r2b = 16 * t2b, r2e = min(16 * t2e, p.out_f);
+    const bool has1 = r1e > r1b, has2 = r2e > r2b;
+    const int in_pad = p.kb1 * 64;
+
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    // Put every weight byte of this CTA in flight before anything else.
+    if (has1) issue_slab(vch, p.vbits, r1b, r1e, p.wv, &bars[0], tid == 0);
+    if (has2) issue_slab(uch, p.ubits, r2b, r2e, p.wu, &bars[1], tid == 0);
+    if (has1) {
+        stage_row<T>(s2s, static_cast<const T *>(p.s2), p.in_f, in_pad);
+        if (p.x_in_smem)
+            for (int b = 0; b < p.batch; ++b)
+                stage_row<T>(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f, p.in_f, in_pad);
+    }
+    __syncthreads();
+
+    bool ok = true;
+    // ------------------------------------------------------------------ stage 1
+    if (has1) {
+        ok = mbar_wait(&bars[0], 0, &p.ctrl->status);
+        const int kbeg = (p.kb1 * warp) / kWarps, kend = (p.kb1 * (warp + 1)) / kWarps;
+        const uint32_t *sw = reinterpret_cast<const uint32_t *>(s2s);
+        const T *xg = static_cast<const T *>(p.x) + (size_t)g * p.in_f;
+        const uint32_t *xsw = reinterpret_cast<const uint32_t *>(xs + (size_t)g * in_pad);
+        const bool xrow = g < p.batch;
+        const int sh0 = 8 * (t & 1);
+        for (int tile = t1b; tile < t1e; ++tile) {
+            const int lt = tile - t1b;
+            const bool vA = ok && (16 * tile + g < p.rank), vB = ok && (16 * tile + g + 8 < p.rank);
+            const uint32_t *rowA = vch + (size_t)(lt * 16 + g) * p.wv;
+            const uint32_t *rowB = rowA + (size_t)8 * p.wv;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int kb = kbeg; kb < kend; ++kb) {
+                const int wi = 2 * kb + (t >> 1);
+                const uint32_t wA = (vA && wi < p.wv) ? rowA[wi] << sh0 : 0u;
+                const uint32_t wB = (vB && wi < p.wv) ? rowB[wi] << sh0 : 0u;
+                const int kc = 64 * kb + 16 * t;
+                uint32_t sp[8], xp[8];
+                load16_smem(sw + kc / 2, sp);
+                if (!xrow) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) xp[j] = 0u;
+                } else if (p.x_in_smem) {
+                    load16_smem(xsw + kc / 2, xp);
+                } else {
+                    load16_global<T>(xg, kc, p.in_f, xp);
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t a0 = lop_sign(wA << (2 * j), sp[2 * j]);
+                    const uint32_t a1 = lop_sign(wB << (2 * j), sp[2 * j]);
+                    const uint32_t a2 = lop_sign(wA << (2 * j + 1), sp[2 * j + 1]);
+                    const uint32_t a3 = lop_sign(wB << (2 * j + 1), sp[2 * j + 1]);
+                    E::mma(acc, a0, a1, a2, a3, xp[2 * j], xp[2 * j + 1]);
+                }
+            }
+            float *rw = red + warp * 128;
+            rw[g * 8 + 2 * t] = acc[0];
+            rw[g * 8 + 2 * t + 1] = acc[1];
+            rw[(g + 8) * 8 + 2 * t] = acc[2];
+            rw[(g + 8) * 8 + 2 * t + 1] = acc[3];
+            __syncthreads();
+            for (int i = tid; i < 16 * p.batch; i += kThreads) {
+                const int b = i >> 4, row = i & 15;
+                float s = 0.f;
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) s += red[w * 128 + row * 8 + b];
+                const int k = 16 * tile + row;
+                if (k < p.rank) {
+                    if (p.smid) s *= E::to_f(static_cast<const T *>(p.smid)[k]);
+                    p.interm[(size_t)b * p.rank + k] = s;
+                }
+            }
+            __syncthreads();
+        }
+    }
+
+    if (p.mode == kFused) {
+        if (!grid_barrier(p.ctrl, (unsigned)G)) ok = false;
+    }
+
+    // ------------------------------------------------------------------ stage 2
+    if (has2) {
+        const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles (hi/lo per batch row)
+        const int kp2 = p.kb2 * 64;
+        const int bstride = kp2 + 8;  // +16 B per column row: conflict-free 128-bit loads
+        for (int idx = tid; idx < nt * 8 * kp2; idx += kThreads) {
+            const int col = idx / kp2, k = idx - col * kp2;
+            const int b = (col >> 3) * 4 + ((col & 7) >> 1);
+            const float v = (b < p.batch && k < p.rank) ? __ldcg(p.interm + (size_t)b * p.rank + k) : 0.f;
+            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+            bsm[(size_t)col * bstride + k] = (col & 1) ? __float2bfloat16_rn(v - __bfloat162float(hi)) : hi;
+        }
+        __syncthreads();
+        if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
+        const int kbeg = (p.kb2 * warp) / kWarps, kend = (p.kb2 * (warp + 1)) / kWarps;
+        const int sh0 = 8 * (t & 1);
+        constexpr uint32_t kOne = 0x3F803F80u;  // bf16 (1.0, 1.0)
+        for (int tile = t2b; tile < t2e; ++tile) {
+            const int lt = tile - t2b;
+            const bool vA = ok && (16 * tile + g < p.out_f), vB = ok && (16 * tile + g + 8 < p.out_f);
+            const uint32_t *rowA = uch + (size_t)(lt * 16 + g) * p.wu;
+            const uint32_t *rowB = rowA + (size_t)8 * p.wu;
+            float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int kb = kbeg; kb < kend; ++kb) {
+                const int wi = 2 * kb + (t >> 1);
+                const uint32_t wA = (vA && wi < p.wu) ? rowA[wi] << sh0 : 0u;
+                const uint32_t wB = (vB && wi < p.wu) ? rowB[wi] << sh0 : 0u;
+                const int kc = 64 * kb + 16 * t;
+                uint32_t b0[8];
+                load16_smem(bsm + (size_t)g * bstride + kc, b0);
+                uint32_t a[4][4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    a[j][0] = lop_sign(wA << (2 * j), kOne);
+                    a[j][1] = lop_sign(wB << (2 * j), kOne);
+                    a[j][2] = lop_sign(wA << (2 * j + 1), kOne);
+                    a[j][3] = lop_sign(wB << (2 * j + 1), kOne);
+                    mma_bf16_16816(acc0, a[j][0], a[j][1], a[j][2], a[j][3], b0[2 * j], b0[2 * j + 1]);
+                }
+                if (nt == 2) {
+                    uint32_t b1[8];
+                    load16_smem(bsm + (size_t)(8 + g) * bstride + kc, b1);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        mma_bf16_16816(acc1, a[j][0], a[j][1], a[j][2], a[j][3], b1[2 * j], b1[2 * j + 1]);
+                }
+            }
+            float *rw = red + warp * 256;
+            rw[g * 8 + 2 * t] = acc0[0];
+            rw[g * 8 + 2 * t + 1] = acc0[1];
+            rw[(g + 8) * 8 + 2 * t] = acc0[2];
+            rw[(g + 8) * 8 + 2 * t + 1] = acc0[3];
+            rw[128 + g * 8 + 2 * t] = acc1[0];
+            rw[128 + g * 8 + 2 * t + 1] = acc1[1];
+            rw[128 + (g + 8) * 8 + 2 * t] = acc1[2];
+            rw[128 + (g + 8) * 8 + 2 * t + 1] = acc1[3];
+            __syncthreads();
+            for (int i = tid; i < 16 * p.batch; i += kThreads) {
+                const int b = i >> 4, row = i & 15;
+                const int half = (b >> 2) * 128, col = 2 * (b & 3);
+                float s = 0.f;
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) s += red[w * 256 + half + row * 8 + col] + red[w * 256 + half + row * 8 + col + 1];
+                const int m = 16 * tile + row;
+                if (m < p.out_f) {
+                    const float v = s * E::to_f(static_cast<const T *>(p.s1)[m]);
+                    static_cast<T *>(p.y)[(size_t)b * p.out_f + m] = E::out(v);
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+struct Plan {
+    int mode = kFused;
+    int grid = 0, grid1 = 0, grid2 = 0;
+    size_t smem = 0, smem1 = 0, smem2 = 0;
+    Params prm{};
+    Params prm1{}, prm2{};
+};
+
+static inline uint32_t align128(size_t v) { return (uint32_t)((v + 127) & ~size_t(127)); }
+
+// Shared-memory layout for a launch whose CTAs own at most `rows1`/`rows2` rows.
+static size_t layout(Params &p, int rows1, int rows2, bool stage1, bool stage2, bool x_in_smem) {
+    size_t off = 128;  // mbarriers
+    p.off_red = (uint32_t)off;
+    off = align128(off + (size_t)kWarps * 256 * sizeof(float));
+    const size_t in_pad = (size_t)p.kb1 * 64;
+    p.off_s2 = (uint32_t)off;
+    if (stage1) off = align128(off + in_pad * 2);
+    // region shared by stage-1 data (x, V slab) and the stage-2 B operand
+    const size_t region = off;
+    p.off_x = (uint32_t)region;
+    size_t r1 = 0;
+    if (stage1) {
+        r1 = x_in_smem ? align128((size_t)p.batch * in_pad * 2) : 0;
+        p.off_v = (uint32_t)(region + r1);
+        r1 += align128((size_t)rows1 * p.wv * 4 + 16);
+    } else {
+        p.off_v = (uint32_t)region;
+    }
+    size_t rb = 0;
+    if (stage2) {
+        const int nt = p.batch <= 4 ? 1 : 2;
+        rb = align128((size_t)nt * 8 * ((size_t)p.kb2 * 64 + 8) * 2);
+    }
+    p.off_b = (uint32_t)region;
+    off = region + (r1 > rb ? r1 : rb);
+    p.off_u = (uint32_t)off;
+    if (stage2) off = align128(off + (size_t)rows2 * p.wu * 4 + 16);
+    p.x_in_smem = x_in_smem ? 1 : 0;
+    return off;
+}
+
+static int make_plan(int dev, const Params &base, Plan &plan) {
+    const DeviceInfo &di = device_info(dev);
+    const size_t cap = (size_t)di.max_smem_optin - kStaticSmemReserve;
+    const int sms = di.sms;
+    Params p = base;
+    // fused: one CTA per SM, tiles spread evenly
+    const int G = sms;
+    const int rows1 = 16 * ((p.tiles1 + G - 1) / G), rows2 = 16 * ((p.tiles2 + G - 1) / G);
+    for (int xs = 1; xs >= 0; --xs) {
+        Params q = p;
+        q.mode = kFused;
+        const size_t need = layout(q, rows1, rows2, true, true, xs != 0);
+        if (need <= cap && di.coop) {
+            plan.mode = kFused;
+            plan.grid = G;
+            plan.smem = need;
+            plan.prm = q;
+            return NQ_OK;
+        }
+    }
+    // two ordinary launches, one 16-row tile per CTA
+    for (int xs = 1; xs >= 0; --xs) {
+        Params q1 = p, q2 = p;
+        q1.mode = kStage1;
+        q2.mode = kStage2;
+        const size_t n1 = layout(q1, 16, 0, true, false, xs != 0);
+        const size_t n2 = layout(q2, 0, 16, false, true, false);
+        if (n1 <= cap && n2 <= cap) {
+            plan.mode = kStage1 | kStage2 | 4;  // marker: split
+            plan.grid1 = p.tiles1;
+            plan.grid2 = p.tiles2;
+            plan.smem1 = n1;
+            plan.smem2 = n2;
+            plan.prm1 = q1;
+            plan.prm2 = q2;
+            return NQ_OK;
+        }
+    }
+    return fail(NQ_ERR_UNSUPPORTED, "layer too large for the shared-memory budget (in=%d rank=%d out=%d)", p.in_f,
+                p.rank, p.out_f);
+}
+
+template <typename T>
+static int launch(const Plan &plan, cudaStream_t stream) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             device_info(dev).max_smem_optin - kStaticSmemReserve);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
+        attr_set[dev] = true;
+    }
+    if (plan.mode == kFused) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(plan.grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = plan.smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<T>, plan.prm);
+        return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv fused launch");
+    }
+    gemv_kernel<T><<<plan.grid1, kThreads, plan.smem1, stream>>>(plan.prm1);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "gemv stage-1 launch");
+    gemv_kernel<T><<<plan.grid2, kThreads, plan.smem2, stream>>>(plan.prm2);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv stage-2 launch");
+}
+
+}  // namespace gemv
+}  // namespace nq
+
+extern "C" {
+
+size_t nq_gemv_workspace_bytes(int64_t batch, int64_t rank) {
+    (void)batch;  // batches above 8 reuse the same 8-row interm buffer, launch after launch
+    if (rank <= 0) return 0;
+    const size_t interm = (size_t)nq::gemv::kMaxBatch * (size_t)rank * sizeof(float);
+    return sizeof(nq::Ctrl) + ((interm + 255) & ~size_t(255));
+}
+
+int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features, const void *scale_pre,
+            const int32_t *v_bits, int64_t rank, const void *scale_mid, const int32_t *u_bits,
+            int64_t out_features, const void *scale_post, void *y, void *workspace, size_t workspace_bytes,
+            void *stream) {
+    using namespace nq;
+    using namespace nq::gemv;
+    if (dtype != NQ_DTYPE_F16 && dtype != NQ_DTYPE_BF16)
+        return fail(NQ_ERR_UNSUPPORTED, "dtype must be NQ_DTYPE_F16 or NQ_DTYPE_BF16 (got %d)", dtype);
+    if (!x || !scale_pre || !v_bits || !u_bits || !scale_post || !y)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (batch <= 0 || in_features <= 0 || rank <= 0 || out_features <= 0)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "sizes must be positive (batch=%lld in=%lld rank=%lld out=%lld)",
+                    (long long)batch, (long long)in_features, (long long)rank, (long long)out_features);
+    if (in_features > (1 << 24) || rank > (1 << 20) || out_features > (1 << 24))
+        return fail(NQ_ERR_UNSUPPORTED, "sizes beyond the supported range");
+    const uintptr_t a2 = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(scale_pre) |
+                         reinterpret_cast<uintptr_t>(scale_post) | reinterpret_cast<uintptr_t>(y) |
+                         reinterpret_cast<uintptr_t>(scale_mid);
+    if (a2 & 1) return fail(NQ_ERR_INVALID_ARGUMENT, "16-bit tensors must be 2-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(v_bits) | reinterpret_cast<uintptr_t>(u_bits)) & 15)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "sign planes must be 16-byte aligned");
+    const size_t need = nq_gemv_workspace_bytes(batch, rank);
+    if (!workspace || workspace_bytes < need)
+        return fail(NQ_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    const DeviceInfo &di = device_info(dev);
+    if (di.cc_major != 10) return fail(NQ_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", dev,
+                                       di.cc_major, di.cc_minor);
+
+    Params base{};
+    base.s2 = scale_pre;
+    base.vbits = reinterpret_cast<const uint32_t *>(v_bits);
+    base.smid = scale_mid;
+    base.ubits = reinterpret_cast<const uint32_t *>(u_bits);
+    base.s1 = scale_post;
+    base.ctrl = static_cast<Ctrl *>(workspace);
+    base.interm = reinterpret_cast<float *>(static_cast<char *>(workspace) + sizeof(Ctrl));
+    base.in_f = (int)in_features;
+    base.rank = (int)rank;
+    base.out_f = (int)out_features;
+    base.wv = (int)((in_features + 31) / 32);
+    base.wu = (int)((rank + 31) / 32);
+    base.kb1 = (base.wv + 1) / 2;
+    base.kb2 = (base.wu + 1) / 2;
+    base.tiles1 = (int)((rank + 15) / 16);
+    base.tiles2 = (int)((out_features + 15) / 16);
+    const size_t esz = 2;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int64_t b0 = 0; b0 < batch; b0 += kMaxBatch) {
+        Params p = base;
+        p.batch = (int)((batch - b0) < kMaxBatch ? (batch - b0) : kMaxBatch);
+        p.x = static_cast<const char *>(x) + (size_t)b0 * in_features * esz;
+        p.y = static_cast<char *>(y) + (size_t)b0 * out_features * esz;
+        Plan plan;
+        int st = make_plan(dev, p, plan);
+        if (st) return st;
+        st = (dtype == NQ_DTYPE_F16) ? launch<__half>(plan, s) : launch<__nv_bfloat16>(plan, s);
+        if (st) return st;
+    }
+    return NQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,342 @@
+// Thin PyTorch dispatcher layer over the nq_b200 C ABI.
+//
+// Registers the reference's op namespace `binary_kernels` with the reference schemas
+// (src/nanoquant/kernel/pybind.cpp:83-125), so NanoQuantLinear._prepare_kernel and
+// get_kernel_function (src/nanoquant/kernel/utils.py:33-48) bind these kernels
+// unchanged, plus the `nq_b200` namespace for packing and the explicit GEMV / GEMM.
+// Every op has a CUDA and a Meta implementation.  Kernels run on the current CUDA
+// stream of the input's device; nothing synchronises (except pack_signs with
+// check=True, which must read the invalid-value count back).
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include <map>
+#include <mutex>
+#include <optional>
+#include <string>
+#include <utility>
+
+#include "../../include/nq_b200.h"
+
+namespace {
+
+#define NQ_TORCH_CHECK(call)                                                                          \
+    do {                                                                                              \
+        const int nq_st_ = (call);                                                                    \
+        TORCH_CHECK(nq_st_ == NQ_OK, "nq_b200: ", nq_status_string(nq_st_), ": ", nq_last_error_message()); \
+    } while (0)
+
+#define CHECK_CUDA_CONT(x, st)                                                        \
+    do {                                                                              \
+        TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor");                      \
+        TORCH_CHECK((x).is_contiguous(), #x " must be contiguous");                   \
+        TORCH_CHECK((x).scalar_type() == (st), #x " must be ", c10::toString(st), " tensor"); \
+    } while (0)
+
+int dtype_code(at::ScalarType st) {
+    if (st == at::kHalf) return NQ_DTYPE_F16;
+    if (st == at::kBFloat16) return NQ_DTYPE_BF16;
+    TORCH_CHECK(false, "Support only Half or BFloat16");
+}
+
+int order_code(const std::string &m) {
+    if (m == "lsb_first") return NQ_BITS_LSB_FIRST;
+    if (m == "half2") return NQ_BITS_HALF2;
+    TORCH_CHECK_VALUE(false, "Unsupported method: '", m, "'. Supported methods are 'lsb_first', 'half2'.");
+}
+
+cudaStream_t cur_stream(const at::Tensor &t) { return c10::cuda::getCurrentCUDAStream(t.device().index()).stream(); }
+
+// Zero-initialised workspace per (device, stream), grown on demand and kept for the
+// life of the process (its control block must start zeroed; kernels keep it so).
+at::Tensor workspace_for(const at::Tensor &like, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<int, cudaStream_t>, at::Tensor> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair((int)like.device().index(), cur_stream(like));
+    auto it = cache.find(key);
+    if (it == cache.end() || (size_t)it->second.numel() < bytes) {
+        size_t cap = bytes < (1u << 20) ? (1u << 20) : bytes;
+        at::Tensor ws = at::zeros({(int64_t)cap}, like.options().dtype(at::kByte));
+        cache[key] = ws;
+        return ws;
+    }
+    return it->second;
+}
+
+// reference parameter_sweep sets (src/nanoquant/kernel/cuda/gemv_kernel.cu:351-354)
+void check_choice(const char *name, int64_t v, std::initializer_list<int64_t> allowed) {
+    bool found = false;
+    std::string choices;
+    for (int64_t a : allowed) {
+        if (a == v) found = true;
+        if (!choices.empty()) choices += ", ";
+        choices += std::to_string(a);
+    }
+    TORCH_CHECK_VALUE(found, name, " should be one of [", choices, "], but ", v, " was given");
+}
+
+int64_t gemm_min_rows() {
+    static int64_t v = [] {
+        const char *e = std::getenv("NQ_GEMM_MIN_ROWS");
+        return e ? std::atoll(e) : (int64_t)33;
+    }();
+    return v;
+}
+
+struct LayerArgs {
+    at::Tensor x, s2, vbits, s1;
+    std::optional<at::Tensor> smid;
+    at::Tensor ubits;
+    int64_t rows, in_f, rank, out_f;
+};
+
+LayerArgs check_layer(const at::Tensor &x, const at::Tensor &s2, const at::Tensor &vbits,
+                      const std::optional<at::Tensor> &smid, const at::Tensor &ubits, const at::Tensor &s1) {
+    const auto st = x.scalar_type();
+    dtype_code(st);
+    CHECK_CUDA_CONT(x, st);
+    CHECK_CUDA_CONT(s2, st);
+    CHECK_CUDA_CONT(s1, st);
+    CHECK_CUDA_CONT(vbits, at::kInt);
+    CHECK_CUDA_CONT(ubits, at::kInt);
+    TORCH_CHECK(x.dim() == 1 || x.dim() == 2, "x must be 1-D or 2-D [rows, in_features]");
+    LayerArgs a{x, s2, vbits, s1, std::nullopt, ubits, 0, 0, 0, 0};
+    a.rows = x.dim() == 1 ? 1 : x.size(0);
+    a.in_f = x.size(-1);
+    a.rank = vbits.size(0);
+    a.out_f = s1.numel();
+    TORCH_CHECK(vbits.dim() == 2 && vbits.size(1) == (a.in_f + 31) / 32, "V planes must be [rank, ceil(in/32)]");
+    TORCH_CHECK(ubits.dim() == 2 && ubits.size(0) == a.out_f && ubits.size(1) == (a.rank + 31) / 32,
+                "U planes must be [out, ceil(rank/32)]");
+    TORCH_CHECK(s2.numel() == a.in_f, "scale_pre size mismatch");
+    if (smid.has_value() && smid->defined()) {
+        CHECK_CUDA_CONT((*smid), st);
+        TORCH_CHECK(smid->numel() == a.rank, "scale_l size mismatch");
+        a.smid = *smid;
+    }
+    for (const at::Tensor *t : {&s2, &vbits, &ubits, &s1})
+        TORCH_CHECK(t->device() == x.device(), "all tensors must be on the same device");
+    return a;
+}
+
+at::Tensor run_gemv(const LayerArgs &a) {
+    c10::cuda::CUDAGuard guard(a.x.device());
+    auto y = at::empty({a.rows, a.out_f}, a.x.options());
+    const size_t wsb = nq_gemv_workspace_bytes(a.rows, a.rank);
+    at::Tensor ws = workspace_for(a.x, wsb);
+    NQ_TORCH_CHECK(nq_gemv(dtype_code(a.x.scalar_type()), a.x.data_ptr(), a.rows, a.in_f, a.s2.data_ptr(),
+                           a.vbits.data_ptr<int32_t>(), a.rank, a.smid ? a.smid->data_ptr() : nullptr,
+                           a.ubits.data_ptr<int32_t>(), a.out_f, a.s1.data_ptr(), y.data_ptr(), ws.data_ptr(),
+                           (size_t)ws.numel(), cur_stream(a.x)));
+    return y;
+}
+
+at::Tensor run_gemm(const LayerArgs &a, bool precise) {
+    c10::cuda::CUDAGuard guard(a.x.device());
+    auto y = at::empty({a.rows, a.out_f}, a.x.options());
+    const size_t wsb = nq_gemm_workspace_bytes(a.rows, a.rank);
+    at::Tensor ws = at::empty({(int64_t)wsb}, a.x.options().dtype(at::kByte));
+    NQ_TORCH_CHECK(nq_gemm(dtype_code(a.x.scalar_type()), a.x.data_ptr(), a.rows, a.in_f, a.s2.data_ptr(),
+                           a.vbits.data_ptr<int32_t>(), a.rank, a.smid ? a.smid->data_ptr() : nullptr,
+                           a.ubits.data_ptr<int32_t>(), a.out_f, a.s1.data_ptr(), precise ? 1 : 0, y.data_ptr(),
+                           ws.data_ptr(), wsb, cur_stream(a.x)));
+    return y;
+}
+
+bool gemm_ok(const LayerArgs &a) {
+    return a.rows >= gemm_min_rows() && a.in_f % 8 == 0 &&
+           (reinterpret_cast<uintptr_t>(a.x.data_ptr()) & 15) == 0;
+}
+
+at::Tensor forward_auto(const LayerArgs &a) {
+    at::Tensor y = gemm_ok(a) ? run_gemm(a, true) : run_gemv(a);
+    return a.x.dim() == 1 ? y.squeeze(0) : y;
+}
+
+// ------------------------------------------------------------------ binary_kernels (reference schemas)
+
+at::Tensor nanoquant_dyn_forward_cuda(const at::Tensor &x, const at::Tensor &scale_g, const at::Tensor &Ubits,
+                                      const std::optional<at::Tensor> &scale_l, const at::Tensor &Vbits,
+                                      const at::Tensor &scale_h, int64_t num_thread_stage1,
+                                      int64_t num_thread_stage2, int64_t num_row_per_warp_stage1,
+                                      int64_t num_row_per_warp_stage2, int64_t num_acc_stage1,
+                                      int64_t num_acc_stage2, int64_t num_pipeline_stage1,
+                                      int64_t num_pipeline_stage2) {
+    // The tuning knobs select among the reference's template instances; this build
+    // chooses its own launch shape but accepts and validates the same values.
+    check_choice("n_th1", num_thread_stage1, {64, 128, 256});
+    check_choice("n_rpw1", num_row_per_warp_stage1, {1, 2, 4, 8});
+    check_choice("n_acc1", num_acc_stage1, {1, 2});
+    check_choice("n_pipe1", num_pipeline_stage1, {1, 2, 4, 8, 16});
+    check_choice("n_th2", num_thread_stage2, {64, 128, 256});
+    check_choice("n_rpw2", num_row_per_warp_stage2, {1, 2, 4, 8});
+    check_choice("n_acc2", num_acc_stage2, {1, 2});
+    check_choice("n_pipe2", num_pipeline_stage2, {1, 2, 4, 8, 16});
+    // Argument names follow the reference op: Ubits = the module's V planes [rank, in/32],
+    // scale_l = scale_mid, Vbits = the module's U planes [out, rank/32], scale_h = scale_post.
+    return forward_auto(check_layer(x, scale_g, Ubits, scale_l, Vbits, scale_h));
+}
+
+at::Tensor nanoquant_dyn_forward_meta(const at::Tensor &x, const at::Tensor &scale_g, const at::Tensor &Ubits,
+                                      const std::optional<at::Tensor> &scale_l, const at::Tensor &Vbits,
+                                      const at::Tensor &scale_h, int64_t, int64_t, int64_t, int64_t, int64_t,
+                                      int64_t, int64_t, int64_t) {
+    auto shape = x.sizes().vec();
+    shape.back() = scale_h.size(0);
+    return at::empty(shape, x.options());
+}
+
+// ------------------------------------------------------------------ nq_b200 namespace
+
+at::Tensor pack_signs_cuda(const at::Tensor &signs, const std::string &method, bool check) {
+    TORCH_CHECK_TYPE(signs.scalar_type() == at::kChar, "Input tensor must be int8.");
+    TORCH_CHECK(signs.is_cuda(), "signs must be a CUDA tensor");
+    TORCH_CHECK(signs.dim() == 2, "signs must be 2-D [rows, cols]");
+    const int order = order_code(method);
+    c10::cuda::CUDAGuard guard(signs.device());
+    at::Tensor s = signs.contiguous();
+    const int64_t rows = s.size(0), cols = s.size(1);
+    auto out = at::empty({rows, (cols + 31) / 32}, s.options().dtype(at::kInt));
+    if (rows == 0 || cols == 0) return out;
+    at::Tensor bad;
+    if (check) bad = at::zeros({1}, s.options().dtype(at::kInt));
+    NQ_TORCH_CHECK(nq_pack_signs(s.data_ptr<int8_t>(), rows, cols, order, out.data_ptr<int32_t>(),
+                                 check ? bad.data_ptr<int32_t>() : nullptr, cur_stream(s)));
+    if (check) {
+        const int n = bad.item<int>();
+        TORCH_CHECK_VALUE(n == 0, "Cannot pack: factors must contain only -1 and +1 (", n, " other values)");
+    }
+    return out;
+}
+
+at::Tensor pack_signs_meta(const at::Tensor &signs, const std::string &method, bool check) {
+    order_code(method);
+    return at::empty({signs.size(0), (signs.size(1) + 31) / 32}, signs.options().dtype(at::kInt));
+}
+
+at::Tensor unpack_signs_cuda(const at::Tensor &packed, int64_t rows, int64_t cols, const std::string &method) {
+    TORCH_CHECK_VALUE(packed.dim() == 2, "Unsupported packed tensor format. Expected 2D tensor, got ", packed.dim(),
+                      " dimensions.");
+    TORCH_CHECK_VALUE(packed.size(0) == rows && packed.size(1) == (cols + 31) / 32,
+                      "Unsupported packed tensor shape. Expected (", rows, ", ", (cols + 31) / 32, "), got ",
+                      packed.sizes());
+    const int order = order_code(method);
+    CHECK_CUDA_CONT(packed, at::kInt);
+    c10::cuda::CUDAGuard guard(packed.device());
+    auto out = at::empty({rows, cols}, packed.options().dtype(at::kChar));
+    if (rows == 0 || cols == 0) return out;
+    NQ_TORCH_CHECK(nq_unpack_signs(packed.data_ptr<int32_t>(), rows, cols, order, out.data_ptr<int8_t>(),
+                                   cur_stream(packed)));
+    return out;
+}
+
+at::Tensor unpack_signs_meta(const at::Tensor &packed, int64_t rows, int64_t cols, const std::string &method) {
+    return at::empty({rows, cols}, packed.options().dtype(at::kChar));
+}
+
+at::Tensor repack_signs_cuda(const at::Tensor &packed, int64_t cols, const std::string &src_method,
+                             const std::string &dst_method) {
+    CHECK_CUDA_CONT(packed, at::kInt);
+    TORCH_CHECK(packed.dim() == 2 && packed.size(1) == (cols + 31) / 32, "packed must be [rows, ceil(cols/32)]");
+    const int so = order_code(src_method), dso = order_code(dst_method);
+    c10::cuda::CUDAGuard guard(packed.device());
+    auto out = at::empty_like(packed);
+    if (packed.numel() == 0) return out;
+    NQ_TORCH_CHECK(nq_repack_signs(packed.data_ptr<int32_t>(), packed.size(0), cols, so, dso, out.data_ptr<int32_t>(),
+                                   cur_stream(packed)));
+    return out;
+}
+
+at::Tensor repack_signs_meta(const at::Tensor &packed, int64_t, const std::string &, const std::string &) {
+    return at::empty_like(packed);
+}
+
+at::Tensor gemv_cuda(const at::Tensor &x, const at::Tensor &s2, const at::Tensor &vbits,
+                     const std::optional<at::Tensor> &smid, const at::Tensor &ubits, const at::Tensor &s1) {
+    auto a = check_layer(x, s2, vbits, smid, ubits, s1);
+    at::Tensor y = run_gemv(a);
+    return x.dim() == 1 ? y.squeeze(0) : y;
+}
+
+at::Tensor gemm_cuda(const at::Tensor &x, const at::Tensor &s2, const at::Tensor &vbits,
+                     const std::optional<at::Tensor> &smid, const at::Tensor &ubits, const at::Tensor &s1,
+                     bool precise) {
+    auto a = check_layer(x, s2, vbits, smid, ubits, s1);
+    at::Tensor y = run_gemm(a, precise);
+    return x.dim() == 1 ? y.squeeze(0) : y;
+}
+
+at::Tensor linear_cuda(const at::Tensor &x, const at::Tensor &s2, const at::Tensor &vbits,
+                       const std::optional<at::Tensor> &smid, const at::Tensor &ubits, const at::Tensor &s1) {
+    return forward_auto(check_layer(x, s2, vbits, smid, ubits, s1));
+}
+
+at::Tensor layer_meta(const at::Tensor &x, const at::Tensor &, const at::Tensor &, const std::optional<at::Tensor> &,
+                      const at::Tensor &, const at::Tensor &s1) {
+    auto shape = x.sizes().vec();
+    shape.back() = s1.numel();
+    return at::empty(shape, x.options());
+}
+
+at::Tensor gemm_meta(const at::Tensor &x, const at::Tensor &s2, const at::Tensor &v, const std::optional<at::Tensor> &m,
+                     const at::Tensor &u, const at::Tensor &s1, bool) {
+    return layer_meta(x, s2, v, m, u, s1);
+}
+
+}  // namespace
+
+TORCH_LIBRARY(binary_kernels, m) {
+    m.def(
+        "nanoquant_dyn_forward("
+        "Tensor x, Tensor scale_g, Tensor Ubits, Tensor? scale_l, Tensor Vbits, Tensor scale_h, "
+        "int num_thread_stage1=128, int num_thread_stage2=128, int num_row_per_warp_stage1=2, "
+        "int num_row_per_warp_stage2=2, int num_acc_stage1=4, int num_acc_stage2=4, "
+        "int num_pipeline_stage1=2, int num_pipeline_stage2=2) -> Tensor");
+    m.def(
+        "marlin_onebit_forward("
+        "Tensor x, Tensor weight, Tensor? scale_g, Tensor? scale_h, Tensor(a!) workspace) -> Tensor");
+    m.def(
+        "marlin_nanoquant_forward("
+        "Tensor x, Tensor weight_u, Tensor weight_v, Tensor? scale_g, Tensor? scale_l, Tensor? scale_h, "
+        "Tensor(a!) workspace) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(binary_kernels, CUDA, m) { m.impl("nanoquant_dyn_forward", &nanoquant_dyn_forward_cuda); }
+
+TORCH_LIBRARY_IMPL(binary_kernels, Meta, m) { m.impl("nanoquant_dyn_forward", &nanoquant_dyn_forward_meta); }
+
+TORCH_LIBRARY(nq_b200, m) {
+    m.def("pack_signs(Tensor signs, str method='lsb_first', bool check=False) -> Tensor");
+    m.def("unpack_signs(Tensor packed, int rows, int cols, str method='lsb_first') -> Tensor");
+    m.def("repack_signs(Tensor packed, int cols, str src_method, str dst_method) -> Tensor");
+    m.def(
+        "gemv(Tensor x, Tensor scale_pre, Tensor v_bits, Tensor? scale_mid, Tensor u_bits, Tensor scale_post) -> "
+        "Tensor");
+    m.def(
+        "gemm(Tensor x, Tensor scale_pre, Tensor v_bits, Tensor? scale_mid, Tensor u_bits, Tensor scale_post, "
+        "bool precise=True) -> Tensor");
+    m.def(
+        "linear(Tensor x, Tensor scale_pre, Tensor v_bits, Tensor? scale_mid, Tensor u_bits, Tensor scale_post) -> "
+        "Tensor");
+}
+
+TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
+    m.impl("pack_signs", &pack_signs_cuda);
+    m.impl("unpack_signs", &unpack_signs_cuda);
+    m.impl("repack_signs", &repack_signs_cuda);
+    m.impl("gemv", &gemv_cuda);
+    m.impl("gemm", &gemm_cuda);
+    m.impl("linear", &linear_cuda);
+}
+
+TORCH_LIBRARY_IMPL(nq_b200, Meta, m) {
+    m.impl("pack_signs", &pack_signs_meta);
+    m.impl("unpack_signs", &unpack_signs_meta);
+    m.impl("repack_signs", &repack_signs_meta);
+    m.impl("gemv", &layer_meta);
+    m.impl("gemm", &gemm_meta);
+    m.impl("linear", &layer_meta);
+}

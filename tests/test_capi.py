@@ -1,0 +1,79 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol the header
+declares, and rejects bad arguments on the host before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from nanoquant_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "nq_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"NQ_API\s+[\w\s\*]*?\b(nq_\w+)\s*\(", text)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_symbols()
+    for n in ("nq_pack_signs", "nq_unpack_signs", "nq_repack_signs", "nq_gemv", "nq_gemv_workspace_bytes",
+              "nq_gemm", "nq_gemm_workspace_bytes", "nq_workspace_reset", "nq_workspace_status"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.CUDA_LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert set(declared_symbols()) <= set(_lib._SIGNATURES)
+
+
+def test_status_strings_and_version():
+    lib = _lib.cuda_lib()
+    assert lib.nq_abi_version() == 1
+    assert lib.nq_status_string(0) == b"ok"
+    assert b"timed out" in lib.nq_status_string(_lib.NQ_ERR_DEVICE_TIMEOUT)
+
+
+def test_workspace_sizes():
+    lib = _lib.cuda_lib()
+    assert lib.nq_gemv_workspace_bytes(1, 1126) == 256 + ((8 * 1126 * 4 + 255) // 256) * 256
+    assert lib.nq_gemv_workspace_bytes(64, 1126) == lib.nq_gemv_workspace_bytes(1, 1126)
+    assert lib.nq_gemv_workspace_bytes(1, 0) == 0
+    assert lib.nq_gemm_workspace_bytes(2048, 2054) >= 256
+
+
+@pytest.mark.parametrize("case", ["null_x", "bad_dtype", "zero_batch", "small_ws"])
+def test_gemv_rejects_bad_arguments_on_host(case):
+    lib = _lib.cuda_lib()
+    fake = ctypes.c_void_p(0x10000)  # never dereferenced: validation fails first
+    args = dict(dtype=0, x=fake, batch=1, in_f=64, s2=fake, vb=fake, rank=16, smid=None, ub=fake, out_f=32,
+                s1=fake, y=fake, ws=fake, wsb=lib.nq_gemv_workspace_bytes(1, 16))
+    expect = {"null_x": _lib.NQ_ERR_INVALID_ARGUMENT, "bad_dtype": _lib.NQ_ERR_UNSUPPORTED,
+              "zero_batch": _lib.NQ_ERR_INVALID_ARGUMENT, "small_ws": _lib.NQ_ERR_WORKSPACE}[case]
+    if case == "null_x":
+        args["x"] = None
+    elif case == "bad_dtype":
+        args["dtype"] = 7
+    elif case == "zero_batch":
+        args["batch"] = 0
+    else:
+        args["wsb"] = 16
+    st = lib.nq_gemv(args["dtype"], args["x"], args["batch"], args["in_f"], args["s2"], args["vb"], args["rank"],
+                     args["smid"], args["ub"], args["out_f"], args["s1"], args["y"], args["ws"], args["wsb"], None)
+    assert st == expect
+    assert lib.nq_last_error_message()
+
+
+def test_pack_rejects_bad_arguments_on_host():
+    lib = _lib.cuda_lib()
+    fake = ctypes.c_void_p(0x10000)
+    assert lib.nq_pack_signs(None, 2, 2, 0, fake, None, None) == _lib.NQ_ERR_INVALID_ARGUMENT
+    assert lib.nq_pack_signs(fake, 0, 2, 0, fake, None, None) == _lib.NQ_ERR_INVALID_ARGUMENT
+    assert lib.nq_pack_signs(fake, 2, 2, 5, fake, None, None) == _lib.NQ_ERR_INVALID_ARGUMENT
+    assert lib.nq_unpack_signs(fake, 2, -1, 0, fake, None) == _lib.NQ_ERR_INVALID_ARGUMENT
+    assert lib.nq_repack_signs(fake, 2, 2, 0, 9, fake, None) == _lib.NQ_ERR_INVALID_ARGUMENT
+    with pytest.raises(_lib.NQError):
+        _lib.check(_lib.NQ_ERR_INVALID_ARGUMENT)

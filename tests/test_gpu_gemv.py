@@ -1,0 +1,136 @@
+"""Fused decode GEMV parity on the GPU against the reference goldens and the float64
+oracle.  Tolerance (written in nq_testutil.assert_close_to_oracle): rel-L2 <= 1e-3 per
+layer against the oracle rounded to the output dtype, and for fp16 also against the
+unrounded float64 oracle."""
+import numpy as np
+import pytest
+import torch
+
+import nanoquant_b200 as nq
+from oracle import oracle as orc
+
+from .golden_data import GOLDEN, layer_from_golden
+from .nq_testutil import DeviceLayer, assert_close_to_oracle, capi_gemv, workspace_status
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name,dtype", [("ragged_b8", "f16"), ("attn_small", "bf16")])
+def test_gemv_reference_golden(name, dtype):
+    d = DeviceLayer(layer_from_golden(name), dtype)
+    y, ws = capi_gemv(d)
+    torch.cuda.synchronize()
+    assert_close_to_oracle(y, GOLDEN[f"layer_{name}_y"].astype(np.float64), dtype)
+    assert workspace_status(ws) == 0
+
+
+def test_gemv_config0_reference_golden():
+    seed, out_f, in_f, rank, batch = (int(v) for v in GOLDEN["cfg0_meta"])
+    d = DeviceLayer(orc.make_layer(seed, out_f, in_f, rank, batch, "f16"), "f16")
+    y, _ = capi_gemv(d)
+    assert_close_to_oracle(y, GOLDEN["cfg0_y"].astype(np.float64), "f16")
+
+
+SHAPES = [  # (out, in, rank): Llama-2-7B layers at the benchmark ranks and the reference-formula ranks
+    (4096, 4096, 1126), (11008, 4096, 2054), (4096, 11008, 2054), (4096, 4096, 1088), (11008, 4096, 1600),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("batch", [1, 8])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_gemv_llama_shapes(shape, batch, dtype):
+    out_f, in_f, rank = shape
+    L = orc.make_layer(out_f + rank + batch, out_f, in_f, rank, batch, dtype, with_mid=(batch == 8))
+    d = DeviceLayer(L, dtype)
+    y, ws = capi_gemv(d)
+    assert_close_to_oracle(y, d.oracle(), dtype)
+    assert workspace_status(ws) == 0
+
+
+@pytest.mark.parametrize("batch", [2, 3, 4, 5])
+def test_gemv_batch_sizes(batch):
+    L = orc.make_layer(batch, 4096, 4096, 1126, batch, "f16", with_mid=True)
+    d = DeviceLayer(L, "f16")
+    y, _ = capi_gemv(d)
+    assert_close_to_oracle(y, d.oracle(), "f16")
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1), (7, 5, 3), (100, 70, 33), (33, 130, 17), (17, 8, 40), (1000, 200, 96),
+                                   (130, 96, 47)])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_gemv_ragged_shapes(shape, dtype):
+    out_f, in_f, rank = shape
+    L = orc.make_layer(sum(shape), out_f, in_f, rank, 3, dtype, with_mid=True)
+    d = DeviceLayer(L, dtype)
+    y, _ = capi_gemv(d)
+    assert_close_to_oracle(y, d.oracle(), dtype)
+
+
+def test_gemv_batch_above_eight_runs_in_chunks():
+    L = orc.make_layer(21, 1024, 512, 200, 19, "bf16", with_mid=False)
+    d = DeviceLayer(L, "bf16")
+    y, _ = capi_gemv(d)
+    assert_close_to_oracle(y, d.oracle(), "bf16")
+
+
+def test_gemv_split_mode_for_large_layer():
+    """70B down-projection geometry exceeds the fused shared-memory budget and runs as
+    two launches; results must be identical in quality."""
+    L = orc.make_layer(70, 8192, 28672, 3488, 1, "bf16")
+    d = DeviceLayer(L, "bf16")
+    y, ws = capi_gemv(d)
+    assert_close_to_oracle(y, d.oracle(), "bf16")
+    assert workspace_status(ws) == 0
+
+
+def test_gemv_deterministic_and_workspace_reusable():
+    L = orc.make_layer(5, 11008, 4096, 2054, 2, "f16")
+    d = DeviceLayer(L, "f16")
+    y1, ws = capi_gemv(d)
+    outs = [capi_gemv(d, workspace=ws)[0] for _ in range(5)]
+    for y in outs:
+        assert torch.equal(y, y1)
+    assert workspace_status(ws) == 0
+
+
+def test_gemv_fp16_clamp_matches_reference():
+    """Outputs beyond the fp16 range clamp to +-64504 (reference cuda_utils.cuh:80-86)."""
+    L = orc.make_layer(9, 64, 256, 32, 1, "f16", s1_std=1.0)
+    L.s1[:] = 60000.0
+    d = DeviceLayer(L, "f16")
+    y, _ = capi_gemv(d)
+    ref = d.oracle()
+    yk = y.float().cpu().numpy()
+    big = np.abs(ref) > 64504
+    assert big.any()
+    np.testing.assert_array_equal(np.abs(yk[big]), 64504.0)
+
+
+def test_reference_op_and_module_drop_in():
+    """torch.ops.binary_kernels.nanoquant_dyn_forward with the reference's argument order
+    and knobs, and the module's gemv / b200 kernel types."""
+    L = orc.make_layer(3, 4096, 4096, 1126, 4, "f16", with_mid=True)
+    d = DeviceLayer(L, "f16")
+    y = torch.ops.binary_kernels.nanoquant_dyn_forward(d.x, d.s2, d.vb, d.smid, d.ub, d.s1, 128, 128, 2, 2, 1, 1,
+                                                       8, 8)
+    ref = d.oracle()
+    assert_close_to_oracle(y, ref, "f16")
+    with pytest.raises(ValueError):  # the reference's own schema default num_acc=4 is outside its sweep
+        torch.ops.binary_kernels.nanoquant_dyn_forward(d.x, d.s2, d.vb, d.smid, d.ub, d.s1)
+    # 1-D input -> 1-D output, like the reference
+    y1 = torch.ops.binary_kernels.nanoquant_dyn_forward(d.x[0], d.s2, d.vb, d.smid, d.ub, d.s1, 128, 128, 2, 2, 1,
+                                                        1, 8, 8)
+    assert y1.shape == (4096,)
+    # the module: dense factors in, prepared for "gemv"
+    m = nq.NanoQuantLinear.from_factors(torch.from_numpy(L.V).cuda().float(), torch.from_numpy(L.U).cuda().float(),
+                                        d.s2.float(), d.s1.float(), d.smid.float())
+    for kt in ("gemv", "b200"):
+        m2 = nq.NanoQuantLinear.from_factors(torch.from_numpy(L.V).cuda().float(),
+                                             torch.from_numpy(L.U).cuda().float(), d.s2.float(), d.s1.float(),
+                                             d.smid.float())
+        m2._prepare_kernel(kt, torch.float16)
+        y3 = m2(d.x.view(2, 2, -1))
+        assert y3.shape == (2, 2, 4096)
+        assert_close_to_oracle(y3.view(4, -1), ref, "f16")
+    assert m is not None
