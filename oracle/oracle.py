@@ -120,6 +120,21 @@ def forward(x, s2, v_bits, rank, smid, u_bits, s1, method: str = "lsb_first", re
     return (y, t) if return_interm else y
 
 
+def forward_dense(x, s2, V, smid, U, s1, round_t: Optional[str] = None):
+    """float64 BLAS form of the same math on dense +-1 factors V [rank, in], U [out, rank]
+    (linear.py:282-291), for large batches.  ``round_t`` rounds the intermediate
+    t = smid * (V (s2 * x)) to "bf16"/"f16" first, emulating a kernel that stores it at
+    that precision (the reference's own fp16/bf16 intermediate, gemm.cpp:119)."""
+    x = np.atleast_2d(np.asarray(x, dtype=np.float64))
+    t = (x * np.asarray(s2, dtype=np.float64).reshape(1, -1)) @ np.asarray(V, dtype=np.float64).T
+    if smid is not None:
+        t = t * np.asarray(smid, dtype=np.float64).reshape(1, -1)
+    if round_t is not None:
+        t = round_to(t.astype(np.float32), round_t).astype(np.float64)
+    y = t @ np.asarray(U, dtype=np.float64).T
+    return y * np.asarray(s1, dtype=np.float64).reshape(1, -1)
+
+
 def dense_forward_torch(x, s2, V, smid, U, s1):
     """The reference CPU path: _compute_forward on dense +-1 factors (linear.py:282-291)."""
     import torch.nn.functional as F

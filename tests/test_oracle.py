@@ -73,3 +73,11 @@ def test_generator_is_deterministic():
     assert abs(a.mean()) < 0.1 and 0.9 < a.std() < 1.1
     s = orc.random_signs(9, 100, 100)
     assert set(np.unique(s)) == {-1, 1} and abs(s.mean()) < 0.05
+
+
+@pytest.mark.parametrize("name", LAYER_NAMES)
+def test_dense_float64_form_matches_packed_oracle(name):
+    L = layer_from_golden(name)
+    y = orc.forward_dense(L.x, L.s2, L.V, L.smid, L.U, L.s1)
+    assert orc.rel_l2(y, L.reference("lsb_first")) < 1e-12
+    assert orc.rel_l2(y, GOLDEN[f"layer_{name}_y"]) < 2e-6
