@@ -48,7 +48,7 @@ struct Params {
     const uint32_t *ubits;    // [out, wu]
     const void *s1;           // [out]
     void *y;                  // [batch, out]
-    float *interm;            // [batch, rank]
+    float *interm;            // [batch, ldi], ldi = kb2 * 64 >= rank
     Ctrl *ctrl;
     int batch, in_f, rank, out_f;
     int wv, wu;               // words per V row / U row
@@ -109,20 +109,28 @@ __device__ __forceinline__ void load16_smem(const void *p, uint32_t (&v)[8]) {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-// Issue the bulk copy of rows [r0, r1) of a plane with `w` words per row into smem.
-// The 16-byte-multiple prefix goes through the TMA engine (signalled on `bar`),
-// the remaining <16 bytes are copied by plain loads (caller syncs afterwards).
-__device__ __forceinline__ void issue_slab(uint32_t *dst, const uint32_t *plane, int r0, int r1, int w,
-                                           uint64_t *bar, bool leader) {
+// Bytes of the 16-byte-multiple prefix of rows [r0, r1) of a plane with `w` words per row.
+__device__ __forceinline__ uint32_t slab_bulk_bytes(int r0, int r1, int w) {
     const uint32_t words = (r1 > r0) ? (uint32_t)(r1 - r0) * (uint32_t)w : 0u;
-    const uint32_t bytes = words * 4u;
-    const uint32_t bulk = bytes & ~15u;
+    return (words * 4u) & ~15u;
+}
+
+// Rows [r0, r1) of a plane -> smem: the 16-byte-multiple prefix through the TMA engine
+// (leader thread, completion on `bar`), the remaining <16 bytes by plain loads.
+__device__ __forceinline__ void copy_slab(uint32_t *dst, const uint32_t *plane, int r0, int r1, int w, uint64_t *bar,
+                                          bool leader) {
+    const uint32_t words = (r1 > r0) ? (uint32_t)(r1 - r0) * (uint32_t)w : 0u;
+    const uint32_t bulk = (words * 4u) & ~15u;
     const uint32_t *src = plane + (size_t)r0 * w;
-    if (leader) {
-        mbar_arrive_expect_tx(bar, bulk);
-        if (bulk) bulk_g2s_pieces(dst, src, bulk, bar);
-    }
+    if (leader && bulk) bulk_g2s_pieces(dst, src, bulk, bar);
     for (uint32_t i = bulk / 4 + threadIdx.x; i < words; i += kThreads) dst[i] = __ldg(src + i);
+}
+
+// Zero the padding columns [n, npad) of a staged 16-bit row.
+template <typename T>
+__device__ __forceinline__ void zero_tail(T *dst, int n, int npad) {
+    uint16_t *d = reinterpret_cast<uint16_t *>(dst);
+    for (int c = n + threadIdx.x; c < npad; c += kThreads) d[c] = 0;
 }
 
 template <typename T>
@@ -149,6 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     const int r2b = 16 * t2b, r2e = min(16 * t2e, p.out_f);
     const bool has1 = r1e > r1b, has2 = r2e > r2b;
     const int in_pad = p.kb1 * 64;
+    const int ldi = p.kb2 * 64;  // interm row stride (floats), a multiple of 64 and >= rank
 
     if (tid == 0) {
         mbar_init(&bars[0], 1);
@@ -156,14 +165,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         fence_mbar_init();
     }
     __syncthreads();
-    // Put every weight byte of this CTA in flight before anything else.
-    if (has1) issue_slab(vch, p.vbits, r1b, r1e, p.wv, &bars[0], tid == 0);
-    if (has2) issue_slab(uch, p.ubits, r2b, r2e, p.wu, &bars[1], tid == 0);
+    // Put every byte this CTA needs in flight before anything else: V slab, s2 and x rows
+    // (when 16-byte aligned) on barrier 0, the U slab on barrier 1.
+    const bool vec_rows = ((reinterpret_cast<uintptr_t>(p.s2) | reinterpret_cast<uintptr_t>(p.x)) & 15) == 0 &&
+                          (p.in_f % 8) == 0;
     if (has1) {
-        stage_row<T>(s2s, static_cast<const T *>(p.s2), p.in_f, in_pad);
-        if (p.x_in_smem)
-            for (int b = 0; b < p.batch; ++b)
-                stage_row<T>(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f, p.in_f, in_pad);
+        uint32_t bytes0 = slab_bulk_bytes(r1b, r1e, p.wv);
+        if (vec_rows) bytes0 += (uint32_t)p.in_f * 2u * (1u + (p.x_in_smem ? (uint32_t)p.batch : 0u));
+        if (tid == 0) mbar_arrive_expect_tx(&bars[0], bytes0);
+        copy_slab(vch, p.vbits, r1b, r1e, p.wv, &bars[0], tid == 0);
+        if (vec_rows) {
+            if (tid == 0) {
+                bulk_g2s_pieces(s2s, p.s2, (uint32_t)p.in_f * 2u, &bars[0]);
+                if (p.x_in_smem)
+                    for (int b = 0; b < p.batch; ++b)
+                        bulk_g2s_pieces(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f,
+                                        (uint32_t)p.in_f * 2u, &bars[0]);
+            }
+            zero_tail<T>(s2s, p.in_f, in_pad);
+            if (p.x_in_smem)
+                for (int b = 0; b < p.batch; ++b) zero_tail<T>(xs + (size_t)b * in_pad, p.in_f, in_pad);
+        } else {
+            stage_row<T>(s2s, static_cast<const T *>(p.s2), p.in_f, in_pad);
+            if (p.x_in_smem)
+                for (int b = 0; b < p.batch; ++b)
+                    stage_row<T>(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f, p.in_f,
+                                 in_pad);
+        }
+    }
+    if (has2) {
+        if (tid == 0) mbar_arrive_expect_tx(&bars[1], slab_bulk_bytes(r2b, r2e, p.wu));
+        copy_slab(uch, p.ubits, r2b, r2e, p.wu, &bars[1], tid == 0);
     }
     __syncthreads();
 
@@ -221,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 const int k = 16 * tile + row;
                 if (k < p.rank) {
                     if (p.smid) s *= E::to_f(static_cast<const T *>(p.smid)[k]);
-                    p.interm[(size_t)b * p.rank + k] = s;
+                    p.interm[(size_t)b * ldi + k] = s;
                 }
             }
             __syncthreads();
@@ -237,12 +269,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles (hi/lo per batch row)
         const int kp2 = p.kb2 * 64;
         const int bstride = kp2 + 8;  // +16 B per column row: conflict-free 128-bit loads
-        for (int idx = tid; idx < nt * 8 * kp2; idx += kThreads) {
-            const int col = idx / kp2, k = idx - col * kp2;
-            const int b = (col >> 3) * 4 + ((col & 7) >> 1);
-            const float v = (b < p.batch && k < p.rank) ? __ldcg(p.interm + (size_t)b * p.rank + k) : 0.f;
-            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-            bsm[(size_t)col * bstride + k] = (col & 1) ? __float2bfloat16_rn(v - __bfloat162float(hi)) : hi;
+        // B operand: column 2b holds bf16(t[b]) and column 2b+1 the bf16 remainder, for
+        // b < 4 * nt.  Loads are issued in batches of 8 independent float4 per thread.
+        const int items = nt * 4 * (kp2 / 4);  // (batch row, 4-column chunk) pairs
+        for (int base = 0; base < items; base += 8 * kThreads) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int it = base + u * kThreads + tid;
+                const int b = it / (kp2 / 4), c4 = it - b * (kp2 / 4);
+                v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (it < items && b < p.batch && 4 * c4 < p.rank)
+                    v[u] = __ldcg(reinterpret_cast<const float4 *>(p.interm + (size_t)b * ldi) + c4);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int it = base + u * kThreads + tid;
+                if (it >= items) continue;
+                const int b = it / (kp2 / 4), c4 = it - b * (kp2 / 4);
+                const int k = 4 * c4;
+                const float f[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                uint32_t hi[2], lo[2];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    float a = (k + 2 * j < p.rank) ? f[2 * j] : 0.f;
+                    float c = (k + 2 * j + 1 < p.rank) ? f[2 * j + 1] : 0.f;
+                    const __nv_bfloat16 ha = __float2bfloat16_rn(a), hc = __float2bfloat16_rn(c);
+                    const __nv_bfloat16 la = __float2bfloat16_rn(a - __bfloat162float(ha));
+                    const __nv_bfloat16 lc = __float2bfloat16_rn(c - __bfloat162float(hc));
+                    hi[j] = (uint32_t)__bfloat16_as_ushort(ha) | ((uint32_t)__bfloat16_as_ushort(hc) << 16);
+                    lo[j] = (uint32_t)__bfloat16_as_ushort(la) | ((uint32_t)__bfloat16_as_ushort(lc) << 16);
+                }
+                const int col = (b >> 2) * 8 + 2 * (b & 3);
+                *reinterpret_cast<uint2 *>(bsm + (size_t)col * bstride + k) = make_uint2(hi[0], hi[1]);
+                *reinterpret_cast<uint2 *>(bsm + (size_t)(col + 1) * bstride + k) = make_uint2(lo[0], lo[1]);
+            }
         }
         __syncthreads();
         if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
@@ -431,7 +492,8 @@ extern "C" {
 size_t nq_gemv_workspace_bytes(int64_t batch, int64_t rank) {
     (void)batch;  // batches above 8 reuse the same 8-row interm buffer, launch after launch
     if (rank <= 0) return 0;
-    const size_t interm = (size_t)nq::gemv::kMaxBatch * (size_t)rank * sizeof(float);
+    const size_t ldi = (size_t)((rank + 63) / 64) * 64;  // >= kb2 * 64 for every rank
+    const size_t interm = (size_t)nq::gemv::kMaxBatch * ldi * sizeof(float);
     return sizeof(nq::Ctrl) + ((interm + 255) & ~size_t(255));
 }
 
