@@ -21,9 +21,8 @@ constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
 
 // Workspace control block (first 256 bytes of a GEMV/GEMM workspace).
 struct Ctrl {
-    unsigned int bar_count;  // grid-barrier arrivals in the current generation
-    unsigned int bar_gen;    // grid-barrier generation
-    int status;              // first device-side error (nq_status), 0 if none
+    unsigned long long arrivals;  // grid-barrier arrivals, monotonic (never reset)
+    int status;                   // first device-side error (nq_status), 0 if none
     unsigned int pad[61];
 };
 static_assert(sizeof(Ctrl) == 256, "control block is 256 bytes");
@@ -125,41 +124,46 @@ __device__ __forceinline__ void bulk_g2s_pieces(void *dst, const void *src, uint
     }
 }
 
-__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int *p) {
-    unsigned int v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
-__device__ __forceinline__ void st_release_gpu(unsigned int *p, unsigned int v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ unsigned long long atom_add_release_gpu_u64(unsigned long long *p, unsigned long long v) {
+    unsigned long long old;
+    asm volatile("atom.add.release.gpu.global.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
 }
 
-// Self-resetting grid barrier for a cooperative launch (all CTAs co-resident).
-// `ctrl->bar_count` must be 0 before the first use; it is 0 again after each use.
+// Grid barrier for a cooperative launch (all CTAs co-resident).  Arrivals increment a
+// monotonic 64-bit counter; the barrier of arrival `old` completes when the counter
+// reaches the next multiple of `nblocks`, so the last arrival releases everybody with
+// its own atomic and nothing has to be reset (the counter starts at 0 with the
+// workspace and every launch adds exactly `nblocks`).  Pollers back off with nanosleep.
 // Bounded: gives up after kWaitTimeoutNs, records NQ_ERR_DEVICE_TIMEOUT, returns false.
 __device__ __forceinline__ bool grid_barrier(Ctrl *ctrl, unsigned int nblocks) {
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
         int ok = 1;
-        const unsigned int gen = ld_acquire_gpu(&ctrl->bar_gen);
         __threadfence();
-        const unsigned int arrived = atomicAdd(&ctrl->bar_count, 1u) + 1u;
-        if (arrived == nblocks) {
-            atomicExch(&ctrl->bar_count, 0u);
-            __threadfence();
-            st_release_gpu(&ctrl->bar_gen, gen + 1u);
-        } else {
+        const unsigned long long old = atom_add_release_gpu_u64(&ctrl->arrivals, 1ull);
+        const unsigned long long target = (old / nblocks + 1ull) * nblocks;
+        if (old + 1ull < target) {
             const uint64_t t0 = globaltimer_ns();
-            while (ld_acquire_gpu(&ctrl->bar_gen) == gen) {
+            unsigned int ns = 20;
+            while (ld_acquire_gpu_u64(&ctrl->arrivals) < target) {
                 if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
                     record_status(&ctrl->status, NQ_ERR_DEVICE_TIMEOUT);
                     ok = 0;
                     break;
                 }
+                __nanosleep(ns);
+                if (ns < 160) ns += 20;
             }
         }
+        __threadfence();
         s_ok = ok;
     }
     __syncthreads();

@@ -28,12 +28,14 @@
 //    the stages.  The barrier resets itself, so the workspace stays reusable.
 // Layers too large for the per-CTA shared-memory budget run the same kernel as two
 // ordinary launches (stage 1 then stage 2, one 16-row tile per CTA).
+#include <algorithm>
+
 #include "nq_common.cuh"
 
 namespace nq {
 namespace gemv {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxBatch = 8;
 constexpr int kStaticSmemReserve = 1024;  // static __shared__ of the kernel (grid barrier flag)
@@ -56,12 +58,12 @@ struct Params {
     int tiles1, tiles2;       // 16-row tiles per stage
     int mode;
     int x_in_smem;
-    uint32_t off_red, off_s2, off_x, off_v, off_u, off_b;
+    uint32_t off_red, off_s2, off_x, off_v, off_u;
 };
 
 __device__ __forceinline__ void tile_range(int tiles, int c, int G, int &b, int &e) {
-    b = (int)(((long long)tiles * c) / G);
-    e = (int)(((long long)tiles * (c + 1)) / G);
+    b = (tiles * c) / G;  // tiles <= 2^16 and G <= 2^10 keep this within 32 bits
+    e = (tiles * (c + 1)) / G;
 }
 
 // Copy `n` 16-bit values into a zero-padded shared row of `npad` values.
@@ -133,6 +135,48 @@ __device__ __forceinline__ void zero_tail(T *dst, int n, int npad) {
     for (int c = n + threadIdx.x; c < npad; c += kThreads) d[c] = 0;
 }
 
+// Per-warp work item: one 16-row tile over a contiguous range of 64-column K blocks.
+// Items of a CTA are (tile, K slice) pairs with KS slices per tile, KS = max(1, warps / tiles),
+// so every warp has work whatever the tile count; partial 16x8 tiles meet in `red`.
+__device__ __forceinline__ void item_of(int item, int KS, int kb, int &lt, int &kbeg, int &kend) {
+    lt = item / KS;
+    const int ks = item - lt * KS;
+    kbeg = (kb * ks) / KS;
+    kend = (kb * (ks + 1)) / KS;
+}
+
+__device__ __forceinline__ void store_partial(float *r, const float (&acc)[4], int g, int t) {
+    r[g * 8 + 2 * t] = acc[0];
+    r[g * 8 + 2 * t + 1] = acc[1];
+    r[(g + 8) * 8 + 2 * t] = acc[2];
+    r[(g + 8) * 8 + 2 * t + 1] = acc[3];
+}
+
+// 16 consecutive floats of t (fp32, L2-resident) as 8 bf16 pairs of their hi or lo part;
+// values at k >= rank read as zero (the buffer beyond rank holds other layers' data).
+__device__ __forceinline__ void load_t_pairs(const float *row, int kc, int rank, bool lo, uint32_t (&v)[8]) {
+    float f[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float4 a = __ldcg(reinterpret_cast<const float4 *>(row + kc) + q);
+        f[4 * q] = a.x; f[4 * q + 1] = a.y; f[4 * q + 2] = a.z; f[4 * q + 3] = a.w;
+    }
+    if (kc + 16 > rank) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) f[i] = (kc + i < rank) ? f[i] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(f[2 * j]), h1 = __float2bfloat16_rn(f[2 * j + 1]);
+        __nv_bfloat16 e0 = h0, e1 = h1;
+        if (lo) {
+            e0 = __float2bfloat16_rn(f[2 * j] - __bfloat162float(h0));
+            e1 = __float2bfloat16_rn(f[2 * j + 1] - __bfloat162float(h1));
+        }
+        v[j] = (uint32_t)__bfloat16_as_ushort(e0) | ((uint32_t)__bfloat16_as_ushort(e1) << 16);
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -148,7 +192,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     T *xs = reinterpret_cast<T *>(smem + p.off_x);
     uint32_t *vch = reinterpret_cast<uint32_t *>(smem + p.off_v);
     uint32_t *uch = reinterpret_cast<uint32_t *>(smem + p.off_u);
-    __nv_bfloat16 *bsm = reinterpret_cast<__nv_bfloat16 *>(smem + p.off_b);
 
     int t1b = 0, t1e = 0, t2b = 0, t2e = 0;
     if (do1) tile_range(p.tiles1, c, G, t1b, t1e);
@@ -157,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     const int r2b = 16 * t2b, r2e = min(16 * t2e, p.out_f);
     const bool has1 = r1e > r1b, has2 = r2e > r2b;
     const int in_pad = p.kb1 * 64;
-    const int ldi = p.kb2 * 64;  // interm row stride (floats), a multiple of 64 and >= rank
+    const int ldi = p.kb2 * 64;  // t row stride (floats), a multiple of 64 and >= rank
 
     if (tid == 0) {
         mbar_init(&bars[0], 1);
@@ -200,21 +243,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     __syncthreads();
 
     bool ok = true;
+    const int sh0 = 8 * (t & 1);
     // ------------------------------------------------------------------ stage 1
     if (has1) {
         ok = mbar_wait(&bars[0], 0, &p.ctrl->status);
-        const int kbeg = (p.kb1 * warp) / kWarps, kend = (p.kb1 * (warp + 1)) / kWarps;
         const uint32_t *sw = reinterpret_cast<const uint32_t *>(s2s);
         const T *xg = static_cast<const T *>(p.x) + (size_t)g * p.in_f;
         const uint32_t *xsw = reinterpret_cast<const uint32_t *>(xs + (size_t)g * in_pad);
         const bool xrow = g < p.batch;
-        const int sh0 = 8 * (t & 1);
-        for (int tile = t1b; tile < t1e; ++tile) {
-            const int lt = tile - t1b;
+        const int ntiles = t1e - t1b;
+        const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
+        for (int item = warp; item < items; item += kWarps) {
+            int lt, kbeg, kend;
+            item_of(item, KS, p.kb1, lt, kbeg, kend);
+            const int tile = t1b + lt;
             const bool vA = ok && (16 * tile + g < p.rank), vB = ok && (16 * tile + g + 8 < p.rank);
             const uint32_t *rowA = vch + (size_t)(lt * 16 + g) * p.wv;
             const uint32_t *rowB = rowA + (size_t)8 * p.wv;
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            float acc[4][4] = {};
+#pragma unroll 2
             for (int kb = kbeg; kb < kend; ++kb) {
                 const int wi = 2 * kb + (t >> 1);
                 const uint32_t wA = (vA && wi < p.wv) ? rowA[wi] << sh0 : 0u;
@@ -236,133 +283,107 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                     const uint32_t a1 = lop_sign(wB << (2 * j), sp[2 * j]);
                     const uint32_t a2 = lop_sign(wA << (2 * j + 1), sp[2 * j + 1]);
                     const uint32_t a3 = lop_sign(wB << (2 * j + 1), sp[2 * j + 1]);
-                    E::mma(acc, a0, a1, a2, a3, xp[2 * j], xp[2 * j + 1]);
+                    E::mma(acc[j], a0, a1, a2, a3, xp[2 * j], xp[2 * j + 1]);
                 }
             }
-            float *rw = red + warp * 128;
-            rw[g * 8 + 2 * t] = acc[0];
-            rw[g * 8 + 2 * t + 1] = acc[1];
-            rw[(g + 8) * 8 + 2 * t] = acc[2];
-            rw[(g + 8) * 8 + 2 * t + 1] = acc[3];
-            __syncthreads();
-            for (int i = tid; i < 16 * p.batch; i += kThreads) {
-                const int b = i >> 4, row = i & 15;
-                float s = 0.f;
+            float sum[4];
 #pragma unroll
-                for (int w = 0; w < kWarps; ++w) s += red[w * 128 + row * 8 + b];
-                const int k = 16 * tile + row;
-                if (k < p.rank) {
-                    if (p.smid) s *= E::to_f(static_cast<const T *>(p.smid)[k]);
-                    p.interm[(size_t)b * ldi + k] = s;
-                }
+            for (int i = 0; i < 4; ++i) sum[i] = (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
+            store_partial(red + item * 256, sum, g, t);
+        }
+        __syncthreads();
+        for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
+            const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
+            const int b = rem >> 4, row = rem & 15;
+            float s = 0.f;
+            for (int ks = 0; ks < KS; ++ks) s += red[(lt * KS + ks) * 256 + row * 8 + b];
+            const int k = 16 * (t1b + lt) + row;
+            if (k < p.rank) {
+                if (p.smid) s *= E::to_f(static_cast<const T *>(p.smid)[k]);
+                p.interm[(size_t)b * ldi + k] = s;
             }
-            __syncthreads();
         }
     }
 
     if (p.mode == kFused) {
         if (!grid_barrier(p.ctrl, (unsigned)G)) ok = false;
+    } else if (has1 && do2) {
+        __syncthreads();
     }
 
     // ------------------------------------------------------------------ stage 2
     if (has2) {
-        const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles (hi/lo per batch row)
-        const int kp2 = p.kb2 * 64;
-        const int bstride = kp2 + 8;  // +16 B per column row: conflict-free 128-bit loads
-        // B operand: column 2b holds bf16(t[b]) and column 2b+1 the bf16 remainder, for
-        // b < 4 * nt.  Loads are issued in batches of 8 independent float4 per thread.
-        const int items = nt * 4 * (kp2 / 4);  // (batch row, 4-column chunk) pairs
-        for (int base = 0; base < items; base += 8 * kThreads) {
-            float4 v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int it = base + u * kThreads + tid;
-                const int b = it / (kp2 / 4), c4 = it - b * (kp2 / 4);
-                v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (it < items && b < p.batch && 4 * c4 < p.rank)
-                    v[u] = __ldcg(reinterpret_cast<const float4 *>(p.interm + (size_t)b * ldi) + c4);
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int it = base + u * kThreads + tid;
-                if (it >= items) continue;
-                const int b = it / (kp2 / 4), c4 = it - b * (kp2 / 4);
-                const int k = 4 * c4;
-                const float f[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-                uint32_t hi[2], lo[2];
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    float a = (k + 2 * j < p.rank) ? f[2 * j] : 0.f;
-                    float c = (k + 2 * j + 1 < p.rank) ? f[2 * j + 1] : 0.f;
-                    const __nv_bfloat16 ha = __float2bfloat16_rn(a), hc = __float2bfloat16_rn(c);
-                    const __nv_bfloat16 la = __float2bfloat16_rn(a - __bfloat162float(ha));
-                    const __nv_bfloat16 lc = __float2bfloat16_rn(c - __bfloat162float(hc));
-                    hi[j] = (uint32_t)__bfloat16_as_ushort(ha) | ((uint32_t)__bfloat16_as_ushort(hc) << 16);
-                    lo[j] = (uint32_t)__bfloat16_as_ushort(la) | ((uint32_t)__bfloat16_as_ushort(lc) << 16);
-                }
-                const int col = (b >> 2) * 8 + 2 * (b & 3);
-                *reinterpret_cast<uint2 *>(bsm + (size_t)col * bstride + k) = make_uint2(hi[0], hi[1]);
-                *reinterpret_cast<uint2 *>(bsm + (size_t)(col + 1) * bstride + k) = make_uint2(lo[0], lo[1]);
-            }
-        }
-        __syncthreads();
         if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
-        const int kbeg = (p.kb2 * warp) / kWarps, kend = (p.kb2 * (warp + 1)) / kWarps;
-        const int sh0 = 8 * (t & 1);
+        const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles: (hi, lo) of 4 batch rows each
+        const int ntiles = t2e - t2b;
+        const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
         constexpr uint32_t kOne = 0x3F803F80u;  // bf16 (1.0, 1.0)
-        for (int tile = t2b; tile < t2e; ++tile) {
-            const int lt = tile - t2b;
+        // B column g of n-tile q is the hi (g even) or lo (g odd) part of batch row 4q + g/2
+        const int b0 = g >> 1, b1 = 4 + (g >> 1);
+        const bool lo = (g & 1) != 0;
+        const float *trow0 = p.interm + (size_t)b0 * ldi;
+        const float *trow1 = p.interm + (size_t)b1 * ldi;
+        for (int item = warp; item < items; item += kWarps) {
+            int lt, kbeg, kend;
+            item_of(item, KS, p.kb2, lt, kbeg, kend);
+            const int tile = t2b + lt;
             const bool vA = ok && (16 * tile + g < p.out_f), vB = ok && (16 * tile + g + 8 < p.out_f);
             const uint32_t *rowA = uch + (size_t)(lt * 16 + g) * p.wu;
             const uint32_t *rowB = rowA + (size_t)8 * p.wu;
-            float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+            float acc0[4][4] = {}, acc1[4][4] = {};
+#pragma unroll 2
             for (int kb = kbeg; kb < kend; ++kb) {
                 const int wi = 2 * kb + (t >> 1);
                 const uint32_t wA = (vA && wi < p.wu) ? rowA[wi] << sh0 : 0u;
                 const uint32_t wB = (vB && wi < p.wu) ? rowB[wi] << sh0 : 0u;
                 const int kc = 64 * kb + 16 * t;
-                uint32_t b0[8];
-                load16_smem(bsm + (size_t)g * bstride + kc, b0);
-                uint32_t a[4][4];
+                uint32_t bp0[8], bp1[8];
+                if (b0 < p.batch) {
+                    load_t_pairs(trow0, kc, p.rank, lo, bp0);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) bp0[j] = 0u;
+                }
+                if (nt == 2 && b1 < p.batch) {
+                    load_t_pairs(trow1, kc, p.rank, lo, bp1);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) bp1[j] = 0u;
+                }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    a[j][0] = lop_sign(wA << (2 * j), kOne);
-                    a[j][1] = lop_sign(wB << (2 * j), kOne);
-                    a[j][2] = lop_sign(wA << (2 * j + 1), kOne);
-                    a[j][3] = lop_sign(wB << (2 * j + 1), kOne);
-                    mma_bf16_16816(acc0, a[j][0], a[j][1], a[j][2], a[j][3], b0[2 * j], b0[2 * j + 1]);
-                }
-                if (nt == 2) {
-                    uint32_t b1[8];
-                    load16_smem(bsm + (size_t)(8 + g) * bstride + kc, b1);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        mma_bf16_16816(acc1, a[j][0], a[j][1], a[j][2], a[j][3], b1[2 * j], b1[2 * j + 1]);
+                    const uint32_t a0 = lop_sign(wA << (2 * j), kOne);
+                    const uint32_t a1 = lop_sign(wB << (2 * j), kOne);
+                    const uint32_t a2 = lop_sign(wA << (2 * j + 1), kOne);
+                    const uint32_t a3 = lop_sign(wB << (2 * j + 1), kOne);
+                    mma_bf16_16816(acc0[j], a0, a1, a2, a3, bp0[2 * j], bp0[2 * j + 1]);
+                    if (nt == 2) mma_bf16_16816(acc1[j], a0, a1, a2, a3, bp1[2 * j], bp1[2 * j + 1]);
                 }
             }
-            float *rw = red + warp * 256;
-            rw[g * 8 + 2 * t] = acc0[0];
-            rw[g * 8 + 2 * t + 1] = acc0[1];
-            rw[(g + 8) * 8 + 2 * t] = acc0[2];
-            rw[(g + 8) * 8 + 2 * t + 1] = acc0[3];
-            rw[128 + g * 8 + 2 * t] = acc1[0];
-            rw[128 + g * 8 + 2 * t + 1] = acc1[1];
-            rw[128 + (g + 8) * 8 + 2 * t] = acc1[2];
-            rw[128 + (g + 8) * 8 + 2 * t + 1] = acc1[3];
-            __syncthreads();
-            for (int i = tid; i < 16 * p.batch; i += kThreads) {
-                const int b = i >> 4, row = i & 15;
-                const int half = (b >> 2) * 128, col = 2 * (b & 3);
-                float s = 0.f;
+            float s0[4], s1v[4];
 #pragma unroll
-                for (int w = 0; w < kWarps; ++w) s += red[w * 256 + half + row * 8 + col] + red[w * 256 + half + row * 8 + col + 1];
-                const int m = 16 * tile + row;
-                if (m < p.out_f) {
-                    const float v = s * E::to_f(static_cast<const T *>(p.s1)[m]);
-                    static_cast<T *>(p.y)[(size_t)b * p.out_f + m] = E::out(v);
-                }
+            for (int i = 0; i < 4; ++i) {
+                s0[i] = (acc0[0][i] + acc0[1][i]) + (acc0[2][i] + acc0[3][i]);
+                s1v[i] = (acc1[0][i] + acc1[1][i]) + (acc1[2][i] + acc1[3][i]);
             }
-            __syncthreads();
+            store_partial(red + item * 256, s0, g, t);
+            store_partial(red + item * 256 + 128, s1v, g, t);
+        }
+        __syncthreads();
+        for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
+            const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
+            const int b = rem >> 4, row = rem & 15;
+            const int half = (b >> 2) * 128, col = 2 * (b & 3);
+            float s = 0.f;
+            for (int ks = 0; ks < KS; ++ks) {
+                const float *r = red + (lt * KS + ks) * 256 + half + row * 8 + col;
+                s += r[0] + r[1];
+            }
+            const int m = 16 * (t2b + lt) + row;
+            if (m < p.out_f) {
+                const float v = s * E::to_f(static_cast<const T *>(p.s1)[m]);
+                static_cast<T *>(p.y)[(size_t)b * p.out_f + m] = E::out(v);
+            }
         }
     }
 }
@@ -380,29 +401,20 @@ static inline uint32_t align128(size_t v) { return (uint32_t)((v + 127) & ~size_
 // Shared-memory layout for a launch whose CTAs own at most `rows1`/`rows2` rows.
 static size_t layout(Params &p, int rows1, int rows2, bool stage1, bool stage2, bool x_in_smem) {
     size_t off = 128;  // mbarriers
+    const int items = std::max(kWarps, std::max(rows1, rows2) / 16);
     p.off_red = (uint32_t)off;
-    off = align128(off + (size_t)kWarps * 256 * sizeof(float));
+    off = align128(off + (size_t)items * 256 * sizeof(float));
     const size_t in_pad = (size_t)p.kb1 * 64;
     p.off_s2 = (uint32_t)off;
-    if (stage1) off = align128(off + in_pad * 2);
-    // region shared by stage-1 data (x, V slab) and the stage-2 B operand
-    const size_t region = off;
-    p.off_x = (uint32_t)region;
-    size_t r1 = 0;
+    p.off_x = (uint32_t)off;
+    p.off_v = (uint32_t)off;
     if (stage1) {
-        r1 = x_in_smem ? align128((size_t)p.batch * in_pad * 2) : 0;
-        p.off_v = (uint32_t)(region + r1);
-        r1 += align128((size_t)rows1 * p.wv * 4 + 16);
-    } else {
-        p.off_v = (uint32_t)region;
+        off = align128(off + in_pad * 2);
+        p.off_x = (uint32_t)off;
+        if (x_in_smem) off = align128(off + (size_t)p.batch * in_pad * 2);
+        p.off_v = (uint32_t)off;
+        off = align128(off + (size_t)rows1 * p.wv * 4 + 16);
     }
-    size_t rb = 0;
-    if (stage2) {
-        const int nt = p.batch <= 4 ? 1 : 2;
-        rb = align128((size_t)nt * 8 * ((size_t)p.kb2 * 64 + 8) * 2);
-    }
-    p.off_b = (uint32_t)region;
-    off = region + (r1 > rb ? r1 : rb);
     p.off_u = (uint32_t)off;
     if (stage2) off = align128(off + (size_t)rows2 * p.wu * 4 + 16);
     p.x_in_smem = x_in_smem ? 1 : 0;
