@@ -50,7 +50,7 @@ struct Params {
     const uint32_t *ubits;    // [out, wu]
     const void *s1;           // [out]
     void *y;                  // [batch, out]
-    float *interm;            // [batch, ldi], ldi = kb2 * 64 >= rank
+    __nv_bfloat16 *tb;        // stage-2 B operand [16 columns][ldi]: (hi, lo) of t for 8 batch rows
     Ctrl *ctrl;
     int batch, in_f, rank, out_f;
     int wv, wu;               // words per V row / U row
@@ -152,29 +152,15 @@ __device__ __forceinline__ void store_partial(float *r, const float (&acc)[4], i
     r[(g + 8) * 8 + 2 * t + 1] = acc[3];
 }
 
-// 16 consecutive floats of t (fp32, L2-resident) as 8 bf16 pairs of their hi or lo part;
-// values at k >= rank read as zero (the buffer beyond rank holds other layers' data).
-__device__ __forceinline__ void load_t_pairs(const float *row, int kc, int rank, bool lo, uint32_t (&v)[8]) {
-    float f[16];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const float4 a = __ldcg(reinterpret_cast<const float4 *>(row + kc) + q);
-        f[4 * q] = a.x; f[4 * q + 1] = a.y; f[4 * q + 2] = a.z; f[4 * q + 3] = a.w;
+// 8 bf16 pairs (16 values along k) of one B column, written by stage 1 (L2-resident);
+// zeros when the column belongs to a batch row that does not exist.
+__device__ __forceinline__ void load_t_pairs(const __nv_bfloat16 *p, bool valid, uint32_t (&v)[8]) {
+    uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a;
+    if (valid) {
+        a = __ldcg(reinterpret_cast<const uint4 *>(p));
+        b = __ldcg(reinterpret_cast<const uint4 *>(p) + 1);
     }
-    if (kc + 16 > rank) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) f[i] = (kc + i < rank) ? f[i] : 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const __nv_bfloat16 h0 = __float2bfloat16_rn(f[2 * j]), h1 = __float2bfloat16_rn(f[2 * j + 1]);
-        __nv_bfloat16 e0 = h0, e1 = h1;
-        if (lo) {
-            e0 = __float2bfloat16_rn(f[2 * j] - __bfloat162float(h0));
-            e1 = __float2bfloat16_rn(f[2 * j + 1] - __bfloat162float(h1));
-        }
-        v[j] = (uint32_t)__bfloat16_as_ushort(e0) | ((uint32_t)__bfloat16_as_ushort(e1) << 16);
-    }
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
 template <typename T>
@@ -200,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     const int r2b = 16 * t2b, r2e = min(16 * t2e, p.out_f);
     const bool has1 = r1e > r1b, has2 = r2e > r2b;
     const int in_pad = p.kb1 * 64;
-    const int ldi = p.kb2 * 64;  // t row stride (floats), a multiple of 64 and >= rank
+    const int ldi = p.kb2 * 64;  // stride of a B column (bf16 values), a multiple of 64 and >= rank
 
     if (tid == 0) {
         mbar_init(&bars[0], 1);
@@ -220,10 +206,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         if (vec_rows) {
             if (tid == 0) {
                 bulk_g2s_pieces(s2s, p.s2, (uint32_t)p.in_f * 2u, &bars[0]);
-                if (p.x_in_smem)
-                    for (int b = 0; b < p.batch; ++b)
-                        bulk_g2s_pieces(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f,
-                                        (uint32_t)p.in_f * 2u, &bars[0]);
+                if (p.x_in_smem) {
+                    if (in_pad == p.in_f)
+                        bulk_g2s_pieces(xs, p.x, (uint32_t)p.batch * (uint32_t)p.in_f * 2u, &bars[0]);
+                    else
+                        for (int b = 0; b < p.batch; ++b)
+                            bulk_g2s_pieces(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f,
+                                            (uint32_t)p.in_f * 2u, &bars[0]);
+                }
             }
             zero_tail<T>(s2s, p.in_f, in_pad);
             if (p.x_in_smem)
@@ -300,9 +290,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             const int k = 16 * (t1b + lt) + row;
             if (k < p.rank) {
                 if (p.smid) s *= E::to_f(static_cast<const T *>(p.smid)[k]);
-                p.interm[(size_t)b * ldi + k] = s;
+                const __nv_bfloat16 hi = __float2bfloat16_rn(s);
+                const int col = (b >> 2) * 8 + 2 * (b & 3);
+                p.tb[(size_t)col * ldi + k] = hi;
+                p.tb[(size_t)(col + 1) * ldi + k] = __float2bfloat16_rn(s - __bfloat162float(hi));
             }
         }
+        // the CTA owning the last tile zeroes the K padding [rank, ldi) of every column
+        if (t1e == p.tiles1)
+            for (int i = tid; i < 16 * (ldi - p.rank); i += kThreads) {
+                const int col = i / (ldi - p.rank);
+                p.tb[(size_t)col * ldi + p.rank + (i - col * (ldi - p.rank))] = __float2bfloat16_rn(0.f);
+            }
     }
 
     if (p.mode == kFused) {
@@ -318,11 +317,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         const int ntiles = t2e - t2b;
         const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
         constexpr uint32_t kOne = 0x3F803F80u;  // bf16 (1.0, 1.0)
-        // B column g of n-tile q is the hi (g even) or lo (g odd) part of batch row 4q + g/2
+        // B column g of n-tile q is the hi (g even) or lo (g odd) part of batch row 4q + g/2,
+        // stored ready-made by stage 1 as bf16 pairs along k
         const int b0 = g >> 1, b1 = 4 + (g >> 1);
-        const bool lo = (g & 1) != 0;
-        const float *trow0 = p.interm + (size_t)b0 * ldi;
-        const float *trow1 = p.interm + (size_t)b1 * ldi;
+        const __nv_bfloat16 *trow0 = p.tb + (size_t)g * ldi;
+        const __nv_bfloat16 *trow1 = p.tb + (size_t)(8 + g) * ldi;
         for (int item = warp; item < items; item += kWarps) {
             int lt, kbeg, kend;
             item_of(item, KS, p.kb2, lt, kbeg, kend);
@@ -338,18 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 const uint32_t wB = (vB && wi < p.wu) ? rowB[wi] << sh0 : 0u;
                 const int kc = 64 * kb + 16 * t;
                 uint32_t bp0[8], bp1[8];
-                if (b0 < p.batch) {
-                    load_t_pairs(trow0, kc, p.rank, lo, bp0);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) bp0[j] = 0u;
-                }
-                if (nt == 2 && b1 < p.batch) {
-                    load_t_pairs(trow1, kc, p.rank, lo, bp1);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) bp1[j] = 0u;
-                }
+                load_t_pairs(trow0 + kc, b0 < p.batch, bp0);
+                load_t_pairs(trow1 + kc, nt == 2 && b1 < p.batch, bp1);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const uint32_t a0 = lop_sign(wA << (2 * j), kOne);
@@ -504,8 +493,8 @@ extern "C" {
 size_t nq_gemv_workspace_bytes(int64_t batch, int64_t rank) {
     (void)batch;  // batches above 8 reuse the same 8-row interm buffer, launch after launch
     if (rank <= 0) return 0;
-    const size_t ldi = (size_t)((rank + 63) / 64) * 64;  // >= kb2 * 64 for every rank
-    const size_t interm = (size_t)nq::gemv::kMaxBatch * ldi * sizeof(float);
+    const size_t ldi = (size_t)((rank + 63) / 64) * 64;  // == kb2 * 64
+    const size_t interm = (size_t)2 * nq::gemv::kMaxBatch * ldi * sizeof(__nv_bfloat16);
     return sizeof(nq::Ctrl) + ((interm + 255) & ~size_t(255));
 }
 
@@ -550,7 +539,7 @@ int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features, const 
     base.ubits = reinterpret_cast<const uint32_t *>(u_bits);
     base.s1 = scale_post;
     base.ctrl = static_cast<Ctrl *>(workspace);
-    base.interm = reinterpret_cast<float *>(static_cast<char *>(workspace) + sizeof(Ctrl));
+    base.tb = reinterpret_cast<__nv_bfloat16 *>(static_cast<char *>(workspace) + sizeof(Ctrl));
     base.in_f = (int)in_features;
     base.rank = (int)rank;
     base.out_f = (int)out_features;
