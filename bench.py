@@ -1,0 +1,367 @@
+"""Benchmark: batch-1 greedy decode tokens/s of a Llama-2-7B-architecture decoder whose
+every linear is a NanoQuant layer at the benchmark ranks (~0.55 bpw), after a 2048-token
+random-id prompt, tensor-parallel over N GPUs (one process per GPU, NCCL all-reduce per
+attention / MLP block).  Also reports the fused decode GEMV against the HBM roofline and
+the reference's CPU path on this host.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nq|reference] [--model NAME]
+
+For N > 1 run under torch.distributed.run (one rank per GPU).  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "batch-1 decode tokens/s (7B shape, 0.55 bpw)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="nq", choices=["nq", "reference"])
+    ap.add_argument("--model", default="llama2-7b")
+    ap.add_argument("--prompt", type=int, default=2048)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample length")
+    return ap.parse_args()
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                             device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per GEMV launch from the committed ncu summary (key: value lines), if any."""
+    p = os.path.join(ROOT, "profiles", "gemv_llama2_7b_decode.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.lines, self.proc = gpu, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------------------
+# CPU baseline: the reference's CPU path (dense +-1 factors, _compute_forward) on this host
+# --------------------------------------------------------------------------------------
+def cpu_reference_token_time(cfg, context: int, seconds: float):
+    """Seconds per decode token of the reference CPU path, from a bounded sample: one decoder
+    layer (7 dense-factor NanoQuant linears in float32 via oracle.dense_forward_torch, the
+    reference's _compute_forward, plus attention over `context` cached positions and the
+    norms) timed repeatedly for ~`seconds`, scaled by the layer count, plus the fp32 lm_head."""
+    from oracle import oracle as orc
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    sign = lambda r, c: (torch.randint(0, 2, (r, c), generator=g, dtype=torch.int8) * 2 - 1).float()  # noqa: E731
+    lin = {}
+    for p in ("q", "k", "v", "o", "gate", "up", "down"):
+        out_f, in_f = cfg.io(p)
+        r = cfg.ranks[p]
+        lin[p] = (sign(r, in_f), sign(out_f, r), torch.rand(in_f, generator=g), torch.rand(out_f, generator=g))
+    kc = torch.randn(cfg.kv_heads, context, cfg.head_dim, generator=g)
+    vc = torch.randn(cfg.kv_heads, context, cfg.head_dim, generator=g)
+    lm = torch.randn(cfg.vocab, cfg.hidden, generator=g) * 0.02
+    x0 = torch.randn(1, cfg.hidden, generator=g)
+    rep = cfg.heads // cfg.kv_heads
+
+    def layer(x):
+        def f(p, v):
+            V, U, s2, s1 = lin[p]
+            return orc.dense_forward_torch(v, s2, V, None, U, s1)
+        h = torch.nn.functional.rms_norm(x, (cfg.hidden,))
+        q = f("q", h).view(cfg.heads, 1, cfg.head_dim)
+        f("k", h), f("v", h)
+        a = torch.nn.functional.scaled_dot_product_attention(q, kc.repeat_interleave(rep, 0),
+                                                             vc.repeat_interleave(rep, 0))
+        x = x + f("o", a.reshape(1, -1))
+        h = torch.nn.functional.rms_norm(x, (cfg.hidden,))
+        return x + f("down", torch.nn.functional.silu(f("gate", h)) * f("up", h))
+
+    with torch.no_grad():
+        layer(x0)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            layer(x0)
+            n += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        t_layer = (time.perf_counter() - t0) / n
+        t1 = time.perf_counter()
+        for _ in range(3):
+            torch.nn.functional.rms_norm(x0, (cfg.hidden,)) @ lm.t()
+        t_head = (time.perf_counter() - t1) / 3
+    return cfg.layers * t_layer + t_head, threads, n
+
+
+def config_block(cfg, args, world):
+    return {"workload": f"{cfg.name} 0.55bpw batch-{args.batch} greedy decode after a {args.prompt}-token "
+                        f"random-id prompt",
+            "model": cfg.name, "global_batch": args.batch, "seq_len": args.prompt,
+            "parallelism": f"tp{world}", "ranks": dict(cfg.ranks),
+            "l2": "working set > L2 (weights + KV cache read per token)"}
+
+
+def run_reference(args, world, rank):
+    from nanoquant_b200.decoder import CONFIGS
+    cfg = CONFIGS[args.model]
+    if rank != 0:
+        return
+    sample = max(1.0, args.cpu_seconds / max(1, args.steps + args.warmup))
+    times = []
+    for i in range(args.warmup + args.steps):
+        t, cores, n = cpu_reference_token_time(cfg, args.prompt + i, sample)
+        if i >= args.warmup:
+            times.append(t)
+    sec = sum(times) / len(times)
+    val = args.batch / sec
+    line = {"impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random +-1 factors and token ids)", "config": config_block(cfg, args, world),
+            "cpu_baseline": {"value": round(val, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": f"per step: one decoder layer (7 dense-factor linears, attention, norms) "
+                                       f"timed ~{sample:.1f}s, x{cfg.layers} layers + lm_head"},
+            "e2e": {"value": round(val, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def gemv_roofline(dec, reps: int = 5):
+    """Average duration of the fused GEMV over one token's worth of launches (every quantized
+    linear of this rank, replayed from a CUDA graph) and its algorithmic bytes per launch."""
+    lins = list(dec.quant_linears())
+    xs = [torch.randn(dec.batch, q.in_features, device=dec.device, dtype=dec.dtype) for q in lins]
+    s = torch.cuda.Stream(device=dec.device)
+    s.wait_stream(torch.cuda.current_stream(dec.device))
+    with torch.cuda.stream(s):
+        for q, x in zip(lins, xs):
+            q.gemv(x)
+    torch.cuda.current_stream(dec.device).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for q, x in zip(lins, xs):
+            q.gemv(x)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize(dec.device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream(dec.device)
+    e0.record(cur)
+    for _ in range(reps):
+        g.replay()
+    e1.record(cur)
+    torch.cuda.synchronize(dec.device)
+    us_per_launch = e0.elapsed_time(e1) * 1e3 / (reps * len(lins))
+    B = dec.batch
+    alg = sum(q.nbytes() + 2 * B * (q.in_features + q.out_features) for q in lins) / len(lins)
+    del g
+    return alg, us_per_launch, len(lins)
+
+
+def run_nq(args, world, rank, local):
+    from nanoquant_b200.decoder import CONFIGS, Decoder
+    cfg = CONFIGS[args.model]
+    dev = torch.device("cuda", local)
+    group = torch.distributed.group.WORLD if world > 1 else None
+    max_seq = args.prompt + args.warmup + 2 * args.steps + 16
+    dec = Decoder(cfg, max_seq=max_seq, batch=args.batch, tp_rank=rank, tp=world, group=group, seed=1234,
+                  dtype=torch.float16, device=dev)
+    g = torch.Generator().manual_seed(42)
+    prompt = torch.randint(0, cfg.vocab, (args.prompt,), generator=g)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    first = dec.prefill(prompt.to(dev))
+    e1.record()
+    torch.cuda.synchronize(dev)
+    prefill_ms = e0.elapsed_time(e1)
+    graphed = dec.capture(warmup=2)
+    cur = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------- device-timed decode (inputs resident in HBM)
+    for _ in range(args.warmup):
+        graphed.replay()
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        e0.record(cur)
+        for _ in range(args.steps):
+            graphed.replay()
+        e1.record(cur)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    ms_per_step = ms / args.steps
+    value = args.batch * args.steps / (ms / 1e3)
+
+    # ---------------- end to end through the public step API (host token ids in and out)
+    host_in = torch.empty(args.batch, dtype=torch.long).pin_memory()
+    host_out = torch.empty(args.batch, dtype=torch.long).pin_memory()
+    host_in.copy_(dec.next_tokens.cpu())
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0.record(cur)
+    for _ in range(args.steps):
+        graphed.generate(host_in, host_out)
+        host_in.copy_(host_out)
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e = args.batch * args.steps / (e2e_ms / 1e3)
+    graphed.release()
+
+    # ---------------- dominant kernel vs the HBM roofline
+    alg_bytes, us_launch, n_lin = gemv_roofline(dec)
+    peak, peak_kind = peaks()
+    achieved = alg_bytes / (us_launch * 1e-6) / 1e9
+    launches_per_step = cfg.layers * (7 + 2 + 1 + 2 + 1) + 1  # gemv x7, rmsnorm x2, rope, attention x2, silu; final norm
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        t, cores, n = cpu_reference_token_time(cfg, args.prompt, args.cpu_seconds)
+        cpu = {"value": round(args.batch / t, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"one decoder layer (reference _compute_forward on dense +-1 fp32 factors x7, attention "
+                         f"over {args.prompt} positions, norms) repeated {n}x in ~{args.cpu_seconds:.0f}s, "
+                         f"scaled x{cfg.layers} layers + fp32 lm_head"}
+
+    if world > 1:
+        torch.distributed.barrier(device_ids=[local])
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+                "data": "synthetic (seeded random +-1 factors, fp16 scales, random token ids)",
+                "config": config_block(cfg, args, world),
+                "e2e": {"value": round(e2e, 3), "unit": "tokens/s", "h2d_bytes_per_step": 8 * args.batch,
+                        "d2h_bytes_per_step": 8 * args.batch},
+                "roofline": {"bound": "hbm", "kernel": "gemv_kernel (fused decode GEMV)",
+                             "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                             "frac": round(achieved / peak, 5), "peak_source": peak_kind,
+                             "traffic": profile_traffic(), "bytes_per_launch": round(alg_bytes, 1),
+                             "us_per_launch": round(us_launch, 3), "launches_measured": n_lin},
+                "cpu_baseline": cpu,
+                "clocks": clocks.summary(),
+                "gpu_launches": launches_per_step * args.steps,
+                "prefill_ms": round(prefill_ms, 2), "first_token": int(first[0])}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier(device_ids=[local])
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_nq(args, world, rank, local)
+    if world > 1 and torch.distributed.is_initialized():
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

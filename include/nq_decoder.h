@@ -1,0 +1,48 @@
+/*
+ * nq_decoder.h -- C ABI of the kernels that sit around the quantized linears in a
+ * Llama-architecture decoder step (no reference counterpart as kernels: the reference
+ * runs these parts as stock HF / PyTorch modules, src/nanoquant/kernel/test_decode.py).
+ * Conventions are those of nq_b200.h: device pointers, void* cudaStream_t, nq_status.
+ */
+#ifndef NQ_DECODER_H_
+#define NQ_DECODER_H_
+
+#include "nq_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* h = x (+ residual_in) rounded to dtype; residual_out = h (may be NULL);
+ * out = weight * dtype(h * rsqrt(mean(h^2) + eps)).  x, out: [rows, hidden]. */
+NQ_API int nq_rmsnorm(int dtype, const void *x, const void *residual_in, void *residual_out,
+                      const void *weight, void *out, int64_t rows, int64_t hidden, float eps,
+                      void *stream);
+
+/* Rotary embedding (rotate-half pairs (i, i + head_dim/2), angle pos * theta^(-2i/head_dim))
+ * applied in place to q [n_tokens, hq, head_dim] and k [n_tokens, hkv, head_dim]; the rotated
+ * k and the untouched v [n_tokens, hkv, head_dim] are written to the caches
+ * [batch][hkv][max_seq][head_dim] at row batch_of[t] (t itself when NULL), position positions[t]. */
+NQ_API int nq_rope_cache(int dtype, void *q, void *k, const void *v, const int32_t *positions,
+                         const int32_t *batch_of, void *k_cache, void *v_cache, int64_t n_tokens,
+                         int64_t hq, int64_t hkv, int64_t head_dim, int64_t max_seq, float theta,
+                         void *stream);
+
+/* Single-query attention over the first seq_len[b] cache positions (device int32 [batch]),
+ * split over 256-position chunks and combined: out [batch, hq, head_dim].  head_dim 128,
+ * hq / hkv in {1, 2, 4, 8}.  Workspace: nq_decode_attention_workspace_bytes(). */
+NQ_API size_t nq_decode_attention_workspace_bytes(int64_t batch, int64_t hq, int64_t head_dim,
+                                                  int64_t max_seq);
+NQ_API int nq_decode_attention(int dtype, const void *q, const void *k_cache, const void *v_cache,
+                               const int32_t *seq_len, void *out, int64_t batch, int64_t hq,
+                               int64_t hkv, int64_t head_dim, int64_t max_seq, void *workspace,
+                               size_t workspace_bytes, void *stream);
+
+/* out = dtype(silu(gate)) * up, elementwise over n values. */
+NQ_API int nq_silu_mul(int dtype, const void *gate, const void *up, void *out, int64_t n,
+                       void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NQ_DECODER_H_ */

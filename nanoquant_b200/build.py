@@ -41,7 +41,7 @@ def _run(cmd, verbose):
 
 def build_cuda(force=False, verbose=False) -> str:
     cu = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    deps = cu + glob.glob(os.path.join(CSRC, "*.cuh")) + [os.path.join(INCLUDE, "nq_b200.h")]
+    deps = cu + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
     if force or _stale(CUDA_LIB, deps):
         os.makedirs(OUT, exist_ok=True)
         cmd = [NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
@@ -55,7 +55,7 @@ def build_cuda(force=False, verbose=False) -> str:
 def build_torch(force=False, verbose=False) -> str:
     import torch.utils.cpp_extension as ext
     src = os.path.join(CSRC, "torch_ops.cpp")
-    deps = [src, os.path.join(INCLUDE, "nq_b200.h"), CUDA_LIB]
+    deps = [src, CUDA_LIB] + glob.glob(os.path.join(INCLUDE, "*.h"))
     if force or _stale(TORCH_LIB, deps):
         os.makedirs(OUT, exist_ok=True)
         import torch

@@ -19,6 +19,7 @@
 #include <utility>
 
 #include "../../include/nq_b200.h"
+#include "../../include/nq_decoder.h"
 
 namespace {
 
@@ -286,6 +287,105 @@ at::Tensor gemm_meta(const at::Tensor &x, const at::Tensor &s2, const at::Tensor
     return layer_meta(x, s2, v, m, u, s1);
 }
 
+
+// ------------------------------------------------------------------ decoder-step kernels
+
+std::tuple<at::Tensor, at::Tensor> rmsnorm_cuda(const at::Tensor &x, const std::optional<at::Tensor> &residual,
+                                                const at::Tensor &weight, double eps) {
+    const auto st = x.scalar_type();
+    CHECK_CUDA_CONT(x, st);
+    CHECK_CUDA_CONT(weight, st);
+    const int64_t hidden = x.size(-1), rows = x.numel() / hidden;
+    TORCH_CHECK(weight.numel() == hidden, "weight size mismatch");
+    c10::cuda::CUDAGuard guard(x.device());
+    auto out = at::empty_like(x);
+    auto res_out = at::empty_like(x);
+    const void *rin = nullptr;
+    if (residual.has_value() && residual->defined()) {
+        CHECK_CUDA_CONT((*residual), st);
+        TORCH_CHECK(residual->numel() == x.numel(), "residual size mismatch");
+        rin = residual->data_ptr();
+    }
+    NQ_TORCH_CHECK(nq_rmsnorm(dtype_code(st), x.data_ptr(), rin, res_out.data_ptr(), weight.data_ptr(),
+                              out.data_ptr(), rows, hidden, (float)eps, cur_stream(x)));
+    return {out, res_out};
+}
+
+std::tuple<at::Tensor, at::Tensor> rmsnorm_meta(const at::Tensor &x, const std::optional<at::Tensor> &,
+                                                const at::Tensor &, double) {
+    return {at::empty_like(x), at::empty_like(x)};
+}
+
+void rope_cache_cuda(at::Tensor &q, at::Tensor &k, const at::Tensor &v, const at::Tensor &positions,
+                     const std::optional<at::Tensor> &batch_of, at::Tensor &k_cache, at::Tensor &v_cache,
+                     double theta) {
+    const auto st = q.scalar_type();
+    CHECK_CUDA_CONT(q, st);
+    CHECK_CUDA_CONT(k, st);
+    CHECK_CUDA_CONT(v, st);
+    CHECK_CUDA_CONT(k_cache, st);
+    CHECK_CUDA_CONT(v_cache, st);
+    CHECK_CUDA_CONT(positions, at::kInt);
+    TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.sizes() == k.sizes(), "q [n, hq, d], k/v [n, hkv, d]");
+    TORCH_CHECK(k_cache.dim() == 4 && k_cache.sizes() == v_cache.sizes(), "caches [batch, hkv, max_seq, d]");
+    const int64_t n = q.size(0), hq = q.size(1), d = q.size(2), hkv = k.size(1);
+    TORCH_CHECK(k.size(0) == n && k.size(2) == d && k_cache.size(1) == hkv && k_cache.size(3) == d, "shape mismatch");
+    TORCH_CHECK(positions.numel() == n, "one position per token row");
+    const int32_t *bo = nullptr;
+    if (batch_of.has_value() && batch_of->defined()) {
+        CHECK_CUDA_CONT((*batch_of), at::kInt);
+        TORCH_CHECK(batch_of->numel() == n, "one batch index per token row");
+        bo = batch_of->data_ptr<int32_t>();
+    } else {
+        TORCH_CHECK(n <= k_cache.size(0), "without batch_of, token row t writes cache row t");
+    }
+    c10::cuda::CUDAGuard guard(q.device());
+    NQ_TORCH_CHECK(nq_rope_cache(dtype_code(st), q.data_ptr(), k.data_ptr(), v.data_ptr(), positions.data_ptr<int32_t>(),
+                                 bo, k_cache.data_ptr(), v_cache.data_ptr(), n, hq, hkv, d, k_cache.size(2),
+                                 (float)theta, cur_stream(q)));
+}
+
+void rope_cache_meta(at::Tensor &, at::Tensor &, const at::Tensor &, const at::Tensor &,
+                     const std::optional<at::Tensor> &, at::Tensor &, at::Tensor &, double) {}
+
+at::Tensor decode_attention_cuda(const at::Tensor &q, const at::Tensor &k_cache, const at::Tensor &v_cache,
+                                 const at::Tensor &seq_len) {
+    const auto st = q.scalar_type();
+    CHECK_CUDA_CONT(q, st);
+    CHECK_CUDA_CONT(k_cache, st);
+    CHECK_CUDA_CONT(v_cache, st);
+    CHECK_CUDA_CONT(seq_len, at::kInt);
+    TORCH_CHECK(q.dim() == 3 && k_cache.dim() == 4, "q [batch, hq, d], caches [batch, hkv, max_seq, d]");
+    const int64_t b = q.size(0), hq = q.size(1), d = q.size(2), hkv = k_cache.size(1), ms = k_cache.size(2);
+    TORCH_CHECK(k_cache.size(0) >= b && seq_len.numel() == b, "batch mismatch");
+    c10::cuda::CUDAGuard guard(q.device());
+    auto out = at::empty_like(q);
+    const size_t wsb = nq_decode_attention_workspace_bytes(b, hq, d, ms);
+    auto ws = at::empty({(int64_t)wsb}, q.options().dtype(at::kByte));
+    NQ_TORCH_CHECK(nq_decode_attention(dtype_code(st), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                       seq_len.data_ptr<int32_t>(), out.data_ptr(), b, hq, hkv, d, ms, ws.data_ptr(),
+                                       wsb, cur_stream(q)));
+    return out;
+}
+
+at::Tensor decode_attention_meta(const at::Tensor &q, const at::Tensor &, const at::Tensor &, const at::Tensor &) {
+    return at::empty_like(q);
+}
+
+at::Tensor silu_mul_cuda(const at::Tensor &gate, const at::Tensor &up) {
+    const auto st = gate.scalar_type();
+    CHECK_CUDA_CONT(gate, st);
+    CHECK_CUDA_CONT(up, st);
+    TORCH_CHECK(gate.sizes() == up.sizes(), "gate and up must have the same shape");
+    c10::cuda::CUDAGuard guard(gate.device());
+    auto out = at::empty_like(gate);
+    NQ_TORCH_CHECK(nq_silu_mul(dtype_code(st), gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(),
+                               cur_stream(gate)));
+    return out;
+}
+
+at::Tensor silu_mul_meta(const at::Tensor &gate, const at::Tensor &) { return at::empty_like(gate); }
+
 }  // namespace
 
 TORCH_LIBRARY(binary_kernels, m) {
@@ -321,6 +421,12 @@ TORCH_LIBRARY(nq_b200, m) {
     m.def(
         "linear(Tensor x, Tensor scale_pre, Tensor v_bits, Tensor? scale_mid, Tensor u_bits, Tensor scale_post) -> "
         "Tensor");
+    m.def("rmsnorm(Tensor x, Tensor? residual, Tensor weight, float eps) -> (Tensor, Tensor)");
+    m.def(
+        "rope_cache(Tensor(a!) q, Tensor(b!) k, Tensor v, Tensor positions, Tensor? batch_of, Tensor(c!) k_cache, "
+        "Tensor(d!) v_cache, float theta) -> ()");
+    m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seq_len) -> Tensor");
+    m.def("silu_mul(Tensor gate, Tensor up) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
@@ -330,6 +436,10 @@ TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
     m.impl("gemv", &gemv_cuda);
     m.impl("gemm", &gemm_cuda);
     m.impl("linear", &linear_cuda);
+    m.impl("rmsnorm", &rmsnorm_cuda);
+    m.impl("rope_cache", &rope_cache_cuda);
+    m.impl("decode_attention", &decode_attention_cuda);
+    m.impl("silu_mul", &silu_mul_cuda);
 }
 
 TORCH_LIBRARY_IMPL(nq_b200, Meta, m) {
@@ -339,4 +449,8 @@ TORCH_LIBRARY_IMPL(nq_b200, Meta, m) {
     m.impl("gemv", &layer_meta);
     m.impl("gemm", &gemm_meta);
     m.impl("linear", &layer_meta);
+    m.impl("rmsnorm", &rmsnorm_meta);
+    m.impl("rope_cache", &rope_cache_meta);
+    m.impl("decode_attention", &decode_attention_meta);
+    m.impl("silu_mul", &silu_mul_meta);
 }

@@ -1,0 +1,306 @@
+"""Llama-architecture decoder whose linear layers are NanoQuant layers on the B200 kernels,
+tensor-parallel over one process per GPU.
+
+This is the harness the reference benchmarks decode with (src/nanoquant/kernel/test_decode.py:
+HF LlamaForCausalLM with every nn.Linear swapped for NanoQuantLinear, StaticCache, greedy
+decode with the step captured as a CUDA graph), rebuilt around the kernels of this package:
+
+* every projection is a NanoQuant layer (half2 sign planes + fp16 scales) run by
+  ``torch.ops.nq_b200.linear`` (fused GEMV for decode, tcgen05 GEMM for prefill);
+* RMSNorm (+ residual add), RoPE + KV-cache write, split-KV decode attention and SwiGLU are
+  this package's kernels; prefill attention uses PyTorch's fused SDPA (causal, GQA);
+* the decode step reads token ids / positions from device buffers and advances them itself,
+  so a captured graph replays one autoregressive step with no host work.
+
+Tensor parallelism (one all-reduce per attention block and per MLP block):
+* q/k/v and gate/up are column-parallel: each rank holds the U rows of its heads / FFN
+  columns (U split by output rows) and the full V;
+* o and down receive their input sharded by heads / FFN columns, so each rank holds the V
+  columns of its shard (V split by input columns) and the full U; by linearity the ranks'
+  outputs s1 * U(smid * V_shard (s2 * x_shard)) sum to the full layer, which the all-reduce does.
+Weights are random (seeded) with the per-layer ranks of the benchmark configs; every rank
+draws the same global planes and keeps its slice, so any TP degree computes the same model.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+PROJ = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    name: str
+    vocab: int
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    ranks: Dict[str, int] = field(hash=False)
+    rms_eps: float = 1e-5
+    rope_theta: float = 10000.0
+
+    def io(self, proj: str):
+        """(out_features, in_features) of a projection."""
+        h, d = self.hidden, self.head_dim
+        return {"q": (self.heads * d, h), "k": (self.kv_heads * d, h), "v": (self.kv_heads * d, h),
+                "o": (h, self.heads * d), "gate": (self.ffn, h), "up": (self.ffn, h), "down": (h, self.ffn)}[proj]
+
+    def packed_bytes_per_token(self) -> int:
+        """Sign-plane + scale bytes of every quantized linear (one decode token, TP=1)."""
+        tot = 0
+        for p in PROJ:
+            out_f, in_f = self.io(p)
+            r = self.ranks[p]
+            tot += 4 * r * ((in_f + 31) // 32) + 4 * out_f * ((r + 31) // 32) + 2 * (in_f + out_f)
+        return tot * self.layers
+
+
+def uniform_rank(bits: float, out_f: int, in_f: int) -> int:
+    """The reference rank planner: floor((bits*a*b/(a+b) - 16) / 32) * 32 (src/nanoquant/utils/utils.py:273-289)."""
+    return int(((bits * out_f * in_f / (out_f + in_f)) - 16) // 32 * 32)
+
+
+LLAMA2_7B = DecoderConfig("llama2-7b", 32000, 4096, 32, 32, 32, 128, 11008,
+                          {"q": 1126, "k": 1126, "v": 1126, "o": 1126, "gate": 2054, "up": 2054, "down": 2054})
+LLAMA3_70B = DecoderConfig("llama3-70b", 128256, 8192, 80, 64, 8, 128, 28672,
+                           {"q": 2208, "k": 480, "v": 480, "o": 2208, "gate": 3488, "up": 3488, "down": 3488},
+                           rope_theta=500000.0)
+TINY = DecoderConfig("tiny", 512, 256, 2, 2, 1, 128, 512,
+                     {"q": 96, "k": 40, "v": 40, "o": 96, "gate": 130, "up": 130, "down": 130})
+CONFIGS = {c.name: c for c in (LLAMA2_7B, LLAMA3_70B, TINY)}
+
+
+class QuantLinearShard:
+    """This rank's part of one NanoQuant layer, in the kernel layout (half2 planes)."""
+
+    def __init__(self, vb, ub, s2, smid, s1):
+        self.vb, self.ub, self.s2, self.smid, self.s1 = vb, ub, s2, smid, s1
+        self.rank = vb.shape[0]
+        self.in_features = s2.numel()
+        self.out_features = s1.numel()
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        return torch.ops.nq_b200.linear(x, self.s2, self.vb, self.smid, self.ub, self.s1)
+
+    def gemv(self, x):
+        return torch.ops.nq_b200.gemv(x, self.s2, self.vb, self.smid, self.ub, self.s1)
+
+    def nbytes(self) -> int:
+        t = 4 * (self.vb.numel() + self.ub.numel()) + 2 * (self.s2.numel() + self.s1.numel())
+        return t + (2 * self.smid.numel() if self.smid is not None else 0)
+
+
+def _random_planes(gen, rows: int, cols: int, device) -> torch.Tensor:
+    """i.i.d. +-1 signs as half2 planes [rows, ceil(cols/32)], padding bits cleared (+1)."""
+    w = (cols + 31) // 32
+    p = torch.randint(-2 ** 31, 2 ** 31 - 1, (rows, w), generator=gen, dtype=torch.int32, device=device)
+    tail = cols - 32 * (w - 1)
+    if tail < 32:
+        # half2 order: column j of the last word sits at bit 15 - j//2 + 16*(j%2)
+        mask = 0
+        for j in range(tail):
+            mask |= 1 << (15 - j // 2 + 16 * (j % 2))
+        if mask >= 2 ** 31:
+            mask -= 2 ** 32
+        p[:, -1] &= mask
+    return p
+
+
+def _word_slice(cols: int, part: int, nparts: int):
+    """Split `cols` columns at multiples of 32 into `nparts` contiguous shards."""
+    words = (cols + 31) // 32
+    w0, w1 = words * part // nparts, words * (part + 1) // nparts
+    return 32 * w0, min(32 * w1, cols), w0, w1
+
+
+def _make_layer(cfg: DecoderConfig, proj: str, layer: int, seed: int, tp_rank: int, tp: int, dtype, device,
+                with_mid: bool = False) -> QuantLinearShard:
+    out_f, in_f = cfg.io(proj)
+    r = cfg.ranks[proj]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed * 1000003 + layer * 17 + PROJ.index(proj))
+    vb = _random_planes(gen, r, in_f, device)
+    ub = _random_planes(gen, out_f, r, device)
+    # variance-preserving scale magnitudes: |N(0,1)|/sqrt(in) for s2 and |N(0,1)|/sqrt(r) for s1,
+    # so activations stay O(1) through a random-init network (values do not affect timing)
+    s2 = (torch.randn(in_f, generator=gen, device=device).abs() / math.sqrt(in_f)).to(dtype)
+    s1 = (torch.randn(out_f, generator=gen, device=device).abs() / math.sqrt(r)).to(dtype)
+    smid = (torch.randn(r, generator=gen, device=device).abs() + 0.5).to(dtype) if with_mid else None
+    if tp == 1:
+        return QuantLinearShard(vb, ub, s2, smid, s1)
+    if proj in ("q", "k", "v", "gate", "up"):  # column-parallel: U rows of this rank's outputs
+        n = out_f // tp
+        sl = slice(tp_rank * n, (tp_rank + 1) * n)
+        return QuantLinearShard(vb, ub[sl].contiguous(), s2, smid, s1[sl].contiguous())
+    # row-parallel: V columns of this rank's input shard (shards are multiples of 32 columns)
+    n = in_f // tp
+    c0, c1 = tp_rank * n, (tp_rank + 1) * n
+    assert c0 % 32 == 0 and c1 % 32 == 0, "input shards must be word aligned"
+    return QuantLinearShard(vb[:, c0 // 32:c1 // 32].contiguous(), ub, s2[c0:c1].contiguous(), smid, s1)
+
+
+class Decoder:
+    """One TP shard of the decoder plus its KV cache and a graph-capturable decode step."""
+
+    def __init__(self, cfg: DecoderConfig, max_seq: int, batch: int = 1, tp_rank: int = 0, tp: int = 1,
+                 group=None, seed: int = 0, dtype=torch.float16, device=None, with_mid: bool = False):
+        _lib.load_torch_ops()
+        assert cfg.heads % tp == 0 and cfg.kv_heads % tp == 0 and cfg.ffn % tp == 0
+        self.cfg, self.max_seq, self.batch, self.tp, self.tp_rank, self.group = cfg, max_seq, batch, tp, tp_rank, group
+        self.dtype = dtype
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        dev = self.device
+        self.hq, self.hkv = cfg.heads // tp, cfg.kv_heads // tp
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed * 7919 + 1)
+        self.embed = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=dev) * 0.02).to(dtype)
+        self.lm_head = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=dev) * 0.02).to(dtype)
+        self.final_norm = torch.ones(cfg.hidden, device=dev, dtype=dtype)
+        self.layers = []
+        for li in range(cfg.layers):
+            lay = {p: _make_layer(cfg, p, li, seed, tp_rank, tp, dtype, dev, with_mid) for p in PROJ}
+            lay["in_norm"] = torch.ones(cfg.hidden, device=dev, dtype=dtype)
+            lay["post_norm"] = torch.ones(cfg.hidden, device=dev, dtype=dtype)
+            self.layers.append(lay)
+        self.k_cache = torch.zeros(cfg.layers, batch, self.hkv, max_seq, cfg.head_dim, device=dev, dtype=dtype)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        # decode-step state, all on the device
+        self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.seq_len = torch.ones(batch, dtype=torch.int32, device=dev)
+        self.next_tokens = torch.zeros(batch, dtype=torch.long, device=dev)
+
+    # ------------------------------------------------------------------ pieces
+    def _all_reduce(self, t: torch.Tensor):
+        if self.tp > 1:
+            torch.distributed.all_reduce(t, group=self.group)
+        return t
+
+    def quant_linears(self):
+        for lay in self.layers:
+            for p in PROJ:
+                yield lay[p]
+
+    def weight_bytes(self) -> int:
+        """Bytes one decode token reads on this rank: quantized linears + lm_head (+ norms)."""
+        return sum(q.nbytes() for q in self.quant_linears()) + self.lm_head.numel() * 2
+
+    # ------------------------------------------------------------------ prefill
+    @torch.no_grad()
+    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
+        """Run the prompt (batch 1, [T] token ids) through the model, fill the caches and
+        return the first generated token (greedy).  Sets the decode state."""
+        assert self.batch == 1 and prompt.dim() == 1
+        cfg, T = self.cfg, prompt.numel()
+        assert T < self.max_seq
+        D = cfg.head_dim
+        pos = torch.arange(T, dtype=torch.int32, device=self.device)
+        bidx = torch.zeros(T, dtype=torch.int32, device=self.device)
+        h = F.embedding(prompt.to(self.device), self.embed)
+        residual = None
+        for li, lay in enumerate(self.layers):
+            x, residual = torch.ops.nq_b200.rmsnorm(h, residual, lay["in_norm"], cfg.rms_eps)
+            q = lay["q"](x).view(T, self.hq, D)
+            k = lay["k"](x).view(T, self.hkv, D)
+            v = lay["v"](x).view(T, self.hkv, D)
+            torch.ops.nq_b200.rope_cache(q, k, v, pos, bidx, self.k_cache[li], self.v_cache[li], cfg.rope_theta)
+            a = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0),
+                                               v.transpose(0, 1).unsqueeze(0), is_causal=True,
+                                               enable_gqa=self.hq != self.hkv)
+            a = a.squeeze(0).transpose(0, 1).reshape(T, self.hq * D).contiguous()
+            o = self._all_reduce(lay["o"](a))
+            x, residual = torch.ops.nq_b200.rmsnorm(o, residual, lay["post_norm"], cfg.rms_eps)
+            act = torch.ops.nq_b200.silu_mul(lay["gate"](x), lay["up"](x))
+            h = self._all_reduce(lay["down"](act))
+        x, _ = torch.ops.nq_b200.rmsnorm(h[-1:].contiguous(), residual[-1:].contiguous(), self.final_norm,
+                                         cfg.rms_eps)
+        nxt = torch.argmax(x @ self.lm_head.t(), dim=-1)
+        self.tokens.copy_(nxt)
+        self.pos.fill_(T)
+        self.seq_len.fill_(T + 1)
+        return nxt
+
+    # ------------------------------------------------------------------ decode
+    @torch.no_grad()
+    def step_logits(self) -> torch.Tensor:
+        """Logits for the current tokens at the current positions (writes the caches)."""
+        cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
+        h = F.embedding(self.tokens, self.embed)
+        residual = None
+        for li, lay in enumerate(self.layers):
+            x, residual = torch.ops.nq_b200.rmsnorm(h, residual, lay["in_norm"], cfg.rms_eps)
+            q = lay["q"](x).view(B, self.hq, D)
+            k = lay["k"](x).view(B, self.hkv, D)
+            v = lay["v"](x).view(B, self.hkv, D)
+            torch.ops.nq_b200.rope_cache(q, k, v, self.pos, None, self.k_cache[li], self.v_cache[li],
+                                         cfg.rope_theta)
+            a = torch.ops.nq_b200.decode_attention(q, self.k_cache[li], self.v_cache[li], self.seq_len)
+            o = self._all_reduce(lay["o"](a.view(B, self.hq * D)))
+            x, residual = torch.ops.nq_b200.rmsnorm(o, residual, lay["post_norm"], cfg.rms_eps)
+            act = torch.ops.nq_b200.silu_mul(lay["gate"](x), lay["up"](x))
+            h = self._all_reduce(lay["down"](act))
+        x, _ = torch.ops.nq_b200.rmsnorm(h, residual, self.final_norm, cfg.rms_eps)
+        return x @ self.lm_head.t()
+
+    @torch.no_grad()
+    def step(self) -> torch.Tensor:
+        """One greedy decode step: next token from the current one, then advance the state."""
+        logits = self.step_logits()
+        self.next_tokens.copy_(torch.argmax(logits, dim=-1))
+        self.tokens.copy_(self.next_tokens)
+        self.pos.add_(1)
+        self.seq_len.add_(1)
+        return self.next_tokens
+
+    def capture(self, warmup: int = 2) -> "GraphedStep":
+        return GraphedStep(self, warmup)
+
+
+class GraphedStep:
+    """The decode step captured once as a CUDA graph; replay() = one autoregressive token.
+
+    The graph advances the device-side state (tokens, positions) itself; warm-up steps run
+    eagerly before capture and are rolled back so the caller's position is unchanged."""
+
+    def __init__(self, dec: Decoder, warmup: int = 2):
+        self.dec = dec
+        saved = (dec.tokens.clone(), dec.pos.clone(), dec.seq_len.clone())
+        s = torch.cuda.Stream(device=dec.device)
+        s.wait_stream(torch.cuda.current_stream(dec.device))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                dec.step()
+        torch.cuda.current_stream(dec.device).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            dec.step()
+        dec.tokens.copy_(saved[0])
+        dec.pos.copy_(saved[1])
+        dec.seq_len.copy_(saved[2])
+        torch.cuda.synchronize(dec.device)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.dec.next_tokens
+
+    def generate(self, host_tokens: torch.Tensor, host_out: torch.Tensor) -> torch.Tensor:
+        """The user-facing step: host token ids (pinned int64 [batch]) in, next token ids out
+        (written into the pinned ``host_out``), synchronised on the current stream."""
+        self.dec.tokens.copy_(host_tokens, non_blocking=True)
+        self.graph.replay()
+        host_out.copy_(self.dec.next_tokens, non_blocking=True)
+        torch.cuda.current_stream(self.dec.device).synchronize()
+        return host_out
+
+    def release(self):
+        self.graph = None
