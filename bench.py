@@ -31,7 +31,7 @@ METRIC = "batch-1 decode tokens/s (7B shape, 0.55 bpw)"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="nq", choices=["nq", "reference"])
     ap.add_argument("--model", default="llama2-7b")
