@@ -94,6 +94,29 @@ NQ_API int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features,
             void *stream);
 
 /* ---------------------------------------------------------------------------------
+ * Allocation-free decode GEMV.  No counterpart in the reference: its kernels allocate their
+ * intermediate with the torch caching allocator on every call (gemv_kernel.cu:345-346).
+ * For callers that cannot allocate device memory -- a plugin or custom-op interface that
+ * receives only input and output buffers, or a process that fixes its device memory at
+ * start-up and must not call cudaMalloc later -- this runs nq_gemv with scratch held in a
+ * static device array of this library (NQ_GEMV_STATIC_MAX_RANK caps the rank; about 128 KiB,
+ * resident on every GPU that loads the library until the process exits).  Arguments and
+ * results are those of nq_gemv, minus the workspace.
+ *   - It calls no cudaMalloc / cudaFree and no allocating library routine.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress);
+ *     make that first call before any stream capture.
+ *   - Every call clears the scratch's control block (barrier counter, status word) on
+ *     `stream`, then launches; all calls share the one array, so calls that may overlap on
+ *     the GPU (different streams without ordering) race and must be serialised by the caller.
+ *   - rank > NQ_GEMV_STATIC_MAX_RANK returns NQ_ERR_UNSUPPORTED without launching.
+ * ------------------------------------------------------------------------------- */
+#define NQ_GEMV_STATIC_MAX_RANK 4096
+NQ_API int nq_gemv_static(int dtype, const void *x, int64_t batch, int64_t in_features,
+                          const void *scale_pre, const int32_t *v_bits, int64_t rank,
+                          const void *scale_mid, const int32_t *u_bits, int64_t out_features,
+                          const void *scale_post, void *y, void *stream);
+
+/* ---------------------------------------------------------------------------------
  * Prefill GEMM: replaces marlin_nanoquant_cuda (src/nanoquant/kernel/cuda/gemm.cpp:112-122,
  * schema src/nanoquant/kernel/pybind.cpp:99-104) on the same HALF2 planes the GEMV uses.
  * tcgen05 tensor-core contraction in two stages, T = (x*s2) V^T * smid then y = (T U^T) * s1.

@@ -29,6 +29,7 @@
 // Layers too large for the per-CTA shared-memory budget run the same kernel as two
 // ordinary launches (stage 1 then stage 2, one 16-row tile per CTA).
 #include <algorithm>
+#include <mutex>
 
 #include "nq_common.cuh"
 
@@ -563,6 +564,71 @@ int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features, const 
         if (st) return st;
     }
     return NQ_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ allocation-free entry point
+// Some callers cannot allocate device memory: a plugin or custom-op interface that hands the
+// kernel only its input and output buffers (no allocator, no workspace), or a serving process
+// that fixes its device memory at start-up and must not call cudaMalloc afterwards (it can
+// synchronise the whole device).  nq_gemv_static serves them with scratch that lives in this
+// library's own device image: a file-scope static array, resident on every GPU that loads the
+// library until the process exits.
+namespace nq {
+namespace gemv {
+
+constexpr int kStaticMaxRank = NQ_GEMV_STATIC_MAX_RANK;
+// control block + stage-2 operand [16 columns][round_up(rank, 64)] bf16 at the largest rank
+constexpr size_t kStaticScratchBytes = sizeof(Ctrl) + (size_t)2 * kMaxBatch * kStaticMaxRank * 2;
+static_assert(kStaticMaxRank % 64 == 0, "the scratch holds whole 64-column K blocks");
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device.  In host code the array's name
+// is only a host-side stand-in, so the address comes from cudaGetSymbolAddress, once per
+// device, with that device current.
+static int static_scratch(void **out) {
+    static std::mutex mu;
+    static void *addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(NQ_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static GEMV scratch)");
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return NQ_OK;
+}
+
+}  // namespace gemv
+}  // namespace nq
+
+extern "C" {
+
+int nq_gemv_static(int dtype, const void *x, int64_t batch, int64_t in_features, const void *scale_pre,
+                   const int32_t *v_bits, int64_t rank, const void *scale_mid, const int32_t *u_bits,
+                   int64_t out_features, const void *scale_post, void *y, void *stream) {
+    using namespace nq;
+    using namespace nq::gemv;
+    if (rank > kStaticMaxRank)
+        return fail(NQ_ERR_UNSUPPORTED, "nq_gemv_static supports rank <= %d (got %lld); use nq_gemv with a workspace",
+                    kStaticMaxRank, (long long)rank);
+    if (rank <= 0) return fail(NQ_ERR_INVALID_ARGUMENT, "rank must be positive");
+    void *scratch = nullptr;
+    int st = static_scratch(&scratch);
+    if (st) return st;
+    // The grid-barrier counter and the status word start from zero on every call; the
+    // stage-2 operand needs no clearing (each launch writes what it reads).
+    cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(Ctrl), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static GEMV control block)");
+    return nq_gemv(dtype, x, batch, in_features, scale_pre, v_bits, rank, scale_mid, u_bits, out_features, scale_post,
+                   y, scratch, kStaticScratchBytes, stream);
 }
 
 }  // extern "C"
