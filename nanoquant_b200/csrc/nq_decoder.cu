@@ -42,7 +42,68 @@ __device__ __forceinline__ float block_sum(float v, float *sh) {
 }
 
 // ------------------------------------------------------------------ RMSNorm
-// h = x (+ residual), rounded to T; residual_out = h; out = weight * T(h * rsqrt(mean(h^2) + eps))
+// h = x (+ residual), rounded to T; residual_out = h; out = weight * T(h * rsqrt(mean(h^2) + eps)).
+// One CTA per row; each thread keeps its 8-element chunks in registers between the two
+// passes, and all its loads are issued before any is used.
+constexpr int kNormThreads = 256;
+constexpr int kNormChunks = 4;  // hidden <= 256 * 8 * 4 = 8192 on the vector path
+
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(const T *__restrict__ x, const T *__restrict__ res_in,
+                                                                   T *__restrict__ res_out, const T *__restrict__ w,
+                                                                   T *__restrict__ out, int hidden, float eps) {
+    __shared__ float sh[32];
+    const size_t row = blockIdx.x;
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * hidden);
+    const uint4 *rr = res_in ? reinterpret_cast<const uint4 *>(res_in + row * hidden) : nullptr;
+    const uint4 *wr = reinterpret_cast<const uint4 *>(w);
+    const int n8 = hidden / 8;
+    uint4 xv[kNormChunks], rv[kNormChunks], wv[kNormChunks];
+#pragma unroll
+    for (int c = 0; c < kNormChunks; ++c) {
+        const int i = threadIdx.x + c * kNormThreads;
+        if (i < n8) {
+            xv[c] = __ldg(xr + i);
+            wv[c] = __ldg(wr + i);
+            if (rr) rv[c] = __ldg(rr + i);
+        }
+    }
+    float ss = 0.f;
+    float h[kNormChunks][8];
+#pragma unroll
+    for (int c = 0; c < kNormChunks; ++c) {
+        const int i = threadIdx.x + c * kNormThreads;
+        if (i >= n8) continue;
+        const T *xe = reinterpret_cast<const T *>(&xv[c]);
+        const T *re = reinterpret_cast<const T *>(&rv[c]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float v = tof(xe[j]);
+            if (rr) v = tof(fromf<T>(v + tof(re[j])));
+            h[c][j] = v;
+            ss += v * v;
+        }
+    }
+    const float inv = rsqrtf(block_sum(ss, sh) / (float)hidden + eps);
+#pragma unroll
+    for (int c = 0; c < kNormChunks; ++c) {
+        const int i = threadIdx.x + c * kNormThreads;
+        if (i >= n8) continue;
+        const T *we = reinterpret_cast<const T *>(&wv[c]);
+        uint4 o, hr;
+        T *oe = reinterpret_cast<T *>(&o);
+        T *he = reinterpret_cast<T *>(&hr);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            he[j] = fromf<T>(h[c][j]);
+            oe[j] = fromf<T>(tof(we[j]) * tof(fromf<T>(h[c][j] * inv)));
+        }
+        reinterpret_cast<uint4 *>(out + row * hidden)[i] = o;
+        if (res_out) reinterpret_cast<uint4 *>(res_out + row * hidden)[i] = rr ? hr : xv[c];
+    }
+}
+
+// Scalar fallback for rows that are not 16-byte aligned or longer than the vector path.
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const T *__restrict__ x, const T *__restrict__ res_in,
                                                       T *__restrict__ res_out, const T *__restrict__ w,
@@ -118,6 +179,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const T *__res
     __shared__ float qs[GRP][D];
     __shared__ float sc[GRP][kChunk];
     __shared__ float red[GRP][kAttnThreads / 32];
+    __shared__ float osm[(kAttnThreads / 32) * GRP * D];  // per-warp partial P.V sums
     const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int hq = hkv * GRP;
     const int L = seq_len[b];
@@ -194,18 +256,37 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const T *__res
         if (l == 0) red[g][w] = s;
     }
     __syncthreads();
-    // P.V: thread d accumulates dimension d for every head of the group
-    for (int d = threadIdx.x; d < D; d += kAttnThreads) {
-        float o[GRP];
+    // P.V: warp w takes positions p0 + w, p0 + w + 4, ...; lane l holds dimensions 4l..4l+3
+    // (8-byte coalesced loads), then the four warps' partial sums meet in shared memory.
+    static_assert(D == 128 && kAttnThreads == 128, "P.V layout assumes 4 warps x 32 lanes x 4 dims");
+    float o[GRP][4];
 #pragma unroll
-        for (int g = 0; g < GRP; ++g) o[g] = 0.f;
-        for (int p = p0; p < p1; ++p) {
-            const float vv = tof(vb[(size_t)p * D + d]);
+    for (int g = 0; g < GRP; ++g) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+#pragma unroll 4
+    for (int p = p0 + w; p < p1; p += kAttnThreads / 32) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2 *>(vb + (size_t)p * D) + l);
+        const T *e = reinterpret_cast<const T *>(&u);
+        const float v0 = tof(e[0]), v1 = tof(e[1]), v2 = tof(e[2]), v3 = tof(e[3]);
 #pragma unroll
-            for (int g = 0; g < GRP; ++g) o[g] += sc[g][p - p0] * vv;
+        for (int g = 0; g < GRP; ++g) {
+            const float pw = sc[g][p - p0];
+            o[g][0] += pw * v0;
+            o[g][1] += pw * v1;
+            o[g][2] += pw * v2;
+            o[g][3] += pw * v3;
         }
+    }
 #pragma unroll
-        for (int g = 0; g < GRP; ++g) po[(size_t)g * nsplit * (D + 2) + d] = o[g];
+    for (int g = 0; g < GRP; ++g)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) osm[(w * GRP + g) * D + 4 * l + i] = o[g][i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < GRP * D; i += kAttnThreads) {
+        const int g = i / D, d = i - g * D;
+        float acc = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < kAttnThreads / 32; ++ww) acc += osm[(ww * GRP + g) * D + d];
+        po[(size_t)g * nsplit * (D + 2) + d] = acc;
     }
     if (threadIdx.x == 0) {
 #pragma unroll
@@ -264,7 +345,18 @@ int nq_rmsnorm(int dtype, const void *x, const void *residual_in, void *residual
     using namespace nq;
     if (!x || !weight || !out || rows <= 0 || hidden <= 0) return fail(NQ_ERR_INVALID_ARGUMENT, "bad rmsnorm args");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (dtype == NQ_DTYPE_F16)
+    const bool vec = hidden % 8 == 0 && hidden <= 8 * dec::kNormThreads * dec::kNormChunks &&
+                     (((uintptr_t)x | (uintptr_t)residual_in | (uintptr_t)residual_out | (uintptr_t)weight |
+                       (uintptr_t)out) & 15) == 0;
+    if (vec && dtype == NQ_DTYPE_F16)
+        dec::rmsnorm_vec_kernel<__half><<<(unsigned)rows, dec::kNormThreads, 0, s>>>(
+            (const __half *)x, (const __half *)residual_in, (__half *)residual_out, (const __half *)weight,
+            (__half *)out, (int)hidden, eps);
+    else if (vec && dtype == NQ_DTYPE_BF16)
+        dec::rmsnorm_vec_kernel<__nv_bfloat16><<<(unsigned)rows, dec::kNormThreads, 0, s>>>(
+            (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)residual_in, (__nv_bfloat16 *)residual_out,
+            (const __nv_bfloat16 *)weight, (__nv_bfloat16 *)out, (int)hidden, eps);
+    else if (dtype == NQ_DTYPE_F16)
         dec::rmsnorm_kernel<__half><<<(unsigned)rows, 256, 0, s>>>(
             (const __half *)x, (const __half *)residual_in, (__half *)residual_out, (const __half *)weight,
             (__half *)out, (int)hidden, eps);

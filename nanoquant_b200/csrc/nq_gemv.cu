@@ -40,6 +40,7 @@ constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxBatch = 8;
 constexpr int kStaticSmemReserve = 1024;  // static __shared__ of the kernel (grid barrier flag)
+constexpr int kFoldMaxBatch = 2;         // batch rows for which stage 1 folds s2 into the B operand
 
 enum Mode : int { kStage1 = 1, kStage2 = 2, kFused = 3 };
 
@@ -54,12 +55,15 @@ struct Params {
     __nv_bfloat16 *tb;        // stage-2 B operand [16 columns][ldi]: (hi, lo) of t for 8 batch rows
     Ctrl *ctrl;
     int batch, in_f, rank, out_f;
-    int wv, wu;               // words per V row / U row
+    int wv, wu;               // words per V row / U row in HBM
+    int wvs, wus;             // words per row of the V / U slab in shared memory
+    int v_rows, u_rows;       // slabs copied row by row (padded stride) instead of in one piece
     int kb1, kb2;             // 64-column K blocks per stage
     int tiles1, tiles2;       // 16-row tiles per stage
     int mode;
     int x_in_smem;
-    uint32_t off_red, off_s2, off_x, off_v, off_u;
+    int fold;                 // stage 1 uses B = bf16 hi/lo of x*s2 and A = +-1
+    uint32_t off_red, off_s2, off_x, off_xs2, off_v, off_u, off_s1;
 };
 
 __device__ __forceinline__ void tile_range(int tiles, int c, int G, int &b, int &e) {
@@ -67,7 +71,7 @@ __device__ __forceinline__ void tile_range(int tiles, int c, int G, int &b, int 
     e = (tiles * (c + 1)) / G;
 }
 
-// Copy `n` 16-bit values into a zero-padded shared row of `npad` values.
+// Copy `n` 16-bit values into a zero-padded shared row of `npad` values (unaligned inputs).
 template <typename T>
 __device__ __forceinline__ void stage_row(T *dst, const T *src, int n, int npad) {
     const bool vec = ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
@@ -112,20 +116,29 @@ __device__ __forceinline__ void load16_smem(const void *p, uint32_t (&v)[8]) {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-// Bytes of the 16-byte-multiple prefix of rows [r0, r1) of a plane with `w` words per row.
-__device__ __forceinline__ uint32_t slab_bulk_bytes(int r0, int r1, int w) {
+// Bytes the TMA engine delivers for rows [r0, r1) of a plane with `w` words per row:
+// every row when copied row by row, else the 16-byte-multiple prefix of the slab.
+__device__ __forceinline__ uint32_t slab_bulk_bytes(int r0, int r1, int w, bool by_rows) {
     const uint32_t words = (r1 > r0) ? (uint32_t)(r1 - r0) * (uint32_t)w : 0u;
-    return (words * 4u) & ~15u;
+    return by_rows ? words * 4u : (words * 4u) & ~15u;
 }
 
-// Rows [r0, r1) of a plane -> smem: the 16-byte-multiple prefix through the TMA engine
-// (leader thread, completion on `bar`), the remaining <16 bytes by plain loads.
-__device__ __forceinline__ void copy_slab(uint32_t *dst, const uint32_t *plane, int r0, int r1, int w, uint64_t *bar,
-                                          bool leader) {
+// Rows [r0, r1) of a plane -> smem.  By rows (w % 4 == 0): one bulk copy per row into a
+// padded stride `ws`, issued by the lanes of warp `issuer`.  Otherwise the slab keeps
+// stride w: the 16-byte-multiple prefix goes through the TMA engine (leader thread), the
+// remaining <16 bytes by plain loads (the caller syncs afterwards).
+__device__ __forceinline__ void copy_slab(uint32_t *dst, const uint32_t *plane, int r0, int r1, int w, int ws,
+                                          bool by_rows, uint64_t *bar, int issuer) {
+    const uint32_t *src = plane + (size_t)r0 * w;
+    if (by_rows) {
+        if ((int)(threadIdx.x >> 5) == issuer)
+            for (int r = (int)(threadIdx.x & 31); r < r1 - r0; r += 32)
+                bulk_g2s(dst + (size_t)r * ws, src + (size_t)r * w, (uint32_t)w * 4u, bar);
+        return;
+    }
     const uint32_t words = (r1 > r0) ? (uint32_t)(r1 - r0) * (uint32_t)w : 0u;
     const uint32_t bulk = (words * 4u) & ~15u;
-    const uint32_t *src = plane + (size_t)r0 * w;
-    if (leader && bulk) bulk_g2s_pieces(dst, src, bulk, bar);
+    if ((int)threadIdx.x == issuer * 32 && bulk) bulk_g2s_pieces(dst, src, bulk, bar);
     for (uint32_t i = bulk / 4 + threadIdx.x; i < words; i += kThreads) dst[i] = __ldg(src + i);
 }
 
@@ -153,7 +166,7 @@ __device__ __forceinline__ void store_partial(float *r, const float (&acc)[4], i
     r[(g + 8) * 8 + 2 * t + 1] = acc[3];
 }
 
-// 8 bf16 pairs (16 values along k) of one B column, written by stage 1 (L2-resident);
+// 8 bf16 pairs (16 values along k) of one B column in global memory (L2-resident);
 // zeros when the column belongs to a batch row that does not exist.
 __device__ __forceinline__ void load_t_pairs(const __nv_bfloat16 *p, bool valid, uint32_t (&v)[8]) {
     uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a;
@@ -162,6 +175,24 @@ __device__ __forceinline__ void load_t_pairs(const __nv_bfloat16 *p, bool valid,
         b = __ldcg(reinterpret_cast<const uint4 *>(p) + 1);
     }
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// bf16 (hi, lo) pairs of two floats: hi = bf16(v), lo = bf16(v - hi)
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat16 ha = __float2bfloat16_rn(a), hb = __float2bfloat16_rn(b);
+    const __nv_bfloat16 la = __float2bfloat16_rn(a - __bfloat162float(ha));
+    const __nv_bfloat16 lb = __float2bfloat16_rn(b - __bfloat162float(hb));
+    hi = (uint32_t)__bfloat16_as_ushort(ha) | ((uint32_t)__bfloat16_as_ushort(hb) << 16);
+    lo = (uint32_t)__bfloat16_as_ushort(la) | ((uint32_t)__bfloat16_as_ushort(lb) << 16);
+}
+
+// A fragment of a +-1 (bf16) tile: rows g / g+8 words already shifted by 8*(t&1).
+__device__ __forceinline__ void sign_frag(uint32_t wA, uint32_t wB, int j, uint32_t (&a)[4]) {
+    constexpr uint32_t kOne = 0x3F803F80u;  // bf16 (1.0, 1.0)
+    a[0] = lop_sign(wA << (2 * j), kOne);
+    a[1] = lop_sign(wB << (2 * j), kOne);
+    a[2] = lop_sign(wA << (2 * j + 1), kOne);
+    a[3] = lop_sign(wB << (2 * j + 1), kOne);
 }
 
 template <typename T>
@@ -177,8 +208,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     float *red = reinterpret_cast<float *>(smem + p.off_red);
     T *s2s = reinterpret_cast<T *>(smem + p.off_s2);
     T *xs = reinterpret_cast<T *>(smem + p.off_x);
+    __nv_bfloat16 *xs2 = reinterpret_cast<__nv_bfloat16 *>(smem + p.off_xs2);
     uint32_t *vch = reinterpret_cast<uint32_t *>(smem + p.off_v);
     uint32_t *uch = reinterpret_cast<uint32_t *>(smem + p.off_u);
+    T *s1s = reinterpret_cast<T *>(smem + p.off_s1);
 
     int t1b = 0, t1e = 0, t2b = 0, t2e = 0;
     if (do1) tile_range(p.tiles1, c, G, t1b, t1e);
@@ -196,16 +229,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     }
     __syncthreads();
     // Put every byte this CTA needs in flight before anything else: V slab, s2 and x rows
-    // (when 16-byte aligned) on barrier 0, the U slab on barrier 1.
+    // (when 16-byte aligned) on barrier 0; the U slab and this CTA's s1 slice on barrier 1.
     const bool vec_rows = ((reinterpret_cast<uintptr_t>(p.s2) | reinterpret_cast<uintptr_t>(p.x)) & 15) == 0 &&
                           (p.in_f % 8) == 0;
     if (has1) {
-        uint32_t bytes0 = slab_bulk_bytes(r1b, r1e, p.wv);
-        if (vec_rows) bytes0 += (uint32_t)p.in_f * 2u * (1u + (p.x_in_smem ? (uint32_t)p.batch : 0u));
-        if (tid == 0) mbar_arrive_expect_tx(&bars[0], bytes0);
-        copy_slab(vch, p.vbits, r1b, r1e, p.wv, &bars[0], tid == 0);
-        if (vec_rows) {
-            if (tid == 0) {
+        if (tid == 0) {
+            uint32_t bytes0 = slab_bulk_bytes(r1b, r1e, p.wv, p.v_rows);
+            if (vec_rows) bytes0 += (uint32_t)p.in_f * 2u * (1u + (p.x_in_smem ? (uint32_t)p.batch : 0u));
+            mbar_arrive_expect_tx(&bars[0], bytes0);
+            if (vec_rows) {
                 bulk_g2s_pieces(s2s, p.s2, (uint32_t)p.in_f * 2u, &bars[0]);
                 if (p.x_in_smem) {
                     if (in_pad == p.in_f)
@@ -216,6 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                                             (uint32_t)p.in_f * 2u, &bars[0]);
                 }
             }
+        }
+        __syncwarp();
+        copy_slab(vch, p.vbits, r1b, r1e, p.wv, p.wvs, p.v_rows, &bars[0], 0);
+        if (vec_rows) {
             zero_tail<T>(s2s, p.in_f, in_pad);
             if (p.x_in_smem)
                 for (int b = 0; b < p.batch; ++b) zero_tail<T>(xs + (size_t)b * in_pad, p.in_f, in_pad);
@@ -228,8 +264,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         }
     }
     if (has2) {
-        if (tid == 0) mbar_arrive_expect_tx(&bars[1], slab_bulk_bytes(r2b, r2e, p.wu));
-        copy_slab(uch, p.ubits, r2b, r2e, p.wu, &bars[1], tid == 0);
+        // s1 slice: 16-byte-multiple prefix by the TMA engine, the tail by plain loads
+        const T *s1src = static_cast<const T *>(p.s1) + r2b;
+        const bool s1_vec = (reinterpret_cast<uintptr_t>(s1src) & 15) == 0;
+        const uint32_t s1_bulk = s1_vec ? ((uint32_t)(r2e - r2b) * 2u) & ~15u : 0u;
+        if (tid == 32) {
+            mbar_arrive_expect_tx(&bars[1], slab_bulk_bytes(r2b, r2e, p.wu, p.u_rows) + s1_bulk);
+            if (s1_bulk) bulk_g2s(s1s, s1src, s1_bulk, &bars[1]);
+        }
+        __syncwarp();
+        copy_slab(uch, p.ubits, r2b, r2e, p.wu, p.wus, p.u_rows, &bars[1], 1);
+        for (int i = (int)(s1_bulk / 2) + tid; i < r2e - r2b; i += kThreads) s1s[i] = s1src[i];
     }
     __syncthreads();
 
@@ -238,10 +283,32 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     // ------------------------------------------------------------------ stage 1
     if (has1) {
         ok = mbar_wait(&bars[0], 0, &p.ctrl->status);
+        const int nxc = 2 * p.batch;  // folded B columns: hi / lo of x*s2 per batch row
+        if (p.fold) {
+            // xs2[col][k] = bf16 hi (col even) / lo (col odd) of x[col/2][k] * s2[k], k < in_pad
+            for (int i = tid; i < p.batch * (in_pad / 8); i += kThreads) {
+                const int b = i / (in_pad / 8), k = 8 * (i - b * (in_pad / 8));
+                const uint4 xv = p.x_in_smem ? *reinterpret_cast<const uint4 *>(xs + (size_t)b * in_pad + k)
+                                             : make_uint4(0u, 0u, 0u, 0u);
+                const uint4 sv = *reinterpret_cast<const uint4 *>(s2s + k);
+                const T *xe = reinterpret_cast<const T *>(&xv);
+                const T *se = reinterpret_cast<const T *>(&sv);
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    split_pair(E::to_f(xe[2 * j]) * E::to_f(se[2 * j]), E::to_f(xe[2 * j + 1]) * E::to_f(se[2 * j + 1]),
+                               hi[j], lo[j]);
+                *reinterpret_cast<uint4 *>(xs2 + (size_t)(2 * b) * in_pad + k) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4 *>(xs2 + (size_t)(2 * b + 1) * in_pad + k) =
+                    make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+            __syncthreads();
+        }
         const uint32_t *sw = reinterpret_cast<const uint32_t *>(s2s);
         const T *xg = static_cast<const T *>(p.x) + (size_t)g * p.in_f;
         const uint32_t *xsw = reinterpret_cast<const uint32_t *>(xs + (size_t)g * in_pad);
-        const bool xrow = g < p.batch;
+        const __nv_bfloat16 *xcol = xs2 + (size_t)g * in_pad;
+        const bool xrow = g < p.batch, fcol = g < nxc;
         const int ntiles = t1e - t1b;
         const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
         for (int item = warp; item < items; item += kWarps) {
@@ -249,32 +316,55 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             item_of(item, KS, p.kb1, lt, kbeg, kend);
             const int tile = t1b + lt;
             const bool vA = ok && (16 * tile + g < p.rank), vB = ok && (16 * tile + g + 8 < p.rank);
-            const uint32_t *rowA = vch + (size_t)(lt * 16 + g) * p.wv;
-            const uint32_t *rowB = rowA + (size_t)8 * p.wv;
+            const uint32_t *rowA = vch + (size_t)(lt * 16 + g) * p.wvs;
+            const uint32_t *rowB = rowA + (size_t)8 * p.wvs;
             float acc[4][4] = {};
+            if (p.fold) {
 #pragma unroll 2
-            for (int kb = kbeg; kb < kend; ++kb) {
-                const int wi = 2 * kb + (t >> 1);
-                const uint32_t wA = (vA && wi < p.wv) ? rowA[wi] << sh0 : 0u;
-                const uint32_t wB = (vB && wi < p.wv) ? rowB[wi] << sh0 : 0u;
-                const int kc = 64 * kb + 16 * t;
-                uint32_t sp[8], xp[8];
-                load16_smem(sw + kc / 2, sp);
-                if (!xrow) {
+                for (int kb = kbeg; kb < kend; ++kb) {
+                    const int wi = 2 * kb + (t >> 1);
+                    const uint32_t wA = (vA && wi < p.wv) ? rowA[wi] << sh0 : 0u;
+                    const uint32_t wB = (vB && wi < p.wv) ? rowB[wi] << sh0 : 0u;
+                    const int kc = 64 * kb + 16 * t;
+                    uint32_t bp[8];
+                    if (fcol) {
+                        load16_smem(xcol + kc, bp);
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) xp[j] = 0u;
-                } else if (p.x_in_smem) {
-                    load16_smem(xsw + kc / 2, xp);
-                } else {
-                    load16_global<T>(xg, kc, p.in_f, xp);
+                        for (int j = 0; j < 8; ++j) bp[j] = 0u;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t a[4];
+                        sign_frag(wA, wB, j, a);
+                        mma_bf16_16816(acc[j], a[0], a[1], a[2], a[3], bp[2 * j], bp[2 * j + 1]);
+                    }
                 }
+            } else {
+#pragma unroll 2
+                for (int kb = kbeg; kb < kend; ++kb) {
+                    const int wi = 2 * kb + (t >> 1);
+                    const uint32_t wA = (vA && wi < p.wv) ? rowA[wi] << sh0 : 0u;
+                    const uint32_t wB = (vB && wi < p.wv) ? rowB[wi] << sh0 : 0u;
+                    const int kc = 64 * kb + 16 * t;
+                    uint32_t sp[8], xp[8];
+                    load16_smem(sw + kc / 2, sp);
+                    if (!xrow) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t a0 = lop_sign(wA << (2 * j), sp[2 * j]);
-                    const uint32_t a1 = lop_sign(wB << (2 * j), sp[2 * j]);
-                    const uint32_t a2 = lop_sign(wA << (2 * j + 1), sp[2 * j + 1]);
-                    const uint32_t a3 = lop_sign(wB << (2 * j + 1), sp[2 * j + 1]);
-                    E::mma(acc[j], a0, a1, a2, a3, xp[2 * j], xp[2 * j + 1]);
+                        for (int j = 0; j < 8; ++j) xp[j] = 0u;
+                    } else if (p.x_in_smem) {
+                        load16_smem(xsw + kc / 2, xp);
+                    } else {
+                        load16_global<T>(xg, kc, p.in_f, xp);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t a0 = lop_sign(wA << (2 * j), sp[2 * j]);
+                        const uint32_t a1 = lop_sign(wB << (2 * j), sp[2 * j]);
+                        const uint32_t a2 = lop_sign(wA << (2 * j + 1), sp[2 * j + 1]);
+                        const uint32_t a3 = lop_sign(wB << (2 * j + 1), sp[2 * j + 1]);
+                        E::mma(acc[j], a0, a1, a2, a3, xp[2 * j], xp[2 * j + 1]);
+                    }
                 }
             }
             float sum[4];
@@ -287,7 +377,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
             const int b = rem >> 4, row = rem & 15;
             float s = 0.f;
-            for (int ks = 0; ks < KS; ++ks) s += red[(lt * KS + ks) * 256 + row * 8 + b];
+            if (p.fold) {
+                for (int ks = 0; ks < KS; ++ks) {
+                    const float *r = red + (lt * KS + ks) * 256 + row * 8 + 2 * b;
+                    s += r[0] + r[1];
+                }
+            } else {
+                for (int ks = 0; ks < KS; ++ks) s += red[(lt * KS + ks) * 256 + row * 8 + b];
+            }
             const int k = 16 * (t1b + lt) + row;
             if (k < p.rank) {
                 if (p.smid) s *= E::to_f(static_cast<const T *>(p.smid)[k]);
@@ -317,37 +414,44 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles: (hi, lo) of 4 batch rows each
         const int ntiles = t2e - t2b;
         const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
-        constexpr uint32_t kOne = 0x3F803F80u;  // bf16 (1.0, 1.0)
         // B column g of n-tile q is the hi (g even) or lo (g odd) part of batch row 4q + g/2,
         // stored ready-made by stage 1 as bf16 pairs along k
         const int b0 = g >> 1, b1 = 4 + (g >> 1);
+        const bool v0 = b0 < p.batch, v1 = nt == 2 && b1 < p.batch;
         const __nv_bfloat16 *trow0 = p.tb + (size_t)g * ldi;
         const __nv_bfloat16 *trow1 = p.tb + (size_t)(8 + g) * ldi;
+        constexpr int kChunkKb = 4;  // K blocks whose B fragments are fetched together
         for (int item = warp; item < items; item += kWarps) {
             int lt, kbeg, kend;
             item_of(item, KS, p.kb2, lt, kbeg, kend);
             const int tile = t2b + lt;
             const bool vA = ok && (16 * tile + g < p.out_f), vB = ok && (16 * tile + g + 8 < p.out_f);
-            const uint32_t *rowA = uch + (size_t)(lt * 16 + g) * p.wu;
-            const uint32_t *rowB = rowA + (size_t)8 * p.wu;
+            const uint32_t *rowA = uch + (size_t)(lt * 16 + g) * p.wus;
+            const uint32_t *rowB = rowA + (size_t)8 * p.wus;
             float acc0[4][4] = {}, acc1[4][4] = {};
-#pragma unroll 2
-            for (int kb = kbeg; kb < kend; ++kb) {
-                const int wi = 2 * kb + (t >> 1);
-                const uint32_t wA = (vA && wi < p.wu) ? rowA[wi] << sh0 : 0u;
-                const uint32_t wB = (vB && wi < p.wu) ? rowB[wi] << sh0 : 0u;
-                const int kc = 64 * kb + 16 * t;
-                uint32_t bp0[8], bp1[8];
-                load_t_pairs(trow0 + kc, b0 < p.batch, bp0);
-                load_t_pairs(trow1 + kc, nt == 2 && b1 < p.batch, bp1);
+            for (int kb0 = kbeg; kb0 < kend; kb0 += kChunkKb) {
+                uint32_t bp0[kChunkKb][8], bp1[kChunkKb][8];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t a0 = lop_sign(wA << (2 * j), kOne);
-                    const uint32_t a1 = lop_sign(wB << (2 * j), kOne);
-                    const uint32_t a2 = lop_sign(wA << (2 * j + 1), kOne);
-                    const uint32_t a3 = lop_sign(wB << (2 * j + 1), kOne);
-                    mma_bf16_16816(acc0[j], a0, a1, a2, a3, bp0[2 * j], bp0[2 * j + 1]);
-                    if (nt == 2) mma_bf16_16816(acc1[j], a0, a1, a2, a3, bp1[2 * j], bp1[2 * j + 1]);
+                for (int q = 0; q < kChunkKb; ++q) {
+                    const int kc = 64 * (kb0 + q) + 16 * t;
+                    const bool in = kb0 + q < kend;
+                    load_t_pairs(trow0 + kc, in && v0, bp0[q]);
+                    load_t_pairs(trow1 + kc, in && v1, bp1[q]);
+                }
+#pragma unroll
+                for (int q = 0; q < kChunkKb; ++q) {
+                    const int kb = kb0 + q;
+                    if (kb >= kend) break;
+                    const int wi = 2 * kb + (t >> 1);
+                    const uint32_t wA = (vA && wi < p.wu) ? rowA[wi] << sh0 : 0u;
+                    const uint32_t wB = (vB && wi < p.wu) ? rowB[wi] << sh0 : 0u;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t a[4];
+                        sign_frag(wA, wB, j, a);
+                        mma_bf16_16816(acc0[j], a[0], a[1], a[2], a[3], bp0[q][2 * j], bp0[q][2 * j + 1]);
+                        if (nt == 2) mma_bf16_16816(acc1[j], a[0], a[1], a[2], a[3], bp1[q][2 * j], bp1[q][2 * j + 1]);
+                    }
                 }
             }
             float s0[4], s1v[4];
@@ -371,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
             const int m = 16 * (t2b + lt) + row;
             if (m < p.out_f) {
-                const float v = s * E::to_f(static_cast<const T *>(p.s1)[m]);
+                const float v = s * E::to_f(s1s[m - r2b]);
                 static_cast<T *>(p.y)[(size_t)b * p.out_f + m] = E::out(v);
             }
         }
@@ -388,25 +492,48 @@ struct Plan {
 
 static inline uint32_t align128(size_t v) { return (uint32_t)((v + 127) & ~size_t(127)); }
 
+// Shared-memory row stride (words) for a plane with w words per row copied row by row:
+// a multiple of 4 words (16-byte aligned rows) that is an odd multiple of 4, so rows
+// g = 0..7 of an MMA tile start in 8 different 4-bank groups and the per-k sign-word
+// loads are conflict free.
+static inline int padded_stride(int w) {
+    int s = (w + 3) & ~3;
+    if (((s / 4) & 1) == 0) s += 4;
+    return s;
+}
+
 // Shared-memory layout for a launch whose CTAs own at most `rows1`/`rows2` rows.
-static size_t layout(Params &p, int rows1, int rows2, bool stage1, bool stage2, bool x_in_smem) {
+static size_t layout(Params &p, int rows1, int rows2, bool stage1, bool stage2, bool x_in_smem, bool fold) {
     size_t off = 128;  // mbarriers
     const int items = std::max(kWarps, std::max(rows1, rows2) / 16);
     p.off_red = (uint32_t)off;
     off = align128(off + (size_t)items * 256 * sizeof(float));
     const size_t in_pad = (size_t)p.kb1 * 64;
-    p.off_s2 = (uint32_t)off;
-    p.off_x = (uint32_t)off;
-    p.off_v = (uint32_t)off;
+    p.v_rows = (p.wv % 4) == 0;
+    p.u_rows = (p.wu % 4) == 0;
+    p.wvs = p.v_rows ? padded_stride(p.wv) : p.wv;
+    p.wus = p.u_rows ? padded_stride(p.wu) : p.wu;
+    p.off_s2 = p.off_x = p.off_xs2 = p.off_v = (uint32_t)off;
+    p.fold = 0;
     if (stage1) {
         off = align128(off + in_pad * 2);
         p.off_x = (uint32_t)off;
         if (x_in_smem) off = align128(off + (size_t)p.batch * in_pad * 2);
+        p.off_xs2 = (uint32_t)off;
+        if (fold && x_in_smem) {
+            p.fold = 1;
+            off = align128(off + (size_t)2 * p.batch * in_pad * 2);
+        }
         p.off_v = (uint32_t)off;
-        off = align128(off + (size_t)rows1 * p.wv * 4 + 16);
+        off = align128(off + (size_t)rows1 * p.wvs * 4 + 16);
     }
     p.off_u = (uint32_t)off;
-    if (stage2) off = align128(off + (size_t)rows2 * p.wu * 4 + 16);
+    p.off_s1 = (uint32_t)off;
+    if (stage2) {
+        off = align128(off + (size_t)rows2 * p.wus * 4 + 16);
+        p.off_s1 = (uint32_t)off;
+        off = align128(off + (size_t)rows2 * 2 + 16);
+    }
     p.x_in_smem = x_in_smem ? 1 : 0;
     return off;
 }
@@ -416,13 +543,15 @@ static int make_plan(int dev, const Params &base, Plan &plan) {
     const size_t cap = (size_t)di.max_smem_optin - kStaticSmemReserve;
     const int sms = di.sms;
     Params p = base;
-    // fused: one CTA per SM, tiles spread evenly
+    // fused: one CTA per SM, tiles spread evenly; prefer x staged and the folded operand
     const int G = sms;
     const int rows1 = 16 * ((p.tiles1 + G - 1) / G), rows2 = 16 * ((p.tiles2 + G - 1) / G);
-    for (int xs = 1; xs >= 0; --xs) {
+    const int variants[3][2] = {{1, 1}, {1, 0}, {0, 0}};  // (x in smem, fold)
+    for (const auto &v : variants) {
+        if (v[1] && p.batch > kFoldMaxBatch) continue;
         Params q = p;
         q.mode = kFused;
-        const size_t need = layout(q, rows1, rows2, true, true, xs != 0);
+        const size_t need = layout(q, rows1, rows2, true, true, v[0] != 0, v[1] != 0);
         if (need <= cap && di.coop) {
             plan.mode = kFused;
             plan.grid = G;
@@ -432,12 +561,13 @@ static int make_plan(int dev, const Params &base, Plan &plan) {
         }
     }
     // two ordinary launches, one 16-row tile per CTA
-    for (int xs = 1; xs >= 0; --xs) {
+    for (const auto &v : variants) {
+        if (v[1] && p.batch > kFoldMaxBatch) continue;
         Params q1 = p, q2 = p;
         q1.mode = kStage1;
         q2.mode = kStage2;
-        const size_t n1 = layout(q1, 16, 0, true, false, xs != 0);
-        const size_t n2 = layout(q2, 0, 16, false, true, false);
+        const size_t n1 = layout(q1, 16, 0, true, false, v[0] != 0, v[1] != 0);
+        const size_t n2 = layout(q2, 0, 16, false, true, false, false);
         if (n1 <= cap && n2 <= cap) {
             plan.mode = kStage1 | kStage2 | 4;  // marker: split
             plan.grid1 = p.tiles1;

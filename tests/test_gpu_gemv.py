@@ -137,3 +137,23 @@ def test_reference_op_and_module_drop_in():
         y3 = m2(d.x.view(2, 2, -1))
         assert y3.shape == (2, 2, 4096)
         assert_close_to_oracle(y3.view(4, -1), ref_mod, "f16")
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_gemv_unaligned_vectors(batch):
+    """x, s2 and s1 given as views at a 2-byte offset (only 2-byte alignment is required):
+    the kernel must take its plain-load paths instead of the bulk copies."""
+    L = orc.make_layer(77 + batch, 1000, 512, 200, batch, "f16", with_mid=True)
+    d = DeviceLayer(L, "f16")
+
+    def shifted(t):
+        buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=t.device)
+        v = buf[1:1 + t.numel()].view(t.shape)
+        v.copy_(t)
+        assert v.data_ptr() % 16 != 0
+        return v
+
+    d.x, d.s2, d.s1 = shifted(d.x), shifted(d.s2), shifted(d.s1)
+    y, ws = capi_gemv(d)
+    assert_close_to_oracle(y, d.oracle(), "f16")
+    assert workspace_status(ws) == 0
