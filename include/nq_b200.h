@@ -94,6 +94,28 @@ NQ_API int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features,
             void *stream);
 
 /* ---------------------------------------------------------------------------------
+ * Grouped decode GEMV: up to 3 NanoQuant layers that read the same x (the q/k/v or
+ * gate/up projections of a decoder block) in ONE launch; layer l behaves exactly like
+ * nq_gemv on its own arguments.  No single reference counterpart: the reference calls
+ * nanoquant_dyn_forward once per layer (src/nanoquant/modules/linear.py:155-164).
+ * Workspace: nq_gemv_group_workspace_bytes(n_layers, ranks); same rules as nq_gemv.
+ * ------------------------------------------------------------------------------- */
+typedef struct {
+    const void *scale_pre;     /* [in] */
+    const int32_t *v_bits;     /* [rank, ceil(in/32)], HALF2 */
+    int64_t rank;
+    const void *scale_mid;     /* [rank] or NULL */
+    const int32_t *u_bits;     /* [out, ceil(rank/32)], HALF2 */
+    int64_t out_features;
+    const void *scale_post;    /* [out] */
+    void *y;                   /* [batch, out] */
+} nq_gemv_layer;
+NQ_API size_t nq_gemv_group_workspace_bytes(int n_layers, const int64_t *ranks);
+NQ_API int nq_gemv_group(int dtype, const void *x, int64_t batch, int64_t in_features, int n_layers,
+                         const nq_gemv_layer *layers, void *workspace, size_t workspace_bytes,
+                         void *stream);
+
+/* ---------------------------------------------------------------------------------
  * Allocation-free decode GEMV.  No counterpart in the reference: its kernels allocate their
  * intermediate with the torch caching allocator on every call (gemv_kernel.cu:345-346).
  * For callers that cannot allocate device memory -- a plugin or custom-op interface that

@@ -28,6 +28,13 @@ NQ_DTYPE_BF16 = 1
 NQ_BITS_LSB_FIRST = 0
 NQ_BITS_HALF2 = 1
 
+
+class GemvLayer(ctypes.Structure):
+    """nq_gemv_layer of include/nq_b200.h."""
+    _fields_ = [("scale_pre", ctypes.c_void_p), ("v_bits", ctypes.c_void_p), ("rank", ctypes.c_int64),
+                ("scale_mid", ctypes.c_void_p), ("u_bits", ctypes.c_void_p), ("out_features", ctypes.c_int64),
+                ("scale_post", ctypes.c_void_p), ("y", ctypes.c_void_p)]
+
 _lock = threading.Lock()
 _cuda = None
 _torch_loaded = False
@@ -45,6 +52,9 @@ _SIGNATURES = {
     "nq_gemv": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64,
                            _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p,
                            _c.c_size_t, _c.c_void_p]),
+    "nq_gemv_group_workspace_bytes": (_c.c_size_t, [_c.c_int, _c.c_void_p]),
+    "nq_gemv_group": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_void_p, _c.c_void_p,
+                                 _c.c_size_t, _c.c_void_p]),
     "nq_gemv_static": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p,
                                   _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p,
                                   _c.c_void_p]),

@@ -44,28 +44,6 @@ constexpr int kFoldMaxBatch = 2;         // batch rows for which stage 1 folds s
 
 enum Mode : int { kStage1 = 1, kStage2 = 2, kFused = 3 };
 
-struct Params {
-    const void *x;            // [batch, in]
-    const void *s2;           // [in]
-    const uint32_t *vbits;    // [rank, wv]
-    const void *smid;         // [rank] or null
-    const uint32_t *ubits;    // [out, wu]
-    const void *s1;           // [out]
-    void *y;                  // [batch, out]
-    __nv_bfloat16 *tb;        // stage-2 B operand [16 columns][ldi]: (hi, lo) of t for 8 batch rows
-    Ctrl *ctrl;
-    int batch, in_f, rank, out_f;
-    int wv, wu;               // words per V row / U row in HBM
-    int wvs, wus;             // words per row of the V / U slab in shared memory
-    int v_rows, u_rows;       // slabs copied row by row (padded stride) instead of in one piece
-    int kb1, kb2;             // 64-column K blocks per stage
-    int tiles1, tiles2;       // 16-row tiles per stage
-    int mode;
-    int x_in_smem;
-    int fold;                 // stage 1 uses B = bf16 hi/lo of x*s2 and A = +-1
-    uint32_t off_red, off_s2, off_x, off_xs2, off_v, off_u, off_s1;
-};
-
 __device__ __forceinline__ void tile_range(int tiles, int c, int G, int &b, int &e) {
     b = (tiles * c) / G;  // tiles <= 2^16 and G <= 2^10 keep this within 32 bits
     e = (tiles * (c + 1)) / G;
@@ -195,6 +173,52 @@ __device__ __forceinline__ void sign_frag(uint32_t wA, uint32_t wB, int j, uint3
     a[3] = lop_sign(wB << (2 * j + 1), kOne);
 }
 
+constexpr int kMaxGroup = 3;  // layers sharing one input x in a single launch (q/k/v, gate/up)
+
+// One NanoQuant layer of a launch group.
+struct Member {
+    const void *s2;            // scale_pre [in]
+    const uint32_t *vbits;     // V planes [rank, wv]
+    const void *smid;          // scale_mid [rank] or null
+    const uint32_t *ubits;     // U planes [out, wu]
+    const void *s1;            // scale_post [out]
+    void *y;                   // [batch, out]
+    __nv_bfloat16 *tb;         // stage-2 B operand [16 columns][ldi]: (hi, lo) of t for 8 batch rows
+    int rank, out_f, wu, kb2, ldi;
+    int tiles1, tiles2;        // 16-row tiles of this layer in stage 1 / stage 2
+    int t1_start, t2_start;    // its first tile in the group's concatenated tile lists
+    int u_rows, wus;           // U slab copied row by row (wu % 4 == 0) and its smem row stride
+};
+
+struct Params {
+    const void *x;             // [batch, in], shared by every member
+    Ctrl *ctrl;
+    int batch, in_f, wv, kb1, nm;
+    Member m[kMaxGroup];
+    int tiles1, tiles2;        // totals over members
+    int wvs, v_rows;           // V slab smem stride (words) and row-by-row copy flag (wv % 4 == 0)
+    int mode, x_in_smem, fold;
+    uint32_t off_red, off_s2, off_x, off_xs2, off_v, off_u, off_s1;
+};
+
+__device__ __forceinline__ int member_of1(const Params &p, int tile) {
+    int l = 0;
+    while (l + 1 < p.nm && tile >= p.m[l + 1].t1_start) ++l;
+    return l;
+}
+__device__ __forceinline__ int member_of2(const Params &p, int tile) {
+    int l = 0;
+    while (l + 1 < p.nm && tile >= p.m[l + 1].t2_start) ++l;
+    return l;
+}
+
+// The part of a CTA's stage-2 tile range [t2b, t2e) that belongs to member l:
+// tiles [a, b) (global indices); a >= b when there is none.
+__device__ __forceinline__ void seg_tiles(const Member &mb, int t2b, int t2e, int &a, int &b) {
+    a = max(t2b, mb.t2_start);
+    b = min(t2e, mb.t2_start + mb.tiles2);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -206,21 +230,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     float *red = reinterpret_cast<float *>(smem + p.off_red);
-    T *s2s = reinterpret_cast<T *>(smem + p.off_s2);
-    T *xs = reinterpret_cast<T *>(smem + p.off_x);
-    __nv_bfloat16 *xs2 = reinterpret_cast<__nv_bfloat16 *>(smem + p.off_xs2);
-    uint32_t *vch = reinterpret_cast<uint32_t *>(smem + p.off_v);
-    uint32_t *uch = reinterpret_cast<uint32_t *>(smem + p.off_u);
-    T *s1s = reinterpret_cast<T *>(smem + p.off_s1);
+    T *s2s = reinterpret_cast<T *>(smem + p.off_s2);              // [nm][in_pad]
+    T *xs = reinterpret_cast<T *>(smem + p.off_x);                // [batch][in_pad]
+    __nv_bfloat16 *xs2 = reinterpret_cast<__nv_bfloat16 *>(smem + p.off_xs2);  // [nm][2*batch][in_pad]
+    uint32_t *vch = reinterpret_cast<uint32_t *>(smem + p.off_v); // [16 * tiles][wvs]
+    uint32_t *uch = reinterpret_cast<uint32_t *>(smem + p.off_u); // per-member segments
+    T *s1s = reinterpret_cast<T *>(smem + p.off_s1);              // [16 * tiles]
 
     int t1b = 0, t1e = 0, t2b = 0, t2e = 0;
     if (do1) tile_range(p.tiles1, c, G, t1b, t1e);
     if (do2) tile_range(p.tiles2, c, G, t2b, t2e);
-    const int r1b = 16 * t1b, r1e = min(16 * t1e, p.rank);
-    const int r2b = 16 * t2b, r2e = min(16 * t2e, p.out_f);
-    const bool has1 = r1e > r1b, has2 = r2e > r2b;
+    const bool has1 = t1e > t1b, has2 = t2e > t2b;
     const int in_pad = p.kb1 * 64;
-    const int ldi = p.kb2 * 64;  // stride of a B column (bf16 values), a multiple of 64 and >= rank
 
     if (tid == 0) {
         mbar_init(&bars[0], 1);
@@ -228,17 +249,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         fence_mbar_init();
     }
     __syncthreads();
-    // Put every byte this CTA needs in flight before anything else: V slab, s2 and x rows
-    // (when 16-byte aligned) on barrier 0; the U slab and this CTA's s1 slice on barrier 1.
-    const bool vec_rows = ((reinterpret_cast<uintptr_t>(p.s2) | reinterpret_cast<uintptr_t>(p.x)) & 15) == 0 &&
-                          (p.in_f % 8) == 0;
+    // Put every byte this CTA needs in flight before anything else: V rows, s2 and x rows
+    // (when 16-byte aligned) on barrier 0; U rows and the s1 slices on barrier 1.
+    bool vec_rows = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 && (p.in_f % 8) == 0;
+    for (int l = 0; l < p.nm; ++l) vec_rows = vec_rows && (reinterpret_cast<uintptr_t>(p.m[l].s2) & 15) == 0;
     if (has1) {
         if (tid == 0) {
-            uint32_t bytes0 = slab_bulk_bytes(r1b, r1e, p.wv, p.v_rows);
-            if (vec_rows) bytes0 += (uint32_t)p.in_f * 2u * (1u + (p.x_in_smem ? (uint32_t)p.batch : 0u));
+            uint32_t bytes0 = 0;
+            for (int l = 0; l < p.nm; ++l) {
+                const Member &mb = p.m[l];
+                const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
+                if (a < b)
+                    bytes0 += slab_bulk_bytes(16 * (a - mb.t1_start), min(16 * (b - mb.t1_start), mb.rank), p.wv,
+                                              p.v_rows);
+            }
+            if (vec_rows) bytes0 += (uint32_t)p.in_f * 2u * ((uint32_t)p.nm + (p.x_in_smem ? (uint32_t)p.batch : 0u));
             mbar_arrive_expect_tx(&bars[0], bytes0);
             if (vec_rows) {
-                bulk_g2s_pieces(s2s, p.s2, (uint32_t)p.in_f * 2u, &bars[0]);
+                for (int l = 0; l < p.nm; ++l)
+                    bulk_g2s_pieces(s2s + (size_t)l * in_pad, p.m[l].s2, (uint32_t)p.in_f * 2u, &bars[0]);
                 if (p.x_in_smem) {
                     if (in_pad == p.in_f)
                         bulk_g2s_pieces(xs, p.x, (uint32_t)p.batch * (uint32_t)p.in_f * 2u, &bars[0]);
@@ -250,31 +279,64 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
         }
         __syncwarp();
-        copy_slab(vch, p.vbits, r1b, r1e, p.wv, p.wvs, p.v_rows, &bars[0], 0);
-        if (vec_rows) {
-            zero_tail<T>(s2s, p.in_f, in_pad);
-            if (p.x_in_smem)
-                for (int b = 0; b < p.batch; ++b) zero_tail<T>(xs + (size_t)b * in_pad, p.in_f, in_pad);
-        } else {
-            stage_row<T>(s2s, static_cast<const T *>(p.s2), p.in_f, in_pad);
-            if (p.x_in_smem)
-                for (int b = 0; b < p.batch; ++b)
+        for (int l = 0; l < p.nm; ++l) {
+            const Member &mb = p.m[l];
+            const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
+            if (a < b)
+                copy_slab(vch + (size_t)16 * (a - t1b) * p.wvs, mb.vbits, 16 * (a - mb.t1_start),
+                          min(16 * (b - mb.t1_start), mb.rank), p.wv, p.wvs, p.v_rows, &bars[0], 0);
+        }
+        for (int l = 0; l < p.nm; ++l) {
+            if (vec_rows) {
+                zero_tail<T>(s2s + (size_t)l * in_pad, p.in_f, in_pad);
+            } else {
+                stage_row<T>(s2s + (size_t)l * in_pad, static_cast<const T *>(p.m[l].s2), p.in_f, in_pad);
+            }
+        }
+        if (p.x_in_smem)
+            for (int b = 0; b < p.batch; ++b) {
+                if (vec_rows)
+                    zero_tail<T>(xs + (size_t)b * in_pad, p.in_f, in_pad);
+                else
                     stage_row<T>(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f, p.in_f,
                                  in_pad);
-        }
+            }
     }
     if (has2) {
-        // s1 slice: 16-byte-multiple prefix by the TMA engine, the tail by plain loads
-        const T *s1src = static_cast<const T *>(p.s1) + r2b;
-        const bool s1_vec = (reinterpret_cast<uintptr_t>(s1src) & 15) == 0;
-        const uint32_t s1_bulk = s1_vec ? ((uint32_t)(r2e - r2b) * 2u) & ~15u : 0u;
+        // U rows and s1 slices, one segment per member; segment k of the smem U region
+        // starts after the previous segments' rows (each at its member's stride).
         if (tid == 32) {
-            mbar_arrive_expect_tx(&bars[1], slab_bulk_bytes(r2b, r2e, p.wu, p.u_rows) + s1_bulk);
-            if (s1_bulk) bulk_g2s(s1s, s1src, s1_bulk, &bars[1]);
+            uint32_t bytes1 = 0;
+            for (int l = 0; l < p.nm; ++l) {
+                const Member &mb = p.m[l];
+                int a, b;
+                seg_tiles(mb, t2b, t2e, a, b);
+                if (a >= b) continue;
+                const int r0 = 16 * (a - mb.t2_start), r1 = min(16 * (b - mb.t2_start), mb.out_f);
+                bytes1 += slab_bulk_bytes(r0, r1, mb.wu, mb.u_rows);
+                const T *s1src = static_cast<const T *>(mb.s1) + r0;
+                if ((reinterpret_cast<uintptr_t>(s1src) & 15) == 0) bytes1 += ((uint32_t)(r1 - r0) * 2u) & ~15u;
+            }
+            mbar_arrive_expect_tx(&bars[1], bytes1);
         }
         __syncwarp();
-        copy_slab(uch, p.ubits, r2b, r2e, p.wu, p.wus, p.u_rows, &bars[1], 1);
-        for (int i = (int)(s1_bulk / 2) + tid; i < r2e - r2b; i += kThreads) s1s[i] = s1src[i];
+        uint32_t uoff = 0;  // words
+        for (int l = 0; l < p.nm; ++l) {
+            const Member &mb = p.m[l];
+            int a, b;
+            seg_tiles(mb, t2b, t2e, a, b);
+            if (a >= b) continue;
+            const int r0 = 16 * (a - mb.t2_start), r1 = min(16 * (b - mb.t2_start), mb.out_f);
+            copy_slab(uch + uoff, mb.ubits, r0, r1, mb.wu, mb.wus, mb.u_rows, &bars[1], 1);
+            uoff += (uint32_t)(16 * (b - a)) * (uint32_t)mb.wus;
+            uoff = (uoff + 3u) & ~3u;  // keep every segment 16-byte aligned
+            const T *s1src = static_cast<const T *>(mb.s1) + r0;
+            T *s1dst = s1s + 16 * (a - t2b);
+            const uint32_t s1_bulk =
+                (reinterpret_cast<uintptr_t>(s1src) & 15) == 0 ? ((uint32_t)(r1 - r0) * 2u) & ~15u : 0u;
+            if (tid == 32 && s1_bulk) bulk_g2s(s1dst, s1src, s1_bulk, &bars[1]);
+            for (int i = (int)(s1_bulk / 2) + tid; i < r1 - r0; i += kThreads) s1dst[i] = s1src[i];
+        }
     }
     __syncthreads();
 
@@ -283,14 +345,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     // ------------------------------------------------------------------ stage 1
     if (has1) {
         ok = mbar_wait(&bars[0], 0, &p.ctrl->status);
-        const int nxc = 2 * p.batch;  // folded B columns: hi / lo of x*s2 per batch row
+        const int nxc = 2 * p.batch;  // folded B columns per member: hi / lo of x*s2 per batch row
         if (p.fold) {
-            // xs2[col][k] = bf16 hi (col even) / lo (col odd) of x[col/2][k] * s2[k], k < in_pad
-            for (int i = tid; i < p.batch * (in_pad / 8); i += kThreads) {
-                const int b = i / (in_pad / 8), k = 8 * (i - b * (in_pad / 8));
-                const uint4 xv = p.x_in_smem ? *reinterpret_cast<const uint4 *>(xs + (size_t)b * in_pad + k)
-                                             : make_uint4(0u, 0u, 0u, 0u);
-                const uint4 sv = *reinterpret_cast<const uint4 *>(s2s + k);
+            // xs2[l][col][k] = bf16 hi (col even) / lo (col odd) of x[col/2][k] * s2_l[k]
+            const int chunks = in_pad / 8;
+            for (int i = tid; i < p.nm * p.batch * chunks; i += kThreads) {
+                const int lb = i / chunks, k = 8 * (i - lb * chunks);
+                const int l = lb / p.batch, b = lb - l * p.batch;
+                const uint4 xv = *reinterpret_cast<const uint4 *>(xs + (size_t)b * in_pad + k);
+                const uint4 sv = *reinterpret_cast<const uint4 *>(s2s + (size_t)l * in_pad + k);
                 const T *xe = reinterpret_cast<const T *>(&xv);
                 const T *se = reinterpret_cast<const T *>(&sv);
                 uint32_t hi[4], lo[4];
@@ -298,16 +361,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 for (int j = 0; j < 4; ++j)
                     split_pair(E::to_f(xe[2 * j]) * E::to_f(se[2 * j]), E::to_f(xe[2 * j + 1]) * E::to_f(se[2 * j + 1]),
                                hi[j], lo[j]);
-                *reinterpret_cast<uint4 *>(xs2 + (size_t)(2 * b) * in_pad + k) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4 *>(xs2 + (size_t)(2 * b + 1) * in_pad + k) =
-                    make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                __nv_bfloat16 *dst = xs2 + ((size_t)l * nxc + 2 * b) * in_pad + k;
+                *reinterpret_cast<uint4 *>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4 *>(dst + in_pad) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
             __syncthreads();
         }
-        const uint32_t *sw = reinterpret_cast<const uint32_t *>(s2s);
         const T *xg = static_cast<const T *>(p.x) + (size_t)g * p.in_f;
         const uint32_t *xsw = reinterpret_cast<const uint32_t *>(xs + (size_t)g * in_pad);
-        const __nv_bfloat16 *xcol = xs2 + (size_t)g * in_pad;
         const bool xrow = g < p.batch, fcol = g < nxc;
         const int ntiles = t1e - t1b;
         const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
@@ -315,11 +376,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             int lt, kbeg, kend;
             item_of(item, KS, p.kb1, lt, kbeg, kend);
             const int tile = t1b + lt;
-            const bool vA = ok && (16 * tile + g < p.rank), vB = ok && (16 * tile + g + 8 < p.rank);
+            const int l = member_of1(p, tile);
+            const int row0 = 16 * (tile - p.m[l].t1_start), rank = p.m[l].rank;
+            const bool vA = ok && (row0 + g < rank), vB = ok && (row0 + g + 8 < rank);
             const uint32_t *rowA = vch + (size_t)(lt * 16 + g) * p.wvs;
             const uint32_t *rowB = rowA + (size_t)8 * p.wvs;
             float acc[4][4] = {};
             if (p.fold) {
+                const __nv_bfloat16 *xcol = xs2 + ((size_t)l * nxc + g) * in_pad;
 #pragma unroll 2
                 for (int kb = kbeg; kb < kend; ++kb) {
                     const int wi = 2 * kb + (t >> 1);
@@ -341,6 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                     }
                 }
             } else {
+                const uint32_t *sw = reinterpret_cast<const uint32_t *>(s2s + (size_t)l * in_pad);
 #pragma unroll 2
                 for (int kb = kbeg; kb < kend; ++kb) {
                     const int wi = 2 * kb + (t >> 1);
@@ -385,21 +450,29 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             } else {
                 for (int ks = 0; ks < KS; ++ks) s += red[(lt * KS + ks) * 256 + row * 8 + b];
             }
-            const int k = 16 * (t1b + lt) + row;
-            if (k < p.rank) {
-                if (p.smid) s *= E::to_f(static_cast<const T *>(p.smid)[k]);
+            const int tile = t1b + lt;
+            const int l = member_of1(p, tile);
+            const Member &mb = p.m[l];
+            const int k = 16 * (tile - mb.t1_start) + row;
+            if (k < mb.rank) {
+                if (mb.smid) s *= E::to_f(static_cast<const T *>(mb.smid)[k]);
                 const __nv_bfloat16 hi = __float2bfloat16_rn(s);
                 const int col = (b >> 2) * 8 + 2 * (b & 3);
-                p.tb[(size_t)col * ldi + k] = hi;
-                p.tb[(size_t)(col + 1) * ldi + k] = __float2bfloat16_rn(s - __bfloat162float(hi));
+                mb.tb[(size_t)col * mb.ldi + k] = hi;
+                mb.tb[(size_t)(col + 1) * mb.ldi + k] = __float2bfloat16_rn(s - __bfloat162float(hi));
             }
         }
-        // the CTA owning the last tile zeroes the K padding [rank, ldi) of every column
-        if (t1e == p.tiles1)
-            for (int i = tid; i < 16 * (ldi - p.rank); i += kThreads) {
-                const int col = i / (ldi - p.rank);
-                p.tb[(size_t)col * ldi + p.rank + (i - col * (ldi - p.rank))] = __float2bfloat16_rn(0.f);
-            }
+        // the CTA owning a member's last stage-1 tile zeroes that member's K padding [rank, ldi)
+        for (int l = 0; l < p.nm; ++l) {
+            const Member &mb = p.m[l];
+            const int last = mb.t1_start + mb.tiles1 - 1;
+            const int padw = mb.ldi - mb.rank;
+            if (last >= t1b && last < t1e && padw > 0)
+                for (int i = tid; i < 16 * padw; i += kThreads) {
+                    const int col = i / padw;
+                    mb.tb[(size_t)col * mb.ldi + mb.rank + (i - col * padw)] = __float2bfloat16_rn(0.f);
+                }
+        }
     }
 
     if (p.mode == kFused) {
@@ -418,16 +491,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         // stored ready-made by stage 1 as bf16 pairs along k
         const int b0 = g >> 1, b1 = 4 + (g >> 1);
         const bool v0 = b0 < p.batch, v1 = nt == 2 && b1 < p.batch;
-        const __nv_bfloat16 *trow0 = p.tb + (size_t)g * ldi;
-        const __nv_bfloat16 *trow1 = p.tb + (size_t)(8 + g) * ldi;
         constexpr int kChunkKb = 4;  // K blocks whose B fragments are fetched together
         for (int item = warp; item < items; item += kWarps) {
-            int lt, kbeg, kend;
-            item_of(item, KS, p.kb2, lt, kbeg, kend);
+            const int lt = item / KS, ks = item - lt * KS;
             const int tile = t2b + lt;
-            const bool vA = ok && (16 * tile + g < p.out_f), vB = ok && (16 * tile + g + 8 < p.out_f);
-            const uint32_t *rowA = uch + (size_t)(lt * 16 + g) * p.wus;
-            const uint32_t *rowB = rowA + (size_t)8 * p.wus;
+            const int l = member_of2(p, tile);
+            const Member &mb = p.m[l];
+            const int kbeg = (mb.kb2 * ks) / KS, kend = (mb.kb2 * (ks + 1)) / KS;
+            // this tile's rows in the smem U region: after the earlier members' segments
+            uint32_t uoff = 0;
+            for (int q = 0; q < l; ++q) {
+                int a, b;
+                seg_tiles(p.m[q], t2b, t2e, a, b);
+                if (a < b) uoff = ((uoff + (uint32_t)(16 * (b - a)) * (uint32_t)p.m[q].wus) + 3u) & ~3u;
+            }
+            int a0, b0s;
+            seg_tiles(mb, t2b, t2e, a0, b0s);
+            const int row0 = 16 * (tile - mb.t2_start);
+            const bool vA = ok && (row0 + g < mb.out_f), vB = ok && (row0 + g + 8 < mb.out_f);
+            const uint32_t *rowA = uch + uoff + (size_t)(16 * (tile - a0) + g) * mb.wus;
+            const uint32_t *rowB = rowA + (size_t)8 * mb.wus;
+            const __nv_bfloat16 *trow0 = mb.tb + (size_t)g * mb.ldi;
+            const __nv_bfloat16 *trow1 = mb.tb + (size_t)(8 + g) * mb.ldi;
             float acc0[4][4] = {}, acc1[4][4] = {};
             for (int kb0 = kbeg; kb0 < kend; kb0 += kChunkKb) {
                 uint32_t bp0[kChunkKb][8], bp1[kChunkKb][8];
@@ -443,8 +528,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                     const int kb = kb0 + q;
                     if (kb >= kend) break;
                     const int wi = 2 * kb + (t >> 1);
-                    const uint32_t wA = (vA && wi < p.wu) ? rowA[wi] << sh0 : 0u;
-                    const uint32_t wB = (vB && wi < p.wu) ? rowB[wi] << sh0 : 0u;
+                    const uint32_t wA = (vA && wi < mb.wu) ? rowA[wi] << sh0 : 0u;
+                    const uint32_t wB = (vB && wi < mb.wu) ? rowB[wi] << sh0 : 0u;
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         uint32_t a[4];
@@ -473,10 +558,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 const float *r = red + (lt * KS + ks) * 256 + half + row * 8 + col;
                 s += r[0] + r[1];
             }
-            const int m = 16 * (t2b + lt) + row;
-            if (m < p.out_f) {
-                const float v = s * E::to_f(s1s[m - r2b]);
-                static_cast<T *>(p.y)[(size_t)b * p.out_f + m] = E::out(v);
+            const int tile = t2b + lt;
+            const int l = member_of2(p, tile);
+            const Member &mb = p.m[l];
+            const int m = 16 * (tile - mb.t2_start) + row;
+            if (m < mb.out_f) {
+                const float v = s * E::to_f(s1s[16 * lt + row]);
+                static_cast<T *>(mb.y)[(size_t)b * mb.out_f + m] = E::out(v);
             }
         }
     }
@@ -502,37 +590,42 @@ static inline int padded_stride(int w) {
     return s;
 }
 
-// Shared-memory layout for a launch whose CTAs own at most `rows1`/`rows2` rows.
-static size_t layout(Params &p, int rows1, int rows2, bool stage1, bool stage2, bool x_in_smem, bool fold) {
+// Shared-memory layout for a launch whose CTAs own at most `tiles1`/`tiles2` tiles.
+static size_t layout(Params &p, int tiles1, int tiles2, bool stage1, bool stage2, bool x_in_smem, bool fold) {
     size_t off = 128;  // mbarriers
-    const int items = std::max(kWarps, std::max(rows1, rows2) / 16);
+    const int items = std::max(kWarps, std::max(tiles1, tiles2));
     p.off_red = (uint32_t)off;
     off = align128(off + (size_t)items * 256 * sizeof(float));
     const size_t in_pad = (size_t)p.kb1 * 64;
     p.v_rows = (p.wv % 4) == 0;
-    p.u_rows = (p.wu % 4) == 0;
     p.wvs = p.v_rows ? padded_stride(p.wv) : p.wv;
-    p.wus = p.u_rows ? padded_stride(p.wu) : p.wu;
+    int max_wus = 0;
+    for (int l = 0; l < p.nm; ++l) {
+        p.m[l].u_rows = (p.m[l].wu % 4) == 0;
+        p.m[l].wus = p.m[l].u_rows ? padded_stride(p.m[l].wu) : p.m[l].wu;
+        max_wus = std::max(max_wus, p.m[l].wus);
+    }
     p.off_s2 = p.off_x = p.off_xs2 = p.off_v = (uint32_t)off;
     p.fold = 0;
     if (stage1) {
-        off = align128(off + in_pad * 2);
+        off = align128(off + (size_t)p.nm * in_pad * 2);
         p.off_x = (uint32_t)off;
         if (x_in_smem) off = align128(off + (size_t)p.batch * in_pad * 2);
         p.off_xs2 = (uint32_t)off;
         if (fold && x_in_smem) {
             p.fold = 1;
-            off = align128(off + (size_t)2 * p.batch * in_pad * 2);
+            off = align128(off + (size_t)p.nm * 2 * p.batch * in_pad * 2);
         }
         p.off_v = (uint32_t)off;
-        off = align128(off + (size_t)rows1 * p.wvs * 4 + 16);
+        off = align128(off + (size_t)16 * tiles1 * p.wvs * 4 + 16);
     }
     p.off_u = (uint32_t)off;
     p.off_s1 = (uint32_t)off;
     if (stage2) {
-        off = align128(off + (size_t)rows2 * p.wus * 4 + 16);
+        // segments of different members are rounded up to 4 words each
+        off = align128(off + ((size_t)16 * tiles2 * max_wus + 4 * (size_t)p.nm) * 4 + 16);
         p.off_s1 = (uint32_t)off;
-        off = align128(off + (size_t)rows2 * 2 + 16);
+        off = align128(off + (size_t)16 * tiles2 * 2 + 16);
     }
     p.x_in_smem = x_in_smem ? 1 : 0;
     return off;
@@ -541,17 +634,16 @@ static size_t layout(Params &p, int rows1, int rows2, bool stage1, bool stage2, 
 static int make_plan(int dev, const Params &base, Plan &plan) {
     const DeviceInfo &di = device_info(dev);
     const size_t cap = (size_t)di.max_smem_optin - kStaticSmemReserve;
-    const int sms = di.sms;
-    Params p = base;
+    const int G = di.sms;
+    const Params &p = base;
     // fused: one CTA per SM, tiles spread evenly; prefer x staged and the folded operand
-    const int G = sms;
-    const int rows1 = 16 * ((p.tiles1 + G - 1) / G), rows2 = 16 * ((p.tiles2 + G - 1) / G);
+    const int tpc1 = (p.tiles1 + G - 1) / G, tpc2 = (p.tiles2 + G - 1) / G;
     const int variants[3][2] = {{1, 1}, {1, 0}, {0, 0}};  // (x in smem, fold)
     for (const auto &v : variants) {
         if (v[1] && p.batch > kFoldMaxBatch) continue;
         Params q = p;
         q.mode = kFused;
-        const size_t need = layout(q, rows1, rows2, true, true, v[0] != 0, v[1] != 0);
+        const size_t need = layout(q, tpc1, tpc2, true, true, v[0] != 0, v[1] != 0);
         if (need <= cap && di.coop) {
             plan.mode = kFused;
             plan.grid = G;
@@ -566,8 +658,8 @@ static int make_plan(int dev, const Params &base, Plan &plan) {
         Params q1 = p, q2 = p;
         q1.mode = kStage1;
         q2.mode = kStage2;
-        const size_t n1 = layout(q1, 16, 0, true, false, v[0] != 0, v[1] != 0);
-        const size_t n2 = layout(q2, 0, 16, false, true, false, false);
+        const size_t n1 = layout(q1, 1, 0, true, false, v[0] != 0, v[1] != 0);
+        const size_t n2 = layout(q2, 0, 1, false, true, false, false);
         if (n1 <= cap && n2 <= cap) {
             plan.mode = kStage1 | kStage2 | 4;  // marker: split
             plan.grid1 = p.tiles1;
@@ -579,8 +671,7 @@ static int make_plan(int dev, const Params &base, Plan &plan) {
             return NQ_OK;
         }
     }
-    return fail(NQ_ERR_UNSUPPORTED, "layer too large for the shared-memory budget (in=%d rank=%d out=%d)", p.in_f,
-                p.rank, p.out_f);
+    return fail(NQ_ERR_UNSUPPORTED, "layer group too large for the shared-memory budget (in=%d)", p.in_f);
 }
 
 template <typename T>
@@ -616,41 +707,40 @@ static int launch(const Plan &plan, cudaStream_t stream) {
     return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv stage-2 launch");
 }
 
-}  // namespace gemv
-}  // namespace nq
+static inline size_t tb_bytes(int64_t rank) { return (size_t)16 * (size_t)((rank + 63) / 64) * 64 * 2; }
 
-extern "C" {
-
-size_t nq_gemv_workspace_bytes(int64_t batch, int64_t rank) {
-    (void)batch;  // batches above 8 reuse the same 8-row interm buffer, launch after launch
-    if (rank <= 0) return 0;
-    const size_t ldi = (size_t)((rank + 63) / 64) * 64;  // == kb2 * 64
-    const size_t interm = (size_t)2 * nq::gemv::kMaxBatch * ldi * sizeof(__nv_bfloat16);
-    return sizeof(nq::Ctrl) + ((interm + 255) & ~size_t(255));
-}
-
-int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features, const void *scale_pre,
-            const int32_t *v_bits, int64_t rank, const void *scale_mid, const int32_t *u_bits,
-            int64_t out_features, const void *scale_post, void *y, void *workspace, size_t workspace_bytes,
-            void *stream) {
-    using namespace nq;
-    using namespace nq::gemv;
+static int group_impl(int dtype, const void *x, int64_t batch, int64_t in_features, int n, const nq_gemv_layer *layers,
+                      void *workspace, size_t workspace_bytes, void *stream) {
     if (dtype != NQ_DTYPE_F16 && dtype != NQ_DTYPE_BF16)
         return fail(NQ_ERR_UNSUPPORTED, "dtype must be NQ_DTYPE_F16 or NQ_DTYPE_BF16 (got %d)", dtype);
-    if (!x || !scale_pre || !v_bits || !u_bits || !scale_post || !y)
-        return fail(NQ_ERR_INVALID_ARGUMENT, "null tensor pointer");
-    if (batch <= 0 || in_features <= 0 || rank <= 0 || out_features <= 0)
-        return fail(NQ_ERR_INVALID_ARGUMENT, "sizes must be positive (batch=%lld in=%lld rank=%lld out=%lld)",
-                    (long long)batch, (long long)in_features, (long long)rank, (long long)out_features);
-    if (in_features > (1 << 24) || rank > (1 << 20) || out_features > (1 << 24))
-        return fail(NQ_ERR_UNSUPPORTED, "sizes beyond the supported range");
-    const uintptr_t a2 = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(scale_pre) |
-                         reinterpret_cast<uintptr_t>(scale_post) | reinterpret_cast<uintptr_t>(y) |
-                         reinterpret_cast<uintptr_t>(scale_mid);
-    if (a2 & 1) return fail(NQ_ERR_INVALID_ARGUMENT, "16-bit tensors must be 2-byte aligned");
-    if ((reinterpret_cast<uintptr_t>(v_bits) | reinterpret_cast<uintptr_t>(u_bits)) & 15)
-        return fail(NQ_ERR_INVALID_ARGUMENT, "sign planes must be 16-byte aligned");
-    const size_t need = nq_gemv_workspace_bytes(batch, rank);
+    if (n < 1 || n > kMaxGroup) return fail(NQ_ERR_INVALID_ARGUMENT, "a group holds 1..%d layers (got %d)", kMaxGroup, n);
+    if (!x || !layers) return fail(NQ_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (batch <= 0 || in_features <= 0)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "sizes must be positive (batch=%lld in=%lld)", (long long)batch,
+                    (long long)in_features);
+    if (in_features > (1 << 24)) return fail(NQ_ERR_UNSUPPORTED, "in_features beyond the supported range");
+    if (reinterpret_cast<uintptr_t>(x) & 1) return fail(NQ_ERR_INVALID_ARGUMENT, "x must be 2-byte aligned");
+    int64_t tiles1 = 0, tiles2 = 0;
+    size_t need = sizeof(Ctrl);
+    for (int l = 0; l < n; ++l) {
+        const nq_gemv_layer &L = layers[l];
+        if (!L.scale_pre || !L.v_bits || !L.u_bits || !L.scale_post || !L.y)
+            return fail(NQ_ERR_INVALID_ARGUMENT, "null tensor pointer in layer %d", l);
+        if (L.rank <= 0 || L.out_features <= 0)
+            return fail(NQ_ERR_INVALID_ARGUMENT, "layer %d: sizes must be positive (rank=%lld out=%lld)", l,
+                        (long long)L.rank, (long long)L.out_features);
+        if (L.rank > (1 << 20) || L.out_features > (1 << 24))
+            return fail(NQ_ERR_UNSUPPORTED, "layer %d: sizes beyond the supported range", l);
+        const uintptr_t a2 = reinterpret_cast<uintptr_t>(L.scale_pre) | reinterpret_cast<uintptr_t>(L.scale_post) |
+                             reinterpret_cast<uintptr_t>(L.y) | reinterpret_cast<uintptr_t>(L.scale_mid);
+        if (a2 & 1) return fail(NQ_ERR_INVALID_ARGUMENT, "layer %d: 16-bit tensors must be 2-byte aligned", l);
+        if ((reinterpret_cast<uintptr_t>(L.v_bits) | reinterpret_cast<uintptr_t>(L.u_bits)) & 15)
+            return fail(NQ_ERR_INVALID_ARGUMENT, "layer %d: sign planes must be 16-byte aligned", l);
+        tiles1 += (L.rank + 15) / 16;
+        tiles2 += (L.out_features + 15) / 16;
+        need += tb_bytes(L.rank);
+    }
+    if (tiles1 > 65536 || tiles2 > 65536) return fail(NQ_ERR_UNSUPPORTED, "layer group too large");
     if (!workspace || workspace_bytes < need)
         return fail(NQ_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
     if (reinterpret_cast<uintptr_t>(workspace) & 255)
@@ -660,33 +750,49 @@ int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features, const 
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     const DeviceInfo &di = device_info(dev);
-    if (di.cc_major != 10) return fail(NQ_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", dev,
-                                       di.cc_major, di.cc_minor);
+    if (di.cc_major != 10)
+        return fail(NQ_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", dev, di.cc_major,
+                    di.cc_minor);
 
     Params base{};
-    base.s2 = scale_pre;
-    base.vbits = reinterpret_cast<const uint32_t *>(v_bits);
-    base.smid = scale_mid;
-    base.ubits = reinterpret_cast<const uint32_t *>(u_bits);
-    base.s1 = scale_post;
     base.ctrl = static_cast<Ctrl *>(workspace);
-    base.tb = reinterpret_cast<__nv_bfloat16 *>(static_cast<char *>(workspace) + sizeof(Ctrl));
     base.in_f = (int)in_features;
-    base.rank = (int)rank;
-    base.out_f = (int)out_features;
     base.wv = (int)((in_features + 31) / 32);
-    base.wu = (int)((rank + 31) / 32);
     base.kb1 = (base.wv + 1) / 2;
-    base.kb2 = (base.wu + 1) / 2;
-    base.tiles1 = (int)((rank + 15) / 16);
-    base.tiles2 = (int)((out_features + 15) / 16);
-    const size_t esz = 2;
+    base.nm = n;
+    char *tbp = static_cast<char *>(workspace) + sizeof(Ctrl);
+    int t1 = 0, t2 = 0;
+    for (int l = 0; l < n; ++l) {
+        const nq_gemv_layer &L = layers[l];
+        Member &mb = base.m[l];
+        mb.s2 = L.scale_pre;
+        mb.vbits = reinterpret_cast<const uint32_t *>(L.v_bits);
+        mb.smid = L.scale_mid;
+        mb.ubits = reinterpret_cast<const uint32_t *>(L.u_bits);
+        mb.s1 = L.scale_post;
+        mb.rank = (int)L.rank;
+        mb.out_f = (int)L.out_features;
+        mb.wu = (int)((L.rank + 31) / 32);
+        mb.kb2 = (mb.wu + 1) / 2;
+        mb.ldi = mb.kb2 * 64;
+        mb.tiles1 = (int)((L.rank + 15) / 16);
+        mb.tiles2 = (int)((L.out_features + 15) / 16);
+        mb.t1_start = t1;
+        mb.t2_start = t2;
+        t1 += mb.tiles1;
+        t2 += mb.tiles2;
+        mb.tb = reinterpret_cast<__nv_bfloat16 *>(tbp);
+        tbp += tb_bytes(L.rank);
+    }
+    base.tiles1 = t1;
+    base.tiles2 = t2;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     for (int64_t b0 = 0; b0 < batch; b0 += kMaxBatch) {
         Params p = base;
         p.batch = (int)((batch - b0) < kMaxBatch ? (batch - b0) : kMaxBatch);
-        p.x = static_cast<const char *>(x) + (size_t)b0 * in_features * esz;
-        p.y = static_cast<char *>(y) + (size_t)b0 * out_features * esz;
+        p.x = static_cast<const char *>(x) + (size_t)b0 * in_features * 2;
+        for (int l = 0; l < n; ++l)
+            p.m[l].y = static_cast<char *>(layers[l].y) + (size_t)b0 * layers[l].out_features * 2;
         Plan plan;
         int st = make_plan(dev, p, plan);
         if (st) return st;
@@ -694,6 +800,47 @@ int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features, const 
         if (st) return st;
     }
     return NQ_OK;
+}
+
+}  // namespace gemv
+}  // namespace nq
+
+extern "C" {
+
+size_t nq_gemv_workspace_bytes(int64_t batch, int64_t rank) {
+    (void)batch;  // batches above 8 reuse the same 8-row operand buffer, launch after launch
+    if (rank <= 0) return 0;
+    return sizeof(nq::Ctrl) + nq::gemv::tb_bytes(rank);
+}
+
+size_t nq_gemv_group_workspace_bytes(int n_layers, const int64_t *ranks) {
+    if (n_layers < 1 || !ranks) return 0;
+    size_t need = sizeof(nq::Ctrl);
+    for (int l = 0; l < n_layers; ++l) {
+        if (ranks[l] <= 0) return 0;
+        need += nq::gemv::tb_bytes(ranks[l]);
+    }
+    return need;
+}
+
+int nq_gemv_group(int dtype, const void *x, int64_t batch, int64_t in_features, int n_layers,
+                  const nq_gemv_layer *layers, void *workspace, size_t workspace_bytes, void *stream) {
+    return nq::gemv::group_impl(dtype, x, batch, in_features, n_layers, layers, workspace, workspace_bytes, stream);
+}
+
+int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features, const void *scale_pre,
+            const int32_t *v_bits, int64_t rank, const void *scale_mid, const int32_t *u_bits, int64_t out_features,
+            const void *scale_post, void *y, void *workspace, size_t workspace_bytes, void *stream) {
+    nq_gemv_layer L;
+    L.scale_pre = scale_pre;
+    L.v_bits = v_bits;
+    L.rank = rank;
+    L.scale_mid = scale_mid;
+    L.u_bits = u_bits;
+    L.out_features = out_features;
+    L.scale_post = scale_post;
+    L.y = y;
+    return nq::gemv::group_impl(dtype, x, batch, in_features, 1, &L, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -17,6 +17,7 @@
 #include <optional>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "../../include/nq_b200.h"
 #include "../../include/nq_decoder.h"
@@ -386,6 +387,85 @@ at::Tensor silu_mul_cuda(const at::Tensor &gate, const at::Tensor &up) {
 
 at::Tensor silu_mul_meta(const at::Tensor &gate, const at::Tensor &) { return at::empty_like(gate); }
 
+
+// ------------------------------------------------------------------ grouped layers sharing one input
+
+std::vector<at::Tensor> run_group(const at::Tensor &x, const std::vector<LayerArgs> &ls) {
+    c10::cuda::CUDAGuard guard(x.device());
+    std::vector<nq_gemv_layer> desc(ls.size());
+    std::vector<int64_t> ranks(ls.size());
+    std::vector<at::Tensor> ys;
+    for (size_t i = 0; i < ls.size(); ++i) {
+        const LayerArgs &a = ls[i];
+        ys.push_back(at::empty({a.rows, a.out_f}, x.options()));
+        desc[i].scale_pre = a.s2.data_ptr();
+        desc[i].v_bits = a.vbits.data_ptr<int32_t>();
+        desc[i].rank = a.rank;
+        desc[i].scale_mid = a.smid ? a.smid->data_ptr() : nullptr;
+        desc[i].u_bits = a.ubits.data_ptr<int32_t>();
+        desc[i].out_features = a.out_f;
+        desc[i].scale_post = a.s1.data_ptr();
+        desc[i].y = ys.back().data_ptr();
+        ranks[i] = a.rank;
+    }
+    const size_t wsb = nq_gemv_group_workspace_bytes((int)ls.size(), ranks.data());
+    at::Tensor ws = workspace_for(x, wsb);
+    NQ_TORCH_CHECK(nq_gemv_group(dtype_code(x.scalar_type()), x.data_ptr(), ls[0].rows, ls[0].in_f, (int)ls.size(),
+                                 desc.data(), ws.data_ptr(), (size_t)ws.numel(), cur_stream(x)));
+    return ys;
+}
+
+std::vector<LayerArgs> check_group(const at::Tensor &x, const std::vector<at::Tensor> &s2,
+                                   const std::vector<at::Tensor> &vbits,
+                                   const std::vector<std::optional<at::Tensor>> &smid,
+                                   const std::vector<at::Tensor> &ubits, const std::vector<at::Tensor> &s1) {
+    const size_t n = s2.size();
+    TORCH_CHECK(n >= 1 && n <= 3, "a layer group holds 1 to 3 layers");
+    TORCH_CHECK(vbits.size() == n && smid.size() == n && ubits.size() == n && s1.size() == n,
+                "every per-layer list must have the same length");
+    std::vector<LayerArgs> ls;
+    for (size_t i = 0; i < n; ++i) ls.push_back(check_layer(x, s2[i], vbits[i], smid[i], ubits[i], s1[i]));
+    return ls;
+}
+
+std::vector<at::Tensor> gemv_group_cuda(const at::Tensor &x, at::TensorList s2, at::TensorList vbits,
+                                        const c10::List<std::optional<at::Tensor>> &smid, at::TensorList ubits,
+                                        at::TensorList s1) {
+    std::vector<std::optional<at::Tensor>> sm(smid.begin(), smid.end());
+    auto ls = check_group(x, s2.vec(), vbits.vec(), sm, ubits.vec(), s1.vec());
+    auto ys = run_group(x, ls);
+    if (x.dim() == 1)
+        for (auto &y : ys) y = y.squeeze(0);
+    return ys;
+}
+
+std::vector<at::Tensor> linear_group_cuda(const at::Tensor &x, at::TensorList s2, at::TensorList vbits,
+                                          const c10::List<std::optional<at::Tensor>> &smid, at::TensorList ubits,
+                                          at::TensorList s1) {
+    std::vector<std::optional<at::Tensor>> sm(smid.begin(), smid.end());
+    auto ls = check_group(x, s2.vec(), vbits.vec(), sm, ubits.vec(), s1.vec());
+    std::vector<at::Tensor> ys;
+    if (gemm_ok(ls[0])) {
+        for (auto &a : ls) ys.push_back(run_gemm(a, true));
+    } else {
+        ys = run_group(x, ls);
+    }
+    if (x.dim() == 1)
+        for (auto &y : ys) y = y.squeeze(0);
+    return ys;
+}
+
+std::vector<at::Tensor> group_meta(const at::Tensor &x, at::TensorList, at::TensorList,
+                                   const c10::List<std::optional<at::Tensor>> &, at::TensorList, at::TensorList s1) {
+    std::vector<at::Tensor> ys;
+    for (const auto &s : s1) {
+        auto shape = x.sizes().vec();
+        shape.back() = s.numel();
+        ys.push_back(at::empty(shape, x.options()));
+    }
+    return ys;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(binary_kernels, m) {
@@ -427,6 +507,12 @@ TORCH_LIBRARY(nq_b200, m) {
         "Tensor(d!) v_cache, float theta) -> ()");
     m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seq_len) -> Tensor");
     m.def("silu_mul(Tensor gate, Tensor up) -> Tensor");
+    m.def(
+        "gemv_group(Tensor x, Tensor[] scale_pre, Tensor[] v_bits, Tensor?[] scale_mid, Tensor[] u_bits, "
+        "Tensor[] scale_post) -> Tensor[]");
+    m.def(
+        "linear_group(Tensor x, Tensor[] scale_pre, Tensor[] v_bits, Tensor?[] scale_mid, Tensor[] u_bits, "
+        "Tensor[] scale_post) -> Tensor[]");
 }
 
 TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
@@ -440,6 +526,8 @@ TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
     m.impl("rope_cache", &rope_cache_cuda);
     m.impl("decode_attention", &decode_attention_cuda);
     m.impl("silu_mul", &silu_mul_cuda);
+    m.impl("gemv_group", &gemv_group_cuda);
+    m.impl("linear_group", &linear_group_cuda);
 }
 
 TORCH_LIBRARY_IMPL(nq_b200, Meta, m) {
@@ -453,4 +541,6 @@ TORCH_LIBRARY_IMPL(nq_b200, Meta, m) {
     m.impl("rope_cache", &rope_cache_meta);
     m.impl("decode_attention", &decode_attention_meta);
     m.impl("silu_mul", &silu_mul_meta);
+    m.impl("gemv_group", &group_meta);
+    m.impl("linear_group", &group_meta);
 }

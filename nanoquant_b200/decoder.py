@@ -100,6 +100,21 @@ class QuantLinearShard:
         return t + (2 * self.smid.numel() if self.smid is not None else 0)
 
 
+class QuantGroup:
+    """Layers that read the same input (q/k/v, gate/up), run as one grouped launch."""
+
+    def __init__(self, *members: QuantLinearShard):
+        self.members = members
+        self.s2 = [m.s2 for m in members]
+        self.vb = [m.vb for m in members]
+        self.smid = [m.smid for m in members]
+        self.ub = [m.ub for m in members]
+        self.s1 = [m.s1 for m in members]
+
+    def __call__(self, x: torch.Tensor):
+        return torch.ops.nq_b200.linear_group(x, self.s2, self.vb, self.smid, self.ub, self.s1)
+
+
 def _random_planes(gen, rows: int, cols: int, device) -> torch.Tensor:
     """i.i.d. +-1 signs as half2 planes [rows, ceil(cols/32)], padding bits cleared (+1)."""
     w = (cols + 31) // 32
@@ -114,13 +129,6 @@ def _random_planes(gen, rows: int, cols: int, device) -> torch.Tensor:
             mask -= 2 ** 32
         p[:, -1] &= mask
     return p
-
-
-def _word_slice(cols: int, part: int, nparts: int):
-    """Split `cols` columns at multiples of 32 into `nparts` contiguous shards."""
-    words = (cols + 31) // 32
-    w0, w1 = words * part // nparts, words * (part + 1) // nparts
-    return 32 * w0, min(32 * w1, cols), w0, w1
 
 
 def _make_layer(cfg: DecoderConfig, proj: str, layer: int, seed: int, tp_rank: int, tp: int, dtype, device,
@@ -169,6 +177,8 @@ class Decoder:
         self.layers = []
         for li in range(cfg.layers):
             lay = {p: _make_layer(cfg, p, li, seed, tp_rank, tp, dtype, dev, with_mid) for p in PROJ}
+            lay["qkv"] = QuantGroup(lay["q"], lay["k"], lay["v"])
+            lay["gate_up"] = QuantGroup(lay["gate"], lay["up"])
             lay["in_norm"] = torch.ones(cfg.hidden, device=dev, dtype=dtype)
             lay["post_norm"] = torch.ones(cfg.hidden, device=dev, dtype=dtype)
             self.layers.append(lay)
@@ -210,9 +220,8 @@ class Decoder:
         residual = None
         for li, lay in enumerate(self.layers):
             x, residual = torch.ops.nq_b200.rmsnorm(h, residual, lay["in_norm"], cfg.rms_eps)
-            q = lay["q"](x).view(T, self.hq, D)
-            k = lay["k"](x).view(T, self.hkv, D)
-            v = lay["v"](x).view(T, self.hkv, D)
+            q, k, v = lay["qkv"](x)
+            q, k, v = q.view(T, self.hq, D), k.view(T, self.hkv, D), v.view(T, self.hkv, D)
             torch.ops.nq_b200.rope_cache(q, k, v, pos, bidx, self.k_cache[li], self.v_cache[li], cfg.rope_theta)
             a = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0),
                                                v.transpose(0, 1).unsqueeze(0), is_causal=True,
@@ -220,7 +229,7 @@ class Decoder:
             a = a.squeeze(0).transpose(0, 1).reshape(T, self.hq * D).contiguous()
             o = self._all_reduce(lay["o"](a))
             x, residual = torch.ops.nq_b200.rmsnorm(o, residual, lay["post_norm"], cfg.rms_eps)
-            act = torch.ops.nq_b200.silu_mul(lay["gate"](x), lay["up"](x))
+            act = torch.ops.nq_b200.silu_mul(*lay["gate_up"](x))
             h = self._all_reduce(lay["down"](act))
         x, _ = torch.ops.nq_b200.rmsnorm(h[-1:].contiguous(), residual[-1:].contiguous(), self.final_norm,
                                          cfg.rms_eps)
@@ -239,15 +248,14 @@ class Decoder:
         residual = None
         for li, lay in enumerate(self.layers):
             x, residual = torch.ops.nq_b200.rmsnorm(h, residual, lay["in_norm"], cfg.rms_eps)
-            q = lay["q"](x).view(B, self.hq, D)
-            k = lay["k"](x).view(B, self.hkv, D)
-            v = lay["v"](x).view(B, self.hkv, D)
+            q, k, v = lay["qkv"](x)
+            q, k, v = q.view(B, self.hq, D), k.view(B, self.hkv, D), v.view(B, self.hkv, D)
             torch.ops.nq_b200.rope_cache(q, k, v, self.pos, None, self.k_cache[li], self.v_cache[li],
                                          cfg.rope_theta)
             a = torch.ops.nq_b200.decode_attention(q, self.k_cache[li], self.v_cache[li], self.seq_len)
             o = self._all_reduce(lay["o"](a.view(B, self.hq * D)))
             x, residual = torch.ops.nq_b200.rmsnorm(o, residual, lay["post_norm"], cfg.rms_eps)
-            act = torch.ops.nq_b200.silu_mul(lay["gate"](x), lay["up"](x))
+            act = torch.ops.nq_b200.silu_mul(*lay["gate_up"](x))
             h = self._all_reduce(lay["down"](act))
         x, _ = torch.ops.nq_b200.rmsnorm(h, residual, self.final_norm, cfg.rms_eps)
         return x @ self.lm_head.t()

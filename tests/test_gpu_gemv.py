@@ -157,3 +157,52 @@ def test_gemv_unaligned_vectors(batch):
     y, ws = capi_gemv(d)
     assert_close_to_oracle(y, d.oracle(), "f16")
     assert workspace_status(ws) == 0
+
+
+def _capi_group(ds, x):
+    from nanoquant_b200 import _lib as L
+    import ctypes as C
+    lib = L.cuda_lib()
+    batch, in_f = x.shape
+    descs = (L.GemvLayer * len(ds))()
+    ys = []
+    for i, d in enumerate(ds):
+        y = torch.empty(batch, d.s1.numel(), dtype=x.dtype, device="cuda")
+        ys.append(y)
+        descs[i] = L.GemvLayer(d.s2.data_ptr(), d.vb.data_ptr(), d.L.rank,
+                               d.smid.data_ptr() if d.smid is not None else None, d.ub.data_ptr(), d.s1.numel(),
+                               d.s1.data_ptr(), y.data_ptr())
+    ranks = (C.c_int64 * len(ds))(*[d.L.rank for d in ds])
+    wsb = lib.nq_gemv_group_workspace_bytes(len(ds), ranks)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    L.check(lib.nq_gemv_group(0 if x.dtype == torch.float16 else 1, C.c_void_p(x.data_ptr()), batch, in_f, len(ds),
+                              descs, C.c_void_p(ws.data_ptr()), wsb, stream_ptr()))
+    return ys, ws
+
+
+@pytest.mark.parametrize("shapes,batch,dtype", [
+    ([(4096, 1126), (4096, 1126), (4096, 1126)], 1, "f16"),            # 7B q/k/v
+    ([(11008, 2054), (11008, 2054)], 1, "f16"),                        # 7B gate/up
+    ([(1024, 552), (128, 120), (128, 120)], 2, "bf16"),                # 70B-like q/k/v (GQA), scaled down
+    ([(500, 200), (130, 33), (77, 96)], 5, "bf16"),                    # ragged, no folding (batch 5)
+])
+def test_gemv_group_matches_single_layers(shapes, batch, dtype):
+    in_f = 4096 if shapes[0][0] >= 4096 else 1024
+    x = None
+    ds = []
+    for i, (out_f, rank) in enumerate(shapes):
+        L = orc.make_layer(100 + i, out_f, in_f, rank, batch, dtype, with_mid=(i == 1))
+        if x is None:
+            x_np = L.x
+        L.x = x_np  # every member reads the same input
+        ds.append(DeviceLayer(L, dtype))
+    x = ds[0].x
+    ys, ws = _capi_group(ds, x)
+    for d, y in zip(ds, ys):
+        assert_close_to_oracle(y, d.oracle(), dtype)
+    assert workspace_status(ws) == 0
+    # and through the torch op used by the decoder
+    ys2 = torch.ops.nq_b200.gemv_group(x, [d.s2 for d in ds], [d.vb for d in ds], [d.smid for d in ds],
+                                       [d.ub for d in ds], [d.s1 for d in ds])
+    for y, y2 in zip(ys, ys2):
+        assert torch.equal(y, y2)
