@@ -218,20 +218,32 @@ def run_reference(args, world, rank):
 
 
 def gemv_roofline(dec, reps: int = 5):
-    """Average duration of the fused GEMV over one token's worth of launches (every quantized
-    linear of this rank, replayed from a CUDA graph) and its algorithmic bytes per launch."""
-    lins = list(dec.quant_linears())
-    xs = [torch.randn(dec.batch, q.in_features, device=dec.device, dtype=dec.dtype) for q in lins]
+    """Average duration of a fused GEMV launch over one token's worth of launches exactly as
+    the decode step issues them (grouped q/k/v, o, grouped gate/up, down for every layer of
+    this rank, replayed from a CUDA graph), and the algorithmic bytes per launch."""
+    units = []  # (callable, algorithmic bytes)
+    B = dec.batch
+    for lay in dec.layers:
+        for key in ("qkv", "o", "gate_up", "down"):
+            unit = lay[key]
+            members = unit.members if hasattr(unit, "members") else (unit,)
+            x = torch.randn(B, members[0].in_features, device=dec.device, dtype=dec.dtype)
+            alg = sum(m.nbytes() + 2 * B * m.out_features for m in members) + 2 * B * members[0].in_features
+            if hasattr(unit, "members"):
+                fn = (lambda u, xx: (lambda: torch.ops.nq_b200.gemv_group(xx, u.s2, u.vb, u.smid, u.ub, u.s1)))(unit, x)
+            else:
+                fn = (lambda u, xx: (lambda: u.gemv(xx)))(unit, x)
+            units.append((fn, alg))
     s = torch.cuda.Stream(device=dec.device)
     s.wait_stream(torch.cuda.current_stream(dec.device))
     with torch.cuda.stream(s):
-        for q, x in zip(lins, xs):
-            q.gemv(x)
+        for fn, _ in units:
+            fn()
     torch.cuda.current_stream(dec.device).wait_stream(s)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=s):
-        for q, x in zip(lins, xs):
-            q.gemv(x)
+        for fn, _ in units:
+            fn()
     for _ in range(2):
         g.replay()
     torch.cuda.synchronize(dec.device)
@@ -242,11 +254,10 @@ def gemv_roofline(dec, reps: int = 5):
         g.replay()
     e1.record(cur)
     torch.cuda.synchronize(dec.device)
-    us_per_launch = e0.elapsed_time(e1) * 1e3 / (reps * len(lins))
-    B = dec.batch
-    alg = sum(q.nbytes() + 2 * B * (q.in_features + q.out_features) for q in lins) / len(lins)
+    us_per_launch = e0.elapsed_time(e1) * 1e3 / (reps * len(units))
+    alg = sum(a for _, a in units) / len(units)
     del g
-    return alg, us_per_launch, len(lins)
+    return alg, us_per_launch, len(units)
 
 
 def run_nq(args, world, rank, local):
