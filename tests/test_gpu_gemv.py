@@ -10,7 +10,7 @@ import nanoquant_b200 as nq
 from oracle import oracle as orc
 
 from .golden_data import GOLDEN, layer_from_golden
-from .nq_testutil import DeviceLayer, assert_close_to_oracle, capi_gemv, workspace_status
+from .nq_testutil import DeviceLayer, assert_close_to_oracle, capi_gemv, stream_ptr, workspace_status
 
 pytestmark = pytest.mark.gpu
 
