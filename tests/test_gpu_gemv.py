@@ -188,11 +188,11 @@ def _capi_group(ds, x):
 ])
 def test_gemv_group_matches_single_layers(shapes, batch, dtype):
     in_f = 4096 if shapes[0][0] >= 4096 else 1024
-    x = None
     ds = []
+    x_np = None
     for i, (out_f, rank) in enumerate(shapes):
         L = orc.make_layer(100 + i, out_f, in_f, rank, batch, dtype, with_mid=(i == 1))
-        if x is None:
+        if x_np is None:
             x_np = L.x
         L.x = x_np  # every member reads the same input
         ds.append(DeviceLayer(L, dtype))
