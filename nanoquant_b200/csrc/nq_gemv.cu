@@ -198,8 +198,7 @@ struct Params {
     int tiles1, tiles2;        // totals over members
     int wvs, v_rows;           // V slab smem stride (words) and row-by-row copy flag (wv % 4 == 0)
     int mode, x_in_smem, fold;
-    int tb_smem;               // stage 2 reads its B operand from a shared-memory copy (batch <= 4)
-    uint32_t off_red, off_s2, off_x, off_xs2, off_v, off_u, off_s1, off_tbs;
+    uint32_t off_red, off_s2, off_x, off_xs2, off_v, off_u, off_s1;
 };
 
 __device__ __forceinline__ int member_of1(const Params &p, int tile) {
@@ -247,7 +246,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     if (tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
-        mbar_init(&bars[2], 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -485,37 +483,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
 
     // ------------------------------------------------------------------ stage 2
     if (has2) {
-        const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles: (hi, lo) of 4 batch rows each
-        // Copy the B columns of every member this CTA serves (written by stage 1 all over
-        // the grid, L2-resident) into bank-padded shared memory once, instead of every warp
-        // fetching them from L2 chunk by chunk.
-        const int ncol = 2 * p.batch;
-        __nv_bfloat16 *tbs = reinterpret_cast<__nv_bfloat16 *>(smem + p.off_tbs);
-        if (p.tb_smem) {
-            if (tid == 0) {
-                fence_proxy_async_global();
-                uint32_t bytes2 = 0;
-                for (int l = 0; l < p.nm; ++l) {
-                    int a, b;
-                    seg_tiles(p.m[l], t2b, t2e, a, b);
-                    if (a < b) bytes2 += (uint32_t)ncol * (uint32_t)p.m[l].ldi * 2u;
-                }
-                mbar_arrive_expect_tx(&bars[2], bytes2);
-                size_t off = 0;
-                for (int l = 0; l < p.nm; ++l) {
-                    const Member &mb = p.m[l];
-                    int a, b;
-                    seg_tiles(mb, t2b, t2e, a, b);
-                    if (a < b)
-                        for (int col = 0; col < ncol; ++col)
-                            bulk_g2s(tbs + off + (size_t)col * (mb.ldi + 8), mb.tb + (size_t)col * mb.ldi,
-                                     (uint32_t)mb.ldi * 2u, &bars[2]);
-                    off += (size_t)ncol * (mb.ldi + 8);
-                }
-            }
-            if (!mbar_wait(&bars[2], 0, &p.ctrl->status)) ok = false;
-        }
         if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
+        const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles: (hi, lo) of 4 batch rows each
         const int ntiles = t2e - t2b;
         const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
         // B column g of n-tile q is the hi (g even) or lo (g odd) part of batch row 4q + g/2,
@@ -544,9 +513,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             const uint32_t *rowB = rowA + (size_t)8 * mb.wus;
             const __nv_bfloat16 *trow0 = mb.tb + (size_t)g * mb.ldi;
             const __nv_bfloat16 *trow1 = mb.tb + (size_t)(8 + g) * mb.ldi;
-            const __nv_bfloat16 *srow = tbs;  // this member's columns in the shared copy
-            for (int q = 0; q < l; ++q) srow += (size_t)ncol * (p.m[q].ldi + 8);
-            srow += (size_t)g * (mb.ldi + 8);
             float acc0[4][4] = {}, acc1[4][4] = {};
             for (int kb0 = kbeg; kb0 < kend; kb0 += kChunkKb) {
                 uint32_t bp0[kChunkKb][8], bp1[kChunkKb][8];
@@ -554,19 +520,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 for (int q = 0; q < kChunkKb; ++q) {
                     const int kc = 64 * (kb0 + q) + 16 * t;
                     const bool in = kb0 + q < kend;
-                    if (p.tb_smem) {
-                        if (in && v0) {
-                            load16_smem(srow + kc, bp0[q]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) bp0[q][j] = 0u;
-                        }
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) bp1[q][j] = 0u;
-                    } else {
-                        load_t_pairs(trow0 + kc, in && v0, bp0[q]);
-                        load_t_pairs(trow1 + kc, in && v1, bp1[q]);
-                    }
+                    load_t_pairs(trow0 + kc, in && v0, bp0[q]);
+                    load_t_pairs(trow1 + kc, in && v1, bp1[q]);
                 }
 #pragma unroll
                 for (int q = 0; q < kChunkKb; ++q) {
@@ -663,14 +618,6 @@ static size_t layout(Params &p, int tiles1, int tiles2, bool stage1, bool stage2
         }
         p.off_v = (uint32_t)off;
         off = align128(off + (size_t)16 * tiles1 * p.wvs * 4 + 16);
-    }
-    p.off_tbs = (uint32_t)off;
-    p.tb_smem = 0;
-    if (stage2 && p.batch <= 4) {
-        size_t tbs = 0;
-        for (int l = 0; l < p.nm; ++l) tbs += (size_t)2 * p.batch * (p.m[l].ldi + 8) * 2;
-        p.tb_smem = 1;
-        off = align128(off + tbs);
     }
     p.off_u = (uint32_t)off;
     p.off_s1 = (uint32_t)off;
