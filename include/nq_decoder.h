@@ -28,15 +28,30 @@ NQ_API int nq_rope_cache(int dtype, void *q, void *k, const void *v, const int32
                          int64_t hq, int64_t hkv, int64_t head_dim, int64_t max_seq, float theta,
                          void *stream);
 
-/* Single-query attention over the first seq_len[b] cache positions (device int32 [batch]),
- * split over 256-position chunks and combined: out [batch, hq, head_dim].  head_dim 128,
- * hq / hkv in {1, 2, 4, 8}.  Workspace: nq_decode_attention_workspace_bytes(). */
+/* Single-query attention over the first seq_len[b] cache positions (device int32 [batch]):
+ * out [batch, hq, head_dim].  One launch: positions are split into chunks (a multiple of 64
+ * positions, at most 64 chunks per head) whose partial results the last chunk to finish
+ * combines.  head_dim 128, hq / hkv in {1, 2, 4, 8}, caches 16-byte aligned.
+ * Workspace: nq_decode_attention_workspace_bytes() bytes, 256-byte aligned, zeroed before its
+ * first use; every call leaves it zeroed again (arrival counters) except for a device-side
+ * error, which nq_workspace_status() reads.  One call at a time per workspace. */
 NQ_API size_t nq_decode_attention_workspace_bytes(int64_t batch, int64_t hq, int64_t head_dim,
                                                   int64_t max_seq);
 NQ_API int nq_decode_attention(int dtype, const void *q, const void *k_cache, const void *v_cache,
                                const int32_t *seq_len, void *out, int64_t batch, int64_t hq,
                                int64_t hkv, int64_t head_dim, int64_t max_seq, void *workspace,
                                size_t workspace_bytes, void *stream);
+
+/* nq_rope_cache followed by nq_decode_attention for one new token per batch row, in one
+ * launch: q [batch, hq, head_dim] and k [batch, hkv, head_dim] are the projections before the
+ * rotary embedding (left unmodified), v [batch, hkv, head_dim]; the rotated k and v are written
+ * to the caches at positions[b] and attention runs over positions 0 .. positions[b].  Rotated
+ * values and cache contents are bit-identical to nq_rope_cache's.  Workspace as above. */
+NQ_API int nq_decode_attention_rope(int dtype, const void *q, const void *k, const void *v,
+                                    const int32_t *positions, void *k_cache, void *v_cache,
+                                    void *out, int64_t batch, int64_t hq, int64_t hkv,
+                                    int64_t head_dim, int64_t max_seq, float theta,
+                                    void *workspace, size_t workspace_bytes, void *stream);
 
 /* out = dtype(silu(gate)) * up, elementwise over n values. */
 NQ_API int nq_silu_mul(int dtype, const void *gate, const void *up, void *out, int64_t n,

@@ -64,6 +64,21 @@ _SIGNATURES = {
                            _c.c_size_t, _c.c_void_p]),
     "nq_workspace_reset": (_c.c_int, [_c.c_void_p, _c.c_size_t, _c.c_void_p]),
     "nq_workspace_status": (_c.c_int, [_c.c_void_p, _c.c_size_t, _c.c_void_p, _c.POINTER(_c.c_int)]),
+    # include/nq_decoder.h
+    "nq_rmsnorm": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p,
+                              _c.c_int64, _c.c_int64, _c.c_float, _c.c_void_p]),
+    "nq_rope_cache": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p,
+                                 _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64,
+                                 _c.c_int64, _c.c_float, _c.c_void_p]),
+    "nq_decode_attention_workspace_bytes": (_c.c_size_t, [_c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64]),
+    "nq_decode_attention": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p,
+                                       _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_void_p,
+                                       _c.c_size_t, _c.c_void_p]),
+    "nq_decode_attention_rope": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p,
+                                            _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int64,
+                                            _c.c_int64, _c.c_int64, _c.c_int64, _c.c_float, _c.c_void_p,
+                                            _c.c_size_t, _c.c_void_p]),
+    "nq_silu_mul": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p]),
 }
 
 

@@ -166,158 +166,322 @@ __global__ void rope_cache_kernel(T *__restrict__ q, T *__restrict__ k, const T 
 }
 
 // ------------------------------------------------------------------ decode attention
-// One CTA = (position chunk, kv head, batch row); it serves all `grp` query heads of
-// the kv head.  Scores: thread-per-position over the chunk; P.V: thread-per-dimension.
-constexpr int kChunk = 256;
-constexpr int kAttnThreads = 128;
+// One CTA = (chunk of positions, kv head, batch row); it serves the `GRP` query heads of the
+// kv head.  A chunk is `nsub` sub-blocks of kSub positions; each sub-block's K and V rows are
+// contiguous in the cache, so one thread brings them into a two-stage shared-memory ring with
+// two bulk copies and every byte of the chunk is in flight at once.  Softmax is online over the
+// sub-blocks.  The chunk's partial (unnormalised output, max, sum of exponentials) goes to the
+// workspace; the CTA that finishes last for its (batch row, kv head) -- found with an atomic
+// counter that it resets afterwards -- combines the partials and writes the output, so there
+// is no second launch.  A head whose sequence fits one chunk writes its output directly.
+//
+// ROPE = true fuses the rotary embedding and the cache write of the new position (the work of
+// rope_cache_kernel, same arithmetic and roundings): every CTA rotates q itself, and the CTA
+// whose chunk holds position pos[b] rotates k, writes k and v to the caches, and patches its
+// shared-memory copy of that row.  The sequence length is then pos[b] + 1.
+constexpr int kSub = 64;           // positions per sub-block (one ring stage)
+constexpr int kAttnThreads = 128;  // 4 warps
+constexpr int kMaxChunks = 64;     // chunk length grows with max_seq to keep at most this many
+constexpr int kHeadDim = 128;
 
-template <typename T, int D, int GRP>
-__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const T *__restrict__ q, const T *__restrict__ kc,
-                                                                  const T *__restrict__ vc,
-                                                                  const int *__restrict__ seq_len, float *__restrict__ part,
-                                                                  int hkv, int max_seq, int nsplit, float scale) {
-    __shared__ float qs[GRP][D];
-    __shared__ float sc[GRP][kChunk];
-    __shared__ float red[GRP][kAttnThreads / 32];
-    __shared__ float osm[(kAttnThreads / 32) * GRP * D];  // per-warp partial P.V sums
-    const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
-    const int hq = hkv * GRP;
-    const int L = seq_len[b];
-    const int p0 = split * kChunk, p1 = min(p0 + kChunk, L);
-    float *po = part + (((size_t)b * hq + (size_t)kh * GRP) * nsplit + split) * (D + 2);
-    if (p0 >= p1) {  // empty chunk
-        for (int g = 0; g < GRP; ++g)
-            if (threadIdx.x == 0) {
-                float *pg = po + (size_t)g * nsplit * (D + 2);
-                pg[D] = -FLT_MAX;
-                pg[D + 1] = 0.f;
-            }
+struct AttnParams {
+    const void *q;      // [batch, hq, D]; already rotated unless ROPE
+    const void *k_new;  // ROPE: [batch, hkv, D] (not rotated yet)
+    const void *v_new;  // ROPE: [batch, hkv, D]
+    const int *pos;     // ROPE: position of the new row per batch row
+    const int *seq_len; // !ROPE: attended positions per batch row
+    void *kc, *vc;      // [batch][hkv][max_seq][D]
+    void *out;          // [batch, hq, D]
+    Ctrl *ctrl;         // status
+    unsigned *count;    // [batch][hkv] arrival counters, zero between launches
+    float *part;        // [batch][hq][nchunk][D + 2]
+    int hkv, max_seq, nchunk, nsub;
+    float scale, log2_theta;
+};
+
+template <typename T>
+__device__ __forceinline__ float2 f2_of(uint32_t w);
+template <>
+__device__ __forceinline__ float2 f2_of<__half>(uint32_t w) {
+    return __half22float2(*reinterpret_cast<__half2 *>(&w));
+}
+template <>
+__device__ __forceinline__ float2 f2_of<__nv_bfloat16>(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162 *>(&w));
+}
+
+__host__ __device__ constexpr size_t attn_stage_bytes() { return 2u * kSub * kHeadDim * 2u; }  // K + V, 2-byte types
+
+template <typename T, int GRP, bool ROPE>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
+    constexpr int D = kHeadDim;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ float mrow[GRP], lrow[GRP], alph[GRP];
+    __shared__ float wts[kMaxChunks];
+    __shared__ float red[2];
+    __shared__ int last;
+    const int tid = threadIdx.x;
+    const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+    const int hq = p.hkv * GRP;
+    const int pos = ROPE ? p.pos[b] : 0;
+    int L = ROPE ? pos + 1 : p.seq_len[b];
+    L = min(L, p.max_seq);
+    const int clen = p.nsub * kSub;
+    const int c0 = chunk * clen;
+    T *out = static_cast<T *>(p.out) + ((size_t)b * hq + (size_t)kh * GRP) * D;
+    if (L <= 0) {  // nothing to attend to: zeros, written once
+        if (chunk == 0)
+            for (int i = tid; i < GRP * D; i += kAttnThreads) out[i] = fromf<T>(0.f);
         return;
     }
-    for (int i = threadIdx.x; i < GRP * D; i += kAttnThreads) {
-        const int g = i / D, d = i - g * D;
-        qs[g][d] = tof(q[((size_t)b * hq + kh * GRP + g) * D + d]) * scale;
+    if (c0 >= L) return;  // beyond the sequence: no partial, not counted
+    const int nact = (L + clen - 1) / clen;
+    const int c1 = min(c0 + clen, L);
+    const int nsb = (c1 - c0 + kSub - 1) / kSub;
+    const int stages = min(2, p.nsub);
+    const size_t head_row0 = ((size_t)b * p.hkv + kh) * (size_t)p.max_seq;
+    const T *kg = static_cast<const T *>(p.kc) + head_row0 * D;
+    const T *vg = static_cast<const T *>(p.vc) + head_row0 * D;
+    T *qsm = reinterpret_cast<T *>(smem + stages * attn_stage_bytes());
+    float *sc = reinterpret_cast<float *>(qsm + GRP * D);  // [GRP][kSub]
+
+    auto issue = [&](int sb) {  // thread 0: K and V rows of sub-block sb into stage sb & 1
+        const int r0 = c0 + sb * kSub, nr = min(kSub, c1 - r0);
+        unsigned char *st = smem + (sb & 1) * attn_stage_bytes();
+        const uint32_t bytes = (uint32_t)nr * D * (uint32_t)sizeof(T);
+        mbar_arrive_expect_tx(&bars[sb & 1], 2u * bytes);
+        bulk_g2s(st, kg + (size_t)r0 * D, bytes, &bars[sb & 1]);
+        bulk_g2s(st + attn_stage_bytes() / 2, vg + (size_t)r0 * D, bytes, &bars[sb & 1]);
+    };
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+        issue(0);
+        if (nsb > 1) issue(1);
+    }
+    if (tid < GRP) {
+        mrow[tid] = -INFINITY;
+        lrow[tid] = 0.f;
+    }
+    // q (rotated here when ROPE) into shared memory; the owner of the new row rotates k too.
+    const bool owner = ROPE && pos >= 0 && pos < p.max_seq && (L - 1) / clen == chunk;
+    T knew_a = fromf<T>(0.f), knew_b = knew_a, vnew_a = knew_a, vnew_b = knew_a;
+    const T *qg = static_cast<const T *>(p.q) + ((size_t)b * hq + (size_t)kh * GRP) * D;
+    if (ROPE) {
+        if (tid < D / 2) {
+            const int j = tid;
+            const float inv_freq = exp2f(-(2.f * j / (float)D) * p.log2_theta);
+            float sn, cs;
+            sincosf((float)pos * inv_freq, &sn, &cs);
+            const float c = tof(fromf<T>(cs)), s = tof(fromf<T>(sn));
+#pragma unroll
+            for (int g = 0; g < GRP; ++g) {
+                const float a = tof(qg[g * D + j]), bb = tof(qg[g * D + j + D / 2]);
+                qsm[g * D + j] = fromf<T>(a * c - bb * s);
+                qsm[g * D + j + D / 2] = fromf<T>(bb * c + a * s);
+            }
+            if (owner) {
+                const size_t kv = ((size_t)b * p.hkv + kh) * D;
+                const T *kn = static_cast<const T *>(p.k_new) + kv;
+                const T *vn = static_cast<const T *>(p.v_new) + kv;
+                const float a = tof(kn[j]), bb = tof(kn[j + D / 2]);
+                knew_a = fromf<T>(a * c - bb * s);
+                knew_b = fromf<T>(bb * c + a * s);
+                vnew_a = vn[j];
+                vnew_b = vn[j + D / 2];
+                T *kd = static_cast<T *>(p.kc) + (head_row0 + pos) * D;
+                T *vd = static_cast<T *>(p.vc) + (head_row0 + pos) * D;
+                kd[j] = knew_a;
+                kd[j + D / 2] = knew_b;
+                vd[j] = vnew_a;
+                vd[j + D / 2] = vnew_b;
+            }
+        }
+    } else {
+        for (int i = tid; i < GRP * D; i += kAttnThreads) qsm[i] = qg[i];
     }
     __syncthreads();
-    const T *kb = kc + (((size_t)b * hkv + kh) * max_seq) * D;
-    const T *vb = vc + (((size_t)b * hkv + kh) * max_seq) * D;
-    for (int pp = threadIdx.x; pp < kChunk; pp += kAttnThreads) {
-        const int p = p0 + pp;
+
+    const int pp = tid >> 1, hh = tid & 1;   // scores: position pp, half hh of the dimensions
+    const int dp = tid & 63, ph = tid >> 6;  // P.V: dimensions 2dp, 2dp+1; positions of parity ph
+    const int w = tid >> 5, l = tid & 31;
+    float o[GRP][2];
+#pragma unroll
+    for (int g = 0; g < GRP; ++g) o[g][0] = o[g][1] = 0.f;
+    for (int sb = 0; sb < nsb; ++sb) {
+        const int nv = min(kSub, c1 - (c0 + sb * kSub));
+        const T *ks = reinterpret_cast<const T *>(smem + (sb & 1) * attn_stage_bytes());
+        T *vs = const_cast<T *>(ks) + kSub * D;
+        mbar_wait(&bars[sb & 1], (uint32_t)(sb >> 1) & 1u, &p.ctrl->status);
+        if (owner && sb == nsb - 1 && tid < D / 2) {  // the new row, as written to the caches
+            const int r = (L - 1) - (c0 + sb * kSub);
+            T *kr = const_cast<T *>(ks) + r * D;
+            kr[tid] = knew_a;
+            kr[tid + D / 2] = knew_b;
+            vs[r * D + tid] = vnew_a;
+            vs[r * D + tid + D / 2] = vnew_b;
+        }
+        if (owner && sb == nsb - 1) __syncthreads();
+        // scores: 16-byte chunks visited in a rotated order so a warp's reads spread over all banks
         float acc[GRP];
 #pragma unroll
         for (int g = 0; g < GRP; ++g) acc[g] = 0.f;
-        if (p < p1) {
-            const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (size_t)p * D);
-#pragma unroll 4
-            for (int c = 0; c < D / 8; ++c) {
-                const uint4 u = __ldg(kr + c);
-                const T *e = reinterpret_cast<const T *>(&u);
+        if (pp < nv) {
+            const T *kr = ks + pp * D + hh * (D / 2);
+            const T *qr = qsm + hh * (D / 2);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float kv = tof(e[j]);
+            for (int cc = 0; cc < 8; ++cc) {
+                const int c8 = 8 * ((cc + pp) & 7);
+                const uint4 kv = *reinterpret_cast<const uint4 *>(kr + c8);
+                const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
-                    for (int g = 0; g < GRP; ++g) acc[g] += kv * qs[g][8 * c + j];
+                for (int g = 0; g < GRP; ++g) {
+                    const uint4 qv = *reinterpret_cast<const uint4 *>(qr + g * D + c8);
+                    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 kf = f2_of<T>(kw[e]), qf = f2_of<T>(qw[e]);
+                        acc[g] = fmaf(kf.x, qf.x, acc[g]);
+                        acc[g] = fmaf(kf.y, qf.y, acc[g]);
+                    }
                 }
             }
         }
 #pragma unroll
-        for (int g = 0; g < GRP; ++g) sc[g][pp] = (p < p1) ? acc[g] : -FLT_MAX;
-    }
-    __syncthreads();
-    // per head: max and sum of exp over the chunk
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    float m[GRP];
+        for (int g = 0; g < GRP; ++g) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
+        if (hh == 0)
 #pragma unroll
-    for (int g = 0; g < GRP; ++g) {
-        float v = -FLT_MAX;
-        for (int pp = threadIdx.x; pp < kChunk; pp += kAttnThreads) v = fmaxf(v, sc[g][pp]);
+            for (int g = 0; g < GRP; ++g) sc[g * kSub + pp] = pp < nv ? acc[g] * p.scale : -INFINITY;
+        __syncthreads();
+        // online softmax: warp w updates heads w, w + 4, ...
+        for (int g = w; g < GRP; g += kAttnThreads / 32) {
+            const float v0 = sc[g * kSub + l], v1 = sc[g * kSub + l + 32];
+            float mx = fmaxf(v0, v1);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (l == 0) red[g][w] = v;
-    }
-    __syncthreads();
+            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mo = mrow[g], mn = fmaxf(mo, mx);
+            const float e0 = expf(v0 - mn), e1 = expf(v1 - mn);
+            sc[g * kSub + l] = e0;
+            sc[g * kSub + l + 32] = e1;
+            float s = e0 + e1;
 #pragma unroll
-    for (int g = 0; g < GRP; ++g) {
-        float v = red[g][0];
-        for (int i = 1; i < kAttnThreads / 32; ++i) v = fmaxf(v, red[g][i]);
-        m[g] = v;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < GRP; ++g) {
-        float s = 0.f;
-        for (int pp = threadIdx.x; pp < kChunk; pp += kAttnThreads) {
-            const float e = (p0 + pp < p1) ? expf(sc[g][pp] - m[g]) : 0.f;
-            sc[g][pp] = e;
-            s += e;
+            for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+            if (l == 0) {
+                const float a = expf(mo - mn);
+                alph[g] = a;
+                lrow[g] = lrow[g] * a + s;
+                mrow[g] = mn;
+            }
         }
+        __syncthreads();
+        // P.V: half2 of V per thread, conflict-free rows; P broadcast from shared memory
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (l == 0) red[g][w] = s;
-    }
-    __syncthreads();
-    // P.V: warp w takes positions p0 + w, p0 + w + 4, ...; lane l holds dimensions 4l..4l+3
-    // (8-byte coalesced loads), then the four warps' partial sums meet in shared memory.
-    static_assert(D == 128 && kAttnThreads == 128, "P.V layout assumes 4 warps x 32 lanes x 4 dims");
-    float o[GRP][4];
-#pragma unroll
-    for (int g = 0; g < GRP; ++g) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+        for (int g = 0; g < GRP; ++g) {
+            o[g][0] *= alph[g];
+            o[g][1] *= alph[g];
+        }
+        const uint32_t *vw = reinterpret_cast<const uint32_t *>(vs) + dp;
 #pragma unroll 4
-    for (int p = p0 + w; p < p1; p += kAttnThreads / 32) {
-        const uint2 u = __ldg(reinterpret_cast<const uint2 *>(vb + (size_t)p * D) + l);
-        const T *e = reinterpret_cast<const T *>(&u);
-        const float v0 = tof(e[0]), v1 = tof(e[1]), v2 = tof(e[2]), v3 = tof(e[3]);
+        for (int q2 = ph; q2 < nv; q2 += 2) {
+            const float2 v = f2_of<T>(vw[q2 * (D / 2)]);
 #pragma unroll
-        for (int g = 0; g < GRP; ++g) {
-            const float pw = sc[g][p - p0];
-            o[g][0] += pw * v0;
-            o[g][1] += pw * v1;
-            o[g][2] += pw * v2;
-            o[g][3] += pw * v3;
+            for (int g = 0; g < GRP; ++g) {
+                const float pw = sc[g * kSub + q2];
+                o[g][0] = fmaf(pw, v.x, o[g][0]);
+                o[g][1] = fmaf(pw, v.y, o[g][1]);
+            }
+        }
+        __syncthreads();  // stage and scores free again
+        if (tid == 0 && sb + 2 < nsb) {
+            fence_proxy_async_smem();
+            issue(sb + 2);
         }
     }
+    // the two position parities meet in shared memory (stage 0 is free: no copy in flight)
+    float *osm = reinterpret_cast<float *>(smem);
+    if (ph == 1)
 #pragma unroll
-    for (int g = 0; g < GRP; ++g)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) osm[(w * GRP + g) * D + 4 * l + i] = o[g][i];
+        for (int g = 0; g < GRP; ++g) {
+            osm[g * D + 2 * dp] = o[g][0];
+            osm[g * D + 2 * dp + 1] = o[g][1];
+        }
     __syncthreads();
-    for (int i = threadIdx.x; i < GRP * D; i += kAttnThreads) {
-        const int g = i / D, d = i - g * D;
-        float acc = 0.f;
-#pragma unroll
-        for (int ww = 0; ww < kAttnThreads / 32; ++ww) acc += osm[(ww * GRP + g) * D + d];
-        po[(size_t)g * nsplit * (D + 2) + d] = acc;
-    }
-    if (threadIdx.x == 0) {
+    if (ph == 0)
 #pragma unroll
         for (int g = 0; g < GRP; ++g) {
-            float s = 0.f;
-            for (int i = 0; i < kAttnThreads / 32; ++i) s += red[g][i];
-            float *pg = po + (size_t)g * nsplit * (D + 2);
-            pg[D] = m[g];
-            pg[D + 1] = s;
+            o[g][0] += osm[g * D + 2 * dp];
+            o[g][1] += osm[g * D + 2 * dp + 1];
         }
+    if (nact == 1) {  // the whole sequence was this chunk
+        if (ph == 0)
+#pragma unroll
+            for (int g = 0; g < GRP; ++g) {
+                const float inv = 1.f / lrow[g];
+                out[g * D + 2 * dp] = fromf<T>(o[g][0] * inv);
+                out[g * D + 2 * dp + 1] = fromf<T>(o[g][1] * inv);
+            }
+        return;
     }
+    float *pbase = p.part + ((size_t)b * hq + (size_t)kh * GRP) * p.nchunk * (D + 2);
+    if (ph == 0)
+#pragma unroll
+        for (int g = 0; g < GRP; ++g) {
+            float *pc = pbase + ((size_t)g * p.nchunk + chunk) * (D + 2);
+            *reinterpret_cast<float2 *>(pc + 2 * dp) = make_float2(o[g][0], o[g][1]);
+            if (dp == 0) *reinterpret_cast<float2 *>(pc + D) = make_float2(mrow[g], lrow[g]);
+        }
+    __threadfence();
+    __syncthreads();
+    unsigned *cnt = p.count + (size_t)b * p.hkv + kh;
+    if (tid == 0) last = atomicAdd(cnt, 1u) == (unsigned)(nact - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // combine: out = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c
+    for (int g = 0; g < GRP; ++g) {
+        const float *pg = pbase + (size_t)g * p.nchunk * (D + 2);
+        float mc = -INFINITY, lc = 0.f;
+        if (tid < nact) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pg + (size_t)tid * (D + 2) + D));
+            mc = ml.x;
+            lc = ml.y;
+        }
+        float mx = mc;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        if (l == 0 && w < 2) red[w] = mx;
+        __syncthreads();
+        const float M = fmaxf(red[0], red[1]);
+        const float wc = tid < nact ? expf(mc - M) : 0.f;
+        if (tid < nact) wts[tid] = wc;
+        float den = wc * lc;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+        __syncthreads();
+        if (l == 0 && w < 2) red[w] = den;
+        __syncthreads();
+        den = red[0] + red[1];
+        float num = 0.f;
+#pragma unroll 8
+        for (int c = 0; c < nact; ++c) num = fmaf(wts[c], __ldcg(pg + (size_t)c * (D + 2) + tid), num);
+        out[g * D + tid] = fromf<T>(num / den);
+        __syncthreads();  // red / wts reused by the next head
+    }
+    if (tid == 0) *cnt = 0u;
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(D) attn_combine_kernel(const float *__restrict__ part, T *__restrict__ out, int hq,
-                                                         int nsplit) {
-    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-    const float *ph = part + ((size_t)b * hq + h) * nsplit * (D + 2);
-    float M = -FLT_MAX;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ph[(size_t)s * (D + 2) + D]);
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-        const float *ps = ph + (size_t)s * (D + 2);
-        const float l = ps[D + 1];
-        if (l <= 0.f) continue;
-        const float wgt = expf(ps[D] - M);
-        num += wgt * ps[d];
-        den += wgt * l;
-    }
-    out[((size_t)b * hq + h) * D + d] = fromf<T>(den > 0.f ? num / den : 0.f);
+// Chunking for a cache of max_seq positions: nsub sub-blocks per chunk, nchunk chunks.
+struct AttnChunks {
+    int nsub, nchunk;
+};
+inline AttnChunks attn_chunks(int64_t max_seq) {
+    const int64_t n64 = (max_seq + kSub - 1) / kSub;
+    const int64_t nsub = (n64 + kMaxChunks - 1) / kMaxChunks;
+    return {(int)nsub, (int)((n64 + nsub - 1) / nsub)};
 }
+inline size_t attn_count_bytes(int64_t batch, int64_t hq) { return ((size_t)batch * hq * 4 + 255) & ~(size_t)255; }
 
 // ------------------------------------------------------------------ SwiGLU
 template <typename T>
@@ -327,6 +491,64 @@ __global__ void silu_mul_kernel(const T *__restrict__ gate, const T *__restrict_
         const T s = fromf<T>(g / (1.f + expf(-g)));
         out[i] = fromf<T>(tof(s) * tof(up[i]));
     }
+}
+
+template <typename T, int GRP, bool ROPE>
+cudaError_t launch_attn(const AttnParams &p, int batch, cudaStream_t s) {
+    const int stages = p.nsub < 2 ? p.nsub : 2;
+    const size_t smem = stages * attn_stage_bytes() + GRP * kHeadDim * sizeof(T) + GRP * kSub * sizeof(float);
+    auto fn = attn_decode_kernel<T, GRP, ROPE>;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    fn<<<dim3((unsigned)p.nchunk, (unsigned)p.hkv, (unsigned)batch), kAttnThreads, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <bool ROPE>
+cudaError_t dispatch_attn(int dtype, int grp, const AttnParams &p, int batch, cudaStream_t s) {
+#define NQ_ATTN_GRP(TT)                                          \
+    switch (grp) {                                               \
+        case 1: return launch_attn<TT, 1, ROPE>(p, batch, s);    \
+        case 2: return launch_attn<TT, 2, ROPE>(p, batch, s);    \
+        case 4: return launch_attn<TT, 4, ROPE>(p, batch, s);    \
+        default: return launch_attn<TT, 8, ROPE>(p, batch, s);   \
+    }
+    if (dtype == NQ_DTYPE_F16) {
+        NQ_ATTN_GRP(__half)
+    }
+    NQ_ATTN_GRP(__nv_bfloat16)
+#undef NQ_ATTN_GRP
+}
+
+// Host checks shared by both attention entry points; fills the workspace pointers of p.
+int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head_dim, int64_t max_seq,
+                 void *workspace, size_t workspace_bytes, AttnParams &p) {
+    if (batch <= 0 || hq <= 0 || hkv <= 0 || max_seq <= 0 || max_seq > INT32_MAX)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "bad decode_attention sizes");
+    if (dtype != NQ_DTYPE_F16 && dtype != NQ_DTYPE_BF16) return fail(NQ_ERR_UNSUPPORTED, "dtype");
+    if (head_dim != kHeadDim) return fail(NQ_ERR_UNSUPPORTED, "decode attention supports head_dim 128");
+    if (hq % hkv) return fail(NQ_ERR_INVALID_ARGUMENT, "query heads must be a multiple of kv heads");
+    const int64_t grp = hq / hkv;
+    if (grp != 1 && grp != 2 && grp != 4 && grp != 8)
+        return fail(NQ_ERR_UNSUPPORTED, "GQA group %lld not in {1,2,4,8}", (long long)grp);
+    if (batch > 65535 || hkv > 65535) return fail(NQ_ERR_UNSUPPORTED, "batch and kv heads must be <= 65535");
+    const size_t need = nq_decode_attention_workspace_bytes(batch, hq, head_dim, max_seq);
+    if (!workspace || workspace_bytes < need) return fail(NQ_ERR_WORKSPACE, "attention workspace needs %zu bytes", need);
+    if (((uintptr_t)workspace) & 255) return fail(NQ_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+    if ((((uintptr_t)p.kc) | ((uintptr_t)p.vc)) & 15) return fail(NQ_ERR_INVALID_ARGUMENT, "caches must be 16B aligned");
+    const AttnChunks ch = attn_chunks(max_seq);
+    unsigned char *ws = static_cast<unsigned char *>(workspace);
+    p.ctrl = reinterpret_cast<Ctrl *>(ws);
+    p.count = reinterpret_cast<unsigned *>(ws + sizeof(Ctrl));
+    p.part = reinterpret_cast<float *>(ws + sizeof(Ctrl) + attn_count_bytes(batch, hq));
+    p.hkv = (int)hkv;
+    p.max_seq = (int)max_seq;
+    p.nchunk = ch.nchunk;
+    p.nsub = ch.nsub;
+    p.scale = 1.0f / sqrtf((float)head_dim);
+    return NQ_OK;
 }
 
 static int sm_count() {
@@ -395,8 +617,10 @@ int nq_rope_cache(int dtype, void *q, void *k, const void *v, const int32_t *pos
 }
 
 size_t nq_decode_attention_workspace_bytes(int64_t batch, int64_t hq, int64_t head_dim, int64_t max_seq) {
-    const int64_t nsplit = (max_seq + nq::dec::kChunk - 1) / nq::dec::kChunk;
-    return (size_t)batch * hq * nsplit * (head_dim + 2) * sizeof(float);
+    if (batch <= 0 || hq <= 0 || head_dim <= 0 || max_seq <= 0) return 0;
+    const nq::dec::AttnChunks ch = nq::dec::attn_chunks(max_seq);
+    return sizeof(nq::Ctrl) + nq::dec::attn_count_bytes(batch, hq) +
+           (size_t)batch * hq * ch.nchunk * (head_dim + 2) * sizeof(float);
 }
 
 int nq_decode_attention(int dtype, const void *q, const void *k_cache, const void *v_cache, const int32_t *seq_len,
@@ -404,46 +628,41 @@ int nq_decode_attention(int dtype, const void *q, const void *k_cache, const voi
                         void *workspace, size_t workspace_bytes, void *stream) {
     using namespace nq;
     using namespace nq::dec;
-    if (!q || !k_cache || !v_cache || !seq_len || !out || batch <= 0 || hq <= 0 || hkv <= 0 || max_seq <= 0)
-        return fail(NQ_ERR_INVALID_ARGUMENT, "bad decode_attention args");
-    if (head_dim != 128) return fail(NQ_ERR_UNSUPPORTED, "decode attention supports head_dim 128");
-    if (hq % hkv) return fail(NQ_ERR_INVALID_ARGUMENT, "query heads must be a multiple of kv heads");
-    const int grp = (int)(hq / hkv);
-    const size_t need = nq_decode_attention_workspace_bytes(batch, hq, head_dim, max_seq);
-    if (!workspace || workspace_bytes < need) return fail(NQ_ERR_WORKSPACE, "attention workspace needs %zu bytes", need);
-    if (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15) return fail(NQ_ERR_INVALID_ARGUMENT, "caches must be 16B aligned");
-    const int nsplit = (int)((max_seq + kChunk - 1) / kChunk);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    dim3 grid((unsigned)nsplit, (unsigned)hkv, (unsigned)batch);
-    const float scale = 1.0f / sqrtf((float)head_dim);
-    float *part = static_cast<float *>(workspace);
-#define NQ_ATTN(TT, G)                                                                                        \
-    attn_split_kernel<TT, 128, G><<<grid, kAttnThreads, 0, s>>>((const TT *)q, (const TT *)k_cache,           \
-                                                                 (const TT *)v_cache, seq_len, part, (int)hkv, \
-                                                                 (int)max_seq, nsplit, scale)
-#define NQ_ATTN_DT(TT)                                     \
-    switch (grp) {                                         \
-        case 1: NQ_ATTN(TT, 1); break;                     \
-        case 2: NQ_ATTN(TT, 2); break;                     \
-        case 4: NQ_ATTN(TT, 4); break;                     \
-        case 8: NQ_ATTN(TT, 8); break;                     \
-        default: return fail(NQ_ERR_UNSUPPORTED, "GQA group %d not in {1,2,4,8}", grp); \
-    }
-    if (dtype == NQ_DTYPE_F16) {
-        NQ_ATTN_DT(__half)
-        attn_combine_kernel<__half, 128><<<dim3((unsigned)hq, (unsigned)batch), 128, 0, s>>>(part, (__half *)out,
-                                                                                          (int)hq, nsplit);
-    } else if (dtype == NQ_DTYPE_BF16) {
-        NQ_ATTN_DT(__nv_bfloat16)
-        attn_combine_kernel<__nv_bfloat16, 128><<<dim3((unsigned)hq, (unsigned)batch), 128, 0, s>>>(
-            part, (__nv_bfloat16 *)out, (int)hq, nsplit);
-    } else {
-        return fail(NQ_ERR_UNSUPPORTED, "dtype");
-    }
-#undef NQ_ATTN_DT
-#undef NQ_ATTN
-    cudaError_t e = cudaGetLastError();
+    if (!q || !k_cache || !v_cache || !seq_len || !out) return fail(NQ_ERR_INVALID_ARGUMENT, "bad decode_attention args");
+    AttnParams p{};
+    p.q = q;
+    p.seq_len = seq_len;
+    p.kc = const_cast<void *>(k_cache);
+    p.vc = const_cast<void *>(v_cache);
+    p.out = out;
+    const int st = attn_prepare(dtype, batch, hq, hkv, head_dim, max_seq, workspace, workspace_bytes, p);
+    if (st != NQ_OK) return st;
+    const cudaError_t e = dispatch_attn<false>(dtype, (int)(hq / hkv), p, (int)batch, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? NQ_OK : cuda_fail(e, "decode attention launch");
+}
+
+int nq_decode_attention_rope(int dtype, const void *q, const void *k, const void *v, const int32_t *positions,
+                             void *k_cache, void *v_cache, void *out, int64_t batch, int64_t hq, int64_t hkv,
+                             int64_t head_dim, int64_t max_seq, float theta, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+    using namespace nq;
+    using namespace nq::dec;
+    if (!q || !k || !v || !positions || !k_cache || !v_cache || !out)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "bad decode_attention_rope args");
+    if (!(theta > 0.f)) return fail(NQ_ERR_INVALID_ARGUMENT, "theta must be positive");
+    AttnParams p{};
+    p.q = q;
+    p.k_new = k;
+    p.v_new = v;
+    p.pos = positions;
+    p.kc = k_cache;
+    p.vc = v_cache;
+    p.out = out;
+    p.log2_theta = log2f(theta);
+    const int st = attn_prepare(dtype, batch, hq, hkv, head_dim, max_seq, workspace, workspace_bytes, p);
+    if (st != NQ_OK) return st;
+    const cudaError_t e = dispatch_attn<true>(dtype, (int)(hq / hkv), p, (int)batch, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? NQ_OK : cuda_fail(e, "decode attention (rope) launch");
 }
 
 int nq_silu_mul(int dtype, const void *gate, const void *up, void *out, int64_t n, void *stream) {

@@ -13,6 +13,7 @@
 #include <torch/library.h>
 
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <optional>
 #include <string>
@@ -51,13 +52,14 @@ int order_code(const std::string &m) {
 
 cudaStream_t cur_stream(const at::Tensor &t) { return c10::cuda::getCurrentCUDAStream(t.device().index()).stream(); }
 
-// Zero-initialised workspace per (device, stream), grown on demand and kept for the
-// life of the process (its control block must start zeroed; kernels keep it so).
-at::Tensor workspace_for(const at::Tensor &like, size_t bytes) {
+// Zero-initialised workspace per (device, stream, slot), grown on demand and kept for the
+// life of the process (its control block must start zeroed; kernels keep it so).  Slot 0
+// serves the linears, slot 1 decode attention.
+at::Tensor workspace_for(const at::Tensor &like, size_t bytes, int slot = 0) {
     static std::mutex mu;
-    static std::map<std::pair<int, cudaStream_t>, at::Tensor> cache;
+    static std::map<std::tuple<int, cudaStream_t, int>, at::Tensor> cache;
     std::lock_guard<std::mutex> lock(mu);
-    const auto key = std::make_pair((int)like.device().index(), cur_stream(like));
+    const auto key = std::make_tuple((int)like.device().index(), cur_stream(like), slot);
     auto it = cache.find(key);
     if (it == cache.end() || (size_t)it->second.numel() < bytes) {
         size_t cap = bytes < (1u << 20) ? (1u << 20) : bytes;
@@ -362,11 +364,42 @@ at::Tensor decode_attention_cuda(const at::Tensor &q, const at::Tensor &k_cache,
     c10::cuda::CUDAGuard guard(q.device());
     auto out = at::empty_like(q);
     const size_t wsb = nq_decode_attention_workspace_bytes(b, hq, d, ms);
-    auto ws = at::empty({(int64_t)wsb}, q.options().dtype(at::kByte));
+    at::Tensor ws = workspace_for(q, wsb, 1);
     NQ_TORCH_CHECK(nq_decode_attention(dtype_code(st), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                                        seq_len.data_ptr<int32_t>(), out.data_ptr(), b, hq, hkv, d, ms, ws.data_ptr(),
-                                       wsb, cur_stream(q)));
+                                       (size_t)ws.numel(), cur_stream(q)));
     return out;
+}
+
+at::Tensor decode_attention_rope_cuda(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v,
+                                      const at::Tensor &positions, at::Tensor &k_cache, at::Tensor &v_cache,
+                                      double theta) {
+    const auto st = q.scalar_type();
+    CHECK_CUDA_CONT(q, st);
+    CHECK_CUDA_CONT(k, st);
+    CHECK_CUDA_CONT(v, st);
+    CHECK_CUDA_CONT(k_cache, st);
+    CHECK_CUDA_CONT(v_cache, st);
+    CHECK_CUDA_CONT(positions, at::kInt);
+    TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.sizes() == k.sizes(), "q [batch, hq, d], k/v [batch, hkv, d]");
+    TORCH_CHECK(k_cache.dim() == 4 && k_cache.sizes() == v_cache.sizes(), "caches [batch, hkv, max_seq, d]");
+    const int64_t b = q.size(0), hq = q.size(1), d = q.size(2), hkv = k.size(1), ms = k_cache.size(2);
+    TORCH_CHECK(k.size(0) == b && k.size(2) == d && k_cache.size(1) == hkv && k_cache.size(3) == d, "shape mismatch");
+    TORCH_CHECK(k_cache.size(0) >= b && positions.numel() == b, "one position per batch row");
+    c10::cuda::CUDAGuard guard(q.device());
+    auto out = at::empty_like(q);
+    const size_t wsb = nq_decode_attention_workspace_bytes(b, hq, d, ms);
+    at::Tensor ws = workspace_for(q, wsb, 1);
+    NQ_TORCH_CHECK(nq_decode_attention_rope(dtype_code(st), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                            positions.data_ptr<int32_t>(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                            out.data_ptr(), b, hq, hkv, d, ms, (float)theta, ws.data_ptr(),
+                                            (size_t)ws.numel(), cur_stream(q)));
+    return out;
+}
+
+at::Tensor decode_attention_rope_meta(const at::Tensor &q, const at::Tensor &, const at::Tensor &, const at::Tensor &,
+                                      at::Tensor &, at::Tensor &, double) {
+    return at::empty_like(q);
 }
 
 at::Tensor decode_attention_meta(const at::Tensor &q, const at::Tensor &, const at::Tensor &, const at::Tensor &) {
@@ -506,6 +539,8 @@ TORCH_LIBRARY(nq_b200, m) {
         "rope_cache(Tensor(a!) q, Tensor(b!) k, Tensor v, Tensor positions, Tensor? batch_of, Tensor(c!) k_cache, "
         "Tensor(d!) v_cache, float theta) -> ()");
     m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seq_len) -> Tensor");
+    m.def("decode_attention_rope(Tensor q, Tensor k, Tensor v, Tensor positions, Tensor(a!) k_cache, "
+          "Tensor(b!) v_cache, float theta) -> Tensor");
     m.def("silu_mul(Tensor gate, Tensor up) -> Tensor");
     m.def(
         "gemv_group(Tensor x, Tensor[] scale_pre, Tensor[] v_bits, Tensor?[] scale_mid, Tensor[] u_bits, "
@@ -525,6 +560,7 @@ TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
     m.impl("rmsnorm", &rmsnorm_cuda);
     m.impl("rope_cache", &rope_cache_cuda);
     m.impl("decode_attention", &decode_attention_cuda);
+    m.impl("decode_attention_rope", &decode_attention_rope_cuda);
     m.impl("silu_mul", &silu_mul_cuda);
     m.impl("gemv_group", &gemv_group_cuda);
     m.impl("linear_group", &linear_group_cuda);
@@ -540,6 +576,7 @@ TORCH_LIBRARY_IMPL(nq_b200, Meta, m) {
     m.impl("rmsnorm", &rmsnorm_meta);
     m.impl("rope_cache", &rope_cache_meta);
     m.impl("decode_attention", &decode_attention_meta);
+    m.impl("decode_attention_rope", &decode_attention_rope_meta);
     m.impl("silu_mul", &silu_mul_meta);
     m.impl("gemv_group", &group_meta);
     m.impl("linear_group", &group_meta);

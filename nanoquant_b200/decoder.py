@@ -8,7 +8,8 @@ decode with the step captured as a CUDA graph), rebuilt around the kernels of th
 * every projection is a NanoQuant layer (half2 sign planes + fp16 scales) run by
   ``torch.ops.nq_b200.linear`` (fused GEMV for decode, tcgen05 GEMM for prefill);
 * RMSNorm (+ residual add), RoPE + KV-cache write, split-KV decode attention and SwiGLU are
-  this package's kernels; prefill attention uses PyTorch's fused SDPA (causal, GQA);
+  this package's kernels (decode runs RoPE, the cache write and attention as one launch);
+  prefill attention uses PyTorch's fused SDPA (causal, GQA);
 * the decode step reads token ids / positions from device buffers and advances them itself,
   so a captured graph replays one autoregressive step with no host work.
 
@@ -250,9 +251,8 @@ class Decoder:
             x, residual = torch.ops.nq_b200.rmsnorm(h, residual, lay["in_norm"], cfg.rms_eps)
             q, k, v = lay["qkv"](x)
             q, k, v = q.view(B, self.hq, D), k.view(B, self.hkv, D), v.view(B, self.hkv, D)
-            torch.ops.nq_b200.rope_cache(q, k, v, self.pos, None, self.k_cache[li], self.v_cache[li],
-                                         cfg.rope_theta)
-            a = torch.ops.nq_b200.decode_attention(q, self.k_cache[li], self.v_cache[li], self.seq_len)
+            a = torch.ops.nq_b200.decode_attention_rope(q, k, v, self.pos, self.k_cache[li], self.v_cache[li],
+                                                        cfg.rope_theta)
             o = self._all_reduce(lay["o"](a.view(B, self.hq * D)))
             x, residual = torch.ops.nq_b200.rmsnorm(o, residual, lay["post_norm"], cfg.rms_eps)
             act = torch.ops.nq_b200.silu_mul(*lay["gate_up"](x))

@@ -8,18 +8,20 @@ import pytest
 
 from nanoquant_b200 import _lib
 
-HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "nq_b200.h")
+INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+HEADERS = [os.path.join(INCLUDE, h) for h in ("nq_b200.h", "nq_decoder.h")]
 
 
 def declared_symbols():
-    text = open(HEADER).read()
+    text = "".join(open(h).read() for h in HEADERS)
     return sorted(set(re.findall(r"NQ_API\s+[\w\s\*]*?\b(nq_\w+)\s*\(", text)))
 
 
 def test_header_declares_expected_entry_points():
     names = declared_symbols()
     for n in ("nq_pack_signs", "nq_unpack_signs", "nq_repack_signs", "nq_gemv", "nq_gemv_workspace_bytes",
-              "nq_gemm", "nq_gemm_workspace_bytes", "nq_workspace_reset", "nq_workspace_status"):
+              "nq_gemm", "nq_gemm_workspace_bytes", "nq_workspace_reset", "nq_workspace_status",
+              "nq_rmsnorm", "nq_rope_cache", "nq_decode_attention", "nq_decode_attention_rope", "nq_silu_mul"):
         assert n in names
 
 
@@ -44,6 +46,38 @@ def test_workspace_sizes():
     assert lib.nq_gemv_workspace_bytes(64, 1126) == lib.nq_gemv_workspace_bytes(1, 1126)
     assert lib.nq_gemv_workspace_bytes(1, 0) == 0
     assert lib.nq_gemm_workspace_bytes(2048, 2054) >= 256
+    # attention: control block + counters (256-byte rounded) + [batch][hq][chunks][130] floats;
+    # 64-position chunks while a head has at most 64 of them, longer chunks beyond
+    assert lib.nq_decode_attention_workspace_bytes(1, 32, 128, 2400) == 256 + 256 + 32 * 38 * 130 * 4
+    assert lib.nq_decode_attention_workspace_bytes(2, 8, 128, 9000) == 256 + 256 + 2 * 8 * 47 * 130 * 4
+    assert lib.nq_decode_attention_workspace_bytes(1, 32, 128, 0) == 0
+
+
+@pytest.mark.parametrize("case", ["head_dim", "group", "small_ws", "unaligned_ws", "null_q"])
+def test_attention_rejects_bad_arguments_on_host(case):
+    lib = _lib.cuda_lib()
+    fake = ctypes.c_void_p(0x10000)  # never dereferenced: every check runs before a launch
+    ws_bytes = lib.nq_decode_attention_workspace_bytes(1, 8, 128, 512)
+    args = dict(q=fake, hq=8, hkv=2, d=128, ws=fake, wsb=ws_bytes)
+    if case == "head_dim":
+        args["d"] = 64
+    elif case == "group":
+        args["hq"], args["hkv"] = 9, 3  # group of 3 is not supported
+    elif case == "small_ws":
+        args["wsb"] = ws_bytes - 1
+    elif case == "unaligned_ws":
+        args["ws"] = ctypes.c_void_p(0x10010)
+    elif case == "null_q":
+        args["q"] = None
+    for rope in (False, True):
+        if rope:
+            st = lib.nq_decode_attention_rope(0, args["q"], fake, fake, fake, fake, fake, fake, 1, args["hq"],
+                                              args["hkv"], args["d"], 512, 10000.0, args["ws"], args["wsb"], None)
+        else:
+            st = lib.nq_decode_attention(0, args["q"], fake, fake, fake, fake, 1, args["hq"], args["hkv"], args["d"],
+                                         512, args["ws"], args["wsb"], None)
+        assert st != 0, (case, rope)
+        assert lib.nq_last_error_message()
 
 
 @pytest.mark.parametrize("case", ["null_x", "bad_dtype", "zero_batch", "small_ws"])

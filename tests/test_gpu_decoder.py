@@ -55,22 +55,83 @@ def test_graph_replay_matches_eager_steps():
     g.release()
 
 
-def test_decode_attention_against_reference():
-    """Split-KV attention (several chunks, GQA group 4) against float32 softmax attention."""
-    B, hq, hkv, D, S = 2, 8, 2, 128, 700
-    g = torch.Generator().manual_seed(0)
-    q = torch.randn(B, hq, D, generator=g).half()
-    kc = torch.randn(B, hkv, S, D, generator=g).half()
-    vc = torch.randn(B, hkv, S, D, generator=g).half()
-    L = torch.tensor([700, 257], dtype=torch.int32)
-    out = torch.ops.nq_b200.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), L.cuda()).float().cpu()
+def _attention_ref(q, kc, vc, L):
+    """float32 softmax attention of q [B, hq, D] over the first L[b] rows of the caches."""
+    B, hq, D = q.shape
+    hkv = kc.shape[1]
+    out = torch.zeros(B, hq, D)
     for b in range(B):
         n = int(L[b])
+        if n == 0:
+            continue
         k = kc[b, :, :n].float().repeat_interleave(hq // hkv, 0)
         v = vc[b, :, :n].float().repeat_interleave(hq // hkv, 0)
         w = torch.softmax((q[b].float()[:, None, :] @ k.transpose(1, 2))[:, 0] / np.sqrt(D), -1)
-        want = (w[:, None, :] @ v)[:, 0]
-        assert orc.rel_l2(out[b].numpy(), want.numpy()) < 2e-3
+        out[b] = (w[:, None, :] @ v)[:, 0]
+    return out
+
+
+ATTN_CASES = [  # (hq, hkv, max_seq, lengths, dtype): groups 1/2/4/8, one and several chunks,
+    (8, 2, 700, [700, 257, 1], torch.float16),      # partial sub-blocks, a length of one,
+    (4, 4, 128, [64, 65], torch.bfloat16),          # exactly one sub-block and one past it,
+    (4, 2, 200, [0, 5], torch.float16),             # an empty sequence (zeros),
+    (16, 2, 9000, [9000, 4097], torch.float16),     # 3 sub-blocks per chunk (two-stage ring)
+    (32, 32, 2400, [2049], torch.bfloat16),         # the 7B decode shape
+]
+
+
+@pytest.mark.parametrize("case", range(len(ATTN_CASES)))
+def test_decode_attention_against_reference(case):
+    """Split-KV attention against float32 softmax attention; a second call on the same
+    workspace gives the same bits (the arrival counters are back at zero)."""
+    hq, hkv, S, lens, dt = ATTN_CASES[case]
+    B, D = len(lens), 128
+    g = torch.Generator().manual_seed(case)
+    q = torch.randn(B, hq, D, generator=g).to(dt)
+    kc = torch.randn(B, hkv, S, D, generator=g).to(dt)
+    vc = torch.randn(B, hkv, S, D, generator=g).to(dt)
+    L = torch.tensor(lens, dtype=torch.int32)
+    args = (q.cuda(), kc.cuda(), vc.cuda(), L.cuda())
+    out = torch.ops.nq_b200.decode_attention(*args)
+    again = torch.ops.nq_b200.decode_attention(*args)
+    assert torch.equal(out, again)
+    out = out.float().cpu()
+    want = _attention_ref(q, kc, vc, L)
+    for b in range(B):
+        if lens[b] == 0:
+            assert torch.count_nonzero(out[b]) == 0
+        else:
+            assert orc.rel_l2(out[b].numpy(), want[b].numpy()) < 2e-3, (b, lens[b])
+
+
+@pytest.mark.parametrize("hq,hkv,S,pos,dt", [
+    (8, 2, 300, [299, 64], torch.float16),
+    (32, 32, 2400, [2048], torch.bfloat16),
+    (16, 2, 9000, [8999, 130], torch.float16),
+])
+def test_decode_attention_rope_matches_rope_cache_then_attention(hq, hkv, S, pos, dt):
+    """The fused entry point: caches bit-identical to rope_cache's writes, output bit-identical
+    to rope_cache + decode_attention, q/k/v inputs untouched."""
+    B, D, theta = len(pos), 128, 10000.0
+    g = torch.Generator().manual_seed(S)
+    q = torch.randn(B, hq, D, generator=g).to(dt).cuda()
+    k = torch.randn(B, hkv, D, generator=g).to(dt).cuda()
+    v = torch.randn(B, hkv, D, generator=g).to(dt).cuda()
+    kc = torch.randn(B, hkv, S, D, generator=g).to(dt).cuda()
+    vc = torch.randn(B, hkv, S, D, generator=g).to(dt).cuda()
+    P = torch.tensor(pos, dtype=torch.int32, device="cuda")
+    kc1, vc1 = kc.clone(), vc.clone()
+    q1, k1 = q.clone(), k.clone()
+    torch.ops.nq_b200.rope_cache(q1, k1, v, P, None, kc1, vc1, theta)
+    want = torch.ops.nq_b200.decode_attention(q1, kc1, vc1, P + 1)
+    kc2, vc2 = kc.clone(), vc.clone()
+    qs, ks, vs = q.clone(), k.clone(), v.clone()
+    got = torch.ops.nq_b200.decode_attention_rope(q, k, v, P, kc2, vc2, theta)
+    assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
+    assert torch.equal(got, want)
+    assert torch.equal(q, qs) and torch.equal(k, ks) and torch.equal(v, vs)
+    ref_out = _attention_ref(q1.cpu(), kc1.cpu(), vc1.cpu(), (P + 1).cpu())
+    assert orc.rel_l2(got.float().cpu().numpy(), ref_out.numpy()) < 2e-3
 
 
 def test_rmsnorm_and_silu_against_torch():
