@@ -35,6 +35,14 @@ class GemvLayer(ctypes.Structure):
                 ("scale_mid", ctypes.c_void_p), ("u_bits", ctypes.c_void_p), ("out_features", ctypes.c_int64),
                 ("scale_post", ctypes.c_void_p), ("y", ctypes.c_void_p)]
 
+
+class ChainPhase(ctypes.Structure):
+    """nq_chain_phase of include/nq_b200.h."""
+    _fields_ = [("n_layers", ctypes.c_int), ("x_mode", ctypes.c_int), ("in_features", ctypes.c_int64),
+                ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p), ("norm_weight", ctypes.c_void_p),
+                ("eps", ctypes.c_float), ("residual", ctypes.c_void_p), ("layers", GemvLayer * 3)]
+
+
 _lock = threading.Lock()
 _cuda = None
 _torch_loaded = False
@@ -58,6 +66,9 @@ _SIGNATURES = {
     "nq_gemv_static": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p,
                                   _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p,
                                   _c.c_void_p]),
+    "nq_gemv_chain_workspace_bytes": (_c.c_size_t, [_c.c_int, _c.c_int64, _c.c_int, _c.c_void_p]),
+    "nq_gemv_chain": (_c.c_int, [_c.c_int, _c.c_int64, _c.c_int, _c.c_void_p, _c.c_void_p, _c.c_size_t,
+                                 _c.c_void_p]),
     "nq_gemm_workspace_bytes": (_c.c_size_t, [_c.c_int64, _c.c_int64]),
     "nq_gemm": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64,
                            _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_void_p,

@@ -203,6 +203,7 @@ struct Elem<__half> {
     __device__ static __forceinline__ __half out(float v) {
         return __float2half_rn(fminf(fmaxf(v, -64504.0f), 64504.0f));
     }
+    __device__ static __forceinline__ __half rn(float v) { return __float2half_rn(v); }
 };
 template <>
 struct Elem<__nv_bfloat16> {
@@ -216,6 +217,7 @@ struct Elem<__nv_bfloat16> {
     __device__ static __forceinline__ __nv_bfloat16 out(float v) {
         return __float2bfloat16_rn(fminf(fmaxf(v, -3.3895313892515355e+38f), 3.3895313892515355e+38f));
     }
+    __device__ static __forceinline__ __nv_bfloat16 rn(float v) { return __float2bfloat16_rn(v); }
 };
 
 // Sign mask of a 16-bit pair: bits 15 and 31 of `w` select the signs of the low and

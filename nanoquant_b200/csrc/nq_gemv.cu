@@ -174,6 +174,7 @@ __device__ __forceinline__ void sign_frag(uint32_t wA, uint32_t wB, int j, uint3
 }
 
 constexpr int kMaxGroup = 3;  // layers sharing one input x in a single launch (q/k/v, gate/up)
+enum ChainXMode : int { kChainPlain = NQ_CHAIN_X_PLAIN, kChainNorm = NQ_CHAIN_X_RMSNORM, kChainSiluMul = NQ_CHAIN_X_SILU_MUL };
 
 // One NanoQuant layer of a launch group.
 struct Member {
@@ -219,12 +220,248 @@ __device__ __forceinline__ void seg_tiles(const Member &mb, int t2b, int t2e, in
     b = min(t2e, mb.t2_start + mb.tiles2);
 }
 
+// ------------------------------------------------------------------ stage bodies
+// Shared by the single-group kernel and the chain kernel.  Stage 1: this CTA's tiles
+// [t1b, t1e) as (tile, K slice) work items over the warps, partial 16x8 tiles into `red`;
+// returns the K slices per tile.
+template <typename T>
+__device__ __forceinline__ int stage1_items(const Params &p, const uint32_t *vch, const T *s2s, const T *xs,
+                                            const __nv_bfloat16 *xs2, float *red, int t1b, int t1e, bool ok) {
+    using E = Elem<T>;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int sh0 = 8 * (t & 1);
+    const int in_pad = p.kb1 * 64;
+    const int nxc = 2 * p.batch;
+    const T *xg = static_cast<const T *>(p.x) + (size_t)g * p.in_f;
+    const uint32_t *xsw = reinterpret_cast<const uint32_t *>(xs + (size_t)g * in_pad);
+    const bool xrow = g < p.batch, fcol = g < nxc;
+    const int ntiles = t1e - t1b;
+    const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
+    for (int item = warp; item < items; item += kWarps) {
+        int lt, kbeg, kend;
+        item_of(item, KS, p.kb1, lt, kbeg, kend);
+        const int tile = t1b + lt;
+        const int l = member_of1(p, tile);
+        const int row0 = 16 * (tile - p.m[l].t1_start), rank = p.m[l].rank;
+        const bool vA = ok && (row0 + g < rank), vB = ok && (row0 + g + 8 < rank);
+        const uint32_t *rowA = vch + (size_t)(lt * 16 + g) * p.wvs;
+        const uint32_t *rowB = rowA + (size_t)8 * p.wvs;
+        float acc[4][4] = {};
+        if (p.fold) {
+            const __nv_bfloat16 *xcol = xs2 + ((size_t)l * nxc + g) * in_pad;
+#pragma unroll 2
+            for (int kb = kbeg; kb < kend; ++kb) {
+                const int wi = 2 * kb + (t >> 1);
+                const uint32_t wA = (vA && wi < p.wv) ? rowA[wi] << sh0 : 0u;
+                const uint32_t wB = (vB && wi < p.wv) ? rowB[wi] << sh0 : 0u;
+                const int kc = 64 * kb + 16 * t;
+                uint32_t bp[8];
+                if (fcol) {
+                    load16_smem(xcol + kc, bp);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) bp[j] = 0u;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t a[4];
+                    sign_frag(wA, wB, j, a);
+                    mma_bf16_16816(acc[j], a[0], a[1], a[2], a[3], bp[2 * j], bp[2 * j + 1]);
+                }
+            }
+        } else {
+            const uint32_t *sw = reinterpret_cast<const uint32_t *>(s2s + (size_t)l * in_pad);
+#pragma unroll 2
+            for (int kb = kbeg; kb < kend; ++kb) {
+                const int wi = 2 * kb + (t >> 1);
+                const uint32_t wA = (vA && wi < p.wv) ? rowA[wi] << sh0 : 0u;
+                const uint32_t wB = (vB && wi < p.wv) ? rowB[wi] << sh0 : 0u;
+                const int kc = 64 * kb + 16 * t;
+                uint32_t sp[8], xp[8];
+                load16_smem(sw + kc / 2, sp);
+                if (!xrow) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) xp[j] = 0u;
+                } else if (p.x_in_smem) {
+                    load16_smem(xsw + kc / 2, xp);
+                } else {
+                    load16_global<T>(xg, kc, p.in_f, xp);
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t a0 = lop_sign(wA << (2 * j), sp[2 * j]);
+                    const uint32_t a1 = lop_sign(wB << (2 * j), sp[2 * j]);
+                    const uint32_t a2 = lop_sign(wA << (2 * j + 1), sp[2 * j + 1]);
+                    const uint32_t a3 = lop_sign(wB << (2 * j + 1), sp[2 * j + 1]);
+                    E::mma(acc[j], a0, a1, a2, a3, xp[2 * j], xp[2 * j + 1]);
+                }
+            }
+        }
+        float sum[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sum[i] = (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
+        store_partial(red + item * 256, sum, g, t);
+    }
+    return KS;
+}
+
+// Stage 1, second half: reduce the K slices, apply scale_mid, store t as bf16 (hi, lo) into
+// each member's stage-2 operand, and zero its K padding (the CTA owning the member's last tile).
+template <typename T>
+__device__ __forceinline__ void stage1_finish(const Params &p, const float *red, int t1b, int t1e, int KS) {
+    using E = Elem<T>;
+    const int tid = threadIdx.x;
+    const int ntiles = t1e - t1b;
+    for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
+        const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
+        const int b = rem >> 4, row = rem & 15;
+        float s = 0.f;
+        if (p.fold) {
+            for (int ks = 0; ks < KS; ++ks) {
+                const float *r = red + (lt * KS + ks) * 256 + row * 8 + 2 * b;
+                s += r[0] + r[1];
+            }
+        } else {
+            for (int ks = 0; ks < KS; ++ks) s += red[(lt * KS + ks) * 256 + row * 8 + b];
+        }
+        const int tile = t1b + lt;
+        const int l = member_of1(p, tile);
+        const Member &mb = p.m[l];
+        const int k = 16 * (tile - mb.t1_start) + row;
+        if (k < mb.rank) {
+            if (mb.smid) s *= E::to_f(static_cast<const T *>(mb.smid)[k]);
+            const __nv_bfloat16 hi = __float2bfloat16_rn(s);
+            const int col = (b >> 2) * 8 + 2 * (b & 3);
+            mb.tb[(size_t)col * mb.ldi + k] = hi;
+            mb.tb[(size_t)(col + 1) * mb.ldi + k] = __float2bfloat16_rn(s - __bfloat162float(hi));
+        }
+    }
+    // the CTA owning a member's last stage-1 tile zeroes that member's K padding [rank, ldi)
+    for (int l = 0; l < p.nm; ++l) {
+        const Member &mb = p.m[l];
+        const int last = mb.t1_start + mb.tiles1 - 1;
+        const int padw = mb.ldi - mb.rank;
+        if (last >= t1b && last < t1e && padw > 0)
+            for (int i = tid; i < 16 * padw; i += kThreads) {
+                const int col = i / padw;
+                mb.tb[(size_t)col * mb.ldi + mb.rank + (i - col * padw)] = __float2bfloat16_rn(0.f);
+            }
+    }
+}
+
+// Stage 2: this CTA's tiles [t2b, t2e) of U against t; partial tiles into `red`; returns KS.
+template <typename T>
+__device__ __forceinline__ int stage2_items(const Params &p, const uint32_t *uch, float *red, int t2b, int t2e,
+                                            bool ok) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int sh0 = 8 * (t & 1);
+    const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles: (hi, lo) of 4 batch rows each
+    const int ntiles = t2e - t2b;
+    const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
+    // B column g of n-tile q is the hi (g even) or lo (g odd) part of batch row 4q + g/2,
+    // stored ready-made by stage 1 as bf16 pairs along k
+    const int b0 = g >> 1, b1 = 4 + (g >> 1);
+    const bool v0 = b0 < p.batch, v1 = nt == 2 && b1 < p.batch;
+    constexpr int kChunkKb = 4;  // K blocks whose B fragments are fetched together
+    for (int item = warp; item < items; item += kWarps) {
+        const int lt = item / KS, ks = item - lt * KS;
+        const int tile = t2b + lt;
+        const int l = member_of2(p, tile);
+        const Member &mb = p.m[l];
+        const int kbeg = (mb.kb2 * ks) / KS, kend = (mb.kb2 * (ks + 1)) / KS;
+        // this tile's rows in the smem U region: after the earlier members' segments
+        uint32_t uoff = 0;
+        for (int q = 0; q < l; ++q) {
+            int a, b;
+            seg_tiles(p.m[q], t2b, t2e, a, b);
+            if (a < b) uoff = ((uoff + (uint32_t)(16 * (b - a)) * (uint32_t)p.m[q].wus) + 3u) & ~3u;
+        }
+        int a0, b0s;
+        seg_tiles(mb, t2b, t2e, a0, b0s);
+        const int row0 = 16 * (tile - mb.t2_start);
+        const bool vA = ok && (row0 + g < mb.out_f), vB = ok && (row0 + g + 8 < mb.out_f);
+        const uint32_t *rowA = uch + uoff + (size_t)(16 * (tile - a0) + g) * mb.wus;
+        const uint32_t *rowB = rowA + (size_t)8 * mb.wus;
+        const __nv_bfloat16 *trow0 = mb.tb + (size_t)g * mb.ldi;
+        const __nv_bfloat16 *trow1 = mb.tb + (size_t)(8 + g) * mb.ldi;
+        float acc0[4][4] = {}, acc1[4][4] = {};
+        for (int kb0 = kbeg; kb0 < kend; kb0 += kChunkKb) {
+            uint32_t bp0[kChunkKb][8], bp1[kChunkKb][8];
+#pragma unroll
+            for (int q = 0; q < kChunkKb; ++q) {
+                const int kc = 64 * (kb0 + q) + 16 * t;
+                const bool in = kb0 + q < kend;
+                load_t_pairs(trow0 + kc, in && v0, bp0[q]);
+                load_t_pairs(trow1 + kc, in && v1, bp1[q]);
+            }
+#pragma unroll
+            for (int q = 0; q < kChunkKb; ++q) {
+                const int kb = kb0 + q;
+                if (kb >= kend) break;
+                const int wi = 2 * kb + (t >> 1);
+                const uint32_t wA = (vA && wi < mb.wu) ? rowA[wi] << sh0 : 0u;
+                const uint32_t wB = (vB && wi < mb.wu) ? rowB[wi] << sh0 : 0u;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t a[4];
+                    sign_frag(wA, wB, j, a);
+                    mma_bf16_16816(acc0[j], a[0], a[1], a[2], a[3], bp0[q][2 * j], bp0[q][2 * j + 1]);
+                    if (nt == 2) mma_bf16_16816(acc1[j], a[0], a[1], a[2], a[3], bp1[q][2 * j], bp1[q][2 * j + 1]);
+                }
+            }
+        }
+        float s0[4], s1v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            s0[i] = (acc0[0][i] + acc0[1][i]) + (acc0[2][i] + acc0[3][i]);
+            s1v[i] = (acc1[0][i] + acc1[1][i]) + (acc1[2][i] + acc1[3][i]);
+        }
+        store_partial(red + item * 256, s0, g, t);
+        store_partial(red + item * 256 + 128, s1v, g, t);
+    }
+    return KS;
+}
+
+// Stage 2, second half: reduce, scale by s1, round, and store y (optionally y = y + res).
+template <typename T>
+__device__ __forceinline__ void stage2_finish(const Params &p, const float *red, const T *s1s, int t2b, int t2e, int KS,
+                                              const void *res) {
+    using E = Elem<T>;
+    const int tid = threadIdx.x;
+    const int ntiles = t2e - t2b;
+    for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
+        const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
+        const int b = rem >> 4, row = rem & 15;
+        const int half = (b >> 2) * 128, col = 2 * (b & 3);
+        float s = 0.f;
+        for (int ks = 0; ks < KS; ++ks) {
+            const float *r = red + (lt * KS + ks) * 256 + half + row * 8 + col;
+            s += r[0] + r[1];
+        }
+        const int tile = t2b + lt;
+        const int l = member_of2(p, tile);
+        const Member &mb = p.m[l];
+        const int m = 16 * (tile - mb.t2_start) + row;
+        if (m < mb.out_f) {
+            const float v = s * E::to_f(s1s[16 * lt + row]);
+            const size_t o = (size_t)b * mb.out_f + m;
+            T out = E::out(v);
+            if (res) {  // residual add on the rounded output; res may alias y (same element, same thread)
+                const unsigned short rb = __ldcg(reinterpret_cast<const unsigned short *>(res) + o);
+                out = E::rn(E::to_f(out) + E::to_f(*reinterpret_cast<const T *>(&rb)));
+            }
+            static_cast<T *>(mb.y)[o] = out;
+        }
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     using E = Elem<T>;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, t = lane & 3;
+    const int tid = threadIdx.x;
     const int G = gridDim.x, c = blockIdx.x;
     const bool do1 = (p.mode & kStage1) != 0, do2 = (p.mode & kStage2) != 0;
 
@@ -341,7 +578,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     __syncthreads();
 
     bool ok = true;
-    const int sh0 = 8 * (t & 1);
     // ------------------------------------------------------------------ stage 1
     if (has1) {
         ok = mbar_wait(&bars[0], 0, &p.ctrl->status);
@@ -367,112 +603,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
             __syncthreads();
         }
-        const T *xg = static_cast<const T *>(p.x) + (size_t)g * p.in_f;
-        const uint32_t *xsw = reinterpret_cast<const uint32_t *>(xs + (size_t)g * in_pad);
-        const bool xrow = g < p.batch, fcol = g < nxc;
-        const int ntiles = t1e - t1b;
-        const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
-        for (int item = warp; item < items; item += kWarps) {
-            int lt, kbeg, kend;
-            item_of(item, KS, p.kb1, lt, kbeg, kend);
-            const int tile = t1b + lt;
-            const int l = member_of1(p, tile);
-            const int row0 = 16 * (tile - p.m[l].t1_start), rank = p.m[l].rank;
-            const bool vA = ok && (row0 + g < rank), vB = ok && (row0 + g + 8 < rank);
-            const uint32_t *rowA = vch + (size_t)(lt * 16 + g) * p.wvs;
-            const uint32_t *rowB = rowA + (size_t)8 * p.wvs;
-            float acc[4][4] = {};
-            if (p.fold) {
-                const __nv_bfloat16 *xcol = xs2 + ((size_t)l * nxc + g) * in_pad;
-#pragma unroll 2
-                for (int kb = kbeg; kb < kend; ++kb) {
-                    const int wi = 2 * kb + (t >> 1);
-                    const uint32_t wA = (vA && wi < p.wv) ? rowA[wi] << sh0 : 0u;
-                    const uint32_t wB = (vB && wi < p.wv) ? rowB[wi] << sh0 : 0u;
-                    const int kc = 64 * kb + 16 * t;
-                    uint32_t bp[8];
-                    if (fcol) {
-                        load16_smem(xcol + kc, bp);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) bp[j] = 0u;
-                    }
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t a[4];
-                        sign_frag(wA, wB, j, a);
-                        mma_bf16_16816(acc[j], a[0], a[1], a[2], a[3], bp[2 * j], bp[2 * j + 1]);
-                    }
-                }
-            } else {
-                const uint32_t *sw = reinterpret_cast<const uint32_t *>(s2s + (size_t)l * in_pad);
-#pragma unroll 2
-                for (int kb = kbeg; kb < kend; ++kb) {
-                    const int wi = 2 * kb + (t >> 1);
-                    const uint32_t wA = (vA && wi < p.wv) ? rowA[wi] << sh0 : 0u;
-                    const uint32_t wB = (vB && wi < p.wv) ? rowB[wi] << sh0 : 0u;
-                    const int kc = 64 * kb + 16 * t;
-                    uint32_t sp[8], xp[8];
-                    load16_smem(sw + kc / 2, sp);
-                    if (!xrow) {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) xp[j] = 0u;
-                    } else if (p.x_in_smem) {
-                        load16_smem(xsw + kc / 2, xp);
-                    } else {
-                        load16_global<T>(xg, kc, p.in_f, xp);
-                    }
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t a0 = lop_sign(wA << (2 * j), sp[2 * j]);
-                        const uint32_t a1 = lop_sign(wB << (2 * j), sp[2 * j]);
-                        const uint32_t a2 = lop_sign(wA << (2 * j + 1), sp[2 * j + 1]);
-                        const uint32_t a3 = lop_sign(wB << (2 * j + 1), sp[2 * j + 1]);
-                        E::mma(acc[j], a0, a1, a2, a3, xp[2 * j], xp[2 * j + 1]);
-                    }
-                }
-            }
-            float sum[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sum[i] = (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
-            store_partial(red + item * 256, sum, g, t);
-        }
+        const int KS1 = stage1_items<T>(p, vch, s2s, xs, xs2, red, t1b, t1e, ok);
         __syncthreads();
-        for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
-            const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
-            const int b = rem >> 4, row = rem & 15;
-            float s = 0.f;
-            if (p.fold) {
-                for (int ks = 0; ks < KS; ++ks) {
-                    const float *r = red + (lt * KS + ks) * 256 + row * 8 + 2 * b;
-                    s += r[0] + r[1];
-                }
-            } else {
-                for (int ks = 0; ks < KS; ++ks) s += red[(lt * KS + ks) * 256 + row * 8 + b];
-            }
-            const int tile = t1b + lt;
-            const int l = member_of1(p, tile);
-            const Member &mb = p.m[l];
-            const int k = 16 * (tile - mb.t1_start) + row;
-            if (k < mb.rank) {
-                if (mb.smid) s *= E::to_f(static_cast<const T *>(mb.smid)[k]);
-                const __nv_bfloat16 hi = __float2bfloat16_rn(s);
-                const int col = (b >> 2) * 8 + 2 * (b & 3);
-                mb.tb[(size_t)col * mb.ldi + k] = hi;
-                mb.tb[(size_t)(col + 1) * mb.ldi + k] = __float2bfloat16_rn(s - __bfloat162float(hi));
-            }
-        }
-        // the CTA owning a member's last stage-1 tile zeroes that member's K padding [rank, ldi)
-        for (int l = 0; l < p.nm; ++l) {
-            const Member &mb = p.m[l];
-            const int last = mb.t1_start + mb.tiles1 - 1;
-            const int padw = mb.ldi - mb.rank;
-            if (last >= t1b && last < t1e && padw > 0)
-                for (int i = tid; i < 16 * padw; i += kThreads) {
-                    const int col = i / padw;
-                    mb.tb[(size_t)col * mb.ldi + mb.rank + (i - col * padw)] = __float2bfloat16_rn(0.f);
-                }
-        }
+        stage1_finish<T>(p, red, t1b, t1e, KS1);
     }
 
     if (p.mode == kFused) {
@@ -484,89 +617,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     // ------------------------------------------------------------------ stage 2
     if (has2) {
         if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
-        const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles: (hi, lo) of 4 batch rows each
-        const int ntiles = t2e - t2b;
-        const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
-        // B column g of n-tile q is the hi (g even) or lo (g odd) part of batch row 4q + g/2,
-        // stored ready-made by stage 1 as bf16 pairs along k
-        const int b0 = g >> 1, b1 = 4 + (g >> 1);
-        const bool v0 = b0 < p.batch, v1 = nt == 2 && b1 < p.batch;
-        constexpr int kChunkKb = 4;  // K blocks whose B fragments are fetched together
-        for (int item = warp; item < items; item += kWarps) {
-            const int lt = item / KS, ks = item - lt * KS;
-            const int tile = t2b + lt;
-            const int l = member_of2(p, tile);
-            const Member &mb = p.m[l];
-            const int kbeg = (mb.kb2 * ks) / KS, kend = (mb.kb2 * (ks + 1)) / KS;
-            // this tile's rows in the smem U region: after the earlier members' segments
-            uint32_t uoff = 0;
-            for (int q = 0; q < l; ++q) {
-                int a, b;
-                seg_tiles(p.m[q], t2b, t2e, a, b);
-                if (a < b) uoff = ((uoff + (uint32_t)(16 * (b - a)) * (uint32_t)p.m[q].wus) + 3u) & ~3u;
-            }
-            int a0, b0s;
-            seg_tiles(mb, t2b, t2e, a0, b0s);
-            const int row0 = 16 * (tile - mb.t2_start);
-            const bool vA = ok && (row0 + g < mb.out_f), vB = ok && (row0 + g + 8 < mb.out_f);
-            const uint32_t *rowA = uch + uoff + (size_t)(16 * (tile - a0) + g) * mb.wus;
-            const uint32_t *rowB = rowA + (size_t)8 * mb.wus;
-            const __nv_bfloat16 *trow0 = mb.tb + (size_t)g * mb.ldi;
-            const __nv_bfloat16 *trow1 = mb.tb + (size_t)(8 + g) * mb.ldi;
-            float acc0[4][4] = {}, acc1[4][4] = {};
-            for (int kb0 = kbeg; kb0 < kend; kb0 += kChunkKb) {
-                uint32_t bp0[kChunkKb][8], bp1[kChunkKb][8];
-#pragma unroll
-                for (int q = 0; q < kChunkKb; ++q) {
-                    const int kc = 64 * (kb0 + q) + 16 * t;
-                    const bool in = kb0 + q < kend;
-                    load_t_pairs(trow0 + kc, in && v0, bp0[q]);
-                    load_t_pairs(trow1 + kc, in && v1, bp1[q]);
-                }
-#pragma unroll
-                for (int q = 0; q < kChunkKb; ++q) {
-                    const int kb = kb0 + q;
-                    if (kb >= kend) break;
-                    const int wi = 2 * kb + (t >> 1);
-                    const uint32_t wA = (vA && wi < mb.wu) ? rowA[wi] << sh0 : 0u;
-                    const uint32_t wB = (vB && wi < mb.wu) ? rowB[wi] << sh0 : 0u;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t a[4];
-                        sign_frag(wA, wB, j, a);
-                        mma_bf16_16816(acc0[j], a[0], a[1], a[2], a[3], bp0[q][2 * j], bp0[q][2 * j + 1]);
-                        if (nt == 2) mma_bf16_16816(acc1[j], a[0], a[1], a[2], a[3], bp1[q][2 * j], bp1[q][2 * j + 1]);
-                    }
-                }
-            }
-            float s0[4], s1v[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                s0[i] = (acc0[0][i] + acc0[1][i]) + (acc0[2][i] + acc0[3][i]);
-                s1v[i] = (acc1[0][i] + acc1[1][i]) + (acc1[2][i] + acc1[3][i]);
-            }
-            store_partial(red + item * 256, s0, g, t);
-            store_partial(red + item * 256 + 128, s1v, g, t);
-        }
+        const int KS2 = stage2_items<T>(p, uch, red, t2b, t2e, ok);
         __syncthreads();
-        for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
-            const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
-            const int b = rem >> 4, row = rem & 15;
-            const int half = (b >> 2) * 128, col = 2 * (b & 3);
-            float s = 0.f;
-            for (int ks = 0; ks < KS; ++ks) {
-                const float *r = red + (lt * KS + ks) * 256 + half + row * 8 + col;
-                s += r[0] + r[1];
-            }
-            const int tile = t2b + lt;
-            const int l = member_of2(p, tile);
-            const Member &mb = p.m[l];
-            const int m = 16 * (tile - mb.t2_start) + row;
-            if (m < mb.out_f) {
-                const float v = s * E::to_f(s1s[16 * lt + row]);
-                static_cast<T *>(mb.y)[(size_t)b * mb.out_f + m] = E::out(v);
-            }
-        }
+        stage2_finish<T>(p, red, s1s, t2b, t2e, KS2, nullptr);
     }
 }
 
@@ -802,10 +855,462 @@ static int group_impl(int dtype, const void *x, int64_t batch, int64_t in_featur
     return NQ_OK;
 }
 
+// ------------------------------------------------------------------ GEMV chain
+// Up to kMaxPhases grouped GEMVs in one cooperative launch.  Every weight byte of phase k
+// (V rows, s2, U rows, s1 of this CTA's tiles) is put in flight one phase ahead: phases 0
+// and 1 at kernel start, phase k+1 right after the grid barrier that opens phase k.  Two
+// shared-memory regions alternate (phase k uses region k & 1), each with its own pair of
+// mbarriers (V side, U side).  Within a phase: x' is formed from global memory (L2) and folded
+// with each member's s2 into the bf16 (hi, lo) B operand, stage 1 runs, a grid barrier, stage 2
+// with the optional residual add, then a grid barrier before the next phase reads the output.
+constexpr int kMaxPhases = NQ_CHAIN_MAX_PHASES;
+constexpr int kNormMaxChunks = 4;  // RMSNorm rows up to kNormMaxChunks * 8 * kThreads values
+
+struct ChainPhase {
+    Params g;           // the phase's grouped GEMV (fold mode, offsets into this phase's region)
+    const void *x2;     // SiLU-mul: up
+    const void *nw;     // RMSNorm weight
+    const void *res;    // residual added to the output, or null
+    float eps;
+    int xmode;
+};
+
+struct ChainParams {
+    ChainPhase ph[kMaxPhases];
+    int nph;
+};
+
+// Issue phase p's weight copies for this CTA: V rows and s2 rows on bv[0], U rows and s1
+// on bv[1].  Each barrier gets exactly one arrival per phase (zero bytes when the CTA has
+// no tile in that stage), so a barrier's k-th completion always belongs to its k-th phase.
+template <typename T>
+__device__ __forceinline__ void chain_issue(const Params &p, uint8_t *smem, uint64_t *bv) {
+    const int tid = threadIdx.x;
+    int t1b, t1e, t2b, t2e;
+    tile_range(p.tiles1, blockIdx.x, gridDim.x, t1b, t1e);
+    tile_range(p.tiles2, blockIdx.x, gridDim.x, t2b, t2e);
+    const bool has1 = t1e > t1b, has2 = t2e > t2b;
+    const int in_pad = p.kb1 * 64;
+    T *s2s = reinterpret_cast<T *>(smem + p.off_s2);
+    uint32_t *vch = reinterpret_cast<uint32_t *>(smem + p.off_v);
+    uint32_t *uch = reinterpret_cast<uint32_t *>(smem + p.off_u);
+    T *s1s = reinterpret_cast<T *>(smem + p.off_s1);
+    if (tid == 0) {
+        uint32_t bytes0 = 0;
+        if (has1) {
+            for (int l = 0; l < p.nm; ++l) {
+                const Member &mb = p.m[l];
+                const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
+                if (a < b)
+                    bytes0 += slab_bulk_bytes(16 * (a - mb.t1_start), min(16 * (b - mb.t1_start), mb.rank), p.wv,
+                                              p.v_rows);
+            }
+            bytes0 += (uint32_t)p.in_f * 2u * (uint32_t)p.nm;
+        }
+        mbar_arrive_expect_tx(&bv[0], bytes0);
+        if (has1)
+            for (int l = 0; l < p.nm; ++l)
+                bulk_g2s_pieces(s2s + (size_t)l * in_pad, p.m[l].s2, (uint32_t)p.in_f * 2u, &bv[0]);
+    }
+    if (tid == 32) {
+        uint32_t bytes1 = 0;
+        if (has2)
+            for (int l = 0; l < p.nm; ++l) {
+                const Member &mb = p.m[l];
+                int a, b;
+                seg_tiles(mb, t2b, t2e, a, b);
+                if (a >= b) continue;
+                const int r0 = 16 * (a - mb.t2_start), r1 = min(16 * (b - mb.t2_start), mb.out_f);
+                bytes1 += slab_bulk_bytes(r0, r1, mb.wu, mb.u_rows);
+                const T *s1src = static_cast<const T *>(mb.s1) + r0;
+                if ((reinterpret_cast<uintptr_t>(s1src) & 15) == 0) bytes1 += ((uint32_t)(r1 - r0) * 2u) & ~15u;
+            }
+        mbar_arrive_expect_tx(&bv[1], bytes1);
+    }
+    __syncwarp();
+    if (has1) {
+        for (int l = 0; l < p.nm; ++l) {
+            const Member &mb = p.m[l];
+            const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
+            if (a < b)
+                copy_slab(vch + (size_t)16 * (a - t1b) * p.wvs, mb.vbits, 16 * (a - mb.t1_start),
+                          min(16 * (b - mb.t1_start), mb.rank), p.wv, p.wvs, p.v_rows, &bv[0], 0);
+        }
+        for (int l = 0; l < p.nm; ++l) zero_tail<T>(s2s + (size_t)l * in_pad, p.in_f, in_pad);
+    }
+    if (has2) {
+        uint32_t uoff = 0;  // words; same segment layout stage2_items assumes
+        for (int l = 0; l < p.nm; ++l) {
+            const Member &mb = p.m[l];
+            int a, b;
+            seg_tiles(mb, t2b, t2e, a, b);
+            if (a >= b) continue;
+            const int r0 = 16 * (a - mb.t2_start), r1 = min(16 * (b - mb.t2_start), mb.out_f);
+            copy_slab(uch + uoff, mb.ubits, r0, r1, mb.wu, mb.wus, mb.u_rows, &bv[1], 1);
+            uoff += (uint32_t)(16 * (b - a)) * (uint32_t)mb.wus;
+            uoff = (uoff + 3u) & ~3u;
+            const T *s1src = static_cast<const T *>(mb.s1) + r0;
+            T *s1dst = s1s + 16 * (a - t2b);
+            const uint32_t s1_bulk =
+                (reinterpret_cast<uintptr_t>(s1src) & 15) == 0 ? ((uint32_t)(r1 - r0) * 2u) & ~15u : 0u;
+            if (tid == 32 && s1_bulk) bulk_g2s(s1dst, s1src, s1_bulk, &bv[1]);
+            for (int i = (int)(s1_bulk / 2) + tid; i < r1 - r0; i += kThreads) s1dst[i] = s1src[i];
+        }
+    }
+}
+
+__device__ __forceinline__ float block_sum_512(float v, float *sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();  // sh may still be read by a previous call
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) s += sh[i];
+    return s;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
+    const T *e = reinterpret_cast<const T *>(&v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = Elem<T>::to_f(e[j]);
+}
+
+// xs2[l][2b (+1)][k] = bf16 hi (lo) of x'[b][k] * s2_l[k], x' formed per ph.xmode from global
+// memory written by earlier phases (read through L2: __ldcg).
+template <typename T>
+__device__ __forceinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, float *sred) {
+    using E = Elem<T>;
+    const Params &p = ph.g;
+    const int tid = threadIdx.x;
+    const int in_pad = p.kb1 * 64, chunks = in_pad / 8, nxc = 2 * p.batch;
+    const int nfull = p.in_f / 8;  // in_f % 8 == 0
+    const T *s2s = reinterpret_cast<const T *>(smem + p.off_s2);
+    __nv_bfloat16 *xs2 = reinterpret_cast<__nv_bfloat16 *>(smem + p.off_xs2);
+    auto emit = [&](int b, int ch, const float (&xf)[8]) {
+        for (int l = 0; l < p.nm; ++l) {
+            float sf[8];
+            unpack8<T>(*reinterpret_cast<const uint4 *>(s2s + (size_t)l * in_pad + 8 * ch), sf);
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) split_pair(xf[2 * j] * sf[2 * j], xf[2 * j + 1] * sf[2 * j + 1], hi[j], lo[j]);
+            __nv_bfloat16 *dst = xs2 + ((size_t)l * nxc + 2 * b) * in_pad + 8 * ch;
+            *reinterpret_cast<uint4 *>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4 *>(dst + in_pad) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+    };
+    for (int b = 0; b < p.batch; ++b) {
+        const uint4 *xr = reinterpret_cast<const uint4 *>(static_cast<const T *>(p.x) + (size_t)b * p.in_f);
+        if (ph.xmode == kChainNorm) {
+            uint4 hv[kNormMaxChunks];
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < kNormMaxChunks; ++j) {
+                const int ch = tid + j * kThreads;
+                if (ch < nfull) {
+                    hv[j] = __ldcg(xr + ch);
+                    float f[8];
+                    unpack8<T>(hv[j], f);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+                }
+            }
+            const float inv = rsqrtf(block_sum_512(ss, sred) / (float)p.in_f + ph.eps);
+            const uint4 *wr = reinterpret_cast<const uint4 *>(ph.nw);
+#pragma unroll
+            for (int j = 0; j < kNormMaxChunks; ++j) {
+                const int ch = tid + j * kThreads;
+                if (ch >= chunks) continue;
+                float xf[8];
+                if (ch < nfull) {
+                    float h[8], w[8];
+                    unpack8<T>(hv[j], h);
+                    unpack8<T>(__ldg(wr + ch), w);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) xf[e] = E::to_f(E::rn(w[e] * E::to_f(E::rn(h[e] * inv))));
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) xf[e] = 0.f;
+                }
+                emit(b, ch, xf);
+            }
+        } else {
+            const uint4 *ur = ph.xmode == kChainSiluMul
+                                  ? reinterpret_cast<const uint4 *>(static_cast<const T *>(ph.x2) + (size_t)b * p.in_f)
+                                  : nullptr;
+            for (int ch = tid; ch < chunks; ch += kThreads) {
+                float xf[8];
+                if (ch >= nfull) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) xf[e] = 0.f;
+                } else if (ur) {
+                    float gt[8], up[8];
+                    unpack8<T>(__ldcg(xr + ch), gt);
+                    unpack8<T>(__ldcg(ur + ch), up);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float sg = E::to_f(E::rn(gt[e] / (1.f + expf(-gt[e]))));
+                        xf[e] = E::to_f(E::rn(sg * up[e]));
+                    }
+                } else {
+                    unpack8<T>(__ldcg(xr + ch), xf);
+                }
+                emit(b, ch, xf);
+            }
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constant__ ChainParams cp) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float sred[kWarps];
+    const int tid = threadIdx.x;
+    const unsigned G = gridDim.x;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // [region][V side, U side]
+    Ctrl *ctrl = cp.ph[0].g.ctrl;
+    if (tid == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    chain_issue<T>(cp.ph[0].g, smem, &bars[0]);
+    if (cp.nph > 1) chain_issue<T>(cp.ph[1].g, smem, &bars[2]);
+    bool ok = true;
+    for (int k = 0; k < cp.nph; ++k) {
+        const ChainPhase &ph = cp.ph[k];
+        const Params &p = ph.g;
+        uint64_t *bv = &bars[2 * (k & 1)];
+        const uint32_t par = (uint32_t)(k >> 1) & 1u;
+        if (k > 0) {
+            if (!grid_barrier(ctrl, G)) ok = false;  // phase k-1's outputs are visible
+            if (k + 1 < cp.nph) {                    // region (k+1)&1 is free: phase k-1 is done
+                fence_proxy_async_smem();
+                chain_issue<T>(cp.ph[k + 1].g, smem, &bars[2 * ((k + 1) & 1)]);
+            }
+        }
+        int t1b, t1e, t2b, t2e;
+        tile_range(p.tiles1, blockIdx.x, G, t1b, t1e);
+        tile_range(p.tiles2, blockIdx.x, G, t2b, t2e);
+        float *red = reinterpret_cast<float *>(smem + p.off_red);
+        if (t1e > t1b) {
+            if (!mbar_wait(&bv[0], par, &ctrl->status)) ok = false;
+            chain_fold<T>(ph, smem, sred);
+            __syncthreads();
+            const __nv_bfloat16 *xs2 = reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2);
+            const int KS1 = stage1_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_v),
+                                            reinterpret_cast<const T *>(smem + p.off_s2),
+                                            reinterpret_cast<const T *>(xs2), xs2, red, t1b, t1e, ok);
+            __syncthreads();
+            stage1_finish<T>(p, red, t1b, t1e, KS1);
+        }
+        if (!grid_barrier(ctrl, G)) ok = false;  // t of every member is complete
+        if (t2e > t2b) {
+            if (!mbar_wait(&bv[1], par, &ctrl->status)) ok = false;
+            const int KS2 = stage2_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_u), red, t2b, t2e, ok);
+            __syncthreads();
+            stage2_finish<T>(p, red, reinterpret_cast<const T *>(smem + p.off_s1), t2b, t2e, KS2, ph.res);
+        }
+    }
+}
+
+// Host: validate the phases, build their Params, lay out shared memory.  `launch` = false
+// plans only (the workspace query).
+static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *phases, void *workspace,
+                      size_t workspace_bytes, void *stream, bool launch, size_t *ws_need) {
+    if (dtype != NQ_DTYPE_F16 && dtype != NQ_DTYPE_BF16)
+        return fail(NQ_ERR_UNSUPPORTED, "dtype must be NQ_DTYPE_F16 or NQ_DTYPE_BF16 (got %d)", dtype);
+    if (n < 1 || n > kMaxPhases) return fail(NQ_ERR_INVALID_ARGUMENT, "a chain holds 1..%d phases (got %d)", kMaxPhases, n);
+    if (!phases) return fail(NQ_ERR_INVALID_ARGUMENT, "null phase array");
+    if (batch < 1 || batch > kFoldMaxBatch)
+        return fail(NQ_ERR_UNSUPPORTED, "a chain runs batch 1..%d (got %lld)", kFoldMaxBatch, (long long)batch);
+    // Planning needs no GPU: without one it assumes a B200 (148 SMs, 227 KiB of shared memory
+    // per block), so the workspace query also works on a build machine.
+    int dev = 0;
+    DeviceInfo di;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) {
+        di = device_info(dev);
+    } else {
+        if (launch) return cuda_fail(e, "cudaGetDevice");
+        cudaGetLastError();
+    }
+    if (launch && di.cc_major != 10)
+        return fail(NQ_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", dev, di.cc_major, di.cc_minor);
+    const int G = di.sms > 0 ? di.sms : 148;
+    const int smem_optin = di.max_smem_optin > 0 ? di.max_smem_optin : 232448;
+    ChainParams cp{};
+    cp.nph = n;
+    size_t need = sizeof(Ctrl);
+    int max_items = kWarps;
+    size_t xs2_bytes = 0, region[2] = {0, 0};
+    const uintptr_t ws_base = reinterpret_cast<uintptr_t>(workspace);
+    for (int k = 0; k < n; ++k) {
+        const nq_chain_phase &P = phases[k];
+        ChainPhase &ph = cp.ph[k];
+        Params &p = ph.g;
+        if (P.n_layers < 1 || P.n_layers > kMaxGroup)
+            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: 1..%d layers (got %d)", k, kMaxGroup, P.n_layers);
+        if (P.x_mode != kChainPlain && P.x_mode != kChainNorm && P.x_mode != kChainSiluMul)
+            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: unknown x_mode %d", k, P.x_mode);
+        if (P.in_features <= 0 || P.in_features % 8 || P.in_features > (1 << 20))
+            return fail(NQ_ERR_UNSUPPORTED, "phase %d: in_features must be a positive multiple of 8 (got %lld)", k,
+                        (long long)P.in_features);
+        if (!P.x || (P.x_mode == kChainSiluMul && !P.x2) || (P.x_mode == kChainNorm && !P.norm_weight))
+            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: missing input tensor", k);
+        if ((reinterpret_cast<uintptr_t>(P.x) | reinterpret_cast<uintptr_t>(P.x2) |
+             reinterpret_cast<uintptr_t>(P.norm_weight)) & 15)
+            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: x, x2 and norm_weight must be 16-byte aligned", k);
+        if (P.x_mode == kChainNorm && P.in_features > (int64_t)kNormMaxChunks * 8 * kThreads)
+            return fail(NQ_ERR_UNSUPPORTED, "phase %d: RMSNorm rows are limited to %d values", k,
+                        kNormMaxChunks * 8 * kThreads);
+        if (P.residual && P.n_layers != 1)
+            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: a residual needs a single-layer phase", k);
+        if (reinterpret_cast<uintptr_t>(P.residual) & 1)
+            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: residual must be 2-byte aligned", k);
+        p.ctrl = static_cast<Ctrl *>(workspace);
+        p.x = P.x;
+        p.batch = (int)batch;
+        p.in_f = (int)P.in_features;
+        p.wv = (int)((P.in_features + 31) / 32);
+        p.kb1 = (p.wv + 1) / 2;
+        p.nm = P.n_layers;
+        p.mode = kFused;
+        p.fold = 1;
+        p.x_in_smem = 0;
+        ph.x2 = P.x2;
+        ph.nw = P.norm_weight;
+        ph.res = P.residual;
+        ph.eps = P.eps;
+        ph.xmode = P.x_mode;
+        int t1 = 0, t2 = 0;
+        for (int l = 0; l < P.n_layers; ++l) {
+            const nq_gemv_layer &L = P.layers[l];
+            if (!L.scale_pre || !L.v_bits || !L.u_bits || !L.scale_post || !L.y)
+                return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d layer %d: null tensor pointer", k, l);
+            if (L.rank <= 0 || L.out_features <= 0 || L.rank > (1 << 20) || L.out_features > (1 << 24))
+                return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d layer %d: bad sizes (rank=%lld out=%lld)", k, l,
+                            (long long)L.rank, (long long)L.out_features);
+            if (reinterpret_cast<uintptr_t>(L.scale_pre) & 15)
+                return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d layer %d: scale_pre must be 16-byte aligned", k, l);
+            if ((reinterpret_cast<uintptr_t>(L.scale_post) | reinterpret_cast<uintptr_t>(L.y) |
+                 reinterpret_cast<uintptr_t>(L.scale_mid)) & 1)
+                return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d layer %d: 16-bit tensors must be 2-byte aligned", k, l);
+            if ((reinterpret_cast<uintptr_t>(L.v_bits) | reinterpret_cast<uintptr_t>(L.u_bits)) & 15)
+                return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d layer %d: sign planes must be 16-byte aligned", k, l);
+            Member &mb = p.m[l];
+            mb.s2 = L.scale_pre;
+            mb.vbits = reinterpret_cast<const uint32_t *>(L.v_bits);
+            mb.smid = L.scale_mid;
+            mb.ubits = reinterpret_cast<const uint32_t *>(L.u_bits);
+            mb.s1 = L.scale_post;
+            mb.y = L.y;
+            mb.rank = (int)L.rank;
+            mb.out_f = (int)L.out_features;
+            mb.wu = (int)((L.rank + 31) / 32);
+            mb.kb2 = (mb.wu + 1) / 2;
+            mb.ldi = mb.kb2 * 64;
+            mb.tiles1 = (int)((L.rank + 15) / 16);
+            mb.tiles2 = (int)((L.out_features + 15) / 16);
+            mb.t1_start = t1;
+            mb.t2_start = t2;
+            t1 += mb.tiles1;
+            t2 += mb.tiles2;
+            mb.tb = reinterpret_cast<__nv_bfloat16 *>(ws_base + need);  // tb regions follow the control block
+            need += tb_bytes(L.rank);
+            mb.u_rows = (mb.wu % 4) == 0;
+            mb.wus = mb.u_rows ? padded_stride(mb.wu) : mb.wu;
+        }
+        if (t1 > 65536 || t2 > 65536) return fail(NQ_ERR_UNSUPPORTED, "phase %d: layer group too large", k);
+        p.tiles1 = t1;
+        p.tiles2 = t2;
+        p.v_rows = (p.wv % 4) == 0;
+        p.wvs = p.v_rows ? padded_stride(p.wv) : p.wv;
+        const int tpc1 = (t1 + G - 1) / G, tpc2 = (t2 + G - 1) / G;
+        max_items = std::max(max_items, std::max(tpc1, tpc2));
+        const size_t in_pad = (size_t)p.kb1 * 64;
+        xs2_bytes = std::max(xs2_bytes, (size_t)p.nm * 2 * (size_t)batch * in_pad * 2);
+        int max_wus = 0;
+        for (int l = 0; l < p.nm; ++l) max_wus = std::max(max_wus, p.m[l].wus);
+        // region-relative offsets; made absolute below
+        size_t off = 0;
+        p.off_s2 = (uint32_t)off;
+        off = align128(off + (size_t)p.nm * in_pad * 2);
+        p.off_v = (uint32_t)off;
+        off = align128(off + (size_t)16 * tpc1 * p.wvs * 4 + 16);
+        p.off_u = (uint32_t)off;
+        off = align128(off + ((size_t)16 * tpc2 * max_wus + 4 * (size_t)p.nm) * 4 + 16);
+        p.off_s1 = (uint32_t)off;
+        off = align128(off + (size_t)16 * tpc2 * 2 + 16);
+        region[k & 1] = std::max(region[k & 1], off);
+    }
+    const size_t off_red = 128;  // four mbarriers first
+    const size_t off_xs2 = align128(off_red + (size_t)max_items * 256 * sizeof(float));
+    const size_t off_r0 = align128(off_xs2 + xs2_bytes);
+    const size_t off_r1 = align128(off_r0 + region[0]);
+    const size_t smem = off_r1 + region[1];
+    const size_t cap = (size_t)smem_optin - kStaticSmemReserve;
+    if (ws_need) *ws_need = need;
+    if (smem > cap)
+        return fail(NQ_ERR_UNSUPPORTED, "chain needs %zu bytes of shared memory per SM (limit %zu)", smem, cap);
+    if (!launch) return NQ_OK;
+    if (!di.coop) return fail(NQ_ERR_UNSUPPORTED, "device %d lacks cooperative launch", dev);
+    if (!workspace || workspace_bytes < need)
+        return fail(NQ_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+    for (int k = 0; k < n; ++k) {
+        Params &p = cp.ph[k].g;
+        const size_t base = (k & 1) ? off_r1 : off_r0;
+        p.off_red = (uint32_t)off_red;
+        p.off_xs2 = (uint32_t)off_xs2;
+        p.off_x = (uint32_t)off_xs2;
+        p.off_s2 += (uint32_t)base;
+        p.off_v += (uint32_t)base;
+        p.off_u += (uint32_t)base;
+        p.off_s1 += (uint32_t)base;
+    }
+    static bool attr_set[2][64] = {};
+    const int ti = dtype == NQ_DTYPE_F16 ? 0 : 1;
+    if (dev >= 0 && dev < 64 && !attr_set[ti][dev]) {
+        e = ti == 0 ? cudaFuncSetAttribute(chain_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cap)
+                    : cudaFuncSetAttribute(chain_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)cap);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain)");
+        attr_set[ti][dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)G);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = ti == 0 ? cudaLaunchKernelEx(&cfg, chain_kernel<__half>, cp) : cudaLaunchKernelEx(&cfg, chain_kernel<__nv_bfloat16>, cp);
+    return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv chain launch");
+}
+
 }  // namespace gemv
 }  // namespace nq
 
 extern "C" {
+
+size_t nq_gemv_chain_workspace_bytes(int dtype, int64_t batch, int n_phases, const nq_chain_phase *phases) {
+    size_t need = 0;
+    const int st = nq::gemv::chain_impl(dtype, batch, n_phases, phases, nullptr, 0, nullptr, false, &need);
+    return st == NQ_OK ? need : 0;
+}
+
+int nq_gemv_chain(int dtype, int64_t batch, int n_phases, const nq_chain_phase *phases, void *workspace,
+                  size_t workspace_bytes, void *stream) {
+    return nq::gemv::chain_impl(dtype, batch, n_phases, phases, workspace, workspace_bytes, stream, true, nullptr);
+}
 
 size_t nq_gemv_workspace_bytes(int64_t batch, int64_t rank) {
     (void)batch;  // batches above 8 reuse the same 8-row operand buffer, launch after launch

@@ -32,6 +32,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
+from . import chain as nqchain
 
 PROJ = ("q", "k", "v", "o", "gate", "up", "down")
 
@@ -162,7 +163,8 @@ class Decoder:
     """One TP shard of the decoder plus its KV cache and a graph-capturable decode step."""
 
     def __init__(self, cfg: DecoderConfig, max_seq: int, batch: int = 1, tp_rank: int = 0, tp: int = 1,
-                 group=None, seed: int = 0, dtype=torch.float16, device=None, with_mid: bool = False):
+                 group=None, seed: int = 0, dtype=torch.float16, device=None, with_mid: bool = False,
+                 chain: bool = True):
         _lib.load_torch_ops()
         assert cfg.heads % tp == 0 and cfg.kv_heads % tp == 0 and cfg.ffn % tp == 0
         self.cfg, self.max_seq, self.batch, self.tp, self.tp_rank, self.group = cfg, max_seq, batch, tp, tp_rank, group
@@ -190,6 +192,17 @@ class Decoder:
         self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.seq_len = torch.ones(batch, dtype=torch.int32, device=dev)
         self.next_tokens = torch.zeros(batch, dtype=torch.long, device=dev)
+        # Decode through GEMV chains (one launch per block besides attention) when the block's
+        # chain can run here: one GPU (the chain has no all-reduce), batch <= 2, and the weight
+        # slabs of consecutive phases fit shared memory.
+        self.chain_ws = None
+        if chain and tp == 1:
+            h = torch.empty(batch, cfg.hidden, device=dev, dtype=dtype)
+            a = torch.empty(batch, self.hq * cfg.head_dim, device=dev, dtype=dtype)
+            phases, _ = self._block_phases(0, a, h, alloc=False)
+            n = nqchain.workspace_bytes(phases, batch)
+            if n:
+                self.chain_ws = torch.zeros(n, dtype=torch.uint8, device=dev)
 
     # ------------------------------------------------------------------ pieces
     def _all_reduce(self, t: torch.Tensor):
@@ -241,9 +254,48 @@ class Decoder:
         return nxt
 
     # ------------------------------------------------------------------ decode
+    def _qkv_phase(self, li: int, h: torch.Tensor, alloc: bool = True):
+        """Block li's q/k/v from RMSNorm(h) (the block's input norm)."""
+        lay, B, dev, dt = self.layers[li], self.batch, self.device, self.dtype
+        outs = [torch.empty(B, m.s1.numel(), device=dev, dtype=dt) for m in lay["qkv"].members] if alloc else None
+        return nqchain.Phase(lay["qkv"].members, h, nqchain.RMSNORM, norm_weight=lay["in_norm"], eps=self.cfg.rms_eps,
+                             out=outs)
+
+    def _block_phases(self, li: int, a: torch.Tensor, h: torch.Tensor, alloc: bool = True):
+        """Chain of block li after attention: o (+ residual into h), gate/up from RMSNorm(h),
+        down from silu(gate) * up (+ residual into h), then block li+1's q/k/v."""
+        cfg, lay, B = self.cfg, self.layers[li], self.batch
+        gate = torch.empty(B, cfg.ffn // self.tp, device=self.device, dtype=self.dtype)
+        up = torch.empty_like(gate)
+        phases = [nqchain.Phase([lay["o"]], a, residual=h, out=[h]),
+                  nqchain.Phase([lay["gate"], lay["up"]], h, nqchain.RMSNORM, norm_weight=lay["post_norm"],
+                                eps=cfg.rms_eps, out=[gate, up]),
+                  nqchain.Phase([lay["down"]], gate, nqchain.SILU_MUL, x2=up, residual=h, out=[h])]
+        if li + 1 < cfg.layers:
+            phases.append(self._qkv_phase(li + 1, h, alloc))
+        return phases, (gate, up)
+
+    @torch.no_grad()
+    def _step_logits_chain(self) -> torch.Tensor:
+        cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
+        h = F.embedding(self.tokens, self.embed)  # the residual stream; the chains update it in place
+        q, k, v = nqchain.run([self._qkv_phase(0, h)], self.chain_ws)[0]
+        for li in range(cfg.layers):
+            a = torch.ops.nq_b200.decode_attention_rope(q.view(B, self.hq, D), k.view(B, self.hkv, D),
+                                                        v.view(B, self.hkv, D), self.pos, self.k_cache[li],
+                                                        self.v_cache[li], cfg.rope_theta)
+            phases, _ = self._block_phases(li, a.view(B, self.hq * D), h)
+            outs = nqchain.run(phases, self.chain_ws)
+            if li + 1 < cfg.layers:
+                q, k, v = outs[3]
+        x, _ = torch.ops.nq_b200.rmsnorm(h, None, self.final_norm, cfg.rms_eps)
+        return x @ self.lm_head.t()
+
     @torch.no_grad()
     def step_logits(self) -> torch.Tensor:
         """Logits for the current tokens at the current positions (writes the caches)."""
+        if self.chain_ws is not None:
+            return self._step_logits_chain()
         cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
         h = F.embedding(self.tokens, self.embed)
         residual = None
