@@ -149,8 +149,11 @@ NQ_API int nq_gemv_static(int dtype, const void *x, int64_t batch, int64_t in_fe
  *   NQ_CHAIN_X_PLAIN     x' = x
  *   NQ_CHAIN_X_RMSNORM   x' = dtype(norm_weight * dtype(x * rsqrt(mean(x^2) + eps)))
  *   NQ_CHAIN_X_SILU_MUL  x' = dtype(dtype(silu(x)) * x2)
+ *   NQ_CHAIN_X_MUL       x' = dtype(x * x2)
  * and with `residual` set (single-layer phases) the output is dtype(dtype(y) + residual),
- * stored to y, which may be the residual buffer itself.  Phases run in order; a phase may
+ * stored to y, which may be the residual buffer itself; bit l of `act` stores layer l's
+ * output as dtype(silu(dtype(y))) instead (a gate whose SiLU is then applied once per value,
+ * not once per consumer: SILU_MUL on (gate, up) equals MUL on (act gate, up), bit for bit).  Phases run in order; a phase may
  * read what earlier phases wrote.  Limits: batch <= 2; in_features % 8 == 0; x, x2,
  * norm_weight and every scale_pre 16-byte aligned; RMSNorm rows <= 16384 values; and the
  * weight slabs of two consecutive phases must fit one SM's shared memory.
@@ -159,15 +162,16 @@ NQ_API int nq_gemv_static(int dtype, const void *x, int64_t batch, int64_t in_fe
  * at a time, as for nq_gemv.
  * ------------------------------------------------------------------------------- */
 #define NQ_CHAIN_MAX_PHASES 4
-enum { NQ_CHAIN_X_PLAIN = 0, NQ_CHAIN_X_RMSNORM = 1, NQ_CHAIN_X_SILU_MUL = 2 };
+enum { NQ_CHAIN_X_PLAIN = 0, NQ_CHAIN_X_RMSNORM = 1, NQ_CHAIN_X_SILU_MUL = 2, NQ_CHAIN_X_MUL = 3 };
 typedef struct {
     int n_layers;              /* 1..3 layers reading the same x' */
     int x_mode;                /* NQ_CHAIN_X_* */
+    int act;                   /* bit l: layer l's output goes through SiLU */
+    float eps;                 /* NQ_CHAIN_X_RMSNORM */
     int64_t in_features;
     const void *x;             /* [batch, in]: the input, the stream to normalise, or the gate */
-    const void *x2;            /* NQ_CHAIN_X_SILU_MUL: up [batch, in] */
+    const void *x2;            /* NQ_CHAIN_X_SILU_MUL / NQ_CHAIN_X_MUL: up [batch, in] */
     const void *norm_weight;   /* NQ_CHAIN_X_RMSNORM: [in] */
-    float eps;                 /* NQ_CHAIN_X_RMSNORM */
     const void *residual;      /* NULL, or [batch, out] added to the output (n_layers == 1) */
     nq_gemv_layer layers[3];
 } nq_chain_phase;

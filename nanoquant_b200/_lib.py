@@ -38,9 +38,9 @@ class GemvLayer(ctypes.Structure):
 
 class ChainPhase(ctypes.Structure):
     """nq_chain_phase of include/nq_b200.h."""
-    _fields_ = [("n_layers", ctypes.c_int), ("x_mode", ctypes.c_int), ("in_features", ctypes.c_int64),
-                ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p), ("norm_weight", ctypes.c_void_p),
-                ("eps", ctypes.c_float), ("residual", ctypes.c_void_p), ("layers", GemvLayer * 3)]
+    _fields_ = [("n_layers", ctypes.c_int), ("x_mode", ctypes.c_int), ("act", ctypes.c_int), ("eps", ctypes.c_float),
+                ("in_features", ctypes.c_int64), ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p),
+                ("norm_weight", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("layers", GemvLayer * 3)]
 
 
 _lock = threading.Lock()

@@ -1,8 +1,9 @@
 """GEMV chains: several grouped decode GEMVs in one cooperative launch (``nq_gemv_chain``).
 
 A phase is a group of 1-3 NanoQuant layers that read the same input x', formed on the fly from
-what earlier phases wrote: x' = x (PLAIN), RMSNorm(x) * weight (RMSNORM), or silu(x) * x2
-(SILU_MUL); a single-layer phase may add a residual to its output, in place.  A decoder block's
+what earlier phases wrote: x' = x (PLAIN), RMSNorm(x) * weight (RMSNORM), silu(x) * x2
+(SILU_MUL) or x * x2 (MUL); a single-layer phase may add a residual to its output, in place, and
+`act` puts chosen layers' outputs through SiLU (a SwiGLU gate, then consumed with MUL).  A decoder block's
 o-projection, MLP and the next block's q/k/v form one chain, so the block costs two launches
 (chain + attention) instead of eight.  The reference runs each of these as its own call
 (src/nanoquant/modules/linear.py:155-164 per linear, HF modules around them).
@@ -16,7 +17,7 @@ import torch
 
 from . import _lib
 
-PLAIN, RMSNORM, SILU_MUL = 0, 1, 2
+PLAIN, RMSNORM, SILU_MUL, MUL = 0, 1, 2, 3
 MAX_PHASES = 4
 _DT = {torch.float16: 0, torch.bfloat16: 1}
 
@@ -31,8 +32,9 @@ class Phase:
 
     def __init__(self, layers: Sequence, x: torch.Tensor, mode: int = PLAIN, x2: Optional[torch.Tensor] = None,
                  norm_weight: Optional[torch.Tensor] = None, eps: float = 1e-5,
-                 residual: Optional[torch.Tensor] = None, out: Optional[Sequence[torch.Tensor]] = None):
-        self.layers, self.x, self.mode, self.x2 = list(layers), x, mode, x2
+                 residual: Optional[torch.Tensor] = None, out: Optional[Sequence[torch.Tensor]] = None,
+                 act: int = 0):
+        self.layers, self.x, self.mode, self.x2, self.act = list(layers), x, mode, x2, act
         self.norm_weight, self.eps, self.residual = norm_weight, eps, residual
         self.out = list(out) if out is not None else None
 
@@ -44,6 +46,7 @@ def _struct(phases: Sequence[Phase], batch: int, alloc: bool):
         c = arr[i]
         c.n_layers = len(ph.layers)
         c.x_mode = ph.mode
+        c.act = ph.act
         c.in_features = ph.layers[0].s2.numel()
         c.x, c.x2, c.norm_weight = _ptr(ph.x), _ptr(ph.x2), _ptr(ph.norm_weight)
         c.eps = ph.eps

@@ -136,34 +136,38 @@ __device__ __forceinline__ unsigned long long atom_add_release_gpu_u64(unsigned 
     return old;
 }
 
-// Grid barrier for a cooperative launch (all CTAs co-resident).  Arrivals increment a
-// monotonic 64-bit counter; the barrier of arrival `old` completes when the counter
-// reaches the next multiple of `nblocks`, so the last arrival releases everybody with
-// its own atomic and nothing has to be reset (the counter starts at 0 with the
-// workspace and every launch adds exactly `nblocks`).  Pollers back off with nanosleep.
+__device__ __forceinline__ void red_add_release_gpu_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Grid barriers for a cooperative launch (all CTAs co-resident).  Arrivals increment a
+// monotonic 64-bit counter that starts at 0 with the workspace; every launch adds exactly
+// nblocks per barrier, so nothing is ever reset.  Thread 0 of each CTA reads the counter
+// once, before its first arrival (grid_barrier_base): all earlier launches' barriers are
+// complete and this launch's first one is not, so the count rounded down to a multiple of
+// nblocks is where this launch started.  Barrier k (1-based) then waits for base + k * nblocks;
+// arrivals are fire-and-forget reductions, so the last arrival costs one trip to L2.
 // Bounded: gives up after kWaitTimeoutNs, records NQ_ERR_DEVICE_TIMEOUT, returns false.
-__device__ __forceinline__ bool grid_barrier(Ctrl *ctrl, unsigned int nblocks) {
+__device__ __forceinline__ unsigned long long grid_barrier_base(Ctrl *ctrl, unsigned int nblocks) {
+    return (ld_acquire_gpu_u64(&ctrl->arrivals) / nblocks) * nblocks;
+}
+
+__device__ __forceinline__ bool grid_barrier(Ctrl *ctrl, unsigned long long target) {
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
         int ok = 1;
         __threadfence();
-        const unsigned long long old = atom_add_release_gpu_u64(&ctrl->arrivals, 1ull);
-        const unsigned long long target = (old / nblocks + 1ull) * nblocks;
-        if (old + 1ull < target) {
-            const uint64_t t0 = globaltimer_ns();
-            unsigned int ns = 20;
-            while (ld_acquire_gpu_u64(&ctrl->arrivals) < target) {
-                if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
-                    record_status(&ctrl->status, NQ_ERR_DEVICE_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
-                __nanosleep(ns);
-                if (ns < 160) ns += 20;
+        red_add_release_gpu_u64(&ctrl->arrivals, 1ull);
+        // plain spin (one L2 poll per round trip): the wait is short and every CTA is resident
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_gpu_u64(&ctrl->arrivals) < target) {
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+                record_status(&ctrl->status, NQ_ERR_DEVICE_TIMEOUT);
+                ok = 0;
+                break;
             }
         }
-        __threadfence();
         s_ok = ok;
     }
     __syncthreads();

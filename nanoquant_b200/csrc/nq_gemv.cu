@@ -127,14 +127,41 @@ __device__ __forceinline__ void zero_tail(T *dst, int n, int npad) {
     for (int c = n + threadIdx.x; c < npad; c += kThreads) d[c] = 0;
 }
 
-// Per-warp work item: one 16-row tile over a contiguous range of 64-column K blocks.
-// Items of a CTA are (tile, K slice) pairs with KS slices per tile, KS = max(1, warps / tiles),
-// so every warp has work whatever the tile count; partial 16x8 tiles meet in `red`.
-__device__ __forceinline__ void item_of(int item, int KS, int kb, int &lt, int &kbeg, int &kend) {
-    lt = item / KS;
-    const int ks = item - lt * KS;
-    kbeg = (kb * ks) / KS;
-    kend = (kb * (ks + 1)) / KS;
+// Work split inside a CTA: its tiles x K blocks form U = tiles * KB units (tile-major); warp w
+// takes the contiguous units [U w / W, U (w+1) / W), which cover at most S consecutive tiles
+// (S from seg_bound), and writes one partial 16x8 tile per covered tile to `red` slot
+// w * S + (tile - first tile of w).  Every warp gets the same amount of K work whatever the
+// tile count, and each tile's partials are summed in warp order, so results are deterministic.
+__host__ __device__ __forceinline__ void warp_units(int U, int w, int &u0, int &u1) {
+    u0 = (U * w) / kWarps;
+    u1 = (U * (w + 1)) / kWarps;
+}
+// Upper bound on the tiles one warp's range covers, for at most `tiles` tiles of KB units.
+__host__ __device__ __forceinline__ int seg_bound(int tiles, int KB) {
+    if (tiles <= 0 || KB <= 0) return 1;
+    const int n = (tiles * KB + kWarps - 1) / kWarps;
+    const int s = (n + KB - 1) / KB + 1;
+    return s < tiles ? s : tiles;
+}
+// The warp whose unit range holds unit x: the largest w with floor(U w / W) <= x.
+__device__ __forceinline__ int warp_of_unit(int U, int x) {
+    const int w = (kWarps * x + kWarps - 1) / U;
+    return w < kWarps - 1 ? w : kWarps - 1;
+}
+// Sum over warps of tile lt's partial at float offset `off` of each slot: the warps that cover
+// tile lt form the interval [warp of its first unit, warp of its last unit] (empty ranges
+// inside the interval stored nothing and are skipped).
+__device__ __forceinline__ float sum_partials(const float *red, int U, int KB, int S, int lt, int off, bool pair) {
+    const int x0 = lt * KB, x1 = min((lt + 1) * KB, U) - 1;
+    float s = 0.f;
+    for (int w = warp_of_unit(U, x0); w <= warp_of_unit(U, x1); ++w) {
+        int u0, u1;
+        warp_units(U, w, u0, u1);
+        if (u0 >= u1) continue;
+        const float *r = red + (w * S + (lt - u0 / KB)) * 256 + off;
+        s += pair ? r[0] + r[1] : r[0];
+    }
+    return s;
 }
 
 __device__ __forceinline__ void store_partial(float *r, const float (&acc)[4], int g, int t) {
@@ -174,7 +201,12 @@ __device__ __forceinline__ void sign_frag(uint32_t wA, uint32_t wB, int j, uint3
 }
 
 constexpr int kMaxGroup = 3;  // layers sharing one input x in a single launch (q/k/v, gate/up)
-enum ChainXMode : int { kChainPlain = NQ_CHAIN_X_PLAIN, kChainNorm = NQ_CHAIN_X_RMSNORM, kChainSiluMul = NQ_CHAIN_X_SILU_MUL };
+enum ChainXMode : int {
+    kChainPlain = NQ_CHAIN_X_PLAIN,
+    kChainNorm = NQ_CHAIN_X_RMSNORM,
+    kChainSiluMul = NQ_CHAIN_X_SILU_MUL,
+    kChainMul = NQ_CHAIN_X_MUL
+};
 
 // One NanoQuant layer of a launch group.
 struct Member {
@@ -199,6 +231,8 @@ struct Params {
     int tiles1, tiles2;        // totals over members
     int wvs, v_rows;           // V slab smem stride (words) and row-by-row copy flag (wv % 4 == 0)
     int mode, x_in_smem, fold;
+    int kbu2;                  // stage-2 K blocks per tile in the work split: the largest member's kb2
+    int seg1, seg2;            // red slots per warp (seg_bound) in stage 1 / stage 2
     uint32_t off_red, off_s2, off_x, off_xs2, off_v, off_u, off_s1;
 };
 
@@ -222,10 +256,9 @@ __device__ __forceinline__ void seg_tiles(const Member &mb, int t2b, int t2e, in
 
 // ------------------------------------------------------------------ stage bodies
 // Shared by the single-group kernel and the chain kernel.  Stage 1: this CTA's tiles
-// [t1b, t1e) as (tile, K slice) work items over the warps, partial 16x8 tiles into `red`;
-// returns the K slices per tile.
+// [t1b, t1e) split over the warps by K-block units (warp_units), partial 16x8 tiles into `red`.
 template <typename T>
-__device__ __forceinline__ int stage1_items(const Params &p, const uint32_t *vch, const T *s2s, const T *xs,
+__device__ __forceinline__ void stage1_items(const Params &p, const uint32_t *vch, const T *s2s, const T *xs,
                                             const __nv_bfloat16 *xs2, float *red, int t1b, int t1e, bool ok) {
     using E = Elem<T>;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -236,11 +269,12 @@ __device__ __forceinline__ int stage1_items(const Params &p, const uint32_t *vch
     const T *xg = static_cast<const T *>(p.x) + (size_t)g * p.in_f;
     const uint32_t *xsw = reinterpret_cast<const uint32_t *>(xs + (size_t)g * in_pad);
     const bool xrow = g < p.batch, fcol = g < nxc;
-    const int ntiles = t1e - t1b;
-    const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
-    for (int item = warp; item < items; item += kWarps) {
-        int lt, kbeg, kend;
-        item_of(item, KS, p.kb1, lt, kbeg, kend);
+    const int ntiles = t1e - t1b, KB = p.kb1, S = p.seg1;
+    int u0, u1;
+    warp_units(ntiles * KB, warp, u0, u1);
+    const int lt0 = u0 / KB;
+    for (int lt = lt0; u0 < u1 && lt * KB < u1; ++lt) {
+        const int kbeg = max(u0 - lt * KB, 0), kend = min(u1 - lt * KB, KB);
         const int tile = t1b + lt;
         const int l = member_of1(p, tile);
         const int row0 = 16 * (tile - p.m[l].t1_start), rank = p.m[l].rank;
@@ -301,30 +335,23 @@ __device__ __forceinline__ int stage1_items(const Params &p, const uint32_t *vch
         float sum[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) sum[i] = (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
-        store_partial(red + item * 256, sum, g, t);
+        store_partial(red + (warp * S + (lt - lt0)) * 256, sum, g, t);
     }
-    return KS;
 }
 
-// Stage 1, second half: reduce the K slices, apply scale_mid, store t as bf16 (hi, lo) into
+// Stage 1, second half: sum the warps' partials, apply scale_mid, store t as bf16 (hi, lo) into
 // each member's stage-2 operand, and zero its K padding (the CTA owning the member's last tile).
 template <typename T>
-__device__ __forceinline__ void stage1_finish(const Params &p, const float *red, int t1b, int t1e, int KS) {
+__device__ __forceinline__ void stage1_finish(const Params &p, const float *red, int t1b, int t1e) {
     using E = Elem<T>;
     const int tid = threadIdx.x;
-    const int ntiles = t1e - t1b;
+    const int ntiles = t1e - t1b, U = ntiles * p.kb1;
     for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
         const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
         const int b = rem >> 4, row = rem & 15;
-        float s = 0.f;
-        if (p.fold) {
-            for (int ks = 0; ks < KS; ++ks) {
-                const float *r = red + (lt * KS + ks) * 256 + row * 8 + 2 * b;
-                s += r[0] + r[1];
-            }
-        } else {
-            for (int ks = 0; ks < KS; ++ks) s += red[(lt * KS + ks) * 256 + row * 8 + b];
-        }
+        const float s0 = p.fold ? sum_partials(red, U, p.kb1, p.seg1, lt, row * 8 + 2 * b, true)
+                                : sum_partials(red, U, p.kb1, p.seg1, lt, row * 8 + b, false);
+        float s = s0;
         const int tile = t1b + lt;
         const int l = member_of1(p, tile);
         const Member &mb = p.m[l];
@@ -350,27 +377,29 @@ __device__ __forceinline__ void stage1_finish(const Params &p, const float *red,
     }
 }
 
-// Stage 2: this CTA's tiles [t2b, t2e) of U against t; partial tiles into `red`; returns KS.
+// Stage 2: this CTA's tiles [t2b, t2e) of U against t, split like stage 1; partials into `red`.
 template <typename T>
-__device__ __forceinline__ int stage2_items(const Params &p, const uint32_t *uch, float *red, int t2b, int t2e,
-                                            bool ok) {
+__device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uch, float *red, int t2b, int t2e,
+                                             bool ok) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int sh0 = 8 * (t & 1);
     const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles: (hi, lo) of 4 batch rows each
-    const int ntiles = t2e - t2b;
-    const int KS = max(1, kWarps / ntiles), items = ntiles * KS;
+    // units: KB = the largest member's K blocks per tile; a smaller member's tiles end early
+    const int ntiles = t2e - t2b, KB = p.kbu2, S = p.seg2;
+    int u0, u1;
+    warp_units(ntiles * KB, warp, u0, u1);
+    const int lt0 = u0 / KB;
     // B column g of n-tile q is the hi (g even) or lo (g odd) part of batch row 4q + g/2,
     // stored ready-made by stage 1 as bf16 pairs along k
     const int b0 = g >> 1, b1 = 4 + (g >> 1);
     const bool v0 = b0 < p.batch, v1 = nt == 2 && b1 < p.batch;
     constexpr int kChunkKb = 4;  // K blocks whose B fragments are fetched together
-    for (int item = warp; item < items; item += kWarps) {
-        const int lt = item / KS, ks = item - lt * KS;
+    for (int lt = lt0; u0 < u1 && lt * KB < u1; ++lt) {
         const int tile = t2b + lt;
         const int l = member_of2(p, tile);
         const Member &mb = p.m[l];
-        const int kbeg = (mb.kb2 * ks) / KS, kend = (mb.kb2 * (ks + 1)) / KS;
+        const int kbeg = max(u0 - lt * KB, 0), kend = min(min(u1 - lt * KB, KB), mb.kb2);
         // this tile's rows in the smem U region: after the earlier members' segments
         uint32_t uoff = 0;
         for (int q = 0; q < l; ++q) {
@@ -418,28 +447,23 @@ __device__ __forceinline__ int stage2_items(const Params &p, const uint32_t *uch
             s0[i] = (acc0[0][i] + acc0[1][i]) + (acc0[2][i] + acc0[3][i]);
             s1v[i] = (acc1[0][i] + acc1[1][i]) + (acc1[2][i] + acc1[3][i]);
         }
-        store_partial(red + item * 256, s0, g, t);
-        store_partial(red + item * 256 + 128, s1v, g, t);
+        store_partial(red + (warp * S + (lt - lt0)) * 256, s0, g, t);
+        store_partial(red + (warp * S + (lt - lt0)) * 256 + 128, s1v, g, t);
     }
-    return KS;
 }
 
 // Stage 2, second half: reduce, scale by s1, round, and store y (optionally y = y + res).
 template <typename T>
-__device__ __forceinline__ void stage2_finish(const Params &p, const float *red, const T *s1s, int t2b, int t2e, int KS,
-                                              const void *res) {
+__device__ __forceinline__ void stage2_finish(const Params &p, const float *red, const T *s1s, int t2b, int t2e,
+                                              const void *res, int act) {
     using E = Elem<T>;
     const int tid = threadIdx.x;
-    const int ntiles = t2e - t2b;
+    const int ntiles = t2e - t2b, U = ntiles * p.kbu2;
     for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
         const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
         const int b = rem >> 4, row = rem & 15;
         const int half = (b >> 2) * 128, col = 2 * (b & 3);
-        float s = 0.f;
-        for (int ks = 0; ks < KS; ++ks) {
-            const float *r = red + (lt * KS + ks) * 256 + half + row * 8 + col;
-            s += r[0] + r[1];
-        }
+        const float s = sum_partials(red, U, p.kbu2, p.seg2, lt, half + row * 8 + col, true);
         const int tile = t2b + lt;
         const int l = member_of2(p, tile);
         const Member &mb = p.m[l];
@@ -448,6 +472,10 @@ __device__ __forceinline__ void stage2_finish(const Params &p, const float *red,
             const float v = s * E::to_f(s1s[16 * lt + row]);
             const size_t o = (size_t)b * mb.out_f + m;
             T out = E::out(v);
+            if ((act >> l) & 1) {  // SiLU on the rounded output, rounded again (the SwiGLU gate)
+                const float g = E::to_f(out);
+                out = E::rn(g / (1.f + expf(-g)));
+            }
             if (res) {  // residual add on the rounded output; res may alias y (same element, same thread)
                 const unsigned short rb = __ldcg(reinterpret_cast<const unsigned short *>(res) + o);
                 out = E::rn(E::to_f(out) + E::to_f(*reinterpret_cast<const T *>(&rb)));
@@ -464,6 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     const int tid = threadIdx.x;
     const int G = gridDim.x, c = blockIdx.x;
     const bool do1 = (p.mode & kStage1) != 0, do2 = (p.mode & kStage2) != 0;
+    unsigned long long bar_base = 0;  // thread 0 only
+    if (tid == 0 && p.mode == kFused) bar_base = grid_barrier_base(p.ctrl, (unsigned)G);
 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     float *red = reinterpret_cast<float *>(smem + p.off_red);
@@ -603,13 +633,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
             __syncthreads();
         }
-        const int KS1 = stage1_items<T>(p, vch, s2s, xs, xs2, red, t1b, t1e, ok);
+        stage1_items<T>(p, vch, s2s, xs, xs2, red, t1b, t1e, ok);
         __syncthreads();
-        stage1_finish<T>(p, red, t1b, t1e, KS1);
+        stage1_finish<T>(p, red, t1b, t1e);
     }
 
     if (p.mode == kFused) {
-        if (!grid_barrier(p.ctrl, (unsigned)G)) ok = false;
+        if (!grid_barrier(p.ctrl, bar_base + (unsigned)G)) ok = false;
     } else if (has1 && do2) {
         __syncthreads();
     }
@@ -617,9 +647,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     // ------------------------------------------------------------------ stage 2
     if (has2) {
         if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
-        const int KS2 = stage2_items<T>(p, uch, red, t2b, t2e, ok);
+        stage2_items<T>(p, uch, red, t2b, t2e, ok);
         __syncthreads();
-        stage2_finish<T>(p, red, s1s, t2b, t2e, KS2, nullptr);
+        stage2_finish<T>(p, red, s1s, t2b, t2e, nullptr, 0);
     }
 }
 
@@ -646,15 +676,21 @@ static inline int padded_stride(int w) {
 // Shared-memory layout for a launch whose CTAs own at most `tiles1`/`tiles2` tiles.
 static size_t layout(Params &p, int tiles1, int tiles2, bool stage1, bool stage2, bool x_in_smem, bool fold) {
     size_t off = 128;  // mbarriers
-    const int items = std::max(kWarps, std::max(tiles1, tiles2));
+    p.kbu2 = 1;
+    for (int l = 0; l < p.nm; ++l) p.kbu2 = std::max(p.kbu2, p.m[l].kb2);
+    p.seg1 = seg_bound(tiles1, p.kb1);
+    p.seg2 = seg_bound(tiles2, p.kbu2);
+    const int slots = kWarps * std::max(stage1 ? p.seg1 : 1, stage2 ? p.seg2 : 1);
     p.off_red = (uint32_t)off;
-    off = align128(off + (size_t)items * 256 * sizeof(float));
+    off = align128(off + (size_t)slots * 256 * sizeof(float));
     const size_t in_pad = (size_t)p.kb1 * 64;
-    p.v_rows = (p.wv % 4) == 0;
+    // row-by-row copies only where a padded stride is needed; a slab whose row length is
+    // already an odd multiple of 4 words (or not a multiple of 4) goes in one contiguous copy
+    p.v_rows = (p.wv % 4) == 0 && padded_stride(p.wv) != p.wv;
     p.wvs = p.v_rows ? padded_stride(p.wv) : p.wv;
     int max_wus = 0;
     for (int l = 0; l < p.nm; ++l) {
-        p.m[l].u_rows = (p.m[l].wu % 4) == 0;
+        p.m[l].u_rows = (p.m[l].wu % 4) == 0 && padded_stride(p.m[l].wu) != p.m[l].wu;
         p.m[l].wus = p.m[l].u_rows ? padded_stride(p.m[l].wu) : p.m[l].wu;
         max_wus = std::max(max_wus, p.m[l].wus);
     }
@@ -873,12 +909,14 @@ struct ChainPhase {
     const void *res;    // residual added to the output, or null
     float eps;
     int xmode;
+    int act;            // bit l: SiLU on member l's output
 };
 
-struct ChainParams {
+struct alignas(16) ChainParams {
     ChainPhase ph[kMaxPhases];
     int nph;
 };
+static_assert(sizeof(ChainParams) % 16 == 0, "copied to shared memory in 16-byte pieces");
 
 // Issue phase p's weight copies for this CTA: V rows and s2 rows on bv[0], U rows and s1
 // on bv[1].  Each barrier gets exactly one arrival per phase (zero bytes when the CTA has
@@ -1001,16 +1039,24 @@ __device__ __forceinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, 
             *reinterpret_cast<uint4 *>(dst + in_pad) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
     };
+    // every global load of a pass is issued before the first use (one L2 round trip per pass)
     for (int b = 0; b < p.batch; ++b) {
         const uint4 *xr = reinterpret_cast<const uint4 *>(static_cast<const T *>(p.x) + (size_t)b * p.in_f);
         if (ph.xmode == kChainNorm) {
-            uint4 hv[kNormMaxChunks];
-            float ss = 0.f;
+            const uint4 *wr = reinterpret_cast<const uint4 *>(ph.nw);
+            uint4 hv[kNormMaxChunks], wv[kNormMaxChunks];
 #pragma unroll
             for (int j = 0; j < kNormMaxChunks; ++j) {
                 const int ch = tid + j * kThreads;
                 if (ch < nfull) {
                     hv[j] = __ldcg(xr + ch);
+                    wv[j] = __ldg(wr + ch);
+                }
+            }
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < kNormMaxChunks; ++j) {
+                if (tid + j * kThreads < nfull) {
                     float f[8];
                     unpack8<T>(hv[j], f);
 #pragma unroll
@@ -1018,7 +1064,6 @@ __device__ __forceinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, 
                 }
             }
             const float inv = rsqrtf(block_sum_512(ss, sred) / (float)p.in_f + ph.eps);
-            const uint4 *wr = reinterpret_cast<const uint4 *>(ph.nw);
 #pragma unroll
             for (int j = 0; j < kNormMaxChunks; ++j) {
                 const int ch = tid + j * kThreads;
@@ -1027,7 +1072,7 @@ __device__ __forceinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, 
                 if (ch < nfull) {
                     float h[8], w[8];
                     unpack8<T>(hv[j], h);
-                    unpack8<T>(__ldg(wr + ch), w);
+                    unpack8<T>(wv[j], w);
 #pragma unroll
                     for (int e = 0; e < 8; ++e) xf[e] = E::to_f(E::rn(w[e] * E::to_f(E::rn(h[e] * inv))));
                 } else {
@@ -1037,41 +1082,107 @@ __device__ __forceinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, 
                 emit(b, ch, xf);
             }
         } else {
-            const uint4 *ur = ph.xmode == kChainSiluMul
-                                  ? reinterpret_cast<const uint4 *>(static_cast<const T *>(ph.x2) + (size_t)b * p.in_f)
-                                  : nullptr;
-            for (int ch = tid; ch < chunks; ch += kThreads) {
-                float xf[8];
-                if (ch >= nfull) {
+            const bool two = ph.xmode == kChainSiluMul || ph.xmode == kChainMul;
+            const bool silu = ph.xmode == kChainSiluMul;
+            const uint4 *ur =
+                two ? reinterpret_cast<const uint4 *>(static_cast<const T *>(ph.x2) + (size_t)b * p.in_f) : nullptr;
+            constexpr int J = 4;
+            for (int base = 0; base < chunks; base += J * kThreads) {
+                uint4 av[J], uv[J];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) xf[e] = 0.f;
-                } else if (ur) {
-                    float gt[8], up[8];
-                    unpack8<T>(__ldcg(xr + ch), gt);
-                    unpack8<T>(__ldcg(ur + ch), up);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float sg = E::to_f(E::rn(gt[e] / (1.f + expf(-gt[e]))));
-                        xf[e] = E::to_f(E::rn(sg * up[e]));
+                for (int j = 0; j < J; ++j) {
+                    const int ch = base + tid + j * kThreads;
+                    if (ch < nfull) {
+                        av[j] = __ldcg(xr + ch);
+                        if (ur) uv[j] = __ldcg(ur + ch);
                     }
-                } else {
-                    unpack8<T>(__ldcg(xr + ch), xf);
                 }
-                emit(b, ch, xf);
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    const int ch = base + tid + j * kThreads;
+                    if (ch >= chunks) continue;
+                    float xf[8];
+                    if (ch >= nfull) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) xf[e] = 0.f;
+                    } else if (ur) {
+                        float gt[8], up[8];
+                        unpack8<T>(av[j], gt);
+                        unpack8<T>(uv[j], up);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const float sg = silu ? E::to_f(E::rn(gt[e] / (1.f + expf(-gt[e])))) : gt[e];
+                            xf[e] = E::to_f(E::rn(sg * up[e]));
+                        }
+                    } else {
+                        unpack8<T>(av[j], xf);
+                    }
+                    emit(b, ch, xf);
+                }
             }
         }
     }
 }
 
+// Phase K of the chain (K is a compile-time index so every parameter access is a fixed offset).
+template <typename T, int K>
+__device__ __forceinline__ void chain_phase(const ChainParams &cp, uint8_t *smem, float *sred, bool &ok,
+                                            unsigned long long bar_base) {
+    if (K >= cp.nph) return;
+    const ChainPhase &ph = cp.ph[K];
+    const Params &p = ph.g;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // [region][V side, U side]
+    uint64_t *bv = &bars[2 * (K & 1)];
+    constexpr uint32_t par = (uint32_t)(K >> 1) & 1u;
+    Ctrl *ctrl = p.ctrl;
+    const unsigned G = gridDim.x;
+    if (K > 0) {
+        if (!grid_barrier(ctrl, bar_base + (unsigned long long)(2 * K) * G)) ok = false;  // phase K-1's outputs
+        if (K + 1 < kMaxPhases && K + 1 < cp.nph) {  // region (K+1)&1 is free: phase K-1 is done
+            fence_proxy_async_smem();
+            chain_issue<T>(cp.ph[(K + 1) % kMaxPhases].g, smem, &bars[2 * ((K + 1) & 1)]);
+        }
+    }
+    int t1b, t1e, t2b, t2e;
+    tile_range(p.tiles1, blockIdx.x, G, t1b, t1e);
+    tile_range(p.tiles2, blockIdx.x, G, t2b, t2e);
+    float *red = reinterpret_cast<float *>(smem + p.off_red);
+    if (t1e > t1b) {
+        if (!mbar_wait(&bv[0], par, &ctrl->status)) ok = false;
+        chain_fold<T>(ph, smem, sred);
+        __syncthreads();
+        const __nv_bfloat16 *xs2 = reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2);
+        stage1_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_v),
+                        reinterpret_cast<const T *>(smem + p.off_s2), reinterpret_cast<const T *>(xs2), xs2, red,
+                        t1b, t1e, ok);
+        __syncthreads();
+        stage1_finish<T>(p, red, t1b, t1e);
+    }
+    if (!grid_barrier(ctrl, bar_base + (unsigned long long)(2 * K + 1) * G)) ok = false;  // t is complete
+    if (t2e > t2b) {
+        if (!mbar_wait(&bv[1], par, &ctrl->status)) ok = false;
+        stage2_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_u), red, t2b, t2e, ok);
+        __syncthreads();
+        stage2_finish<T>(p, red, reinterpret_cast<const T *>(smem + p.off_s1), t2b, t2e, ph.res, ph.act);
+    }
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constant__ ChainParams cp) {
+__global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constant__ ChainParams cpg) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float sred[kWarps];
-    const int tid = threadIdx.x;
-    const unsigned G = gridDim.x;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // [region][V side, U side]
-    Ctrl *ctrl = cp.ph[0].g.ctrl;
-    if (tid == 0) {
+    // The parameter block goes to shared memory in one parallel pass: every later access is a
+    // shared load instead of a (serially dependent) first touch of the parameter cache.
+    __shared__ ChainParams cp;
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(&cpg);
+        uint4 *dst = reinterpret_cast<uint4 *>(&cp);
+        for (int i = threadIdx.x; i < (int)(sizeof(ChainParams) / 16); i += kThreads) dst[i] = src[i];
+    }
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    unsigned long long bar_base = 0;  // thread 0 only
+    if (threadIdx.x == 0) {
+        bar_base = grid_barrier_base(cpg.ph[0].g.ctrl, gridDim.x);
 #pragma unroll
         for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
         fence_mbar_init();
@@ -1080,41 +1191,11 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
     chain_issue<T>(cp.ph[0].g, smem, &bars[0]);
     if (cp.nph > 1) chain_issue<T>(cp.ph[1].g, smem, &bars[2]);
     bool ok = true;
-    for (int k = 0; k < cp.nph; ++k) {
-        const ChainPhase &ph = cp.ph[k];
-        const Params &p = ph.g;
-        uint64_t *bv = &bars[2 * (k & 1)];
-        const uint32_t par = (uint32_t)(k >> 1) & 1u;
-        if (k > 0) {
-            if (!grid_barrier(ctrl, G)) ok = false;  // phase k-1's outputs are visible
-            if (k + 1 < cp.nph) {                    // region (k+1)&1 is free: phase k-1 is done
-                fence_proxy_async_smem();
-                chain_issue<T>(cp.ph[k + 1].g, smem, &bars[2 * ((k + 1) & 1)]);
-            }
-        }
-        int t1b, t1e, t2b, t2e;
-        tile_range(p.tiles1, blockIdx.x, G, t1b, t1e);
-        tile_range(p.tiles2, blockIdx.x, G, t2b, t2e);
-        float *red = reinterpret_cast<float *>(smem + p.off_red);
-        if (t1e > t1b) {
-            if (!mbar_wait(&bv[0], par, &ctrl->status)) ok = false;
-            chain_fold<T>(ph, smem, sred);
-            __syncthreads();
-            const __nv_bfloat16 *xs2 = reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2);
-            const int KS1 = stage1_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_v),
-                                            reinterpret_cast<const T *>(smem + p.off_s2),
-                                            reinterpret_cast<const T *>(xs2), xs2, red, t1b, t1e, ok);
-            __syncthreads();
-            stage1_finish<T>(p, red, t1b, t1e, KS1);
-        }
-        if (!grid_barrier(ctrl, G)) ok = false;  // t of every member is complete
-        if (t2e > t2b) {
-            if (!mbar_wait(&bv[1], par, &ctrl->status)) ok = false;
-            const int KS2 = stage2_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_u), red, t2b, t2e, ok);
-            __syncthreads();
-            stage2_finish<T>(p, red, reinterpret_cast<const T *>(smem + p.off_s1), t2b, t2e, KS2, ph.res);
-        }
-    }
+    static_assert(kMaxPhases == 4, "one chain_phase call per phase");
+    chain_phase<T, 0>(cp, smem, sred, ok, bar_base);
+    chain_phase<T, 1>(cp, smem, sred, ok, bar_base);
+    chain_phase<T, 2>(cp, smem, sred, ok, bar_base);
+    chain_phase<T, 3>(cp, smem, sred, ok, bar_base);
 }
 
 // Host: validate the phases, build their Params, lay out shared memory.  `launch` = false
@@ -1145,7 +1226,7 @@ static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *pha
     ChainParams cp{};
     cp.nph = n;
     size_t need = sizeof(Ctrl);
-    int max_items = kWarps;
+    int max_slots = kWarps;
     size_t xs2_bytes = 0, region[2] = {0, 0};
     const uintptr_t ws_base = reinterpret_cast<uintptr_t>(workspace);
     for (int k = 0; k < n; ++k) {
@@ -1154,12 +1235,15 @@ static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *pha
         Params &p = ph.g;
         if (P.n_layers < 1 || P.n_layers > kMaxGroup)
             return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: 1..%d layers (got %d)", k, kMaxGroup, P.n_layers);
-        if (P.x_mode != kChainPlain && P.x_mode != kChainNorm && P.x_mode != kChainSiluMul)
+        if (P.x_mode != kChainPlain && P.x_mode != kChainNorm && P.x_mode != kChainSiluMul && P.x_mode != kChainMul)
             return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: unknown x_mode %d", k, P.x_mode);
+        if (P.act & ~((1 << P.n_layers) - 1))
+            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: act bit beyond its %d layers", k, P.n_layers);
         if (P.in_features <= 0 || P.in_features % 8 || P.in_features > (1 << 20))
             return fail(NQ_ERR_UNSUPPORTED, "phase %d: in_features must be a positive multiple of 8 (got %lld)", k,
                         (long long)P.in_features);
-        if (!P.x || (P.x_mode == kChainSiluMul && !P.x2) || (P.x_mode == kChainNorm && !P.norm_weight))
+        if (!P.x || ((P.x_mode == kChainSiluMul || P.x_mode == kChainMul) && !P.x2) ||
+            (P.x_mode == kChainNorm && !P.norm_weight))
             return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: missing input tensor", k);
         if ((reinterpret_cast<uintptr_t>(P.x) | reinterpret_cast<uintptr_t>(P.x2) |
              reinterpret_cast<uintptr_t>(P.norm_weight)) & 15)
@@ -1186,6 +1270,7 @@ static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *pha
         ph.res = P.residual;
         ph.eps = P.eps;
         ph.xmode = P.x_mode;
+        ph.act = P.act;
         int t1 = 0, t2 = 0;
         for (int l = 0; l < P.n_layers; ++l) {
             const nq_gemv_layer &L = P.layers[l];
@@ -1221,16 +1306,20 @@ static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *pha
             t2 += mb.tiles2;
             mb.tb = reinterpret_cast<__nv_bfloat16 *>(ws_base + need);  // tb regions follow the control block
             need += tb_bytes(L.rank);
-            mb.u_rows = (mb.wu % 4) == 0;
+            mb.u_rows = (mb.wu % 4) == 0 && padded_stride(mb.wu) != mb.wu;
             mb.wus = mb.u_rows ? padded_stride(mb.wu) : mb.wu;
         }
         if (t1 > 65536 || t2 > 65536) return fail(NQ_ERR_UNSUPPORTED, "phase %d: layer group too large", k);
         p.tiles1 = t1;
         p.tiles2 = t2;
-        p.v_rows = (p.wv % 4) == 0;
+        p.v_rows = (p.wv % 4) == 0 && padded_stride(p.wv) != p.wv;
         p.wvs = p.v_rows ? padded_stride(p.wv) : p.wv;
         const int tpc1 = (t1 + G - 1) / G, tpc2 = (t2 + G - 1) / G;
-        max_items = std::max(max_items, std::max(tpc1, tpc2));
+        p.kbu2 = 1;
+        for (int l = 0; l < p.nm; ++l) p.kbu2 = std::max(p.kbu2, p.m[l].kb2);
+        p.seg1 = seg_bound(tpc1, p.kb1);
+        p.seg2 = seg_bound(tpc2, p.kbu2);
+        max_slots = std::max(max_slots, kWarps * std::max(p.seg1, p.seg2));
         const size_t in_pad = (size_t)p.kb1 * 64;
         xs2_bytes = std::max(xs2_bytes, (size_t)p.nm * 2 * (size_t)batch * in_pad * 2);
         int max_wus = 0;
@@ -1248,11 +1337,12 @@ static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *pha
         region[k & 1] = std::max(region[k & 1], off);
     }
     const size_t off_red = 128;  // four mbarriers first
-    const size_t off_xs2 = align128(off_red + (size_t)max_items * 256 * sizeof(float));
+    const size_t off_xs2 = align128(off_red + (size_t)max_slots * 256 * sizeof(float));
     const size_t off_r0 = align128(off_xs2 + xs2_bytes);
     const size_t off_r1 = align128(off_r0 + region[0]);
     const size_t smem = off_r1 + region[1];
-    const size_t cap = (size_t)smem_optin - kStaticSmemReserve;
+    // static shared memory of the chain kernel: the parameter block plus the usual reserve
+    const size_t cap = (size_t)smem_optin - kStaticSmemReserve - sizeof(ChainParams);
     if (ws_need) *ws_need = need;
     if (smem > cap)
         return fail(NQ_ERR_UNSUPPORTED, "chain needs %zu bytes of shared memory per SM (limit %zu)", smem, cap);

@@ -262,15 +262,16 @@ class Decoder:
                              out=outs)
 
     def _block_phases(self, li: int, a: torch.Tensor, h: torch.Tensor, alloc: bool = True):
-        """Chain of block li after attention: o (+ residual into h), gate/up from RMSNorm(h),
-        down from silu(gate) * up (+ residual into h), then block li+1's q/k/v."""
+        """Chain of block li after attention: o (+ residual into h), gate/up from RMSNorm(h)
+        (SiLU on the gate), down from silu(gate) * up (+ residual into h), then block li+1's q/k/v."""
         cfg, lay, B = self.cfg, self.layers[li], self.batch
         gate = torch.empty(B, cfg.ffn // self.tp, device=self.device, dtype=self.dtype)
         up = torch.empty_like(gate)
+        # the gate's SiLU is applied once per value in its own epilogue; down multiplies by up
         phases = [nqchain.Phase([lay["o"]], a, residual=h, out=[h]),
                   nqchain.Phase([lay["gate"], lay["up"]], h, nqchain.RMSNORM, norm_weight=lay["post_norm"],
-                                eps=cfg.rms_eps, out=[gate, up]),
-                  nqchain.Phase([lay["down"]], gate, nqchain.SILU_MUL, x2=up, residual=h, out=[h])]
+                                eps=cfg.rms_eps, out=[gate, up], act=1),
+                  nqchain.Phase([lay["down"]], gate, nqchain.MUL, x2=up, residual=h, out=[h])]
         if li + 1 < cfg.layers:
             phases.append(self._qkv_phase(li + 1, h, alloc))
         return phases, (gate, up)

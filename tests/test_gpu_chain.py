@@ -55,8 +55,9 @@ def test_single_plain_phase_matches_gemv_bitwise(shape, dt):
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("gate_act", [False, True])
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
-def test_decoder_block_chain_matches_separate_launches(dt):
+def test_decoder_block_chain_matches_separate_launches(dt, gate_act):
     hid, ffn, ra, rm = 4096, 11008, 1126, 2054
     o = layer(hid, hid, ra, dt, 1)
     gate, up = layer(ffn, hid, rm, dt, 2), layer(ffn, hid, rm, dt, 3)
@@ -83,12 +84,15 @@ def test_decoder_block_chain_matches_separate_launches(dt):
     h = h0.clone()
     g_buf, u_buf = torch.empty(1, ffn, device="cuda", dtype=dt), torch.empty(1, ffn, device="cuda", dtype=dt)
     ph = [chain.Phase([o], a, residual=h, out=[h]),
-          chain.Phase([gate, up], h, chain.RMSNORM, norm_weight=post_w, eps=eps, out=[g_buf, u_buf]),
-          chain.Phase([down], g_buf, chain.SILU_MUL, x2=u_buf, residual=h, out=[h]),
+          chain.Phase([gate, up], h, chain.RMSNORM, norm_weight=post_w, eps=eps, out=[g_buf, u_buf],
+                      act=1 if gate_act else 0),
+          chain.Phase([down], g_buf, chain.MUL if gate_act else chain.SILU_MUL, x2=u_buf, residual=h, out=[h]),
           chain.Phase([q, k, v], h, chain.RMSNORM, norm_weight=in_w, eps=eps)]
     ws = ws_for(ph)
     outs = chain.run(ph, ws)
     torch.cuda.synchronize()
+    if gate_act:  # the gate buffer holds dtype(silu(gate))
+        g_out = (g_out.float() / (1 + torch.exp(-g_out.float()))).to(dt)
     assert rel(g_buf, g_out) <= 1e-3 and rel(u_buf, u_out) <= 1e-3
     assert rel(h, h2) <= 1e-3
     for got, want in zip(outs[3], want_qkv):
@@ -98,8 +102,18 @@ def test_decoder_block_chain_matches_separate_launches(dt):
     outs2 = chain.run(ph, ws)
     for got, again in zip(outs[3], outs2[3]):
         assert torch.equal(got, again)
-    st = torch.zeros(1, dtype=torch.int32)
     assert int(ws[8:12].view(torch.int32).cpu()[0]) == 0  # control block status word
+    return h.clone(), [t.clone() for t in outs[3]]
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_gate_silu_then_mul_equals_silu_mul_bitwise(dt):
+    """act on the gate + MUL computes the same bits as SILU_MUL on the raw gate."""
+    h_a, qkv_a = test_decoder_block_chain_matches_separate_launches(dt, False)
+    h_b, qkv_b = test_decoder_block_chain_matches_separate_launches(dt, True)
+    assert torch.equal(h_a, h_b)
+    for a, b in zip(qkv_a, qkv_b):
+        assert torch.equal(a, b)
 
 
 def test_decoder_with_and_without_chains_agree():
