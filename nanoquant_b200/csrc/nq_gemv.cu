@@ -221,6 +221,7 @@ struct Member {
     int tiles1, tiles2;        // 16-row tiles of this layer in stage 1 / stage 2
     int t1_start, t2_start;    // its first tile in the group's concatenated tile lists
     int u_rows, wus;           // U slab copied row by row (wu % 4 == 0) and its smem row stride
+    int tbs, ldis;             // chain: staged t columns in shared memory (element offset, column stride)
 };
 
 struct Params {
@@ -378,13 +379,16 @@ __device__ __forceinline__ void stage1_finish(const Params &p, const float *red,
 }
 
 // Stage 2: this CTA's tiles [t2b, t2e) of U against t, split like stage 1; partials into `red`.
-template <typename T>
+// NT = 8-column B tiles: (hi, lo) of 4 batch rows each, so 1 for batch <= 4.  `tsm`: the
+// members' t columns staged in shared memory (member l at mb.tbs, column stride mb.ldis), or
+// null to read them from global memory (L2).
+template <typename T, int NT>
 __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uch, float *red, int t2b, int t2e,
-                                             bool ok) {
+                                             bool ok, const __nv_bfloat16 *tsm) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int sh0 = 8 * (t & 1);
-    const int nt = p.batch <= 4 ? 1 : 2;  // 8-column B tiles: (hi, lo) of 4 batch rows each
+    constexpr int nt = NT;
     // units: KB = the largest member's K blocks per tile; a smaller member's tiles end early
     const int ntiles = t2e - t2b, KB = p.kbu2, S = p.seg2;
     int u0, u1;
@@ -413,17 +417,26 @@ __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uc
         const bool vA = ok && (row0 + g < mb.out_f), vB = ok && (row0 + g + 8 < mb.out_f);
         const uint32_t *rowA = uch + uoff + (size_t)(16 * (tile - a0) + g) * mb.wus;
         const uint32_t *rowB = rowA + (size_t)8 * mb.wus;
-        const __nv_bfloat16 *trow0 = mb.tb + (size_t)g * mb.ldi;
+        const __nv_bfloat16 *trow0 = tsm ? tsm + mb.tbs + (size_t)g * mb.ldis : mb.tb + (size_t)g * mb.ldi;
         const __nv_bfloat16 *trow1 = mb.tb + (size_t)(8 + g) * mb.ldi;
-        float acc0[4][4] = {}, acc1[4][4] = {};
+        float acc0[4][4] = {}, acc1[NT][4][4] = {};
         for (int kb0 = kbeg; kb0 < kend; kb0 += kChunkKb) {
-            uint32_t bp0[kChunkKb][8], bp1[kChunkKb][8];
+            uint32_t bp0[kChunkKb][8], bp1[NT][kChunkKb][8];
 #pragma unroll
             for (int q = 0; q < kChunkKb; ++q) {
                 const int kc = 64 * (kb0 + q) + 16 * t;
                 const bool in = kb0 + q < kend;
-                load_t_pairs(trow0 + kc, in && v0, bp0[q]);
-                load_t_pairs(trow1 + kc, in && v1, bp1[q]);
+                if (tsm) {
+                    if (in && v0) {
+                        load16_smem(trow0 + kc, bp0[q]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) bp0[q][e] = 0u;
+                    }
+                } else {
+                    load_t_pairs(trow0 + kc, in && v0, bp0[q]);
+                }
+                if (NT == 2) load_t_pairs(trow1 + kc, in && v1, bp1[NT - 1][q]);
             }
 #pragma unroll
             for (int q = 0; q < kChunkKb; ++q) {
@@ -437,7 +450,9 @@ __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uc
                     uint32_t a[4];
                     sign_frag(wA, wB, j, a);
                     mma_bf16_16816(acc0[j], a[0], a[1], a[2], a[3], bp0[q][2 * j], bp0[q][2 * j + 1]);
-                    if (nt == 2) mma_bf16_16816(acc1[j], a[0], a[1], a[2], a[3], bp1[q][2 * j], bp1[q][2 * j + 1]);
+                    if (NT == 2)
+                        mma_bf16_16816(acc1[NT - 1][j], a[0], a[1], a[2], a[3], bp1[NT - 1][q][2 * j],
+                                       bp1[NT - 1][q][2 * j + 1]);
                 }
             }
         }
@@ -445,10 +460,10 @@ __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uc
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             s0[i] = (acc0[0][i] + acc0[1][i]) + (acc0[2][i] + acc0[3][i]);
-            s1v[i] = (acc1[0][i] + acc1[1][i]) + (acc1[2][i] + acc1[3][i]);
+            s1v[i] = (acc1[NT - 1][0][i] + acc1[NT - 1][1][i]) + (acc1[NT - 1][2][i] + acc1[NT - 1][3][i]);
         }
         store_partial(red + (warp * S + (lt - lt0)) * 256, s0, g, t);
-        store_partial(red + (warp * S + (lt - lt0)) * 256 + 128, s1v, g, t);
+        if (NT == 2) store_partial(red + (warp * S + (lt - lt0)) * 256 + 128, s1v, g, t);
     }
 }
 
@@ -647,7 +662,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     // ------------------------------------------------------------------ stage 2
     if (has2) {
         if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
-        stage2_items<T>(p, uch, red, t2b, t2e, ok);
+        if (p.batch <= 4)
+            stage2_items<T, 1>(p, uch, red, t2b, t2e, ok, nullptr);
+        else
+            stage2_items<T, 2>(p, uch, red, t2b, t2e, ok, nullptr);
         __syncthreads();
         stage2_finish<T>(p, red, s1s, t2b, t2e, nullptr, 0);
     }
@@ -922,7 +940,7 @@ static_assert(sizeof(ChainParams) % 16 == 0, "copied to shared memory in 16-byte
 // on bv[1].  Each barrier gets exactly one arrival per phase (zero bytes when the CTA has
 // no tile in that stage), so a barrier's k-th completion always belongs to its k-th phase.
 template <typename T>
-__device__ __forceinline__ void chain_issue(const Params &p, uint8_t *smem, uint64_t *bv) {
+__device__ __noinline__ void chain_issue(const Params &p, uint8_t *smem, uint64_t *bv) {
     const int tid = threadIdx.x;
     int t1b, t1e, t2b, t2e;
     tile_range(p.tiles1, blockIdx.x, gridDim.x, t1b, t1e);
@@ -1019,7 +1037,7 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
 // xs2[l][2b (+1)][k] = bf16 hi (lo) of x'[b][k] * s2_l[k], x' formed per ph.xmode from global
 // memory written by earlier phases (read through L2: __ldcg).
 template <typename T>
-__device__ __forceinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, float *sred) {
+__device__ __noinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, float *sred) {
     using E = Elem<T>;
     const Params &p = ph.g;
     const int tid = threadIdx.x;
@@ -1124,46 +1142,84 @@ __device__ __forceinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, 
     }
 }
 
-// Phase K of the chain (K is a compile-time index so every parameter access is a fixed offset).
-template <typename T, int K>
-__device__ __forceinline__ void chain_phase(const ChainParams &cp, uint8_t *smem, float *sred, bool &ok,
+// Out-of-line entry points of the stage bodies for the chain kernel: each gets its own
+// register allocation instead of sharing one with the phase loop (inlined, they spill).
+template <typename T>
+__device__ __noinline__ void chain_stage1(const Params &p, uint8_t *smem, int t1b, int t1e, bool ok) {
+    const __nv_bfloat16 *xs2 = reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2);
+    float *red = reinterpret_cast<float *>(smem + p.off_red);
+    stage1_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_v), reinterpret_cast<const T *>(smem + p.off_s2),
+                    reinterpret_cast<const T *>(xs2), xs2, red, t1b, t1e, ok);
+    __syncthreads();
+    stage1_finish<T>(p, red, t1b, t1e);
+}
+template <typename T>
+__device__ __noinline__ void chain_stage2(const Params &p, uint8_t *smem, int t2b, int t2e, bool ok, const void *res,
+                                          int act) {
+    float *red = reinterpret_cast<float *>(smem + p.off_red);
+    stage2_items<T, 1>(p, reinterpret_cast<const uint32_t *>(smem + p.off_u), red, t2b, t2e, ok,
+                       reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2));
+    __syncthreads();
+    stage2_finish<T>(p, red, reinterpret_cast<const T *>(smem + p.off_s1), t2b, t2e, res, act);
+}
+
+// Phase k of the chain.  One copy of the code serves every phase (the kernel is already large;
+// a copy per phase would not stay in the instruction cache); the phase descriptor lives in
+// shared memory, so the runtime index costs nothing.
+template <typename T>
+__device__ __forceinline__ void chain_phase(const ChainParams &cp, int k, uint8_t *smem, float *sred, bool &ok,
                                             unsigned long long bar_base) {
-    if (K >= cp.nph) return;
-    const ChainPhase &ph = cp.ph[K];
+    const ChainPhase &ph = cp.ph[k];
     const Params &p = ph.g;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // [region][V side, U side]
-    uint64_t *bv = &bars[2 * (K & 1)];
-    constexpr uint32_t par = (uint32_t)(K >> 1) & 1u;
+    uint64_t *bv = &bars[2 * (k & 1)];
+    const uint32_t par = (uint32_t)(k >> 1) & 1u;
     Ctrl *ctrl = p.ctrl;
     const unsigned G = gridDim.x;
-    if (K > 0) {
-        if (!grid_barrier(ctrl, bar_base + (unsigned long long)(2 * K) * G)) ok = false;  // phase K-1's outputs
-        if (K + 1 < kMaxPhases && K + 1 < cp.nph) {  // region (K+1)&1 is free: phase K-1 is done
+    if (k > 0) {
+        if (!grid_barrier(ctrl, bar_base + (unsigned long long)(2 * k) * G)) ok = false;  // phase k-1's outputs
+        if (k + 1 < cp.nph) {  // region (k+1)&1 is free: phase k-1 is done
             fence_proxy_async_smem();
-            chain_issue<T>(cp.ph[(K + 1) % kMaxPhases].g, smem, &bars[2 * ((K + 1) & 1)]);
+            chain_issue<T>(cp.ph[k + 1].g, smem, &bars[2 * ((k + 1) & 1)]);
         }
     }
     int t1b, t1e, t2b, t2e;
     tile_range(p.tiles1, blockIdx.x, G, t1b, t1e);
     tile_range(p.tiles2, blockIdx.x, G, t2b, t2e);
-    float *red = reinterpret_cast<float *>(smem + p.off_red);
     if (t1e > t1b) {
         if (!mbar_wait(&bv[0], par, &ctrl->status)) ok = false;
         chain_fold<T>(ph, smem, sred);
         __syncthreads();
-        const __nv_bfloat16 *xs2 = reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2);
-        stage1_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_v),
-                        reinterpret_cast<const T *>(smem + p.off_s2), reinterpret_cast<const T *>(xs2), xs2, red,
-                        t1b, t1e, ok);
-        __syncthreads();
-        stage1_finish<T>(p, red, t1b, t1e);
+        chain_stage1<T>(p, smem, t1b, t1e, ok);
     }
-    if (!grid_barrier(ctrl, bar_base + (unsigned long long)(2 * K + 1) * G)) ok = false;  // t is complete
+    if (!grid_barrier(ctrl, bar_base + (unsigned long long)(2 * k + 1) * G)) ok = false;  // t is complete
+    // The t columns of the members this CTA serves go to the (now idle) fold buffer, one bulk
+    // copy per member and column; the barrier completes once per phase (zero bytes if no tile).
+    uint64_t *tbar = &bars[4];
+    if (threadIdx.x == 0) {
+        fence_proxy_async_global();  // t was written through the generic proxy by other CTAs
+        fence_proxy_async_smem();    // the fold buffer was written and read through it here
+        uint32_t bytes = 0;
+        for (int l = 0; l < p.nm && t2e > t2b; ++l) {
+            int a, b;
+            seg_tiles(p.m[l], t2b, t2e, a, b);
+            if (a < b) bytes += (uint32_t)(2 * p.batch) * (uint32_t)p.m[l].ldi * 2u;
+        }
+        mbar_arrive_expect_tx(tbar, bytes);
+        __nv_bfloat16 *tsm = reinterpret_cast<__nv_bfloat16 *>(smem + p.off_xs2);
+        for (int l = 0; l < p.nm && t2e > t2b; ++l) {
+            const Member &mb = p.m[l];
+            int a, b;
+            seg_tiles(mb, t2b, t2e, a, b);
+            if (a >= b) continue;
+            for (int c = 0; c < 2 * p.batch; ++c)
+                bulk_g2s(tsm + mb.tbs + (size_t)c * mb.ldis, mb.tb + (size_t)c * mb.ldi, (uint32_t)mb.ldi * 2u, tbar);
+        }
+    }
     if (t2e > t2b) {
+        if (!mbar_wait(tbar, (uint32_t)k & 1u, &ctrl->status)) ok = false;
         if (!mbar_wait(&bv[1], par, &ctrl->status)) ok = false;
-        stage2_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_u), red, t2b, t2e, ok);
-        __syncthreads();
-        stage2_finish<T>(p, red, reinterpret_cast<const T *>(smem + p.off_s1), t2b, t2e, ph.res, ph.act);
+        chain_stage2<T>(p, smem, t2b, t2e, ok, ph.res, ph.act);
     }
 }
 
@@ -1184,18 +1240,14 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
     if (threadIdx.x == 0) {
         bar_base = grid_barrier_base(cpg.ph[0].g.ctrl, gridDim.x);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);  // 2 regions x (V, U), staged t
         fence_mbar_init();
     }
     __syncthreads();
     chain_issue<T>(cp.ph[0].g, smem, &bars[0]);
     if (cp.nph > 1) chain_issue<T>(cp.ph[1].g, smem, &bars[2]);
     bool ok = true;
-    static_assert(kMaxPhases == 4, "one chain_phase call per phase");
-    chain_phase<T, 0>(cp, smem, sred, ok, bar_base);
-    chain_phase<T, 1>(cp, smem, sred, ok, bar_base);
-    chain_phase<T, 2>(cp, smem, sred, ok, bar_base);
-    chain_phase<T, 3>(cp, smem, sred, ok, bar_base);
+    for (int k = 0; k < cp.nph; ++k) chain_phase<T>(cp, k, smem, sred, ok, bar_base);
 }
 
 // Host: validate the phases, build their Params, lay out shared memory.  `launch` = false
@@ -1322,6 +1374,15 @@ static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *pha
         max_slots = std::max(max_slots, kWarps * std::max(p.seg1, p.seg2));
         const size_t in_pad = (size_t)p.kb1 * 64;
         xs2_bytes = std::max(xs2_bytes, (size_t)p.nm * 2 * (size_t)batch * in_pad * 2);
+        // stage 2 reuses the fold buffer for the members' t columns, column stride ldi + 8
+        // (16 bytes of padding keep the columns on different banks)
+        size_t staged = 0;
+        for (int l = 0; l < p.nm; ++l) {
+            p.m[l].ldis = p.m[l].ldi + 8;
+            p.m[l].tbs = (int)staged;
+            staged += (size_t)2 * batch * p.m[l].ldis;
+        }
+        xs2_bytes = std::max(xs2_bytes, staged * 2);
         int max_wus = 0;
         for (int l = 0; l < p.nm; ++l) max_wus = std::max(max_wus, p.m[l].wus);
         // region-relative offsets; made absolute below
