@@ -39,6 +39,10 @@ def parse():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample length")
+    ap.add_argument("--layer", default=None,
+                    help="per-layer GEMV instead of whole-model decode: out,in,rank (e.g. 11008,4096,2054); "
+                         "prints that layer's GB/s over --copies weight copies cycled through the timed loop")
+    ap.add_argument("--copies", type=int, default=40, help="--layer: distinct weight copies (past L2)")
     return ap.parse_args()
 
 
@@ -365,8 +369,48 @@ def run_nq(args, world, rank, local):
         torch.distributed.destroy_process_group()
 
 
+def run_layer(args):
+    """One NanoQuant layer's fused decode GEMV (the per-layer measurement): --copies distinct
+    seeded weight sets, more bytes than L2 holds, cycled so every launch reads its weights
+    from HBM; algorithmic bytes per launch / device time per launch."""
+    from nanoquant_b200.decoder import QuantLinearShard, _random_planes
+    out_f, in_f, r = (int(v) for v in args.layer.split(","))
+    dev = torch.device("cuda", 0)
+    layers = []
+    for c in range(args.copies):
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1000 + c)
+        vb, ub = _random_planes(gen, r, in_f, dev), _random_planes(gen, out_f, r, dev)
+        s2 = (torch.rand(in_f, generator=gen, device=dev) + 0.5).half()
+        s1 = (torch.rand(out_f, generator=gen, device=dev) * 0.02).half()
+        layers.append(QuantLinearShard(vb, ub, s2, None, s1))
+    x = torch.randn(args.batch, in_f, device=dev).half()
+    alg = layers[0].nbytes() + 2 * args.batch * (in_f + out_f)
+    for i in range(max(args.warmup, 3)):
+        layers[i % args.copies].gemv(x)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = args.steps * args.copies
+    e0.record()
+    for i in range(n):
+        layers[i % args.copies].gemv(x)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / n
+    peak, kind = peaks()
+    gbs = alg / (us * 1e-6) / 1e9
+    print(json.dumps({"metric": "decode GEMV GB/s (algorithmic bytes)", "value": round(gbs, 2), "unit": "GB/s",
+                      "layer": {"out": out_f, "in": in_f, "rank": r, "batch": args.batch}, "us_per_launch": round(us, 3),
+                      "bytes_per_launch": alg, "copies": args.copies, "launches": n,
+                      "roofline": {"bound": "hbm", "peak": peak, "frac": round(gbs / peak, 5), "peak_source": kind},
+                      "dtype": "f16", "data": "synthetic"}), flush=True)
+
+
 def main():
     args = parse()
+    if args.layer:
+        run_layer(args)
+        return
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         run_reference(args, world, rank)

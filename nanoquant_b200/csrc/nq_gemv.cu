@@ -940,7 +940,7 @@ static_assert(sizeof(ChainParams) % 16 == 0, "copied to shared memory in 16-byte
 // on bv[1].  Each barrier gets exactly one arrival per phase (zero bytes when the CTA has
 // no tile in that stage), so a barrier's k-th completion always belongs to its k-th phase.
 template <typename T>
-__device__ __noinline__ void chain_issue(const Params &p, uint8_t *smem, uint64_t *bv) {
+__device__ __forceinline__ void chain_issue(const Params &p, uint8_t *smem, uint64_t *bv) {
     const int tid = threadIdx.x;
     int t1b, t1e, t2b, t2e;
     tile_range(p.tiles1, blockIdx.x, gridDim.x, t1b, t1e);
@@ -1037,7 +1037,7 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
 // xs2[l][2b (+1)][k] = bf16 hi (lo) of x'[b][k] * s2_l[k], x' formed per ph.xmode from global
 // memory written by earlier phases (read through L2: __ldcg).
 template <typename T>
-__device__ __noinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, float *sred) {
+__device__ __forceinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, float *sred) {
     using E = Elem<T>;
     const Params &p = ph.g;
     const int tid = threadIdx.x;
@@ -1142,10 +1142,10 @@ __device__ __noinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, flo
     }
 }
 
-// Out-of-line entry points of the stage bodies for the chain kernel: each gets its own
-// register allocation instead of sharing one with the phase loop (inlined, they spill).
+// The stage bodies as the chain kernel runs them (inlined: out of line, the shared-memory
+// pointers would become generic ones).
 template <typename T>
-__device__ __noinline__ void chain_stage1(const Params &p, uint8_t *smem, int t1b, int t1e, bool ok) {
+__device__ __forceinline__ void chain_stage1(const Params &p, uint8_t *smem, int t1b, int t1e, bool ok) {
     const __nv_bfloat16 *xs2 = reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2);
     float *red = reinterpret_cast<float *>(smem + p.off_red);
     stage1_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_v), reinterpret_cast<const T *>(smem + p.off_s2),
@@ -1154,7 +1154,7 @@ __device__ __noinline__ void chain_stage1(const Params &p, uint8_t *smem, int t1
     stage1_finish<T>(p, red, t1b, t1e);
 }
 template <typename T>
-__device__ __noinline__ void chain_stage2(const Params &p, uint8_t *smem, int t2b, int t2e, bool ok, const void *res,
+__device__ __forceinline__ void chain_stage2(const Params &p, uint8_t *smem, int t2b, int t2e, bool ok, const void *res,
                                           int act) {
     float *red = reinterpret_cast<float *>(smem + p.off_red);
     stage2_items<T, 1>(p, reinterpret_cast<const uint32_t *>(smem + p.off_u), red, t2b, t2e, ok,
@@ -1163,9 +1163,9 @@ __device__ __noinline__ void chain_stage2(const Params &p, uint8_t *smem, int t2
     stage2_finish<T>(p, red, reinterpret_cast<const T *>(smem + p.off_s1), t2b, t2e, res, act);
 }
 
-// Phase k of the chain.  One copy of the code serves every phase (the kernel is already large;
-// a copy per phase would not stay in the instruction cache); the phase descriptor lives in
-// shared memory, so the runtime index costs nothing.
+// Phase k of the chain.  One copy of the code serves every phase (a copy per phase would not
+// stay in the instruction cache); the runtime index into the parameter block becomes indexed
+// constant-bank loads.
 template <typename T>
 __device__ __forceinline__ void chain_phase(const ChainParams &cp, int k, uint8_t *smem, float *sred, bool &ok,
                                             unsigned long long bar_base) {
@@ -1224,21 +1224,13 @@ __device__ __forceinline__ void chain_phase(const ChainParams &cp, int k, uint8_
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constant__ ChainParams cpg) {
+__global__ void __launch_bounds__(kThreads, 1) chain_kernel(const ChainParams cp) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float sred[kWarps];
-    // The parameter block goes to shared memory in one parallel pass: every later access is a
-    // shared load instead of a (serially dependent) first touch of the parameter cache.
-    __shared__ ChainParams cp;
-    {
-        const uint4 *src = reinterpret_cast<const uint4 *>(&cpg);
-        uint4 *dst = reinterpret_cast<uint4 *>(&cp);
-        for (int i = threadIdx.x; i < (int)(sizeof(ChainParams) / 16); i += kThreads) dst[i] = src[i];
-    }
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     unsigned long long bar_base = 0;  // thread 0 only
     if (threadIdx.x == 0) {
-        bar_base = grid_barrier_base(cpg.ph[0].g.ctrl, gridDim.x);
+        bar_base = grid_barrier_base(cp.ph[0].g.ctrl, gridDim.x);
 #pragma unroll
         for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);  // 2 regions x (V, U), staged t
         fence_mbar_init();
@@ -1402,8 +1394,7 @@ static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *pha
     const size_t off_r0 = align128(off_xs2 + xs2_bytes);
     const size_t off_r1 = align128(off_r0 + region[0]);
     const size_t smem = off_r1 + region[1];
-    // static shared memory of the chain kernel: the parameter block plus the usual reserve
-    const size_t cap = (size_t)smem_optin - kStaticSmemReserve - sizeof(ChainParams);
+    const size_t cap = (size_t)smem_optin - kStaticSmemReserve;
     if (ws_need) *ws_need = need;
     if (smem > cap)
         return fail(NQ_ERR_UNSUPPORTED, "chain needs %zu bytes of shared memory per SM (limit %zu)", smem, cap);

@@ -164,7 +164,7 @@ class Decoder:
 
     def __init__(self, cfg: DecoderConfig, max_seq: int, batch: int = 1, tp_rank: int = 0, tp: int = 1,
                  group=None, seed: int = 0, dtype=torch.float16, device=None, with_mid: bool = False,
-                 chain: bool = True):
+                 chain: bool = False):
         _lib.load_torch_ops()
         assert cfg.heads % tp == 0 and cfg.kv_heads % tp == 0 and cfg.ffn % tp == 0
         self.cfg, self.max_seq, self.batch, self.tp, self.tp_rank, self.group = cfg, max_seq, batch, tp, tp_rank, group
@@ -192,9 +192,10 @@ class Decoder:
         self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.seq_len = torch.ones(batch, dtype=torch.int32, device=dev)
         self.next_tokens = torch.zeros(batch, dtype=torch.long, device=dev)
-        # Decode through GEMV chains (one launch per block besides attention) when the block's
-        # chain can run here: one GPU (the chain has no all-reduce), batch <= 2, and the weight
-        # slabs of consecutive phases fit shared memory.
+        # `chain`: decode through GEMV chains (one launch per block besides attention) where the
+        # block's chain can run: one GPU (the chain has no all-reduce), batch <= 2, and the
+        # weight slabs of consecutive phases fit shared memory.  Off by default: on B200 the
+        # chain is still slower than the separate launches it replaces.
         self.chain_ws = None
         if chain and tp == 1:
             h = torch.empty(batch, cfg.hidden, device=dev, dtype=dtype)
