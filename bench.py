@@ -70,17 +70,16 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic():
-    """DRAM bytes per GEMV launch from the committed ncu summary (key: value lines), if any."""
+def profile_traffic(alg_bytes_per_launch: float):
+    """DRAM bytes per GEMV launch: the committed ncu summary's measured DRAM/algorithmic byte
+    ratio (one full capture of a gate/up-shaped launch) applied to this run's average
+    algorithmic bytes per launch, since traffic grows in proportion to the planes read."""
     p = os.path.join(ROOT, "profiles", "gemv_llama2_7b_decode.txt")
     if not os.path.exists(p):
         return None
     for line in open(p):
-        if line.startswith("dram_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].split()[0])
-            except ValueError:
-                return None
+        if line.startswith("dram_per_alg_byte:"):
+            return round(float(line.split(":", 1)[1]) * alg_bytes_per_launch, 1)
     return None
 
 
@@ -357,7 +356,7 @@ def run_nq(args, world, rank, local):
                 "roofline": {"bound": "hbm", "kernel": "gemv_kernel (fused decode GEMV)",
                              "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 5), "peak_source": peak_kind,
-                             "traffic": profile_traffic(), "bytes_per_launch": round(alg_bytes, 1),
+                             "traffic": profile_traffic(alg_bytes), "bytes_per_launch": round(alg_bytes, 1),
                              "us_per_launch": round(us_launch, 3), "launches_measured": n_lin},
                 "cpu_baseline": cpu,
                 "clocks": clocks.summary(),
