@@ -116,6 +116,34 @@ NQ_API int nq_gemv_group(int dtype, const void *x, int64_t batch, int64_t in_fea
                          void *stream);
 
 /* ---------------------------------------------------------------------------------
+ * Grouped decode GEMV whose input is formed in the kernel's prologue from its neighbours'
+ * outputs -- the decoder's RMSNorm (with the residual add) before q/k/v and gate/up, and
+ * SiLU(gate) * up before down -- and whose `act` bit l puts layer l's output through SiLU
+ * (the SwiGLU gate, stored as dtype(silu(dtype(y)))).  No reference counterpart: the reference
+ * runs these neighbours as HF modules between its nanoquant_dyn_forward calls
+ * (src/nanoquant/kernel/test_decode.py).  The layers see x' where, with x_mode
+ *   NQ_CHAIN_X_PLAIN     x' = x
+ *   NQ_CHAIN_X_RMSNORM   h = dtype(x + x2) (h = x when x2 is NULL); residual_out = h when given;
+ *                        x' = dtype(norm_weight * dtype(h * rsqrt(mean(h^2) + eps)))
+ *   NQ_CHAIN_X_SILU_MUL  x' = dtype(dtype(silu(x)) * x2)
+ *   NQ_CHAIN_X_MUL       x' = dtype(x * x2)
+ * (the roundings of nq_rmsnorm and nq_silu_mul; the mean's summation order differs).
+ * Transformed inputs need batch <= 8, in_features % 8 == 0 and 16-byte aligned x, x2,
+ * norm_weight, residual_out and scale_pre.  Workspace as nq_gemv_group.
+ * ------------------------------------------------------------------------------- */
+typedef struct {
+    int x_mode;                /* NQ_CHAIN_X_* (defined below) */
+    float eps;                 /* NQ_CHAIN_X_RMSNORM */
+    const void *x;             /* [batch, in] */
+    const void *x2;            /* residual [batch, in] (RMSNORM, may be NULL) or second factor */
+    const void *norm_weight;   /* [in] (RMSNORM) */
+    void *residual_out;        /* [batch, in] (RMSNORM, may be NULL) */
+} nq_gemv_input;
+NQ_API int nq_gemv_group_ex(int dtype, const nq_gemv_input *input, int64_t batch,
+                            int64_t in_features, int n_layers, const nq_gemv_layer *layers, int act,
+                            void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------------------
  * Allocation-free decode GEMV.  No counterpart in the reference: its kernels allocate their
  * intermediate with the torch caching allocator on every call (gemv_kernel.cu:345-346).
  * For callers that cannot allocate device memory -- a plugin or custom-op interface that

@@ -36,6 +36,12 @@ class GemvLayer(ctypes.Structure):
                 ("scale_post", ctypes.c_void_p), ("y", ctypes.c_void_p)]
 
 
+class GemvInput(ctypes.Structure):
+    """nq_gemv_input of include/nq_b200.h."""
+    _fields_ = [("x_mode", ctypes.c_int), ("eps", ctypes.c_float), ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p),
+                ("norm_weight", ctypes.c_void_p), ("residual_out", ctypes.c_void_p)]
+
+
 class ChainPhase(ctypes.Structure):
     """nq_chain_phase of include/nq_b200.h."""
     _fields_ = [("n_layers", ctypes.c_int), ("x_mode", ctypes.c_int), ("act", ctypes.c_int), ("eps", ctypes.c_float),
@@ -66,6 +72,8 @@ _SIGNATURES = {
     "nq_gemv_static": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p,
                                   _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p,
                                   _c.c_void_p]),
+    "nq_gemv_group_ex": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_void_p, _c.c_int,
+                                    _c.c_void_p, _c.c_size_t, _c.c_void_p]),
     "nq_gemv_chain_workspace_bytes": (_c.c_size_t, [_c.c_int, _c.c_int64, _c.c_int, _c.c_void_p]),
     "nq_gemv_chain": (_c.c_int, [_c.c_int, _c.c_int64, _c.c_int, _c.c_void_p, _c.c_void_p, _c.c_size_t,
                                  _c.c_void_p]),

@@ -234,7 +234,14 @@ struct Params {
     int mode, x_in_smem, fold;
     int kbu2;                  // stage-2 K blocks per tile in the work split: the largest member's kb2
     int seg1, seg2;            // red slots per warp (seg_bound) in stage 1 / stage 2
-    uint32_t off_red, off_s2, off_x, off_xs2, off_v, off_u, off_s1;
+    // input transform of the single-group kernel (fold mode, x staged in shared memory):
+    int xmode;                 // ChainXMode; the input every member reads is x' (not x)
+    const void *x2;            // RMSNORM: added to x first (may be null); MUL / SILU_MUL: second factor
+    const void *nw;            // RMSNORM weight
+    void *res_out;             // RMSNORM: receives x (+ x2), written by the CTA owning stage-1 tile 0
+    float eps;
+    int act;                   // bit l: SiLU on member l's output
+    uint32_t off_red, off_s2, off_x, off_xs2, off_v, off_u, off_s1, off_x2, off_nw;
 };
 
 __device__ __forceinline__ int member_of1(const Params &p, int tile) {
@@ -253,6 +260,25 @@ __device__ __forceinline__ int member_of2(const Params &p, int tile) {
 __device__ __forceinline__ void seg_tiles(const Member &mb, int t2b, int t2e, int &a, int &b) {
     a = max(t2b, mb.t2_start);
     b = min(t2e, mb.t2_start + mb.tiles2);
+}
+
+__device__ __forceinline__ float block_sum_512(float v, float *sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();  // sh may still be read by a previous call
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) s += sh[i];
+    return s;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
+    const T *e = reinterpret_cast<const T *>(&v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = Elem<T>::to_f(e[j]);
 }
 
 // ------------------------------------------------------------------ stage bodies
@@ -500,9 +526,74 @@ __device__ __forceinline__ void stage2_finish(const Params &p, const float *red,
     }
 }
 
+// x' in place in shared memory (x rows, x2 rows and the norm weight staged by the prologue):
+// RMSNORM: h = dtype(x + x2) (x alone without x2), res_out = h (by `owner`),
+// x' = dtype(w * dtype(h * rsqrt(mean(h^2) + eps))); MUL: x' = dtype(x * x2);
+// SILU_MUL: x' = dtype(dtype(silu(x)) * x2).  The same roundings as the separate kernels.
+template <typename T>
+__device__ __forceinline__ void x_transform(const Params &p, T *xs, const T *x2s, const T *nws, int in_pad, bool owner,
+                                            float *sred) {
+    using E = Elem<T>;
+    const int n8 = p.in_f / 8;
+    for (int b = 0; b < p.batch; ++b) {
+        uint4 *xr = reinterpret_cast<uint4 *>(xs + (size_t)b * in_pad);
+        const uint4 *x2r = reinterpret_cast<const uint4 *>(x2s + (size_t)b * in_pad);
+        if (p.xmode == kChainNorm) {
+            uint4 *ro = owner && p.res_out
+                            ? reinterpret_cast<uint4 *>(static_cast<T *>(p.res_out) + (size_t)b * p.in_f)
+                            : nullptr;
+            float ss = 0.f;
+            for (int ch = threadIdx.x; ch < n8; ch += kThreads) {
+                float h[8];
+                unpack8<T>(xr[ch], h);
+                if (p.x2) {
+                    float r[8];
+                    unpack8<T>(x2r[ch], r);
+                    T o[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        o[e] = E::rn(h[e] + r[e]);
+                        h[e] = E::to_f(o[e]);
+                    }
+                    xr[ch] = *reinterpret_cast<const uint4 *>(o);
+                }
+                if (ro) ro[ch] = xr[ch];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss += h[e] * h[e];
+            }
+            const float inv = rsqrtf(block_sum_512(ss, sred) / (float)p.in_f + p.eps);
+            const uint4 *wr = reinterpret_cast<const uint4 *>(nws);
+            for (int ch = threadIdx.x; ch < n8; ch += kThreads) {
+                float h[8], w[8];
+                unpack8<T>(xr[ch], h);
+                unpack8<T>(wr[ch], w);
+                T o[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) o[e] = E::rn(w[e] * E::to_f(E::rn(h[e] * inv)));
+                xr[ch] = *reinterpret_cast<const uint4 *>(o);
+            }
+        } else {
+            const bool silu = p.xmode == kChainSiluMul;
+            for (int ch = threadIdx.x; ch < n8; ch += kThreads) {
+                float a[8], u[8];
+                unpack8<T>(xr[ch], a);
+                unpack8<T>(x2r[ch], u);
+                T o[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float sg = silu ? E::to_f(E::rn(a[e] / (1.f + expf(-a[e])))) : a[e];
+                    o[e] = E::rn(sg * u[e]);
+                }
+                xr[ch] = *reinterpret_cast<const uint4 *>(o);
+            }
+        }
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float sred[kWarps];
     using E = Elem<T>;
     const int tid = threadIdx.x;
     const int G = gridDim.x, c = blockIdx.x;
@@ -546,7 +637,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                                               p.v_rows);
             }
             if (vec_rows) bytes0 += (uint32_t)p.in_f * 2u * ((uint32_t)p.nm + (p.x_in_smem ? (uint32_t)p.batch : 0u));
+            // transform inputs (host guarantees vec_rows and x in shared memory for them)
+            if (p.x2) bytes0 += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
+            if (p.xmode == kChainNorm) bytes0 += (uint32_t)p.in_f * 2u;
             mbar_arrive_expect_tx(&bars[0], bytes0);
+            if (p.x2)
+                for (int b = 0; b < p.batch; ++b)
+                    bulk_g2s_pieces(smem + p.off_x2 + (size_t)b * in_pad * 2,
+                                    static_cast<const T *>(p.x2) + (size_t)b * p.in_f, (uint32_t)p.in_f * 2u, &bars[0]);
+            if (p.xmode == kChainNorm) bulk_g2s_pieces(smem + p.off_nw, p.nw, (uint32_t)p.in_f * 2u, &bars[0]);
             if (vec_rows) {
                 for (int l = 0; l < p.nm; ++l)
                     bulk_g2s_pieces(s2s + (size_t)l * in_pad, p.m[l].s2, (uint32_t)p.in_f * 2u, &bars[0]);
@@ -627,6 +726,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     if (has1) {
         ok = mbar_wait(&bars[0], 0, &p.ctrl->status);
         const int nxc = 2 * p.batch;  // folded B columns per member: hi / lo of x*s2 per batch row
+        if (p.xmode != kChainPlain) {
+            x_transform<T>(p, xs, reinterpret_cast<const T *>(smem + p.off_x2), reinterpret_cast<const T *>(smem + p.off_nw),
+                           in_pad, t1b == 0, sred);
+            __syncthreads();
+        }
         if (p.fold) {
             // xs2[l][col][k] = bf16 hi (col even) / lo (col odd) of x[col/2][k] * s2_l[k]
             const int chunks = in_pad / 8;
@@ -667,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         else
             stage2_items<T, 2>(p, uch, red, t2b, t2e, ok, nullptr);
         __syncthreads();
-        stage2_finish<T>(p, red, s1s, t2b, t2e, nullptr, 0);
+        stage2_finish<T>(p, red, s1s, t2b, t2e, nullptr, p.act);
     }
 }
 
@@ -718,6 +822,10 @@ static size_t layout(Params &p, int tiles1, int tiles2, bool stage1, bool stage2
         off = align128(off + (size_t)p.nm * in_pad * 2);
         p.off_x = (uint32_t)off;
         if (x_in_smem) off = align128(off + (size_t)p.batch * in_pad * 2);
+        p.off_x2 = (uint32_t)off;  // transform inputs, staged next to x
+        if (x_in_smem && p.x2) off = align128(off + (size_t)p.batch * in_pad * 2);
+        p.off_nw = (uint32_t)off;
+        if (x_in_smem && p.xmode == kChainNorm) off = align128(off + (size_t)in_pad * 2);
         p.off_xs2 = (uint32_t)off;
         if (fold && x_in_smem) {
             p.fold = 1;
@@ -748,6 +856,7 @@ static int make_plan(int dev, const Params &base, Plan &plan) {
     const int variants[3][2] = {{1, 1}, {1, 0}, {0, 0}};  // (x in smem, fold)
     for (const auto &v : variants) {
         if (v[1] && p.batch > kFoldMaxBatch) continue;
+        if (p.xmode != kChainPlain && !v[0]) continue;  // a transformed input lives in shared memory
         Params q = p;
         q.mode = kFused;
         const size_t need = layout(q, tpc1, tpc2, true, true, v[0] != 0, v[1] != 0);
@@ -762,6 +871,7 @@ static int make_plan(int dev, const Params &base, Plan &plan) {
     // two ordinary launches, one 16-row tile per CTA
     for (const auto &v : variants) {
         if (v[1] && p.batch > kFoldMaxBatch) continue;
+        if (p.xmode != kChainPlain && !v[0]) continue;
         Params q1 = p, q2 = p;
         q1.mode = kStage1;
         q2.mode = kStage2;
@@ -816,8 +926,37 @@ static int launch(const Plan &plan, cudaStream_t stream) {
 
 static inline size_t tb_bytes(int64_t rank) { return (size_t)16 * (size_t)((rank + 63) / 64) * 64 * 2; }
 
-static int group_impl(int dtype, const void *x, int64_t batch, int64_t in_features, int n, const nq_gemv_layer *layers,
-                      void *workspace, size_t workspace_bytes, void *stream) {
+// The input of a launch group: x, or x' formed from x (and x2, norm_weight) as nq_gemv_input says.
+struct GroupInput {
+    const void *x = nullptr;
+    int xmode = kChainPlain;
+    const void *x2 = nullptr, *nw = nullptr;
+    void *res_out = nullptr;
+    float eps = 0.f;
+    int act = 0;
+};
+
+static int group_impl(int dtype, const GroupInput &in, int64_t batch, int64_t in_features, int n,
+                      const nq_gemv_layer *layers, void *workspace, size_t workspace_bytes, void *stream) {
+    const void *x = in.x;
+    if (n >= 1 && n <= kMaxGroup) {
+        if (in.act & ~((1 << n) - 1)) return fail(NQ_ERR_INVALID_ARGUMENT, "act bit beyond the %d layers", n);
+        if (in.xmode != kChainPlain) {
+            if (in.xmode != kChainNorm && in.xmode != kChainMul && in.xmode != kChainSiluMul)
+                return fail(NQ_ERR_INVALID_ARGUMENT, "unknown x_mode %d", in.xmode);
+            if (batch > kMaxBatch)
+                return fail(NQ_ERR_UNSUPPORTED, "a transformed input supports batch <= %d (got %lld)", kMaxBatch,
+                            (long long)batch);
+            if (in_features % 8) return fail(NQ_ERR_UNSUPPORTED, "a transformed input needs in_features %% 8 == 0");
+            if (in.xmode != kChainNorm && !in.x2) return fail(NQ_ERR_INVALID_ARGUMENT, "x_mode needs x2");
+            if (in.xmode == kChainNorm && !in.nw) return fail(NQ_ERR_INVALID_ARGUMENT, "RMSNORM needs norm_weight");
+            uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(in.x2) |
+                           reinterpret_cast<uintptr_t>(in.nw) | reinterpret_cast<uintptr_t>(in.res_out);
+            for (int l = 0; l < n && layers; ++l) al |= reinterpret_cast<uintptr_t>(layers[l].scale_pre);
+            if (al & 15)
+                return fail(NQ_ERR_INVALID_ARGUMENT, "x, x2, norm_weight, residual_out and scale_pre must be 16-byte aligned");
+        }
+    }
     if (dtype != NQ_DTYPE_F16 && dtype != NQ_DTYPE_BF16)
         return fail(NQ_ERR_UNSUPPORTED, "dtype must be NQ_DTYPE_F16 or NQ_DTYPE_BF16 (got %d)", dtype);
     if (n < 1 || n > kMaxGroup) return fail(NQ_ERR_INVALID_ARGUMENT, "a group holds 1..%d layers (got %d)", kMaxGroup, n);
@@ -893,6 +1032,12 @@ static int group_impl(int dtype, const void *x, int64_t batch, int64_t in_featur
     }
     base.tiles1 = t1;
     base.tiles2 = t2;
+    base.xmode = in.xmode;
+    base.x2 = in.x2;
+    base.nw = in.nw;
+    base.res_out = in.res_out;
+    base.eps = in.eps;
+    base.act = in.act;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     for (int64_t b0 = 0; b0 < batch; b0 += kMaxBatch) {
         Params p = base;
@@ -1013,25 +1158,6 @@ __device__ __forceinline__ void chain_issue(const Params &p, uint8_t *smem, uint
             for (int i = (int)(s1_bulk / 2) + tid; i < r1 - r0; i += kThreads) s1dst[i] = s1src[i];
         }
     }
-}
-
-__device__ __forceinline__ float block_sum_512(float v, float *sh) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    __syncthreads();  // sh may still be read by a previous call
-    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
-    __syncthreads();
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < kWarps; ++i) s += sh[i];
-    return s;
-}
-
-template <typename T>
-__device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
-    const T *e = reinterpret_cast<const T *>(&v);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = Elem<T>::to_f(e[j]);
 }
 
 // xs2[l][2b (+1)][k] = bf16 hi (lo) of x'[b][k] * s2_l[k], x' formed per ph.xmode from global
@@ -1472,7 +1598,23 @@ size_t nq_gemv_group_workspace_bytes(int n_layers, const int64_t *ranks) {
 
 int nq_gemv_group(int dtype, const void *x, int64_t batch, int64_t in_features, int n_layers,
                   const nq_gemv_layer *layers, void *workspace, size_t workspace_bytes, void *stream) {
-    return nq::gemv::group_impl(dtype, x, batch, in_features, n_layers, layers, workspace, workspace_bytes, stream);
+    nq::gemv::GroupInput in;
+    in.x = x;
+    return nq::gemv::group_impl(dtype, in, batch, in_features, n_layers, layers, workspace, workspace_bytes, stream);
+}
+
+int nq_gemv_group_ex(int dtype, const nq_gemv_input *input, int64_t batch, int64_t in_features, int n_layers,
+                     const nq_gemv_layer *layers, int act, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!input) return nq::fail(NQ_ERR_INVALID_ARGUMENT, "null input descriptor");
+    nq::gemv::GroupInput in;
+    in.x = input->x;
+    in.xmode = input->x_mode;
+    in.x2 = input->x2;
+    in.nw = input->norm_weight;
+    in.res_out = input->residual_out;
+    in.eps = input->eps;
+    in.act = act;
+    return nq::gemv::group_impl(dtype, in, batch, in_features, n_layers, layers, workspace, workspace_bytes, stream);
 }
 
 int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features, const void *scale_pre,
@@ -1487,7 +1629,9 @@ int nq_gemv(int dtype, const void *x, int64_t batch, int64_t in_features, const 
     L.out_features = out_features;
     L.scale_post = scale_post;
     L.y = y;
-    return nq::gemv::group_impl(dtype, x, batch, in_features, 1, &L, workspace, workspace_bytes, stream);
+    nq::gemv::GroupInput in;
+    in.x = x;
+    return nq::gemv::group_impl(dtype, in, batch, in_features, 1, &L, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -448,6 +448,55 @@ std::vector<at::Tensor> run_group(const at::Tensor &x, const std::vector<LayerAr
     return ys;
 }
 
+// Grouped GEMV on x' formed in the prologue (RMSNorm with residual, SiLU*up, x*up) with optional
+// SiLU on chosen outputs: one launch for what the decoder otherwise runs as 2-3.
+std::vector<at::Tensor> run_group_ex(const at::Tensor &x, const std::vector<LayerArgs> &ls, int64_t x_mode,
+                                     const std::optional<at::Tensor> &x2, const std::optional<at::Tensor> &nw,
+                                     double eps, const std::optional<at::Tensor> &res_out, int64_t act) {
+    c10::cuda::CUDAGuard guard(x.device());
+    const auto st = x.scalar_type();
+    nq_gemv_input in{};
+    in.x_mode = (int)x_mode;
+    in.eps = (float)eps;
+    in.x = x.data_ptr();
+    if (x2.has_value() && x2->defined()) {
+        CHECK_CUDA_CONT((*x2), st);
+        TORCH_CHECK(x2->numel() == x.numel(), "x2 must have the shape of x");
+        in.x2 = x2->data_ptr();
+    }
+    if (nw.has_value() && nw->defined()) {
+        CHECK_CUDA_CONT((*nw), st);
+        TORCH_CHECK(nw->numel() == ls[0].in_f, "norm_weight must have in_features values");
+        in.norm_weight = nw->data_ptr();
+    }
+    if (res_out.has_value() && res_out->defined()) {
+        CHECK_CUDA_CONT((*res_out), st);
+        TORCH_CHECK(res_out->numel() == x.numel(), "residual_out must have the shape of x");
+        in.residual_out = res_out->data_ptr();
+    }
+    std::vector<nq_gemv_layer> desc(ls.size());
+    std::vector<int64_t> ranks(ls.size());
+    std::vector<at::Tensor> ys;
+    for (size_t i = 0; i < ls.size(); ++i) {
+        const LayerArgs &a = ls[i];
+        ys.push_back(at::empty({a.rows, a.out_f}, x.options()));
+        desc[i].scale_pre = a.s2.data_ptr();
+        desc[i].v_bits = a.vbits.data_ptr<int32_t>();
+        desc[i].rank = a.rank;
+        desc[i].scale_mid = a.smid ? a.smid->data_ptr() : nullptr;
+        desc[i].u_bits = a.ubits.data_ptr<int32_t>();
+        desc[i].out_features = a.out_f;
+        desc[i].scale_post = a.s1.data_ptr();
+        desc[i].y = ys.back().data_ptr();
+        ranks[i] = a.rank;
+    }
+    const size_t wsb = nq_gemv_group_workspace_bytes((int)ls.size(), ranks.data());
+    at::Tensor ws = workspace_for(x, wsb);
+    NQ_TORCH_CHECK(nq_gemv_group_ex(dtype_code(st), &in, ls[0].rows, ls[0].in_f, (int)ls.size(), desc.data(),
+                                    (int)act, ws.data_ptr(), (size_t)ws.numel(), cur_stream(x)));
+    return ys;
+}
+
 std::vector<LayerArgs> check_group(const at::Tensor &x, const std::vector<at::Tensor> &s2,
                                    const std::vector<at::Tensor> &vbits,
                                    const std::vector<std::optional<at::Tensor>> &smid,
@@ -469,6 +518,33 @@ std::vector<at::Tensor> gemv_group_cuda(const at::Tensor &x, at::TensorList s2, 
     auto ys = run_group(x, ls);
     if (x.dim() == 1)
         for (auto &y : ys) y = y.squeeze(0);
+    return ys;
+}
+
+std::vector<at::Tensor> gemv_group_ex_cuda(const at::Tensor &x, const std::optional<at::Tensor> &x2,
+                                           const std::optional<at::Tensor> &norm_weight, double eps, int64_t x_mode,
+                                           const std::optional<at::Tensor> &residual_out, int64_t act,
+                                           at::TensorList s2, at::TensorList vbits,
+                                           const c10::List<std::optional<at::Tensor>> &smid, at::TensorList ubits,
+                                           at::TensorList s1) {
+    std::vector<std::optional<at::Tensor>> sm(smid.begin(), smid.end());
+    auto ls = check_group(x, s2.vec(), vbits.vec(), sm, ubits.vec(), s1.vec());
+    auto ys = run_group_ex(x, ls, x_mode, x2, norm_weight, eps, residual_out, act);
+    if (x.dim() == 1)
+        for (auto &y : ys) y = y.squeeze(0);
+    return ys;
+}
+
+std::vector<at::Tensor> group_ex_meta(const at::Tensor &x, const std::optional<at::Tensor> &,
+                                      const std::optional<at::Tensor> &, double, int64_t, const std::optional<at::Tensor> &,
+                                      int64_t, at::TensorList, at::TensorList, const c10::List<std::optional<at::Tensor>> &,
+                                      at::TensorList, at::TensorList s1) {
+    std::vector<at::Tensor> ys;
+    for (const auto &s : s1) {
+        auto shape = x.sizes().vec();
+        shape.back() = s.numel();
+        ys.push_back(at::empty(shape, x.options()));
+    }
     return ys;
 }
 
@@ -548,6 +624,10 @@ TORCH_LIBRARY(nq_b200, m) {
     m.def(
         "linear_group(Tensor x, Tensor[] scale_pre, Tensor[] v_bits, Tensor?[] scale_mid, Tensor[] u_bits, "
         "Tensor[] scale_post) -> Tensor[]");
+    m.def(
+        "gemv_group_ex(Tensor x, Tensor? x2, Tensor? norm_weight, float eps, int x_mode, Tensor(a!)? residual_out, "
+        "int act, Tensor[] scale_pre, Tensor[] v_bits, Tensor?[] scale_mid, Tensor[] u_bits, Tensor[] scale_post) "
+        "-> Tensor[]");
 }
 
 TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
@@ -563,6 +643,7 @@ TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
     m.impl("decode_attention_rope", &decode_attention_rope_cuda);
     m.impl("silu_mul", &silu_mul_cuda);
     m.impl("gemv_group", &gemv_group_cuda);
+    m.impl("gemv_group_ex", &gemv_group_ex_cuda);
     m.impl("linear_group", &linear_group_cuda);
 }
 
@@ -579,5 +660,6 @@ TORCH_LIBRARY_IMPL(nq_b200, Meta, m) {
     m.impl("decode_attention_rope", &decode_attention_rope_meta);
     m.impl("silu_mul", &silu_mul_meta);
     m.impl("gemv_group", &group_meta);
+    m.impl("gemv_group_ex", &group_ex_meta);
     m.impl("linear_group", &group_meta);
 }

@@ -196,6 +196,9 @@ class Decoder:
         # block's chain can run: one GPU (the chain has no all-reduce), batch <= 2, and the
         # weight slabs of consecutive phases fit shared memory.  Off by default: on B200 the
         # chain is still slower than the separate launches it replaces.
+        # RMSNorm / SiLU*up folded into the GEMV prologues and the gate's SiLU into its epilogue
+        # (nq_gemv_group_ex); batches above 8 use the separate kernels.
+        self.fuse_neighbours = True
         self.chain_ws = None
         if chain and tp == 1:
             h = torch.empty(batch, cfg.hidden, device=dev, dtype=dtype)
@@ -294,10 +297,41 @@ class Decoder:
         return x @ self.lm_head.t()
 
     @torch.no_grad()
+    def _step_logits_fused(self) -> torch.Tensor:
+        """Five launches per block: q/k/v with RMSNorm(x + residual) in its prologue, attention
+        (RoPE + cache write fused), o, gate/up with RMSNorm(o + residual) in its prologue and
+        SiLU on the gate in its epilogue, down with gate * up in its prologue."""
+        cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
+        ops, eps = torch.ops.nq_b200, cfg.rms_eps
+        d = F.embedding(self.tokens, self.embed)  # the first block's input; no residual yet
+        residual = None
+        for li, lay in enumerate(self.layers):
+            g = lay["qkv"]
+            res = torch.empty_like(d)
+            q, k, v = ops.gemv_group_ex(d, residual, lay["in_norm"], eps, nqchain.RMSNORM, res, 0, g.s2, g.vb, g.smid,
+                                        g.ub, g.s1)
+            residual = res
+            a = ops.decode_attention_rope(q.view(B, self.hq, D), k.view(B, self.hkv, D), v.view(B, self.hkv, D),
+                                          self.pos, self.k_cache[li], self.v_cache[li], cfg.rope_theta)
+            o = self._all_reduce(lay["o"](a.view(B, self.hq * D)))
+            g = lay["gate_up"]
+            res = torch.empty_like(o)
+            gate, up = ops.gemv_group_ex(o, residual, lay["post_norm"], eps, nqchain.RMSNORM, res, 1, g.s2, g.vb,
+                                         g.smid, g.ub, g.s1)
+            residual = res
+            dn = lay["down"]
+            d = self._all_reduce(ops.gemv_group_ex(gate, up, None, 0.0, nqchain.MUL, None, 0, [dn.s2], [dn.vb],
+                                                   [dn.smid], [dn.ub], [dn.s1])[0])
+        x, _ = ops.rmsnorm(d, residual, self.final_norm, eps)
+        return x @ self.lm_head.t()
+
+    @torch.no_grad()
     def step_logits(self) -> torch.Tensor:
         """Logits for the current tokens at the current positions (writes the caches)."""
         if self.chain_ws is not None:
             return self._step_logits_chain()
+        if self.fuse_neighbours and self.batch <= 8:
+            return self._step_logits_fused()
         cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
         h = F.embedding(self.tokens, self.embed)
         residual = None

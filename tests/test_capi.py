@@ -145,3 +145,28 @@ def test_chain_planning_without_a_gpu():
     big = [chain.Phase([_fake_layer(64, 20480, 64)], wide, chain.RMSNORM, norm_weight=torch.empty(20480))]
     assert chain.workspace_bytes(big, 1) == 0 and "RMSNorm" in chain.why_not()
     assert chain.workspace_bytes(block * 2, 1) == 0  # more than NQ_CHAIN_MAX_PHASES
+
+
+@pytest.mark.parametrize("case", ["mode", "no_x2", "no_weight", "unaligned", "act", "batch"])
+def test_group_ex_rejects_bad_input_descriptors_on_host(case):
+    lib = _lib.cuda_lib()
+    fake = 0x10000  # never dereferenced: the descriptor checks run first
+    inp = _lib.GemvInput(x_mode=1, eps=1e-5, x=fake, x2=fake, norm_weight=fake, residual_out=fake)
+    layer = _lib.GemvLayer(scale_pre=fake, v_bits=fake, rank=64, scale_mid=None, u_bits=fake, out_features=64,
+                           scale_post=fake, y=fake)
+    batch, act = 1, 0
+    if case == "mode":
+        inp.x_mode = 9
+    elif case == "no_x2":
+        inp.x_mode, inp.x2 = 3, None
+    elif case == "no_weight":
+        inp.norm_weight = None
+    elif case == "unaligned":
+        inp.x2 = fake + 2
+    elif case == "act":
+        act = 2  # bit beyond the single layer
+    elif case == "batch":
+        batch = 9
+    st = lib.nq_gemv_group_ex(0, ctypes.byref(inp), batch, 256, 1, ctypes.byref(layer), act, None, 0, None)
+    assert st in (_lib.NQ_ERR_INVALID_ARGUMENT, _lib.NQ_ERR_UNSUPPORTED), st
+    assert lib.nq_last_error_message()

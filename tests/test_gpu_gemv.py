@@ -206,3 +206,80 @@ def test_gemv_group_matches_single_layers(shapes, batch, dtype):
                                        [d.ub for d in ds], [d.s1 for d in ds])
     for y, y2 in zip(ys, ys2):
         assert torch.equal(y, y2)
+
+
+def _ex_layers(shapes, dt, seed):
+    from nanoquant_b200.decoder import QuantLinearShard, _random_planes
+    out = []
+    for i, (o, n, r) in enumerate(shapes):
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed + i)
+        vb, ub = _random_planes(g, r, n, "cuda"), _random_planes(g, o, r, "cuda")
+        s2 = (torch.rand(n, generator=g, device="cuda") + 0.5).to(dt) / n ** 0.5
+        s1 = (torch.rand(o, generator=g, device="cuda") + 0.5).to(dt) / r ** 0.5
+        out.append(QuantLinearShard(vb, ub, s2, None, s1))
+    return out
+
+
+def _lists(Ls):
+    return [L.s2 for L in Ls], [L.vb for L in Ls], [L.smid for L in Ls], [L.ub for L in Ls], [L.s1 for L in Ls]
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("batch", [1, 2, 5])
+def test_group_ex_input_modes_match_separate_kernels(dt, batch):
+    """nq_gemv_group_ex: x' formed in the prologue.  SILU_MUL and MUL give the bits of
+    silu_mul / a multiply followed by the grouped GEMV; RMSNORM matches rmsnorm followed by
+    the grouped GEMV to rel-L2 1e-3 (the mean is summed in another order) and writes the same
+    residual bits; act puts the chosen outputs through SiLU."""
+    ops = torch.ops.nq_b200
+    Ls = _ex_layers([(1000, 4096, 300), (512, 4096, 160)], dt, 7)
+    lists = _lists(Ls)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(batch)
+    x = torch.randn(batch, 4096, generator=g, device="cuda").to(dt)
+    x2 = torch.randn(batch, 4096, generator=g, device="cuda").to(dt)
+    w = (torch.rand(4096, generator=g, device="cuda") + 0.5).to(dt)
+    # SILU_MUL and MUL: bit-identical to the separate kernels
+    got = ops.gemv_group_ex(x, x2, None, 0.0, 2, None, 0, *lists)
+    want = ops.gemv_group(ops.silu_mul(x, x2), *lists)
+    for a, b in zip(got, want):
+        assert torch.equal(a, b)
+    got = ops.gemv_group_ex(x, x2, None, 0.0, 3, None, 0, *lists)
+    want = ops.gemv_group((x.float() * x2.float()).to(dt), *lists)
+    for a, b in zip(got, want):
+        assert torch.equal(a, b)
+    # RMSNORM with and without the residual
+    for res_in in (x2, None):
+        res_out = torch.empty_like(x)
+        got = ops.gemv_group_ex(x, res_in, w, 1e-5, 1, res_out, 0, *lists)
+        xn, r = ops.rmsnorm(x, res_in, w, 1e-5)
+        want = ops.gemv_group(xn, *lists)
+        assert torch.equal(res_out, r)
+        for a, b in zip(got, want):
+            assert orc.rel_l2(a.float().cpu().numpy(), b.float().cpu().numpy()) <= 1e-3
+    # act on the first member only
+    got = ops.gemv_group_ex(x, None, None, 0.0, 0, None, 1, *lists)
+    want = ops.gemv_group(x, *lists)
+    gate = want[0].float()
+    assert orc.rel_l2(got[0].float().cpu().numpy(), (gate / (1 + torch.exp(-gate))).cpu().numpy()) <= 2e-3
+    assert torch.equal(got[1], want[1])
+
+
+def test_decoder_fused_prologues_match_separate_kernels():
+    """The decode step with the neighbours in the GEMV prologues/epilogue decodes the same
+    tokens as the step with separate RMSNorm / SiLU kernels."""
+    from nanoquant_b200.decoder import TINY, Decoder
+    prompt = torch.randint(0, TINY.vocab, (29,), generator=torch.Generator().manual_seed(4)).cuda()
+    runs = []
+    for fused in (True, False):
+        dec = Decoder(TINY, max_seq=80, seed=5, device="cuda")
+        dec.fuse_neighbours = fused
+        dec.prefill(prompt)
+        logits = dec.step_logits().float()
+        dec.tokens.fill_(int(torch.argmax(logits[0])))
+        dec.pos.add_(1)
+        dec.seq_len.add_(1)
+        runs.append((logits.cpu(), [int(dec.step()[0]) for _ in range(8)]))
+    assert orc.rel_l2(runs[0][0].numpy(), runs[1][0].numpy()) <= 1e-2
+    assert runs[0][1] == runs[1][1]
