@@ -284,9 +284,11 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
 // ------------------------------------------------------------------ stage bodies
 // Shared by the single-group kernel and the chain kernel.  Stage 1: this CTA's tiles
 // [t1b, t1e) split over the warps by K-block units (warp_units), partial 16x8 tiles into `red`.
-template <typename T>
+// FOLD: 1 compiles only the folded-operand path, -1 decides at run time (p.fold).
+template <typename T, int FOLD = -1>
 __device__ __forceinline__ void stage1_items(const Params &p, const uint32_t *vch, const T *s2s, const T *xs,
                                             const __nv_bfloat16 *xs2, float *red, int t1b, int t1e, bool ok) {
+    const bool fold = FOLD >= 0 ? FOLD != 0 : p.fold != 0;
     using E = Elem<T>;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
@@ -309,7 +311,7 @@ __device__ __forceinline__ void stage1_items(const Params &p, const uint32_t *vc
         const uint32_t *rowA = vch + (size_t)(lt * 16 + g) * p.wvs;
         const uint32_t *rowB = rowA + (size_t)8 * p.wvs;
         float acc[4][4] = {};
-        if (p.fold) {
+        if (fold) {
             const __nv_bfloat16 *xcol = xs2 + ((size_t)l * nxc + g) * in_pad;
 #pragma unroll 2
             for (int kb = kbeg; kb < kend; ++kb) {
@@ -368,15 +370,16 @@ __device__ __forceinline__ void stage1_items(const Params &p, const uint32_t *vc
 
 // Stage 1, second half: sum the warps' partials, apply scale_mid, store t as bf16 (hi, lo) into
 // each member's stage-2 operand, and zero its K padding (the CTA owning the member's last tile).
-template <typename T>
+template <typename T, int FOLD = -1>
 __device__ __forceinline__ void stage1_finish(const Params &p, const float *red, int t1b, int t1e) {
     using E = Elem<T>;
+    const bool fold = FOLD >= 0 ? FOLD != 0 : p.fold != 0;
     const int tid = threadIdx.x;
     const int ntiles = t1e - t1b, U = ntiles * p.kb1;
     for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
         const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
         const int b = rem >> 4, row = rem & 15;
-        const float s0 = p.fold ? sum_partials(red, U, p.kb1, p.seg1, lt, row * 8 + 2 * b, true)
+        const float s0 = fold ? sum_partials(red, U, p.kb1, p.seg1, lt, row * 8 + 2 * b, true)
                                 : sum_partials(red, U, p.kb1, p.seg1, lt, row * 8 + b, false);
         float s = s0;
         const int tile = t1b + lt;
@@ -590,11 +593,16 @@ __device__ __forceinline__ void x_transform(const Params &p, T *xs, const T *x2s
     }
 }
 
-template <typename T>
+// DECODE = true: the instantiation for fused launches with x staged and folded (batch <= 2,
+// the decode case) -- only that path is compiled, which keeps its code small enough for the
+// instruction cache; DECODE = false decides every variant at run time.
+template <typename T, bool DECODE>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float sred[kWarps];
     using E = Elem<T>;
+    const bool x_in_smem = DECODE || p.x_in_smem;
+    const bool fold = DECODE || p.fold;
     const int tid = threadIdx.x;
     const int G = gridDim.x, c = blockIdx.x;
     const bool do1 = (p.mode & kStage1) != 0, do2 = (p.mode & kStage2) != 0;
@@ -636,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                     bytes0 += slab_bulk_bytes(16 * (a - mb.t1_start), min(16 * (b - mb.t1_start), mb.rank), p.wv,
                                               p.v_rows);
             }
-            if (vec_rows) bytes0 += (uint32_t)p.in_f * 2u * ((uint32_t)p.nm + (p.x_in_smem ? (uint32_t)p.batch : 0u));
+            if (vec_rows) bytes0 += (uint32_t)p.in_f * 2u * ((uint32_t)p.nm + (x_in_smem ? (uint32_t)p.batch : 0u));
             // transform inputs (host guarantees vec_rows and x in shared memory for them)
             if (p.x2) bytes0 += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
             if (p.xmode == kChainNorm) bytes0 += (uint32_t)p.in_f * 2u;
@@ -649,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             if (vec_rows) {
                 for (int l = 0; l < p.nm; ++l)
                     bulk_g2s_pieces(s2s + (size_t)l * in_pad, p.m[l].s2, (uint32_t)p.in_f * 2u, &bars[0]);
-                if (p.x_in_smem) {
+                if (x_in_smem) {
                     if (in_pad == p.in_f)
                         bulk_g2s_pieces(xs, p.x, (uint32_t)p.batch * (uint32_t)p.in_f * 2u, &bars[0]);
                     else
@@ -674,7 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 stage_row<T>(s2s + (size_t)l * in_pad, static_cast<const T *>(p.m[l].s2), p.in_f, in_pad);
             }
         }
-        if (p.x_in_smem)
+        if (x_in_smem)
             for (int b = 0; b < p.batch; ++b) {
                 if (vec_rows)
                     zero_tail<T>(xs + (size_t)b * in_pad, p.in_f, in_pad);
@@ -731,7 +739,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                            in_pad, t1b == 0, sred);
             __syncthreads();
         }
-        if (p.fold) {
+        if (fold) {
             // xs2[l][col][k] = bf16 hi (col even) / lo (col odd) of x[col/2][k] * s2_l[k]
             const int chunks = in_pad / 8;
             for (int i = tid; i < p.nm * p.batch * chunks; i += kThreads) {
@@ -752,9 +760,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
             __syncthreads();
         }
-        stage1_items<T>(p, vch, s2s, xs, xs2, red, t1b, t1e, ok);
+        stage1_items<T, DECODE ? 1 : -1>(p, vch, s2s, xs, xs2, red, t1b, t1e, ok);
         __syncthreads();
-        stage1_finish<T>(p, red, t1b, t1e);
+        stage1_finish<T, DECODE ? 1 : -1>(p, red, t1b, t1e);
     }
 
     if (p.mode == kFused) {
@@ -766,7 +774,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     // ------------------------------------------------------------------ stage 2
     if (has2) {
         if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
-        if (p.batch <= 4)
+        if (DECODE || p.batch <= 4)
             stage2_items<T, 1>(p, uch, red, t2b, t2e, ok, nullptr);
         else
             stage2_items<T, 2>(p, uch, red, t2b, t2e, ok, nullptr);
@@ -897,12 +905,15 @@ static int launch(const Plan &plan, cudaStream_t stream) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             device_info(dev).max_smem_optin - kStaticSmemReserve);
+        const int cap = device_info(dev).max_smem_optin - kStaticSmemReserve;
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemv_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
         attr_set[dev] = true;
     }
     if (plan.mode == kFused) {
+        const bool decode = plan.prm.fold && plan.prm.x_in_smem && plan.prm.batch <= 4;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(plan.grid);
         cfg.blockDim = dim3(kThreads);
@@ -913,13 +924,14 @@ static int launch(const Plan &plan, cudaStream_t stream) {
         attr[0].val.cooperative = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<T>, plan.prm);
+        cudaError_t e = decode ? cudaLaunchKernelEx(&cfg, gemv_kernel<T, true>, plan.prm)
+                               : cudaLaunchKernelEx(&cfg, gemv_kernel<T, false>, plan.prm);
         return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv fused launch");
     }
-    gemv_kernel<T><<<plan.grid1, kThreads, plan.smem1, stream>>>(plan.prm1);
+    gemv_kernel<T, false><<<plan.grid1, kThreads, plan.smem1, stream>>>(plan.prm1);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gemv stage-1 launch");
-    gemv_kernel<T><<<plan.grid2, kThreads, plan.smem2, stream>>>(plan.prm2);
+    gemv_kernel<T, false><<<plan.grid2, kThreads, plan.smem2, stream>>>(plan.prm2);
     e = cudaGetLastError();
     return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv stage-2 launch");
 }
@@ -1274,10 +1286,10 @@ template <typename T>
 __device__ __forceinline__ void chain_stage1(const Params &p, uint8_t *smem, int t1b, int t1e, bool ok) {
     const __nv_bfloat16 *xs2 = reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2);
     float *red = reinterpret_cast<float *>(smem + p.off_red);
-    stage1_items<T>(p, reinterpret_cast<const uint32_t *>(smem + p.off_v), reinterpret_cast<const T *>(smem + p.off_s2),
+    stage1_items<T, 1>(p, reinterpret_cast<const uint32_t *>(smem + p.off_v), reinterpret_cast<const T *>(smem + p.off_s2),
                     reinterpret_cast<const T *>(xs2), xs2, red, t1b, t1e, ok);
     __syncthreads();
-    stage1_finish<T>(p, red, t1b, t1e);
+    stage1_finish<T, 1>(p, red, t1b, t1e);
 }
 template <typename T>
 __device__ __forceinline__ void chain_stage2(const Params &p, uint8_t *smem, int t2b, int t2e, bool ok, const void *res,
