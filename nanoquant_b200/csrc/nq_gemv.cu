@@ -143,23 +143,28 @@ __host__ __device__ __forceinline__ int seg_bound(int tiles, int KB) {
     const int s = (n + KB - 1) / KB + 1;
     return s < tiles ? s : tiles;
 }
-// The warp whose unit range holds unit x: the largest w with floor(U w / W) <= x.
-__device__ __forceinline__ int warp_of_unit(int U, int x) {
-    const int w = (kWarps * x + kWarps - 1) / U;
-    return w < kWarps - 1 ? w : kWarps - 1;
+// Per-CTA table of the current stage's warp ranges, written by lane 0 of every warp before
+// its partials: first and one-past-last tile covered (first = last when the range is empty).
+// The reduction reads it instead of recomputing ranges (runtime integer divisions).
+struct WarpTab {
+    int lt0[kWarps], lt1[kWarps];
+};
+__device__ __forceinline__ void record_range(WarpTab *wt, int warp, int u0, int u1, int KB) {
+    if ((threadIdx.x & 31) == 0) {
+        wt->lt0[warp] = u0 < u1 ? u0 / KB : 0;
+        wt->lt1[warp] = u0 < u1 ? (u1 - 1) / KB + 1 : 0;
+    }
 }
-// Sum over warps of tile lt's partial at float offset `off` of each slot: the warps that cover
-// tile lt form the interval [warp of its first unit, warp of its last unit] (empty ranges
-// inside the interval stored nothing and are skipped).
-__device__ __forceinline__ float sum_partials(const float *red, int U, int KB, int S, int lt, int off, bool pair) {
-    const int x0 = lt * KB, x1 = min((lt + 1) * KB, U) - 1;
+// Sum over warps, in warp order, of tile lt's partial at float offset `off` of each slot.
+__device__ __forceinline__ float sum_partials(const float *red, const WarpTab *wt, int S, int lt, int off, bool pair) {
     float s = 0.f;
-    for (int w = warp_of_unit(U, x0); w <= warp_of_unit(U, x1); ++w) {
-        int u0, u1;
-        warp_units(U, w, u0, u1);
-        if (u0 >= u1) continue;
-        const float *r = red + (w * S + (lt - u0 / KB)) * 256 + off;
-        s += pair ? r[0] + r[1] : r[0];
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+        const int a = wt->lt0[w];
+        if (lt >= a && lt < wt->lt1[w]) {
+            const float *r = red + (w * S + (lt - a)) * 256 + off;
+            s += pair ? r[0] + r[1] : r[0];
+        }
     }
     return s;
 }
@@ -287,7 +292,8 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
 // FOLD: 1 compiles only the folded-operand path, -1 decides at run time (p.fold).
 template <typename T, int FOLD = -1>
 __device__ __forceinline__ void stage1_items(const Params &p, const uint32_t *vch, const T *s2s, const T *xs,
-                                            const __nv_bfloat16 *xs2, float *red, int t1b, int t1e, bool ok) {
+                                            const __nv_bfloat16 *xs2, float *red, int t1b, int t1e, bool ok,
+                                            WarpTab *wt) {
     const bool fold = FOLD >= 0 ? FOLD != 0 : p.fold != 0;
     using E = Elem<T>;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -302,6 +308,7 @@ __device__ __forceinline__ void stage1_items(const Params &p, const uint32_t *vc
     int u0, u1;
     warp_units(ntiles * KB, warp, u0, u1);
     const int lt0 = u0 / KB;
+    record_range(wt, warp, u0, u1, KB);
     for (int lt = lt0; u0 < u1 && lt * KB < u1; ++lt) {
         const int kbeg = max(u0 - lt * KB, 0), kend = min(u1 - lt * KB, KB);
         const int tile = t1b + lt;
@@ -371,16 +378,16 @@ __device__ __forceinline__ void stage1_items(const Params &p, const uint32_t *vc
 // Stage 1, second half: sum the warps' partials, apply scale_mid, store t as bf16 (hi, lo) into
 // each member's stage-2 operand, and zero its K padding (the CTA owning the member's last tile).
 template <typename T, int FOLD = -1>
-__device__ __forceinline__ void stage1_finish(const Params &p, const float *red, int t1b, int t1e) {
+__device__ __forceinline__ void stage1_finish(const Params &p, const float *red, int t1b, int t1e, const WarpTab *wt) {
     using E = Elem<T>;
     const bool fold = FOLD >= 0 ? FOLD != 0 : p.fold != 0;
     const int tid = threadIdx.x;
-    const int ntiles = t1e - t1b, U = ntiles * p.kb1;
+    const int ntiles = t1e - t1b;
     for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
         const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
         const int b = rem >> 4, row = rem & 15;
-        const float s0 = fold ? sum_partials(red, U, p.kb1, p.seg1, lt, row * 8 + 2 * b, true)
-                                : sum_partials(red, U, p.kb1, p.seg1, lt, row * 8 + b, false);
+        const float s0 = fold ? sum_partials(red, wt, p.seg1, lt, row * 8 + 2 * b, true)
+                                : sum_partials(red, wt, p.seg1, lt, row * 8 + b, false);
         float s = s0;
         const int tile = t1b + lt;
         const int l = member_of1(p, tile);
@@ -413,7 +420,7 @@ __device__ __forceinline__ void stage1_finish(const Params &p, const float *red,
 // null to read them from global memory (L2).
 template <typename T, int NT>
 __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uch, float *red, int t2b, int t2e,
-                                             bool ok, const __nv_bfloat16 *tsm) {
+                                             bool ok, const __nv_bfloat16 *tsm, WarpTab *wt) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int sh0 = 8 * (t & 1);
@@ -423,6 +430,7 @@ __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uc
     int u0, u1;
     warp_units(ntiles * KB, warp, u0, u1);
     const int lt0 = u0 / KB;
+    record_range(wt, warp, u0, u1, KB);
     // B column g of n-tile q is the hi (g even) or lo (g odd) part of batch row 4q + g/2,
     // stored ready-made by stage 1 as bf16 pairs along k
     const int b0 = g >> 1, b1 = 4 + (g >> 1);
@@ -499,15 +507,15 @@ __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uc
 // Stage 2, second half: reduce, scale by s1, round, and store y (optionally y = y + res).
 template <typename T>
 __device__ __forceinline__ void stage2_finish(const Params &p, const float *red, const T *s1s, int t2b, int t2e,
-                                              const void *res, int act) {
+                                              const void *res, int act, const WarpTab *wt) {
     using E = Elem<T>;
     const int tid = threadIdx.x;
-    const int ntiles = t2e - t2b, U = ntiles * p.kbu2;
+    const int ntiles = t2e - t2b;
     for (int i = tid; i < ntiles * 16 * p.batch; i += kThreads) {
         const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
         const int b = rem >> 4, row = rem & 15;
         const int half = (b >> 2) * 128, col = 2 * (b & 3);
-        const float s = sum_partials(red, U, p.kbu2, p.seg2, lt, half + row * 8 + col, true);
+        const float s = sum_partials(red, wt, p.seg2, lt, half + row * 8 + col, true);
         const int tile = t2b + lt;
         const int l = member_of2(p, tile);
         const Member &mb = p.m[l];
@@ -600,6 +608,7 @@ template <typename T, bool DECODE>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float sred[kWarps];
+    __shared__ WarpTab wtab;
     using E = Elem<T>;
     const bool x_in_smem = DECODE || p.x_in_smem;
     const bool fold = DECODE || p.fold;
@@ -760,9 +769,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
             __syncthreads();
         }
-        stage1_items<T, DECODE ? 1 : -1>(p, vch, s2s, xs, xs2, red, t1b, t1e, ok);
+        stage1_items<T, DECODE ? 1 : -1>(p, vch, s2s, xs, xs2, red, t1b, t1e, ok, &wtab);
         __syncthreads();
-        stage1_finish<T, DECODE ? 1 : -1>(p, red, t1b, t1e);
+        stage1_finish<T, DECODE ? 1 : -1>(p, red, t1b, t1e, &wtab);
     }
 
     if (p.mode == kFused) {
@@ -775,11 +784,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     if (has2) {
         if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
         if (DECODE || p.batch <= 4)
-            stage2_items<T, 1>(p, uch, red, t2b, t2e, ok, nullptr);
+            stage2_items<T, 1>(p, uch, red, t2b, t2e, ok, nullptr, &wtab);
         else
-            stage2_items<T, 2>(p, uch, red, t2b, t2e, ok, nullptr);
+            stage2_items<T, 2>(p, uch, red, t2b, t2e, ok, nullptr, &wtab);
         __syncthreads();
-        stage2_finish<T>(p, red, s1s, t2b, t2e, nullptr, p.act);
+        stage2_finish<T>(p, red, s1s, t2b, t2e, nullptr, p.act, &wtab);
     }
 }
 
@@ -814,13 +823,14 @@ static size_t layout(Params &p, int tiles1, int tiles2, bool stage1, bool stage2
     p.off_red = (uint32_t)off;
     off = align128(off + (size_t)slots * 256 * sizeof(float));
     const size_t in_pad = (size_t)p.kb1 * 64;
-    // row-by-row copies only where a padded stride is needed; a slab whose row length is
-    // already an odd multiple of 4 words (or not a multiple of 4) goes in one contiguous copy
-    p.v_rows = (p.wv % 4) == 0 && padded_stride(p.wv) != p.wv;
+    // Every slab goes in one contiguous bulk copy: the copy engine takes row copies one at a
+    // time (a 32-row slab costs ~1.5 us to issue), which outweighs the bank conflicts that an
+    // unpadded stride (a multiple of 32 words) gives the sign-word loads.
+    p.v_rows = 0;
     p.wvs = p.v_rows ? padded_stride(p.wv) : p.wv;
     int max_wus = 0;
     for (int l = 0; l < p.nm; ++l) {
-        p.m[l].u_rows = (p.m[l].wu % 4) == 0 && padded_stride(p.m[l].wu) != p.m[l].wu;
+        p.m[l].u_rows = 0;
         p.m[l].wus = p.m[l].u_rows ? padded_stride(p.m[l].wu) : p.m[l].wu;
         max_wus = std::max(max_wus, p.m[l].wus);
     }
@@ -1283,30 +1293,30 @@ __device__ __forceinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, 
 // The stage bodies as the chain kernel runs them (inlined: out of line, the shared-memory
 // pointers would become generic ones).
 template <typename T>
-__device__ __forceinline__ void chain_stage1(const Params &p, uint8_t *smem, int t1b, int t1e, bool ok) {
+__device__ __forceinline__ void chain_stage1(const Params &p, uint8_t *smem, int t1b, int t1e, bool ok, WarpTab *wt) {
     const __nv_bfloat16 *xs2 = reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2);
     float *red = reinterpret_cast<float *>(smem + p.off_red);
     stage1_items<T, 1>(p, reinterpret_cast<const uint32_t *>(smem + p.off_v), reinterpret_cast<const T *>(smem + p.off_s2),
-                    reinterpret_cast<const T *>(xs2), xs2, red, t1b, t1e, ok);
+                    reinterpret_cast<const T *>(xs2), xs2, red, t1b, t1e, ok, wt);
     __syncthreads();
-    stage1_finish<T, 1>(p, red, t1b, t1e);
+    stage1_finish<T, 1>(p, red, t1b, t1e, wt);
 }
 template <typename T>
 __device__ __forceinline__ void chain_stage2(const Params &p, uint8_t *smem, int t2b, int t2e, bool ok, const void *res,
-                                          int act) {
+                                             int act, WarpTab *wt) {
     float *red = reinterpret_cast<float *>(smem + p.off_red);
     stage2_items<T, 1>(p, reinterpret_cast<const uint32_t *>(smem + p.off_u), red, t2b, t2e, ok,
-                       reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2));
+                       reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2), wt);
     __syncthreads();
-    stage2_finish<T>(p, red, reinterpret_cast<const T *>(smem + p.off_s1), t2b, t2e, res, act);
+    stage2_finish<T>(p, red, reinterpret_cast<const T *>(smem + p.off_s1), t2b, t2e, res, act, wt);
 }
 
 // Phase k of the chain.  One copy of the code serves every phase (a copy per phase would not
 // stay in the instruction cache); the runtime index into the parameter block becomes indexed
 // constant-bank loads.
 template <typename T>
-__device__ __forceinline__ void chain_phase(const ChainParams &cp, int k, uint8_t *smem, float *sred, bool &ok,
-                                            unsigned long long bar_base) {
+__device__ __forceinline__ void chain_phase(const ChainParams &cp, int k, uint8_t *smem, float *sred, WarpTab *wt,
+                                            bool &ok, unsigned long long bar_base) {
     const ChainPhase &ph = cp.ph[k];
     const Params &p = ph.g;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // [region][V side, U side]
@@ -1328,7 +1338,7 @@ __device__ __forceinline__ void chain_phase(const ChainParams &cp, int k, uint8_
         if (!mbar_wait(&bv[0], par, &ctrl->status)) ok = false;
         chain_fold<T>(ph, smem, sred);
         __syncthreads();
-        chain_stage1<T>(p, smem, t1b, t1e, ok);
+        chain_stage1<T>(p, smem, t1b, t1e, ok, wt);
     }
     if (!grid_barrier(ctrl, bar_base + (unsigned long long)(2 * k + 1) * G)) ok = false;  // t is complete
     // The t columns of the members this CTA serves go to the (now idle) fold buffer, one bulk
@@ -1357,7 +1367,7 @@ __device__ __forceinline__ void chain_phase(const ChainParams &cp, int k, uint8_
     if (t2e > t2b) {
         if (!mbar_wait(tbar, (uint32_t)k & 1u, &ctrl->status)) ok = false;
         if (!mbar_wait(&bv[1], par, &ctrl->status)) ok = false;
-        chain_stage2<T>(p, smem, t2b, t2e, ok, ph.res, ph.act);
+        chain_stage2<T>(p, smem, t2b, t2e, ok, ph.res, ph.act, wt);
     }
 }
 
@@ -1365,6 +1375,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const ChainParams cp) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float sred[kWarps];
+    __shared__ WarpTab wtab;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     unsigned long long bar_base = 0;  // thread 0 only
     if (threadIdx.x == 0) {
@@ -1377,7 +1388,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const ChainParams cp
     chain_issue<T>(cp.ph[0].g, smem, &bars[0]);
     if (cp.nph > 1) chain_issue<T>(cp.ph[1].g, smem, &bars[2]);
     bool ok = true;
-    for (int k = 0; k < cp.nph; ++k) chain_phase<T>(cp, k, smem, sred, ok, bar_base);
+    for (int k = 0; k < cp.nph; ++k) chain_phase<T>(cp, k, smem, sred, &wtab, ok, bar_base);
 }
 
 // Host: validate the phases, build their Params, lay out shared memory.  `launch` = false
@@ -1488,13 +1499,13 @@ static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *pha
             t2 += mb.tiles2;
             mb.tb = reinterpret_cast<__nv_bfloat16 *>(ws_base + need);  // tb regions follow the control block
             need += tb_bytes(L.rank);
-            mb.u_rows = (mb.wu % 4) == 0 && padded_stride(mb.wu) != mb.wu;
+            mb.u_rows = 0;
             mb.wus = mb.u_rows ? padded_stride(mb.wu) : mb.wu;
         }
         if (t1 > 65536 || t2 > 65536) return fail(NQ_ERR_UNSUPPORTED, "phase %d: layer group too large", k);
         p.tiles1 = t1;
         p.tiles2 = t2;
-        p.v_rows = (p.wv % 4) == 0 && padded_stride(p.wv) != p.wv;
+        p.v_rows = 0;  // one contiguous copy per slab (see layout())
         p.wvs = p.v_rows ? padded_stride(p.wv) : p.wv;
         const int tpc1 = (t1 + G - 1) / G, tpc2 = (t2 + G - 1) / G;
         p.kbu2 = 1;
