@@ -157,15 +157,19 @@ __device__ __forceinline__ void record_range(WarpTab *wt, int warp, int u0, int 
 }
 // Sum over warps, in warp order, of tile lt's partial at float offset `off` of each slot.
 __device__ __forceinline__ float sum_partials(const float *red, const WarpTab *wt, int S, int lt, int off, bool pair) {
-    float s = 0.f;
+    // branch-free so that all the loads are in flight together; uncovered slots read slot 0
+    float v[kWarps];
+    bool in[kWarps];
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
         const int a = wt->lt0[w];
-        if (lt >= a && lt < wt->lt1[w]) {
-            const float *r = red + (w * S + (lt - a)) * 256 + off;
-            s += pair ? r[0] + r[1] : r[0];
-        }
+        in[w] = lt >= a && lt < wt->lt1[w];
+        const float *r = red + (in[w] ? (w * S + (lt - a)) * 256 + off : off);
+        v[w] = pair ? r[0] + r[1] : r[0];
     }
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += in[w] ? v[w] : 0.f;
     return s;
 }
 
@@ -642,11 +646,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     // Put every byte this CTA needs in flight before anything else: V rows, s2 and x rows
     // (when 16-byte aligned) on barrier 0; U rows and the s1 slices on barrier 1.
     bool vec_rows = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 && (p.in_f % 8) == 0;
-    for (int l = 0; l < p.nm; ++l) vec_rows = vec_rows && (reinterpret_cast<uintptr_t>(p.m[l].s2) & 15) == 0;
+    _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) vec_rows = vec_rows && (reinterpret_cast<uintptr_t>(p.m[l].s2) & 15) == 0;
     if (has1) {
         if (tid == 0) {
             uint32_t bytes0 = 0;
-            for (int l = 0; l < p.nm; ++l) {
+            _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
                 const Member &mb = p.m[l];
                 const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
                 if (a < b)
@@ -664,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                                     static_cast<const T *>(p.x2) + (size_t)b * p.in_f, (uint32_t)p.in_f * 2u, &bars[0]);
             if (p.xmode == kChainNorm) bulk_g2s_pieces(smem + p.off_nw, p.nw, (uint32_t)p.in_f * 2u, &bars[0]);
             if (vec_rows) {
-                for (int l = 0; l < p.nm; ++l)
+                _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm)
                     bulk_g2s_pieces(s2s + (size_t)l * in_pad, p.m[l].s2, (uint32_t)p.in_f * 2u, &bars[0]);
                 if (x_in_smem) {
                     if (in_pad == p.in_f)
@@ -677,14 +681,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
         }
         __syncwarp();
-        for (int l = 0; l < p.nm; ++l) {
+        _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
             const Member &mb = p.m[l];
             const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
             if (a < b)
                 copy_slab(vch + (size_t)16 * (a - t1b) * p.wvs, mb.vbits, 16 * (a - mb.t1_start),
                           min(16 * (b - mb.t1_start), mb.rank), p.wv, p.wvs, p.v_rows, &bars[0], 0);
         }
-        for (int l = 0; l < p.nm; ++l) {
+        _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
             if (vec_rows) {
                 zero_tail<T>(s2s + (size_t)l * in_pad, p.in_f, in_pad);
             } else {
@@ -705,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         // starts after the previous segments' rows (each at its member's stride).
         if (tid == 32) {
             uint32_t bytes1 = 0;
-            for (int l = 0; l < p.nm; ++l) {
+            _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
                 const Member &mb = p.m[l];
                 int a, b;
                 seg_tiles(mb, t2b, t2e, a, b);
@@ -719,7 +723,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         }
         __syncwarp();
         uint32_t uoff = 0;  // words
-        for (int l = 0; l < p.nm; ++l) {
+        _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
             const Member &mb = p.m[l];
             int a, b;
             seg_tiles(mb, t2b, t2e, a, b);
