@@ -621,6 +621,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     const bool do1 = (p.mode & kStage1) != 0, do2 = (p.mode & kStage2) != 0;
     unsigned long long bar_base = 0;  // thread 0 only
     if (tid == 0 && p.mode == kFused) bar_base = grid_barrier_base(p.ctrl, (unsigned)G);
+    // First touches of the parameter block miss the parameter cache; lane 0 of eight warps
+    // reads one field each from different parts of it so that those misses overlap (the
+    // prologue would otherwise take them one after another).
+    if ((tid & 31) == 0 && tid < 8 * 32) {
+        const int w = tid >> 5;
+        const Member &mw = p.m[w < 3 ? w : w - 3];
+        const uintptr_t v = w < 3 ? reinterpret_cast<uintptr_t>(mw.s2) ^ (uintptr_t)mw.t2_start
+                                  : w < 6 ? (uintptr_t)mw.wus ^ reinterpret_cast<uintptr_t>(mw.tb)
+                                          : w == 6 ? reinterpret_cast<uintptr_t>(p.x) ^ (uintptr_t)p.nm
+                                                   : (uintptr_t)p.off_s1 ^ (uintptr_t)p.xmode;
+        if (v == 1) sred[w] = 0.f;  // never true in practice; keeps the loads
+    }
 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     float *red = reinterpret_cast<float *>(smem + p.off_red);
@@ -754,23 +766,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         }
         if (fold) {
             // xs2[l][col][k] = bf16 hi (col even) / lo (col odd) of x[col/2][k] * s2_l[k]
+            // (members and batch rows outside, 8-value chunks inside: no runtime divisions)
             const int chunks = in_pad / 8;
-            for (int i = tid; i < p.nm * p.batch * chunks; i += kThreads) {
-                const int lb = i / chunks, k = 8 * (i - lb * chunks);
-                const int l = lb / p.batch, b = lb - l * p.batch;
-                const uint4 xv = *reinterpret_cast<const uint4 *>(xs + (size_t)b * in_pad + k);
-                const uint4 sv = *reinterpret_cast<const uint4 *>(s2s + (size_t)l * in_pad + k);
-                const T *xe = reinterpret_cast<const T *>(&xv);
-                const T *se = reinterpret_cast<const T *>(&sv);
-                uint32_t hi[4], lo[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    split_pair(E::to_f(xe[2 * j]) * E::to_f(se[2 * j]), E::to_f(xe[2 * j + 1]) * E::to_f(se[2 * j + 1]),
-                               hi[j], lo[j]);
-                __nv_bfloat16 *dst = xs2 + ((size_t)l * nxc + 2 * b) * in_pad + k;
-                *reinterpret_cast<uint4 *>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4 *>(dst + in_pad) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-            }
+            for (int l = 0; l < kMaxGroup; ++l)
+                if (l < p.nm)
+                    for (int b = 0; b < p.batch; ++b)
+                        for (int c8 = tid; c8 < chunks; c8 += kThreads) {
+                            const int k = 8 * c8;
+                            const uint4 xv = *reinterpret_cast<const uint4 *>(xs + (size_t)b * in_pad + k);
+                            const uint4 sv = *reinterpret_cast<const uint4 *>(s2s + (size_t)l * in_pad + k);
+                            const T *xe = reinterpret_cast<const T *>(&xv);
+                            const T *se = reinterpret_cast<const T *>(&sv);
+                            uint32_t hi[4], lo[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                split_pair(E::to_f(xe[2 * j]) * E::to_f(se[2 * j]),
+                                           E::to_f(xe[2 * j + 1]) * E::to_f(se[2 * j + 1]), hi[j], lo[j]);
+                            __nv_bfloat16 *dst = xs2 + ((size_t)l * nxc + 2 * b) * in_pad + k;
+                            *reinterpret_cast<uint4 *>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                            *reinterpret_cast<uint4 *>(dst + in_pad) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        }
             __syncthreads();
         }
         stage1_items<T, DECODE ? 1 : -1>(p, vch, s2s, xs, xs2, red, t1b, t1e, ok, &wtab);
