@@ -120,6 +120,20 @@ __device__ __forceinline__ void copy_slab(uint32_t *dst, const uint32_t *plane, 
     for (uint32_t i = bulk / 4 + threadIdx.x; i < words; i += kThreads) dst[i] = __ldg(src + i);
 }
 
+// A slab of rows [r0, r1) (w words each) copied contiguously: the 16-byte-multiple prefix
+// through the copy engine (one thread) and the rest by plain loads (all threads).
+__device__ __forceinline__ void slab_bulk(uint32_t *dst, const uint32_t *plane, int r0, int r1, int w, uint64_t *bar) {
+    const uint32_t words = (r1 > r0) ? (uint32_t)(r1 - r0) * (uint32_t)w : 0u;
+    const uint32_t bulk = (words * 4u) & ~15u;
+    if (bulk) bulk_g2s_pieces(dst, plane + (size_t)r0 * w, bulk, bar);
+}
+__device__ __forceinline__ void slab_tail(uint32_t *dst, const uint32_t *plane, int r0, int r1, int w) {
+    const uint32_t words = (r1 > r0) ? (uint32_t)(r1 - r0) * (uint32_t)w : 0u;
+    const uint32_t bulk = (words * 4u) & ~15u;
+    const uint32_t *src = plane + (size_t)r0 * w;
+    for (uint32_t i = bulk / 4 + threadIdx.x; i < words; i += kThreads) dst[i] = __ldg(src + i);
+}
+
 // Zero the padding columns [n, npad) of a staged 16-bit row.
 template <typename T>
 __device__ __forceinline__ void zero_tail(T *dst, int n, int npad) {
@@ -649,40 +663,39 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     const bool has1 = t1e > t1b, has2 = t2e > t2b;
     const int in_pad = p.kb1 * 64;
 
+    // Copies are issued by separate warps so that their issue latencies (several hundred cycles
+    // each: the copy engine accepts a request only after translating its source) overlap.
+    // Barrier 0 (V side): warp 0 the s2 rows, warp 1 x and the transform inputs, warp 2 the V
+    // slabs.  Barrier 1 (U side): warp 3 the U slabs, warp 4 the s1 slices.  Each issuing warp
+    // arrives once with the bytes it put in flight (zero when it has none), so a barrier
+    // completes only after every issuer declared its bytes and all of them landed.  Bytes the
+    // copy engine cannot take (unaligned rows, sub-16-byte tails) are loaded by all threads.
+    constexpr int kIssuers0 = 3, kIssuers1 = 2;
     if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        mbar_init(&bars[0], kIssuers0);
+        mbar_init(&bars[1], kIssuers1);
         fence_mbar_init();
     }
     __syncthreads();
-    // Put every byte this CTA needs in flight before anything else: V rows, s2 and x rows
-    // (when 16-byte aligned) on barrier 0; U rows and the s1 slices on barrier 1.
     bool vec_rows = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 && (p.in_f % 8) == 0;
     _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) vec_rows = vec_rows && (reinterpret_cast<uintptr_t>(p.m[l].s2) & 15) == 0;
+    const int warp_id = tid >> 5;
     if (has1) {
-        if (tid == 0) {
-            uint32_t bytes0 = 0;
-            _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
-                const Member &mb = p.m[l];
-                const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
-                if (a < b)
-                    bytes0 += slab_bulk_bytes(16 * (a - mb.t1_start), min(16 * (b - mb.t1_start), mb.rank), p.wv,
-                                              p.v_rows);
-            }
-            if (vec_rows) bytes0 += (uint32_t)p.in_f * 2u * ((uint32_t)p.nm + (x_in_smem ? (uint32_t)p.batch : 0u));
-            // transform inputs (host guarantees vec_rows and x in shared memory for them)
-            if (p.x2) bytes0 += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
-            if (p.xmode == kChainNorm) bytes0 += (uint32_t)p.in_f * 2u;
-            mbar_arrive_expect_tx(&bars[0], bytes0);
-            if (p.x2)
-                for (int b = 0; b < p.batch; ++b)
-                    bulk_g2s_pieces(smem + p.off_x2 + (size_t)b * in_pad * 2,
-                                    static_cast<const T *>(p.x2) + (size_t)b * p.in_f, (uint32_t)p.in_f * 2u, &bars[0]);
-            if (p.xmode == kChainNorm) bulk_g2s_pieces(smem + p.off_nw, p.nw, (uint32_t)p.in_f * 2u, &bars[0]);
-            if (vec_rows) {
-                _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm)
-                    bulk_g2s_pieces(s2s + (size_t)l * in_pad, p.m[l].s2, (uint32_t)p.in_f * 2u, &bars[0]);
-                if (x_in_smem) {
+        if ((tid & 31) == 0 && warp_id < kIssuers0) {
+            uint32_t bytes = 0;
+            if (warp_id == 0) {
+                if (vec_rows) bytes = (uint32_t)p.in_f * 2u * (uint32_t)p.nm;
+                mbar_arrive_expect_tx(&bars[0], bytes);
+                if (vec_rows)
+                    _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm)
+                        bulk_g2s_pieces(s2s + (size_t)l * in_pad, p.m[l].s2, (uint32_t)p.in_f * 2u, &bars[0]);
+            } else if (warp_id == 1) {
+                // transform inputs: the host guarantees vec_rows and x in shared memory for them
+                if (vec_rows && x_in_smem) bytes += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
+                if (p.x2) bytes += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
+                if (p.xmode == kChainNorm) bytes += (uint32_t)p.in_f * 2u;
+                mbar_arrive_expect_tx(&bars[0], bytes);
+                if (vec_rows && x_in_smem) {
                     if (in_pad == p.in_f)
                         bulk_g2s_pieces(xs, p.x, (uint32_t)p.batch * (uint32_t)p.in_f * 2u, &bars[0]);
                     else
@@ -690,15 +703,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                             bulk_g2s_pieces(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f,
                                             (uint32_t)p.in_f * 2u, &bars[0]);
                 }
+                if (p.x2)
+                    for (int b = 0; b < p.batch; ++b)
+                        bulk_g2s_pieces(smem + p.off_x2 + (size_t)b * in_pad * 2,
+                                        static_cast<const T *>(p.x2) + (size_t)b * p.in_f, (uint32_t)p.in_f * 2u,
+                                        &bars[0]);
+                if (p.xmode == kChainNorm) bulk_g2s_pieces(smem + p.off_nw, p.nw, (uint32_t)p.in_f * 2u, &bars[0]);
+            } else {
+                _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+                    const Member &mb = p.m[l];
+                    const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
+                    if (a < b)
+                        bytes += slab_bulk_bytes(16 * (a - mb.t1_start), min(16 * (b - mb.t1_start), mb.rank), p.wv, false);
+                }
+                mbar_arrive_expect_tx(&bars[0], bytes);
+                _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+                    const Member &mb = p.m[l];
+                    const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
+                    if (a < b)
+                        slab_bulk(vch + (size_t)16 * (a - t1b) * p.wvs, mb.vbits, 16 * (a - mb.t1_start),
+                                  min(16 * (b - mb.t1_start), mb.rank), p.wv, &bars[0]);
+                }
             }
         }
-        __syncwarp();
+        // what the copy engine does not carry: slab tails, zero padding, unaligned rows
         _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
             const Member &mb = p.m[l];
             const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
             if (a < b)
-                copy_slab(vch + (size_t)16 * (a - t1b) * p.wvs, mb.vbits, 16 * (a - mb.t1_start),
-                          min(16 * (b - mb.t1_start), mb.rank), p.wv, p.wvs, p.v_rows, &bars[0], 0);
+                slab_tail(vch + (size_t)16 * (a - t1b) * p.wvs, mb.vbits, 16 * (a - mb.t1_start),
+                          min(16 * (b - mb.t1_start), mb.rank), p.wv);
         }
         _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
             if (vec_rows) {
@@ -717,23 +751,44 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
     }
     if (has2) {
-        // U rows and s1 slices, one segment per member; segment k of the smem U region
-        // starts after the previous segments' rows (each at its member's stride).
-        if (tid == 32) {
-            uint32_t bytes1 = 0;
+        // U slabs and s1 slices, one segment per member; segment k of the smem U region starts
+        // after the previous segments' rows (each rounded up to 4 words)
+        if ((tid & 31) == 0 && (warp_id == kIssuers0 || warp_id == kIssuers0 + 1)) {
+            const bool u_side = warp_id == kIssuers0;
+            uint32_t bytes = 0;
             _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
                 const Member &mb = p.m[l];
                 int a, b;
                 seg_tiles(mb, t2b, t2e, a, b);
                 if (a >= b) continue;
                 const int r0 = 16 * (a - mb.t2_start), r1 = min(16 * (b - mb.t2_start), mb.out_f);
-                bytes1 += slab_bulk_bytes(r0, r1, mb.wu, mb.u_rows);
-                const T *s1src = static_cast<const T *>(mb.s1) + r0;
-                if ((reinterpret_cast<uintptr_t>(s1src) & 15) == 0) bytes1 += ((uint32_t)(r1 - r0) * 2u) & ~15u;
+                if (u_side) {
+                    bytes += slab_bulk_bytes(r0, r1, mb.wu, false);
+                } else {
+                    const T *s1src = static_cast<const T *>(mb.s1) + r0;
+                    if ((reinterpret_cast<uintptr_t>(s1src) & 15) == 0) bytes += ((uint32_t)(r1 - r0) * 2u) & ~15u;
+                }
             }
-            mbar_arrive_expect_tx(&bars[1], bytes1);
+            mbar_arrive_expect_tx(&bars[1], bytes);
+            uint32_t uoff = 0;  // words
+            _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+                const Member &mb = p.m[l];
+                int a, b;
+                seg_tiles(mb, t2b, t2e, a, b);
+                if (a >= b) continue;
+                const int r0 = 16 * (a - mb.t2_start), r1 = min(16 * (b - mb.t2_start), mb.out_f);
+                if (u_side) {
+                    slab_bulk(uch + uoff, mb.ubits, r0, r1, mb.wu, &bars[1]);
+                } else {
+                    const T *s1src = static_cast<const T *>(mb.s1) + r0;
+                    const uint32_t s1_bulk =
+                        (reinterpret_cast<uintptr_t>(s1src) & 15) == 0 ? ((uint32_t)(r1 - r0) * 2u) & ~15u : 0u;
+                    if (s1_bulk) bulk_g2s(s1s + 16 * (a - t2b), s1src, s1_bulk, &bars[1]);
+                }
+                uoff += (uint32_t)(16 * (b - a)) * (uint32_t)mb.wus;
+                uoff = (uoff + 3u) & ~3u;
+            }
         }
-        __syncwarp();
         uint32_t uoff = 0;  // words
         _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
             const Member &mb = p.m[l];
@@ -741,14 +796,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             seg_tiles(mb, t2b, t2e, a, b);
             if (a >= b) continue;
             const int r0 = 16 * (a - mb.t2_start), r1 = min(16 * (b - mb.t2_start), mb.out_f);
-            copy_slab(uch + uoff, mb.ubits, r0, r1, mb.wu, mb.wus, mb.u_rows, &bars[1], 1);
+            slab_tail(uch + uoff, mb.ubits, r0, r1, mb.wu);
             uoff += (uint32_t)(16 * (b - a)) * (uint32_t)mb.wus;
             uoff = (uoff + 3u) & ~3u;  // keep every segment 16-byte aligned
             const T *s1src = static_cast<const T *>(mb.s1) + r0;
             T *s1dst = s1s + 16 * (a - t2b);
             const uint32_t s1_bulk =
                 (reinterpret_cast<uintptr_t>(s1src) & 15) == 0 ? ((uint32_t)(r1 - r0) * 2u) & ~15u : 0u;
-            if (tid == 32 && s1_bulk) bulk_g2s(s1dst, s1src, s1_bulk, &bars[1]);
             for (int i = (int)(s1_bulk / 2) + tid; i < r1 - r0; i += kThreads) s1dst[i] = s1src[i];
         }
     }
