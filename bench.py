@@ -43,6 +43,8 @@ def parse():
                     help="per-layer GEMV instead of whole-model decode: out,in,rank (e.g. 11008,4096,2054); "
                          "prints that layer's GB/s over --copies weight copies cycled through the timed loop")
     ap.add_argument("--copies", type=int, default=40, help="--layer: distinct weight copies (past L2)")
+    ap.add_argument("--chain", action="store_true",
+                    help="decode through GEMV chains (one cooperative launch per block besides attention)")
     return ap.parse_args()
 
 
@@ -193,6 +195,8 @@ def config_block(cfg, args, world):
                         f"random-id prompt",
             "model": cfg.name, "global_batch": args.batch, "seq_len": args.prompt,
             "parallelism": f"tp{world}", "ranks": dict(cfg.ranks),
+            "decode_path": "gemv chain per block" if getattr(args, "chain", False) else
+                           "grouped GEMV launches with fused RMSNorm / SwiGLU prologues",
             "l2": "working set > L2 (weights + KV cache read per token)"}
 
 
@@ -270,7 +274,7 @@ def run_nq(args, world, rank, local):
     group = torch.distributed.group.WORLD if world > 1 else None
     max_seq = args.prompt + args.warmup + 2 * args.steps + 16
     dec = Decoder(cfg, max_seq=max_seq, batch=args.batch, tp_rank=rank, tp=world, group=group, seed=1234,
-                  dtype=torch.float16, device=dev)
+                  dtype=torch.float16, device=dev, chain=args.chain)
     g = torch.Generator().manual_seed(42)
     prompt = torch.randint(0, cfg.vocab, (args.prompt,), generator=g)
     torch.cuda.synchronize(dev)

@@ -39,7 +39,8 @@ class GemvLayer(ctypes.Structure):
 class GemvInput(ctypes.Structure):
     """nq_gemv_input of include/nq_b200.h."""
     _fields_ = [("x_mode", ctypes.c_int), ("eps", ctypes.c_float), ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p),
-                ("norm_weight", ctypes.c_void_p), ("residual_out", ctypes.c_void_p)]
+                ("norm_weight", ctypes.c_void_p), ("residual_out", ctypes.c_void_p), ("n_prefetch", ctypes.c_int),
+                ("prefetch", ctypes.c_void_p * 6), ("prefetch_bytes", ctypes.c_uint64 * 6)]
 
 
 class ChainPhase(ctypes.Structure):
@@ -115,7 +116,7 @@ def cuda_lib() -> ctypes.CDLL:
     with _lock:
         if _cuda is None:
             if not os.path.exists(CUDA_LIB_PATH):
-                raise ImportError(f"{CUDA_LIB_PATH} is missing; build it with `python -m nanoquant_b200.build`")
+                raise ImportError(f"{CUDA_LIB_PATH} is missing; build it with `python nanoquant_b200/build.py`")
             lib = ctypes.CDLL(CUDA_LIB_PATH)
             for name, (res, args) in _SIGNATURES.items():
                 fn = getattr(lib, name)
@@ -140,7 +141,7 @@ def load_torch_ops() -> None:
         if _torch_loaded:
             return
         if not os.path.exists(TORCH_LIB_PATH):
-            raise ImportError(f"{TORCH_LIB_PATH} is missing; build it with `python -m nanoquant_b200.build`")
+            raise ImportError(f"{TORCH_LIB_PATH} is missing; build it with `python nanoquant_b200/build.py`")
         import torch
         torch.ops.load_library(TORCH_LIB_PATH)
         _torch_loaded = True
