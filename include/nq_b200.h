@@ -131,7 +131,6 @@ NQ_API int nq_gemv_group(int dtype, const void *x, int64_t batch, int64_t in_fea
  * Transformed inputs need batch <= 8, in_features % 8 == 0 and 16-byte aligned x, x2,
  * norm_weight, residual_out and scale_pre.  Workspace as nq_gemv_group.
  * ------------------------------------------------------------------------------- */
-#define NQ_GEMV_PREFETCH_MAX 6
 typedef struct {
     int x_mode;                /* NQ_CHAIN_X_* (defined below) */
     float eps;                 /* NQ_CHAIN_X_RMSNORM */
@@ -139,12 +138,6 @@ typedef struct {
     const void *x2;            /* residual [batch, in] (RMSNORM, may be NULL) or second factor */
     const void *norm_weight;   /* [in] (RMSNORM) */
     void *residual_out;        /* [batch, in] (RMSNORM, may be NULL) */
-    /* Optional L2 prefetch hints: device ranges the caller's NEXT launches will read (e.g. the
-     * next layer's sign planes); the kernel pulls them into L2 while it runs.  16-byte aligned
-     * starts; lengths are rounded down to 16 bytes; n_prefetch <= NQ_GEMV_PREFETCH_MAX. */
-    int n_prefetch;
-    const void *prefetch[NQ_GEMV_PREFETCH_MAX];
-    uint64_t prefetch_bytes[NQ_GEMV_PREFETCH_MAX];
 } nq_gemv_input;
 NQ_API int nq_gemv_group_ex(int dtype, const nq_gemv_input *input, int64_t batch,
                             int64_t in_features, int n_layers, const nq_gemv_layer *layers, int act,

@@ -39,8 +39,7 @@ class GemvLayer(ctypes.Structure):
 class GemvInput(ctypes.Structure):
     """nq_gemv_input of include/nq_b200.h."""
     _fields_ = [("x_mode", ctypes.c_int), ("eps", ctypes.c_float), ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p),
-                ("norm_weight", ctypes.c_void_p), ("residual_out", ctypes.c_void_p), ("n_prefetch", ctypes.c_int),
-                ("prefetch", ctypes.c_void_p * 6), ("prefetch_bytes", ctypes.c_uint64 * 6)]
+                ("norm_weight", ctypes.c_void_p), ("residual_out", ctypes.c_void_p)]
 
 
 class ChainPhase(ctypes.Structure):

@@ -264,9 +264,6 @@ struct Params {
     void *res_out;             // RMSNORM: receives x (+ x2), written by the CTA owning stage-1 tile 0
     float eps;
     int act;                   // bit l: SiLU on member l's output
-    int npf;                   // L2 prefetch hints for the caller's next launches
-    const void *pf[NQ_GEMV_PREFETCH_MAX];
-    unsigned long long pf_bytes[NQ_GEMV_PREFETCH_MAX];
     uint32_t off_red, off_s2, off_x, off_xs2, off_v, off_u, off_s1, off_x2, off_nw;
 };
 
@@ -811,18 +808,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     }
     __syncthreads();
 
-    // L2 prefetch of what the caller launches next: CTA c takes the c-th 1/G of every range
-    if (tid == 5 * 32 && p.npf > 0) {
-        for (int r = 0; r < p.npf && r < NQ_GEMV_PREFETCH_MAX; ++r) {
-            const unsigned long long n16 = p.pf_bytes[r] / 16;  // whole 16-byte units
-            const unsigned long long a = n16 * (unsigned)c / (unsigned)G, b = n16 * (unsigned)(c + 1) / (unsigned)G;
-            const char *base = static_cast<const char *>(p.pf[r]) + a * 16;
-            for (unsigned long long u = a; u < b; u += (1ull << 16)) {  // pieces of at most 1 MiB
-                const unsigned long long n = b - u < (1ull << 16) ? b - u : (1ull << 16);
-                bulk_prefetch_l2(base + (u - a) * 16, (uint32_t)(n * 16));
-            }
-        }
-    }
     bool ok = true;
     // ------------------------------------------------------------------ stage 1
     if (has1) {
@@ -1045,9 +1030,6 @@ struct GroupInput {
     void *res_out = nullptr;
     float eps = 0.f;
     int act = 0;
-    int npf = 0;
-    const void *pf[NQ_GEMV_PREFETCH_MAX] = {};
-    unsigned long long pf_bytes[NQ_GEMV_PREFETCH_MAX] = {};
 };
 
 static int group_impl(int dtype, const GroupInput &in, int64_t batch, int64_t in_features, int n,
@@ -1152,15 +1134,6 @@ static int group_impl(int dtype, const GroupInput &in, int64_t batch, int64_t in
     base.res_out = in.res_out;
     base.eps = in.eps;
     base.act = in.act;
-    if (in.npf < 0 || in.npf > NQ_GEMV_PREFETCH_MAX)
-        return fail(NQ_ERR_INVALID_ARGUMENT, "n_prefetch must be 0..%d", NQ_GEMV_PREFETCH_MAX);
-    base.npf = in.npf;
-    for (int r = 0; r < in.npf; ++r) {
-        if (!in.pf[r] || (reinterpret_cast<uintptr_t>(in.pf[r]) & 15))
-            return fail(NQ_ERR_INVALID_ARGUMENT, "prefetch range %d must start 16-byte aligned", r);
-        base.pf[r] = in.pf[r];
-        base.pf_bytes[r] = in.pf_bytes[r];
-    }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     for (int64_t b0 = 0; b0 < batch; b0 += kMaxBatch) {
         Params p = base;
@@ -1738,11 +1711,6 @@ int nq_gemv_group_ex(int dtype, const nq_gemv_input *input, int64_t batch, int64
     in.res_out = input->residual_out;
     in.eps = input->eps;
     in.act = act;
-    in.npf = input->n_prefetch;
-    for (int r = 0; r < NQ_GEMV_PREFETCH_MAX && r < input->n_prefetch; ++r) {
-        in.pf[r] = input->prefetch[r];
-        in.pf_bytes[r] = input->prefetch_bytes[r];
-    }
     return nq::gemv::group_impl(dtype, in, batch, in_features, n_layers, layers, workspace, workspace_bytes, stream);
 }
 

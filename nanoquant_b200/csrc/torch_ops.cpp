@@ -452,8 +452,7 @@ std::vector<at::Tensor> run_group(const at::Tensor &x, const std::vector<LayerAr
 // SiLU on chosen outputs: one launch for what the decoder otherwise runs as 2-3.
 std::vector<at::Tensor> run_group_ex(const at::Tensor &x, const std::vector<LayerArgs> &ls, int64_t x_mode,
                                      const std::optional<at::Tensor> &x2, const std::optional<at::Tensor> &nw,
-                                     double eps, const std::optional<at::Tensor> &res_out, int64_t act,
-                                     at::TensorList prefetch) {
+                                     double eps, const std::optional<at::Tensor> &res_out, int64_t act) {
     c10::cuda::CUDAGuard guard(x.device());
     const auto st = x.scalar_type();
     nq_gemv_input in{};
@@ -474,13 +473,6 @@ std::vector<at::Tensor> run_group_ex(const at::Tensor &x, const std::vector<Laye
         CHECK_CUDA_CONT((*res_out), st);
         TORCH_CHECK(res_out->numel() == x.numel(), "residual_out must have the shape of x");
         in.residual_out = res_out->data_ptr();
-    }
-    TORCH_CHECK(prefetch.size() <= NQ_GEMV_PREFETCH_MAX, "at most ", NQ_GEMV_PREFETCH_MAX, " prefetch tensors");
-    in.n_prefetch = (int)prefetch.size();
-    for (size_t r = 0; r < prefetch.size(); ++r) {
-        TORCH_CHECK(prefetch[r].is_cuda() && prefetch[r].is_contiguous(), "prefetch tensors must be contiguous CUDA tensors");
-        in.prefetch[r] = prefetch[r].data_ptr();
-        in.prefetch_bytes[r] = (uint64_t)prefetch[r].numel() * prefetch[r].element_size();
     }
     std::vector<nq_gemv_layer> desc(ls.size());
     std::vector<int64_t> ranks(ls.size());
@@ -534,10 +526,10 @@ std::vector<at::Tensor> gemv_group_ex_cuda(const at::Tensor &x, const std::optio
                                            const std::optional<at::Tensor> &residual_out, int64_t act,
                                            at::TensorList s2, at::TensorList vbits,
                                            const c10::List<std::optional<at::Tensor>> &smid, at::TensorList ubits,
-                                           at::TensorList s1, at::TensorList prefetch) {
+                                           at::TensorList s1) {
     std::vector<std::optional<at::Tensor>> sm(smid.begin(), smid.end());
     auto ls = check_group(x, s2.vec(), vbits.vec(), sm, ubits.vec(), s1.vec());
-    auto ys = run_group_ex(x, ls, x_mode, x2, norm_weight, eps, residual_out, act, prefetch);
+    auto ys = run_group_ex(x, ls, x_mode, x2, norm_weight, eps, residual_out, act);
     if (x.dim() == 1)
         for (auto &y : ys) y = y.squeeze(0);
     return ys;
@@ -546,7 +538,7 @@ std::vector<at::Tensor> gemv_group_ex_cuda(const at::Tensor &x, const std::optio
 std::vector<at::Tensor> group_ex_meta(const at::Tensor &x, const std::optional<at::Tensor> &,
                                       const std::optional<at::Tensor> &, double, int64_t, const std::optional<at::Tensor> &,
                                       int64_t, at::TensorList, at::TensorList, const c10::List<std::optional<at::Tensor>> &,
-                                      at::TensorList, at::TensorList s1, at::TensorList) {
+                                      at::TensorList, at::TensorList s1) {
     std::vector<at::Tensor> ys;
     for (const auto &s : s1) {
         auto shape = x.sizes().vec();
@@ -634,8 +626,8 @@ TORCH_LIBRARY(nq_b200, m) {
         "Tensor[] scale_post) -> Tensor[]");
     m.def(
         "gemv_group_ex(Tensor x, Tensor? x2, Tensor? norm_weight, float eps, int x_mode, Tensor(a!)? residual_out, "
-        "int act, Tensor[] scale_pre, Tensor[] v_bits, Tensor?[] scale_mid, Tensor[] u_bits, Tensor[] scale_post, "
-        "Tensor[] prefetch) -> Tensor[]");
+        "int act, Tensor[] scale_pre, Tensor[] v_bits, Tensor?[] scale_mid, Tensor[] u_bits, Tensor[] scale_post) "
+        "-> Tensor[]");
 }
 
 TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {

@@ -300,35 +300,28 @@ class Decoder:
     def _step_logits_fused(self) -> torch.Tensor:
         """Five launches per block: q/k/v with RMSNorm(x + residual) in its prologue, attention
         (RoPE + cache write fused), o, gate/up with RMSNorm(o + residual) in its prologue and
-        SiLU on the gate in its epilogue, down with gate * up in its prologue.  Every GEMV also
-        pulls the sign planes of the GEMV after it into L2."""
+        SiLU on the gate in its epilogue, down with gate * up in its prologue."""
         cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
         ops, eps = torch.ops.nq_b200, cfg.rms_eps
-        planes = lambda ms: [t for m in ms for t in (m.vb, m.ub)]
         d = F.embedding(self.tokens, self.embed)  # the first block's input; no residual yet
         residual = None
-        L = len(self.layers)
         for li, lay in enumerate(self.layers):
             g = lay["qkv"]
             res = torch.empty_like(d)
             q, k, v = ops.gemv_group_ex(d, residual, lay["in_norm"], eps, nqchain.RMSNORM, res, 0, g.s2, g.vb, g.smid,
-                                        g.ub, g.s1, planes([lay["o"]]))
+                                        g.ub, g.s1)
             residual = res
             a = ops.decode_attention_rope(q.view(B, self.hq, D), k.view(B, self.hkv, D), v.view(B, self.hkv, D),
                                           self.pos, self.k_cache[li], self.v_cache[li], cfg.rope_theta)
-            on = lay["o"]
-            o = self._all_reduce(ops.gemv_group_ex(a.view(B, self.hq * D), None, None, 0.0, nqchain.PLAIN, None, 0,
-                                                   [on.s2], [on.vb], [on.smid], [on.ub], [on.s1],
-                                                   planes(lay["gate_up"].members))[0])
+            o = self._all_reduce(lay["o"](a.view(B, self.hq * D)))
             g = lay["gate_up"]
             res = torch.empty_like(o)
             gate, up = ops.gemv_group_ex(o, residual, lay["post_norm"], eps, nqchain.RMSNORM, res, 1, g.s2, g.vb,
-                                         g.smid, g.ub, g.s1, planes([lay["down"]]))
+                                         g.smid, g.ub, g.s1)
             residual = res
             dn = lay["down"]
-            nxt = planes(self.layers[li + 1]["qkv"].members) if li + 1 < L else []
             d = self._all_reduce(ops.gemv_group_ex(gate, up, None, 0.0, nqchain.MUL, None, 0, [dn.s2], [dn.vb],
-                                                   [dn.smid], [dn.ub], [dn.s1], nxt)[0])
+                                                   [dn.smid], [dn.ub], [dn.s1])[0])
         x, _ = ops.rmsnorm(d, residual, self.final_norm, eps)
         return x @ self.lm_head.t()
 

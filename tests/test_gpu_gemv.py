@@ -241,25 +241,25 @@ def test_group_ex_input_modes_match_separate_kernels(dt, batch):
     x2 = torch.randn(batch, 4096, generator=g, device="cuda").to(dt)
     w = (torch.rand(4096, generator=g, device="cuda") + 0.5).to(dt)
     # SILU_MUL and MUL: bit-identical to the separate kernels
-    got = ops.gemv_group_ex(x, x2, None, 0.0, 2, None, 0, *lists, [])
+    got = ops.gemv_group_ex(x, x2, None, 0.0, 2, None, 0, *lists)
     want = ops.gemv_group(ops.silu_mul(x, x2), *lists)
     for a, b in zip(got, want):
         assert torch.equal(a, b)
-    got = ops.gemv_group_ex(x, x2, None, 0.0, 3, None, 0, *lists, [])
+    got = ops.gemv_group_ex(x, x2, None, 0.0, 3, None, 0, *lists)
     want = ops.gemv_group((x.float() * x2.float()).to(dt), *lists)
     for a, b in zip(got, want):
         assert torch.equal(a, b)
     # RMSNORM with and without the residual
     for res_in in (x2, None):
         res_out = torch.empty_like(x)
-        got = ops.gemv_group_ex(x, res_in, w, 1e-5, 1, res_out, 0, *lists, [])
+        got = ops.gemv_group_ex(x, res_in, w, 1e-5, 1, res_out, 0, *lists)
         xn, r = ops.rmsnorm(x, res_in, w, 1e-5)
         want = ops.gemv_group(xn, *lists)
         assert torch.equal(res_out, r)
         for a, b in zip(got, want):
             assert orc.rel_l2(a.float().cpu().numpy(), b.float().cpu().numpy()) <= 1e-3
     # act on the first member only
-    got = ops.gemv_group_ex(x, None, None, 0.0, 0, None, 1, *lists, [])
+    got = ops.gemv_group_ex(x, None, None, 0.0, 0, None, 1, *lists)
     want = ops.gemv_group(x, *lists)
     gate = want[0].float()
     assert orc.rel_l2(got[0].float().cpu().numpy(), (gate / (1 + torch.exp(-gate))).cpu().numpy()) <= 2e-3
