@@ -1,5 +1,6 @@
 // C ABI bookkeeping: status strings, thread-local error messages, per-device
 // properties and the workspace status word.
+#include <cstdlib>
 #include <mutex>
 
 #include "nq_common.cuh"
@@ -26,6 +27,14 @@ int fail(int status, const char *fmt, ...) {
 int cuda_fail(cudaError_t e, const char *what) {
     set_error("%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
     return NQ_ERR_CUDA;
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("NQ_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
 }
 
 const DeviceInfo &device_info(int dev) {

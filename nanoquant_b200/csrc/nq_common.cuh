@@ -32,6 +32,9 @@ void set_error(const char *fmt, ...);
 int fail(int status, const char *fmt, ...);
 int cuda_fail(cudaError_t e, const char *what);
 
+// Whether launches use programmatic dependent launch (env NQ_PDL=0 turns it off).
+bool pdl_enabled();
+
 struct DeviceInfo {
     int sms = 0;
     int max_smem_optin = 0;
@@ -62,6 +65,12 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+
+// Programmatic dependent launch: let the next kernel on the stream be scheduled once every
+// CTA of this one has started (it then waits in pdl_wait until this grid has completed and its
+// memory is visible), and wait for the previous kernel the same way.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");

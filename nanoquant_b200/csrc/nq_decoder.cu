@@ -53,6 +53,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(const T *__re
                                                                    T *__restrict__ res_out, const T *__restrict__ w,
                                                                    T *__restrict__ out, int hidden, float eps) {
     __shared__ float sh[32];
+    pdl_launch_dependents();
+    pdl_wait();
     const size_t row = blockIdx.x;
     const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * hidden);
     const uint4 *rr = res_in ? reinterpret_cast<const uint4 *>(res_in + row * hidden) : nullptr;
@@ -224,6 +226,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     const int tid = threadIdx.x;
     const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int hq = p.hkv * GRP;
+    pdl_launch_dependents();
+    // Programmatic dependent launch: the RoPE variant (one decode step) reads the positions and
+    // issues its cache copies before waiting for the previous kernel -- the positions change
+    // only between steps and the rows before positions[b] were written by earlier steps; the
+    // plain variant waits first.
+    if (!ROPE) pdl_wait();
     const int pos = ROPE ? p.pos[b] : 0;
     int L = ROPE ? pos + 1 : p.seq_len[b];
     L = min(L, p.max_seq);
@@ -231,6 +239,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     const int c0 = chunk * clen;
     T *out = static_cast<T *>(p.out) + ((size_t)b * hq + (size_t)kh * GRP) * D;
     if (L <= 0) {  // nothing to attend to: zeros, written once
+        if (ROPE) pdl_wait();
         if (chunk == 0)
             for (int i = tid; i < GRP * D; i += kAttnThreads) out[i] = fromf<T>(0.f);
         return;
@@ -265,6 +274,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         mrow[tid] = -INFINITY;
         lrow[tid] = 0.f;
     }
+    if (ROPE) pdl_wait();  // q, k and v of this step come from the previous kernel
     // q (rotated here when ROPE) into shared memory; the owner of the new row rotates k too.
     const bool owner = ROPE && pos >= 0 && pos < p.max_seq && (L - 1) / clen == chunk;
     T knew_a = fromf<T>(0.f), knew_b = knew_a, vnew_a = knew_a, vnew_b = knew_a;
@@ -502,8 +512,17 @@ cudaError_t launch_attn(const AttnParams &p, int batch, cudaStream_t s) {
         const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    fn<<<dim3((unsigned)p.nchunk, (unsigned)p.hkv, (unsigned)batch), kAttnThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)p.nchunk, (unsigned)p.hkv, (unsigned)batch);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
 template <bool ROPE>
@@ -551,6 +570,21 @@ int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head
     return NQ_OK;
 }
 
+// 1-D launch with programmatic dependent launch allowed (the kernel calls pdl_wait itself).
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*fn)(KArgs...), unsigned grid, unsigned block, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, fn, static_cast<KArgs>(args)...);
+}
+
 static int sm_count() {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -571,13 +605,13 @@ int nq_rmsnorm(int dtype, const void *x, const void *residual_in, void *residual
                      (((uintptr_t)x | (uintptr_t)residual_in | (uintptr_t)residual_out | (uintptr_t)weight |
                        (uintptr_t)out) & 15) == 0;
     if (vec && dtype == NQ_DTYPE_F16)
-        dec::rmsnorm_vec_kernel<__half><<<(unsigned)rows, dec::kNormThreads, 0, s>>>(
-            (const __half *)x, (const __half *)residual_in, (__half *)residual_out, (const __half *)weight,
-            (__half *)out, (int)hidden, eps);
+        dec::launch_pdl(dec::rmsnorm_vec_kernel<__half>, (unsigned)rows, dec::kNormThreads, s, (const __half *)x,
+                        (const __half *)residual_in, (__half *)residual_out, (const __half *)weight, (__half *)out,
+                        (int)hidden, eps);
     else if (vec && dtype == NQ_DTYPE_BF16)
-        dec::rmsnorm_vec_kernel<__nv_bfloat16><<<(unsigned)rows, dec::kNormThreads, 0, s>>>(
-            (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)residual_in, (__nv_bfloat16 *)residual_out,
-            (const __nv_bfloat16 *)weight, (__nv_bfloat16 *)out, (int)hidden, eps);
+        dec::launch_pdl(dec::rmsnorm_vec_kernel<__nv_bfloat16>, (unsigned)rows, dec::kNormThreads, s,
+                        (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)residual_in, (__nv_bfloat16 *)residual_out,
+                        (const __nv_bfloat16 *)weight, (__nv_bfloat16 *)out, (int)hidden, eps);
     else if (dtype == NQ_DTYPE_F16)
         dec::rmsnorm_kernel<__half><<<(unsigned)rows, 256, 0, s>>>(
             (const __half *)x, (const __half *)residual_in, (__half *)residual_out, (const __half *)weight,

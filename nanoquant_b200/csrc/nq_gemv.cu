@@ -633,8 +633,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     const int tid = threadIdx.x;
     const int G = gridDim.x, c = blockIdx.x;
     const bool do1 = (p.mode & kStage1) != 0, do2 = (p.mode & kStage2) != 0;
-    unsigned long long bar_base = 0;  // thread 0 only
-    if (tid == 0 && p.mode == kFused) bar_base = grid_barrier_base(p.ctrl, (unsigned)G);
+    unsigned long long bar_base = 0;  // thread 0 only; read after pdl_wait
+    pdl_launch_dependents();
     // First touches of the parameter block miss the parameter cache; lane 0 of eight warps
     // reads one field each from different parts of it so that those misses overlap (the
     // prologue would otherwise take them one after another).
@@ -680,8 +680,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     bool vec_rows = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 && (p.in_f % 8) == 0;
     _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) vec_rows = vec_rows && (reinterpret_cast<uintptr_t>(p.m[l].s2) & 15) == 0;
     const int warp_id = tid >> 5;
+    // Weight-side copies first: they do not depend on the previous kernel, so under programmatic
+    // dependent launch they overlap its tail.  Everything that reads the previous kernel's
+    // output (x and the transform inputs, the barrier counter) comes after pdl_wait.
     if (has1) {
-        if ((tid & 31) == 0 && warp_id < kIssuers0) {
+        if ((tid & 31) == 0 && (warp_id == 0 || warp_id == 2)) {
             uint32_t bytes = 0;
             if (warp_id == 0) {
                 if (vec_rows) bytes = (uint32_t)p.in_f * 2u * (uint32_t)p.nm;
@@ -689,26 +692,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 if (vec_rows)
                     _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm)
                         bulk_g2s_pieces(s2s + (size_t)l * in_pad, p.m[l].s2, (uint32_t)p.in_f * 2u, &bars[0]);
-            } else if (warp_id == 1) {
-                // transform inputs: the host guarantees vec_rows and x in shared memory for them
-                if (vec_rows && x_in_smem) bytes += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
-                if (p.x2) bytes += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
-                if (p.xmode == kChainNorm) bytes += (uint32_t)p.in_f * 2u;
-                mbar_arrive_expect_tx(&bars[0], bytes);
-                if (vec_rows && x_in_smem) {
-                    if (in_pad == p.in_f)
-                        bulk_g2s_pieces(xs, p.x, (uint32_t)p.batch * (uint32_t)p.in_f * 2u, &bars[0]);
-                    else
-                        for (int b = 0; b < p.batch; ++b)
-                            bulk_g2s_pieces(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f,
-                                            (uint32_t)p.in_f * 2u, &bars[0]);
-                }
-                if (p.x2)
-                    for (int b = 0; b < p.batch; ++b)
-                        bulk_g2s_pieces(smem + p.off_x2 + (size_t)b * in_pad * 2,
-                                        static_cast<const T *>(p.x2) + (size_t)b * p.in_f, (uint32_t)p.in_f * 2u,
-                                        &bars[0]);
-                if (p.xmode == kChainNorm) bulk_g2s_pieces(smem + p.off_nw, p.nw, (uint32_t)p.in_f * 2u, &bars[0]);
             } else {
                 _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
                     const Member &mb = p.m[l];
@@ -741,14 +724,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 stage_row<T>(s2s + (size_t)l * in_pad, static_cast<const T *>(p.m[l].s2), p.in_f, in_pad);
             }
         }
-        if (x_in_smem)
-            for (int b = 0; b < p.batch; ++b) {
-                if (vec_rows)
-                    zero_tail<T>(xs + (size_t)b * in_pad, p.in_f, in_pad);
-                else
-                    stage_row<T>(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f, p.in_f,
-                                 in_pad);
-            }
     }
     if (has2) {
         // U slabs and s1 slices, one segment per member; segment k of the smem U region starts
@@ -805,6 +780,42 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 (reinterpret_cast<uintptr_t>(s1src) & 15) == 0 ? ((uint32_t)(r1 - r0) * 2u) & ~15u : 0u;
             for (int i = (int)(s1_bulk / 2) + tid; i < r1 - r0; i += kThreads) s1dst[i] = s1src[i];
         }
+    }
+    __syncthreads();
+
+    pdl_wait();  // the previous kernel on the stream has completed; its outputs are visible
+    if (tid == 0 && p.mode == kFused) bar_base = grid_barrier_base(p.ctrl, (unsigned)G);
+    if (has1) {
+        if (tid == 32) {  // warp 1: x and the transform inputs
+            uint32_t bytes = 0;
+            // transform inputs: the host guarantees vec_rows and x in shared memory for them
+            if (vec_rows && x_in_smem) bytes += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
+            if (p.x2) bytes += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
+            if (p.xmode == kChainNorm) bytes += (uint32_t)p.in_f * 2u;
+            mbar_arrive_expect_tx(&bars[0], bytes);
+            if (vec_rows && x_in_smem) {
+                if (in_pad == p.in_f)
+                    bulk_g2s_pieces(xs, p.x, (uint32_t)p.batch * (uint32_t)p.in_f * 2u, &bars[0]);
+                else
+                    for (int b = 0; b < p.batch; ++b)
+                        bulk_g2s_pieces(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f,
+                                        (uint32_t)p.in_f * 2u, &bars[0]);
+            }
+            if (p.x2)
+                for (int b = 0; b < p.batch; ++b)
+                    bulk_g2s_pieces(smem + p.off_x2 + (size_t)b * in_pad * 2,
+                                    static_cast<const T *>(p.x2) + (size_t)b * p.in_f, (uint32_t)p.in_f * 2u,
+                                    &bars[0]);
+            if (p.xmode == kChainNorm) bulk_g2s_pieces(smem + p.off_nw, p.nw, (uint32_t)p.in_f * 2u, &bars[0]);
+        }
+        if (x_in_smem)
+            for (int b = 0; b < p.batch; ++b) {
+                if (vec_rows)
+                    zero_tail<T>(xs + (size_t)b * in_pad, p.in_f, in_pad);
+                else
+                    stage_row<T>(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f, p.in_f,
+                                 in_pad);
+            }
     }
     __syncthreads();
 
@@ -996,27 +1007,37 @@ static int launch(const Plan &plan, cudaStream_t stream) {
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
         attr_set[dev] = true;
     }
+    // programmatic dependent launch: the kernel waits for its predecessor itself (pdl_wait)
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = stream;
+    cfg.attrs = attr;
     if (plan.mode == kFused) {
         const bool decode = plan.prm.fold && plan.prm.x_in_smem && plan.prm.batch <= 4;
-        cudaLaunchConfig_t cfg = {};
+        attr[na].id = cudaLaunchAttributeCooperative;
+        attr[na].val.cooperative = 1;
+        cfg.numAttrs = na + 1;
         cfg.gridDim = dim3(plan.grid);
-        cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = plan.smem;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeCooperative;
-        attr[0].val.cooperative = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
         cudaError_t e = decode ? cudaLaunchKernelEx(&cfg, gemv_kernel<T, true>, plan.prm)
                                : cudaLaunchKernelEx(&cfg, gemv_kernel<T, false>, plan.prm);
         return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv fused launch");
     }
-    gemv_kernel<T, false><<<plan.grid1, kThreads, plan.smem1, stream>>>(plan.prm1);
-    cudaError_t e = cudaGetLastError();
+    cfg.numAttrs = na;
+    cfg.gridDim = dim3(plan.grid1);
+    cfg.dynamicSmemBytes = plan.smem1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<T, false>, plan.prm1);
     if (e != cudaSuccess) return cuda_fail(e, "gemv stage-1 launch");
-    gemv_kernel<T, false><<<plan.grid2, kThreads, plan.smem2, stream>>>(plan.prm2);
-    e = cudaGetLastError();
+    cfg.gridDim = dim3(plan.grid2);
+    cfg.dynamicSmemBytes = plan.smem2;
+    e = cudaLaunchKernelEx(&cfg, gemv_kernel<T, false>, plan.prm2);
     return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv stage-2 launch");
 }
 
