@@ -8,6 +8,7 @@
 // (src/nanoquant/kernel/test_decode.py loads transformers' LlamaForCausalLM): the
 // residual sum is rounded to the model dtype, RMSNorm computes in float32 and rounds
 // once before the weight multiply, attention accumulates in float32.
+#include <algorithm>
 #include <cfloat>
 
 #include "../../include/nq_decoder.h"
@@ -185,6 +186,7 @@ constexpr int kSub = 64;           // positions per sub-block (one ring stage)
 constexpr int kAttnThreads = 128;  // 4 warps
 constexpr int kMaxChunks = 64;     // chunk length grows with max_seq to keep at most this many
 constexpr int kHeadDim = 128;
+constexpr int kAttnMaxStages = 3;  // copy ring depth: sub-block i+2 in flight while i is used
 
 struct AttnParams {
     const void *q;      // [batch, hq, D]; already rotated unless ROPE
@@ -197,7 +199,7 @@ struct AttnParams {
     Ctrl *ctrl;         // status
     unsigned *count;    // [batch][hkv] arrival counters, zero between launches
     float *part;        // [batch][hq][nchunk][D + 2]
-    int hkv, max_seq, nchunk, nsub;
+    int hkv, max_seq, nchunk, nsub, nst;
     float scale, log2_theta;
 };
 
@@ -218,7 +220,7 @@ template <typename T, int GRP, bool ROPE>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
     constexpr int D = kHeadDim;
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ __align__(8) uint64_t bars[kAttnMaxStages];
     __shared__ float mrow[GRP], lrow[GRP], alph[GRP];
     __shared__ float wts[kMaxChunks];
     __shared__ float red[2];
@@ -248,27 +250,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     const int nact = (L + clen - 1) / clen;
     const int c1 = min(c0 + clen, L);
     const int nsb = (c1 - c0 + kSub - 1) / kSub;
-    const int stages = min(2, p.nsub);
+    const int nst = p.nst;  // ring stages: min(kAttnMaxStages, nsub)
     const size_t head_row0 = ((size_t)b * p.hkv + kh) * (size_t)p.max_seq;
     const T *kg = static_cast<const T *>(p.kc) + head_row0 * D;
     const T *vg = static_cast<const T *>(p.vc) + head_row0 * D;
-    T *qsm = reinterpret_cast<T *>(smem + stages * attn_stage_bytes());
+    T *qsm = reinterpret_cast<T *>(smem + nst * attn_stage_bytes());
     float *sc = reinterpret_cast<float *>(qsm + GRP * D);  // [GRP][kSub]
 
-    auto issue = [&](int sb) {  // thread 0: K and V rows of sub-block sb into stage sb & 1
+    auto issue = [&](int sb) {  // thread 0: K and V rows of sub-block sb into stage sb % nst
         const int r0 = c0 + sb * kSub, nr = min(kSub, c1 - r0);
-        unsigned char *st = smem + (sb & 1) * attn_stage_bytes();
+        const int st = sb % nst;
+        unsigned char *dst = smem + st * attn_stage_bytes();
         const uint32_t bytes = (uint32_t)nr * D * (uint32_t)sizeof(T);
-        mbar_arrive_expect_tx(&bars[sb & 1], 2u * bytes);
-        bulk_g2s(st, kg + (size_t)r0 * D, bytes, &bars[sb & 1]);
-        bulk_g2s(st + attn_stage_bytes() / 2, vg + (size_t)r0 * D, bytes, &bars[sb & 1]);
+        mbar_arrive_expect_tx(&bars[st], 2u * bytes);
+        bulk_g2s(dst, kg + (size_t)r0 * D, bytes, &bars[st]);
+        bulk_g2s(dst + attn_stage_bytes() / 2, vg + (size_t)r0 * D, bytes, &bars[st]);
     };
     if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        for (int i = 0; i < kAttnMaxStages; ++i) mbar_init(&bars[i], 1);
         fence_mbar_init();
-        issue(0);
-        if (nsb > 1) issue(1);
+        for (int sb = 0; sb < nst && sb < nsb; ++sb) issue(sb);
     }
     if (tid < GRP) {
         mrow[tid] = -INFINITY;
@@ -322,9 +323,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     for (int g = 0; g < GRP; ++g) o[g][0] = o[g][1] = 0.f;
     for (int sb = 0; sb < nsb; ++sb) {
         const int nv = min(kSub, c1 - (c0 + sb * kSub));
-        const T *ks = reinterpret_cast<const T *>(smem + (sb & 1) * attn_stage_bytes());
+        const T *ks = reinterpret_cast<const T *>(smem + (sb % nst) * attn_stage_bytes());
         T *vs = const_cast<T *>(ks) + kSub * D;
-        mbar_wait(&bars[sb & 1], (uint32_t)(sb >> 1) & 1u, &p.ctrl->status);
+        mbar_wait(&bars[sb % nst], (uint32_t)(sb / nst) & 1u, &p.ctrl->status);
         if (owner && sb == nsb - 1 && tid < D / 2) {  // the new row, as written to the caches
             const int r = (L - 1) - (c0 + sb * kSub);
             T *kr = const_cast<T *>(ks) + r * D;
@@ -404,9 +405,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             }
         }
         __syncthreads();  // stage and scores free again
-        if (tid == 0 && sb + 2 < nsb) {
+        if (tid == 0 && sb + nst < nsb) {
             fence_proxy_async_smem();
-            issue(sb + 2);
+            issue(sb + nst);
         }
     }
     // the two position parities meet in shared memory (stage 0 is free: no copy in flight)
@@ -486,9 +487,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 struct AttnChunks {
     int nsub, nchunk;
 };
+// The most chunks a cache of max_seq positions is ever split into (sizes the workspace).
 inline AttnChunks attn_chunks(int64_t max_seq) {
     const int64_t n64 = (max_seq + kSub - 1) / kSub;
     const int64_t nsub = (n64 + kMaxChunks - 1) / kMaxChunks;
+    return {(int)nsub, (int)((n64 + nsub - 1) / nsub)};
+}
+// The chunking of a launch: about two CTAs per SM over (batch rows x kv heads), so every CTA
+// streams several sub-blocks through its copy ring; never more chunks than attn_chunks().
+inline AttnChunks attn_chunks_for(int64_t max_seq, int64_t heads_x_batch, int sms) {
+    const int64_t n64 = (max_seq + kSub - 1) / kSub;
+    const int64_t target = std::max<int64_t>(1, (2 * (int64_t)sms) / std::max<int64_t>(1, heads_x_batch));
+    const int64_t nsub = std::max<int64_t>(attn_chunks(max_seq).nsub, (n64 + target - 1) / target);
     return {(int)nsub, (int)((n64 + nsub - 1) / nsub)};
 }
 inline size_t attn_count_bytes(int64_t batch, int64_t hq) { return ((size_t)batch * hq * 4 + 255) & ~(size_t)255; }
@@ -505,8 +515,7 @@ __global__ void silu_mul_kernel(const T *__restrict__ gate, const T *__restrict_
 
 template <typename T, int GRP, bool ROPE>
 cudaError_t launch_attn(const AttnParams &p, int batch, cudaStream_t s) {
-    const int stages = p.nsub < 2 ? p.nsub : 2;
-    const size_t smem = stages * attn_stage_bytes() + GRP * kHeadDim * sizeof(T) + GRP * kSub * sizeof(float);
+    const size_t smem = p.nst * attn_stage_bytes() + GRP * kHeadDim * sizeof(T) + GRP * kSub * sizeof(float);
     auto fn = attn_decode_kernel<T, GRP, ROPE>;
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -542,6 +551,8 @@ cudaError_t dispatch_attn(int dtype, int grp, const AttnParams &p, int batch, cu
 }
 
 // Host checks shared by both attention entry points; fills the workspace pointers of p.
+static int sm_count();
+
 int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head_dim, int64_t max_seq,
                  void *workspace, size_t workspace_bytes, AttnParams &p) {
     if (batch <= 0 || hq <= 0 || hkv <= 0 || max_seq <= 0 || max_seq > INT32_MAX)
@@ -557,7 +568,7 @@ int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head
     if (!workspace || workspace_bytes < need) return fail(NQ_ERR_WORKSPACE, "attention workspace needs %zu bytes", need);
     if (((uintptr_t)workspace) & 255) return fail(NQ_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
     if ((((uintptr_t)p.kc) | ((uintptr_t)p.vc)) & 15) return fail(NQ_ERR_INVALID_ARGUMENT, "caches must be 16B aligned");
-    const AttnChunks ch = attn_chunks(max_seq);
+    const AttnChunks ch = attn_chunks_for(max_seq, batch * hkv, sm_count());
     unsigned char *ws = static_cast<unsigned char *>(workspace);
     p.ctrl = reinterpret_cast<Ctrl *>(ws);
     p.count = reinterpret_cast<unsigned *>(ws + sizeof(Ctrl));
@@ -566,6 +577,7 @@ int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head
     p.max_seq = (int)max_seq;
     p.nchunk = ch.nchunk;
     p.nsub = ch.nsub;
+    p.nst = ch.nsub < kAttnMaxStages ? ch.nsub : kAttnMaxStages;
     p.scale = 1.0f / sqrtf((float)head_dim);
     return NQ_OK;
 }
