@@ -183,10 +183,11 @@ __global__ void rope_cache_kernel(T *__restrict__ q, T *__restrict__ k, const T 
 // whose chunk holds position pos[b] rotates k, writes k and v to the caches, and patches its
 // shared-memory copy of that row.  The sequence length is then pos[b] + 1.
 constexpr int kSub = 64;           // positions per sub-block (one ring stage)
-constexpr int kAttnThreads = 128;  // 4 warps
+constexpr int kAttnThreads = 256;  // 8 warps
 constexpr int kMaxChunks = 64;     // chunk length grows with max_seq to keep at most this many
 constexpr int kHeadDim = 128;
 constexpr int kAttnMaxStages = 3;  // copy ring depth: sub-block i+2 in flight while i is used
+constexpr int kClusterChunks = 8;  // chunks of one head combined through distributed shared memory
 
 struct AttnParams {
     const void *q;      // [batch, hq, D]; already rotated unless ROPE
@@ -200,6 +201,7 @@ struct AttnParams {
     unsigned *count;    // [batch][hkv] arrival counters, zero between launches
     float *part;        // [batch][hq][nchunk][D + 2]
     int hkv, max_seq, nchunk, nsub, nst;
+    int cl;             // chunks of a head combined in a cluster (nchunk <= kClusterChunks)
     float scale, log2_theta;
 };
 
@@ -216,16 +218,37 @@ __device__ __forceinline__ float2 f2_of<__nv_bfloat16>(uint32_t w) {
 
 __host__ __device__ constexpr size_t attn_stage_bytes() { return 2u * kSub * kHeadDim * 2u; }  // K + V, 2-byte types
 
-template <typename T, int GRP, bool ROPE>
+// Cluster helpers (the chunks of one head combine their partials through distributed shared
+// memory; every CTA of a cluster is resident at once, and all reach both cluster barriers).
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(const float *local, uint32_t rank) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
+
+// CL: the kClusterChunks chunks of a head form one cluster and rank 0 combines their partials
+// from distributed shared memory; otherwise partials go to the workspace and the CTA that
+// finishes last for its head (atomic counter, reset after) combines them.
+template <typename T, int GRP, bool ROPE, bool CL>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
     constexpr int D = kHeadDim;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kAttnMaxStages];
     __shared__ float mrow[GRP], lrow[GRP], alph[GRP];
     __shared__ float wts[kMaxChunks];
-    __shared__ float red[2];
+    __shared__ float red[kAttnThreads / 32];
     __shared__ int last;
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int hq = p.hkv * GRP;
     pdl_launch_dependents();
@@ -239,17 +262,21 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     L = min(L, p.max_seq);
     const int clen = p.nsub * kSub;
     const int c0 = chunk * clen;
+    const int c1 = max(c0, min(c0 + clen, L));
+    const bool active = c1 > c0;
     T *out = static_cast<T *>(p.out) + ((size_t)b * hq + (size_t)kh * GRP) * D;
-    if (L <= 0) {  // nothing to attend to: zeros, written once
-        if (ROPE) pdl_wait();
-        if (chunk == 0)
-            for (int i = tid; i < GRP * D; i += kAttnThreads) out[i] = fromf<T>(0.f);
-        return;
+    if (!CL) {
+        if (L <= 0) {  // nothing to attend to: zeros, written once
+            if (ROPE) pdl_wait();
+            if (chunk == 0)
+                for (int i = tid; i < GRP * D; i += kAttnThreads) out[i] = fromf<T>(0.f);
+            return;
+        }
+        if (!active) return;  // beyond the sequence: no partial, not counted
     }
-    if (c0 >= L) return;  // beyond the sequence: no partial, not counted
-    const int nact = (L + clen - 1) / clen;
-    const int c1 = min(c0 + clen, L);
-    const int nsb = (c1 - c0 + kSub - 1) / kSub;
+    // (in a cluster every CTA stays to the end; one past the sequence contributes nothing)
+    const int nact = L > 0 ? (L + clen - 1) / clen : 0;
+    const int nsb = active ? (c1 - c0 + kSub - 1) / kSub : 0;
     const int nst = p.nst;  // ring stages: min(kAttnMaxStages, nsub)
     const size_t head_row0 = ((size_t)b * p.hkv + kh) * (size_t)p.max_seq;
     const T *kg = static_cast<const T *>(p.kc) + head_row0 * D;
@@ -277,7 +304,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     }
     if (ROPE) pdl_wait();  // q, k and v of this step come from the previous kernel
     // q (rotated here when ROPE) into shared memory; the owner of the new row rotates k too.
-    const bool owner = ROPE && pos >= 0 && pos < p.max_seq && (L - 1) / clen == chunk;
+    const bool owner = ROPE && L > 0 && pos >= 0 && pos < p.max_seq && (L - 1) / clen == chunk;
     T knew_a = fromf<T>(0.f), knew_b = knew_a, vnew_a = knew_a, vnew_b = knew_a;
     const T *qg = static_cast<const T *>(p.q) + ((size_t)b * hq + (size_t)kh * GRP) * D;
     if (ROPE) {
@@ -315,9 +342,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     }
     __syncthreads();
 
-    const int pp = tid >> 1, hh = tid & 1;   // scores: position pp, half hh of the dimensions
-    const int dp = tid & 63, ph = tid >> 6;  // P.V: dimensions 2dp, 2dp+1; positions of parity ph
-    const int w = tid >> 5, l = tid & 31;
+    const int pp = tid >> 2, qd = tid & 3;   // scores: position pp, dimensions [32 qd, 32 qd + 32)
+    const int dp = tid & 63, pg = tid >> 6;  // P.V: dimensions 2dp, 2dp+1; positions pg, pg + 4, ...
     float o[GRP][2];
 #pragma unroll
     for (int g = 0; g < GRP; ++g) o[g][0] = o[g][1] = 0.f;
@@ -326,25 +352,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         const T *ks = reinterpret_cast<const T *>(smem + (sb % nst) * attn_stage_bytes());
         T *vs = const_cast<T *>(ks) + kSub * D;
         mbar_wait(&bars[sb % nst], (uint32_t)(sb / nst) & 1u, &p.ctrl->status);
-        if (owner && sb == nsb - 1 && tid < D / 2) {  // the new row, as written to the caches
-            const int r = (L - 1) - (c0 + sb * kSub);
-            T *kr = const_cast<T *>(ks) + r * D;
-            kr[tid] = knew_a;
-            kr[tid + D / 2] = knew_b;
-            vs[r * D + tid] = vnew_a;
-            vs[r * D + tid + D / 2] = vnew_b;
+        if (owner && sb == nsb - 1) {  // the new row, as written to the caches
+            if (tid < D / 2) {
+                const int r = (L - 1) - (c0 + sb * kSub);
+                T *kr = const_cast<T *>(ks) + r * D;
+                kr[tid] = knew_a;
+                kr[tid + D / 2] = knew_b;
+                vs[r * D + tid] = vnew_a;
+                vs[r * D + tid + D / 2] = vnew_b;
+            }
+            __syncthreads();
         }
-        if (owner && sb == nsb - 1) __syncthreads();
-        // scores: 16-byte chunks visited in a rotated order so a warp's reads spread over all banks
-        float acc[GRP];
+        // scores: four threads per position, 16-byte chunks in a rotated order (all banks per
+        // warp), two independent accumulators per head
+        float acc[GRP][2];
 #pragma unroll
-        for (int g = 0; g < GRP; ++g) acc[g] = 0.f;
+        for (int g = 0; g < GRP; ++g) acc[g][0] = acc[g][1] = 0.f;
         if (pp < nv) {
-            const T *kr = ks + pp * D + hh * (D / 2);
-            const T *qr = qsm + hh * (D / 2);
+            const T *kr = ks + pp * D + qd * 32;
+            const T *qr = qsm + qd * 32;
 #pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                const int c8 = 8 * ((cc + pp) & 7);
+            for (int cc = 0; cc < 4; ++cc) {
+                const int c8 = 8 * ((cc + pp) & 3);
                 const uint4 kv = *reinterpret_cast<const uint4 *>(kr + c8);
                 const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
@@ -354,40 +383,43 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const float2 kf = f2_of<T>(kw[e]), qf = f2_of<T>(qw[e]);
-                        acc[g] = fmaf(kf.x, qf.x, acc[g]);
-                        acc[g] = fmaf(kf.y, qf.y, acc[g]);
+                        acc[g][e & 1] = fmaf(kf.x, qf.x, acc[g][e & 1]);
+                        acc[g][e & 1] = fmaf(kf.y, qf.y, acc[g][e & 1]);
                     }
                 }
             }
         }
 #pragma unroll
-        for (int g = 0; g < GRP; ++g) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
-        if (hh == 0)
-#pragma unroll
-            for (int g = 0; g < GRP; ++g) sc[g * kSub + pp] = pp < nv ? acc[g] * p.scale : -INFINITY;
+        for (int g = 0; g < GRP; ++g) {
+            float a = acc[g][0] + acc[g][1];
+            a += __shfl_xor_sync(0xffffffffu, a, 1);
+            a += __shfl_xor_sync(0xffffffffu, a, 2);
+            if (qd == 0) sc[g * kSub + pp] = pp < nv ? a * p.scale : -INFINITY;
+        }
         __syncthreads();
-        // online softmax: warp w updates heads w, w + 4, ...
-        for (int g = w; g < GRP; g += kAttnThreads / 32) {
-            const float v0 = sc[g * kSub + l], v1 = sc[g * kSub + l + 32];
+        // online softmax: warp g updates head g
+        if (w < GRP) {
+            const int g = w;
+            const float v0 = sc[g * kSub + lane], v1 = sc[g * kSub + lane + 32];
             float mx = fmaxf(v0, v1);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
             const float mo = mrow[g], mn = fmaxf(mo, mx);
             const float e0 = expf(v0 - mn), e1 = expf(v1 - mn);
-            sc[g * kSub + l] = e0;
-            sc[g * kSub + l + 32] = e1;
-            float s = e0 + e1;
+            sc[g * kSub + lane] = e0;
+            sc[g * kSub + lane + 32] = e1;
+            float sm = e0 + e1;
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-            if (l == 0) {
+            for (int off = 16; off > 0; off >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
+            if (lane == 0) {
                 const float a = expf(mo - mn);
                 alph[g] = a;
-                lrow[g] = lrow[g] * a + s;
+                lrow[g] = lrow[g] * a + sm;
                 mrow[g] = mn;
             }
         }
         __syncthreads();
-        // P.V: half2 of V per thread, conflict-free rows; P broadcast from shared memory
+        // P.V: half2 of V per thread (conflict-free rows), four position groups
 #pragma unroll
         for (int g = 0; g < GRP; ++g) {
             o[g][0] *= alph[g];
@@ -395,7 +427,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         }
         const uint32_t *vw = reinterpret_cast<const uint32_t *>(vs) + dp;
 #pragma unroll 4
-        for (int q2 = ph; q2 < nv; q2 += 2) {
+        for (int q2 = pg; q2 < nv; q2 += 4) {
             const float2 v = f2_of<T>(vw[q2 * (D / 2)]);
 #pragma unroll
             for (int g = 0; g < GRP; ++g) {
@@ -410,23 +442,61 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             issue(sb + nst);
         }
     }
-    // the two position parities meet in shared memory (stage 0 is free: no copy in flight)
-    float *osm = reinterpret_cast<float *>(smem);
-    if (ph == 1)
+    // the four position groups meet in shared memory (stage 0 is free: no copy in flight)
+    float *osm = reinterpret_cast<float *>(smem);  // [3][GRP][D]
+    if (pg > 0)
 #pragma unroll
         for (int g = 0; g < GRP; ++g) {
-            osm[g * D + 2 * dp] = o[g][0];
-            osm[g * D + 2 * dp + 1] = o[g][1];
+            osm[((pg - 1) * GRP + g) * D + 2 * dp] = o[g][0];
+            osm[((pg - 1) * GRP + g) * D + 2 * dp + 1] = o[g][1];
         }
     __syncthreads();
-    if (ph == 0)
+    if (pg == 0)
 #pragma unroll
-        for (int g = 0; g < GRP; ++g) {
-            o[g][0] += osm[g * D + 2 * dp];
-            o[g][1] += osm[g * D + 2 * dp + 1];
+        for (int g = 0; g < GRP; ++g)
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+                o[g][0] += osm[(q * GRP + g) * D + 2 * dp];
+                o[g][1] += osm[(q * GRP + g) * D + 2 * dp + 1];
+            }
+    if (CL) {
+        // this chunk's partial (unnormalised o, max, sum) in its own shared memory, then rank 0
+        // of the cluster combines all kClusterChunks of them
+        float *part = reinterpret_cast<float *>(smem + 16384);  // [GRP][D + 2], inside stage 0
+        if (pg == 0)
+#pragma unroll
+            for (int g = 0; g < GRP; ++g) {
+                part[g * (D + 2) + 2 * dp] = o[g][0];
+                part[g * (D + 2) + 2 * dp + 1] = o[g][1];
+                if (dp == 0) {
+                    part[g * (D + 2) + D] = mrow[g];
+                    part[g * (D + 2) + D + 1] = lrow[g];
+                }
+            }
+        cluster_sync_all();
+        if (cluster_rank() == 0 && tid < D) {
+            for (int g = 0; g < GRP; ++g) {
+                float M = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < kClusterChunks; ++c) M = fmaxf(M, ld_cluster_f32(part + g * (D + 2) + D, c));
+                float num = 0.f, den = 0.f;
+#pragma unroll
+                for (int c = 0; c < kClusterChunks; ++c) {
+                    const float lc = ld_cluster_f32(part + g * (D + 2) + D + 1, c);
+                    const float mc = ld_cluster_f32(part + g * (D + 2) + D, c);
+                    const float wc = lc > 0.f ? expf(mc - M) : 0.f;
+                    den = fmaf(wc, lc, den);
+                    num = fmaf(wc, ld_cluster_f32(part + g * (D + 2) + tid, c), num);
+                }
+                out[g * D + tid] = fromf<T>(den > 0.f ? num / den : 0.f);
+            }
         }
+        cluster_sync_all();  // the partials stay alive until rank 0 has read them
+        return;
+    }
+    float *pbase = p.part + ((size_t)b * hq + (size_t)kh * GRP) * p.nchunk * (D + 2);
     if (nact == 1) {  // the whole sequence was this chunk
-        if (ph == 0)
+        if (pg == 0)
 #pragma unroll
             for (int g = 0; g < GRP; ++g) {
                 const float inv = 1.f / lrow[g];
@@ -435,8 +505,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             }
         return;
     }
-    float *pbase = p.part + ((size_t)b * hq + (size_t)kh * GRP) * p.nchunk * (D + 2);
-    if (ph == 0)
+    if (pg == 0)
 #pragma unroll
         for (int g = 0; g < GRP; ++g) {
             float *pc = pbase + ((size_t)g * p.nchunk + chunk) * (D + 2);
@@ -450,19 +519,19 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // combine: out = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c
+    // combine: out = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c  (nact <= kMaxChunks = 64)
     for (int g = 0; g < GRP; ++g) {
-        const float *pg = pbase + (size_t)g * p.nchunk * (D + 2);
+        const float *pg_ = pbase + (size_t)g * p.nchunk * (D + 2);
         float mc = -INFINITY, lc = 0.f;
         if (tid < nact) {
-            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pg + (size_t)tid * (D + 2) + D));
+            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pg_ + (size_t)tid * (D + 2) + D));
             mc = ml.x;
             lc = ml.y;
         }
         float mx = mc;
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        if (l == 0 && w < 2) red[w] = mx;
+        if (lane == 0 && w < 2) red[w] = mx;
         __syncthreads();
         const float M = fmaxf(red[0], red[1]);
         const float wc = tid < nact ? expf(mc - M) : 0.f;
@@ -471,13 +540,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
         __syncthreads();
-        if (l == 0 && w < 2) red[w] = den;
+        if (lane == 0 && w < 2) red[w] = den;
         __syncthreads();
         den = red[0] + red[1];
-        float num = 0.f;
+        if (tid < D) {
+            float num = 0.f;
 #pragma unroll 8
-        for (int c = 0; c < nact; ++c) num = fmaf(wts[c], __ldcg(pg + (size_t)c * (D + 2) + tid), num);
-        out[g * D + tid] = fromf<T>(num / den);
+            for (int c = 0; c < nact; ++c) num = fmaf(wts[c], __ldcg(pg_ + (size_t)c * (D + 2) + tid), num);
+            out[g * D + tid] = fromf<T>(num / den);
+        }
         __syncthreads();  // red / wts reused by the next head
     }
     if (tid == 0) *cnt = 0u;
@@ -515,22 +586,34 @@ __global__ void silu_mul_kernel(const T *__restrict__ gate, const T *__restrict_
 
 template <typename T, int GRP, bool ROPE>
 cudaError_t launch_attn(const AttnParams &p, int batch, cudaStream_t s) {
+    // stage 0 also holds the final position-group reduction (16 KB) and the cluster partial
     const size_t smem = p.nst * attn_stage_bytes() + GRP * kHeadDim * sizeof(T) + GRP * kSub * sizeof(float);
-    auto fn = attn_decode_kernel<T, GRP, ROPE>;
+    auto fn = p.cl ? attn_decode_kernel<T, GRP, ROPE, true> : attn_decode_kernel<T, GRP, ROPE, false>;
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)p.nchunk, (unsigned)p.hkv, (unsigned)batch);
+    cfg.gridDim = dim3(p.cl ? (unsigned)kClusterChunks : (unsigned)p.nchunk, (unsigned)p.hkv, (unsigned)batch);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (p.cl) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = kClusterChunks;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
@@ -578,6 +661,7 @@ int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head
     p.nchunk = ch.nchunk;
     p.nsub = ch.nsub;
     p.nst = ch.nsub < kAttnMaxStages ? ch.nsub : kAttnMaxStages;
+    p.cl = ch.nchunk <= kClusterChunks ? 1 : 0;
     p.scale = 1.0f / sqrtf((float)head_dim);
     return NQ_OK;
 }
