@@ -186,7 +186,8 @@ constexpr int kSub = 64;           // positions per sub-block (one ring stage)
 constexpr int kAttnThreads = 256;  // 8 warps
 constexpr int kMaxChunks = 64;     // chunk length grows with max_seq to keep at most this many
 constexpr int kHeadDim = 128;
-constexpr int kAttnMaxStages = 3;  // copy ring depth: sub-block i+2 in flight while i is used
+constexpr int kAttnMaxStages = 6;  // copy ring depth (sub-blocks of K or V in flight)
+constexpr size_t kAttnScoreBytes = 48 * 1024;  // per-chunk score buffer limit (GRP x chunk x 4 B)
 constexpr int kClusterChunks = 8;  // chunks of one head combined through distributed shared memory
 
 struct AttnParams {
@@ -216,7 +217,7 @@ __device__ __forceinline__ float2 f2_of<__nv_bfloat16>(uint32_t w) {
     return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162 *>(&w));
 }
 
-__host__ __device__ constexpr size_t attn_stage_bytes() { return 2u * kSub * kHeadDim * 2u; }  // K + V, 2-byte types
+__host__ __device__ constexpr size_t attn_stage_bytes() { return (size_t)kSub * kHeadDim * 2u; }  // K or V, 2-byte types
 
 // Cluster helpers (the chunks of one head combine their partials through distributed shared
 // memory; every CTA of a cluster is resident at once, and all reach both cluster barriers).
@@ -244,7 +245,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     constexpr int D = kHeadDim;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kAttnMaxStages];
-    __shared__ float mrow[GRP], lrow[GRP], alph[GRP];
+    __shared__ float mrow[GRP], lrow[GRP];
     __shared__ float wts[kMaxChunks];
     __shared__ float red[kAttnThreads / 32];
     __shared__ int last;
@@ -276,29 +277,31 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     }
     // (in a cluster every CTA stays to the end; one past the sequence contributes nothing)
     const int nact = L > 0 ? (L + clen - 1) / clen : 0;
-    const int nsb = active ? (c1 - c0 + kSub - 1) / kSub : 0;
-    const int nst = p.nst;  // ring stages: min(kAttnMaxStages, nsub)
+    const int npos = c1 - c0;                               // positions of this chunk
+    const int nsb = active ? (npos + kSub - 1) / kSub : 0;  // 64-position sub-blocks
+    const int nst = p.nst;                                  // ring stages of one sub-block of K or V
     const size_t head_row0 = ((size_t)b * p.hkv + kh) * (size_t)p.max_seq;
     const T *kg = static_cast<const T *>(p.kc) + head_row0 * D;
     const T *vg = static_cast<const T *>(p.vc) + head_row0 * D;
     T *qsm = reinterpret_cast<T *>(smem + nst * attn_stage_bytes());
-    float *sc = reinterpret_cast<float *>(qsm + GRP * D);  // [GRP][kSub]
+    float *sc = reinterpret_cast<float *>(qsm + GRP * D);  // [GRP][clen]: scores, then P
 
-    auto issue = [&](int sb) {  // thread 0: K and V rows of sub-block sb into stage sb % nst
+    // Copy items 0 .. 2 nsb - 1: the chunk's K sub-blocks, then its V sub-blocks.
+    auto issue = [&](int it) {  // thread 0
+        const bool isv = it >= nsb;
+        const int sb = isv ? it - nsb : it;
         const int r0 = c0 + sb * kSub, nr = min(kSub, c1 - r0);
-        const int st = sb % nst;
-        unsigned char *dst = smem + st * attn_stage_bytes();
+        const int st = it % nst;
         const uint32_t bytes = (uint32_t)nr * D * (uint32_t)sizeof(T);
-        mbar_arrive_expect_tx(&bars[st], 2u * bytes);
-        bulk_g2s(dst, kg + (size_t)r0 * D, bytes, &bars[st]);
-        bulk_g2s(dst + attn_stage_bytes() / 2, vg + (size_t)r0 * D, bytes, &bars[st]);
+        mbar_arrive_expect_tx(&bars[st], bytes);
+        bulk_g2s(smem + st * attn_stage_bytes(), (isv ? vg : kg) + (size_t)r0 * D, bytes, &bars[st]);
     };
     if (tid == 0) {
         for (int i = 0; i < kAttnMaxStages; ++i) mbar_init(&bars[i], 1);
         fence_mbar_init();
-        for (int sb = 0; sb < nst && sb < nsb; ++sb) issue(sb);
+        for (int it = 0; it < nst && it < 2 * nsb; ++it) issue(it);
     }
-    if (tid < GRP) {
+    if (tid < GRP) {  // an empty chunk's partial: no mass (a cluster combine weights it 0)
         mrow[tid] = -INFINITY;
         lrow[tid] = 0.f;
     }
@@ -342,29 +345,21 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     }
     __syncthreads();
 
-    const int pp = tid >> 2, qd = tid & 3;   // scores: position pp, dimensions [32 qd, 32 qd + 32)
-    const int dp = tid & 63, pg = tid >> 6;  // P.V: dimensions 2dp, 2dp+1; positions pg, pg + 4, ...
-    float o[GRP][2];
-#pragma unroll
-    for (int g = 0; g < GRP; ++g) o[g][0] = o[g][1] = 0.f;
-    for (int sb = 0; sb < nsb; ++sb) {
-        const int nv = min(kSub, c1 - (c0 + sb * kSub));
-        const T *ks = reinterpret_cast<const T *>(smem + (sb % nst) * attn_stage_bytes());
-        T *vs = const_cast<T *>(ks) + kSub * D;
-        mbar_wait(&bars[sb % nst], (uint32_t)(sb / nst) & 1u, &p.ctrl->status);
-        if (owner && sb == nsb - 1) {  // the new row, as written to the caches
+    const int rnew = owner ? (L - 1) - c0 : -1;  // chunk row of the new position
+    // ---- phase 1: scores of every position of the chunk (four threads per position, 16-byte
+    // chunks in a rotated order so a warp's reads spread over all banks, two accumulators)
+    const int pp = tid >> 2, qd = tid & 3;
+    for (int it = 0; it < nsb; ++it) {
+        const int nv = min(kSub, npos - it * kSub);
+        T *ks = reinterpret_cast<T *>(smem + (it % nst) * attn_stage_bytes());
+        mbar_wait(&bars[it % nst], (uint32_t)(it / nst) & 1u, &p.ctrl->status);
+        if (rnew >= it * kSub && rnew < it * kSub + kSub) {  // the new key row, as written to the cache
             if (tid < D / 2) {
-                const int r = (L - 1) - (c0 + sb * kSub);
-                T *kr = const_cast<T *>(ks) + r * D;
-                kr[tid] = knew_a;
-                kr[tid + D / 2] = knew_b;
-                vs[r * D + tid] = vnew_a;
-                vs[r * D + tid + D / 2] = vnew_b;
+                ks[(rnew - it * kSub) * D + tid] = knew_a;
+                ks[(rnew - it * kSub) * D + tid + D / 2] = knew_b;
             }
             __syncthreads();
         }
-        // scores: four threads per position, 16-byte chunks in a rotated order (all banks per
-        // warp), two independent accumulators per head
         float acc[GRP][2];
 #pragma unroll
         for (int g = 0; g < GRP; ++g) acc[g][0] = acc[g][1] = 0.f;
@@ -394,52 +389,78 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             float a = acc[g][0] + acc[g][1];
             a += __shfl_xor_sync(0xffffffffu, a, 1);
             a += __shfl_xor_sync(0xffffffffu, a, 2);
-            if (qd == 0) sc[g * kSub + pp] = pp < nv ? a * p.scale : -INFINITY;
+            if (qd == 0 && pp < nv) sc[g * clen + it * kSub + pp] = a * p.scale;
+        }
+        __syncthreads();  // the stage is free again
+        if (tid == 0 && it + nst < 2 * nsb) {
+            fence_proxy_async_smem();
+            issue(it + nst);
+        }
+    }
+    // ---- phase 2: one softmax per head over the whole chunk: P = e^(s - m), l = sum P
+    for (int g = 0; g < GRP && nsb > 0; ++g) {
+        float mx = -INFINITY;
+        for (int i = tid; i < npos; i += kAttnThreads) mx = fmaxf(mx, sc[g * clen + i]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        if (lane == 0) red[w] = mx;
+        __syncthreads();
+        float m = red[0];
+#pragma unroll
+        for (int i = 1; i < kAttnThreads / 32; ++i) m = fmaxf(m, red[i]);
+        float sm = 0.f;
+        for (int i = tid; i < npos; i += kAttnThreads) {
+            const float e = expf(sc[g * clen + i] - m);
+            sc[g * clen + i] = e;
+            sm += e;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
+        __syncthreads();  // everyone has read red (the max) before it is reused
+        if (lane == 0) red[w] = sm;
+        __syncthreads();
+        if (tid == 0) {
+            float l = 0.f;
+#pragma unroll
+            for (int i = 0; i < kAttnThreads / 32; ++i) l += red[i];
+            mrow[g] = m;
+            lrow[g] = l;
         }
         __syncthreads();
-        // online softmax: warp g updates head g
-        if (w < GRP) {
-            const int g = w;
-            const float v0 = sc[g * kSub + lane], v1 = sc[g * kSub + lane + 32];
-            float mx = fmaxf(v0, v1);
+    }
+    // ---- phase 3: P.V over the V sub-blocks (half2 of V per thread, four position groups)
+    const int dp = tid & 63, pg = tid >> 6;
+    float o[GRP][2];
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            const float mo = mrow[g], mn = fmaxf(mo, mx);
-            const float e0 = expf(v0 - mn), e1 = expf(v1 - mn);
-            sc[g * kSub + lane] = e0;
-            sc[g * kSub + lane + 32] = e1;
-            float sm = e0 + e1;
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
-            if (lane == 0) {
-                const float a = expf(mo - mn);
-                alph[g] = a;
-                lrow[g] = lrow[g] * a + sm;
-                mrow[g] = mn;
+    for (int g = 0; g < GRP; ++g) o[g][0] = o[g][1] = 0.f;
+    for (int it = nsb; it < 2 * nsb; ++it) {
+        const int sb = it - nsb;
+        const int nv = min(kSub, npos - sb * kSub);
+        T *vs = reinterpret_cast<T *>(smem + (it % nst) * attn_stage_bytes());
+        mbar_wait(&bars[it % nst], (uint32_t)(it / nst) & 1u, &p.ctrl->status);
+        if (rnew >= sb * kSub && rnew < sb * kSub + kSub) {  // the new value row
+            if (tid < D / 2) {
+                vs[(rnew - sb * kSub) * D + tid] = vnew_a;
+                vs[(rnew - sb * kSub) * D + tid + D / 2] = vnew_b;
             }
-        }
-        __syncthreads();
-        // P.V: half2 of V per thread (conflict-free rows), four position groups
-#pragma unroll
-        for (int g = 0; g < GRP; ++g) {
-            o[g][0] *= alph[g];
-            o[g][1] *= alph[g];
+            __syncthreads();
         }
         const uint32_t *vw = reinterpret_cast<const uint32_t *>(vs) + dp;
+        const float *pb = sc + sb * kSub;
 #pragma unroll 4
         for (int q2 = pg; q2 < nv; q2 += 4) {
             const float2 v = f2_of<T>(vw[q2 * (D / 2)]);
 #pragma unroll
             for (int g = 0; g < GRP; ++g) {
-                const float pw = sc[g * kSub + q2];
+                const float pw = pb[g * clen + q2];
                 o[g][0] = fmaf(pw, v.x, o[g][0]);
                 o[g][1] = fmaf(pw, v.y, o[g][1]);
             }
         }
-        __syncthreads();  // stage and scores free again
-        if (tid == 0 && sb + nst < nsb) {
+        __syncthreads();  // the stage is free again
+        if (tid == 0 && it + nst < 2 * nsb) {
             fence_proxy_async_smem();
-            issue(sb + nst);
+            issue(it + nst);
         }
     }
     // the four position groups meet in shared memory (stage 0 is free: no copy in flight)
@@ -566,10 +587,15 @@ inline AttnChunks attn_chunks(int64_t max_seq) {
 }
 // The chunking of a launch: about two CTAs per SM over (batch rows x kv heads), so every CTA
 // streams several sub-blocks through its copy ring; never more chunks than attn_chunks().
-inline AttnChunks attn_chunks_for(int64_t max_seq, int64_t heads_x_batch, int sms) {
+// The chunk's scores stay in shared memory, so a chunk is at most kAttnScoreBytes / (grp x 4 B)
+// positions; nsub = 0 when max_seq needs longer chunks than that (more than kMaxChunks).
+inline AttnChunks attn_chunks_for(int64_t max_seq, int64_t heads_x_batch, int sms, int grp) {
     const int64_t n64 = (max_seq + kSub - 1) / kSub;
     const int64_t target = std::max<int64_t>(1, (2 * (int64_t)sms) / std::max<int64_t>(1, heads_x_batch));
-    const int64_t nsub = std::max<int64_t>(attn_chunks(max_seq).nsub, (n64 + target - 1) / target);
+    const int64_t nsub_cap = (int64_t)(kAttnScoreBytes / ((size_t)grp * kSub * sizeof(float)));
+    const int64_t nsub_min = attn_chunks(max_seq).nsub;
+    if (nsub_min > nsub_cap) return {0, 0};
+    const int64_t nsub = std::min(nsub_cap, std::max<int64_t>(nsub_min, (n64 + target - 1) / target));
     return {(int)nsub, (int)((n64 + nsub - 1) / nsub)};
 }
 inline size_t attn_count_bytes(int64_t batch, int64_t hq) { return ((size_t)batch * hq * 4 + 255) & ~(size_t)255; }
@@ -586,8 +612,10 @@ __global__ void silu_mul_kernel(const T *__restrict__ gate, const T *__restrict_
 
 template <typename T, int GRP, bool ROPE>
 cudaError_t launch_attn(const AttnParams &p, int batch, cudaStream_t s) {
-    // stage 0 also holds the final position-group reduction (16 KB) and the cluster partial
-    const size_t smem = p.nst * attn_stage_bytes() + GRP * kHeadDim * sizeof(T) + GRP * kSub * sizeof(float);
+    // the ring (>= 2 stages) also holds the final position-group reduction (< 16 KB) and the
+    // cluster partial (at 16 KB) once the chunk is done
+    const size_t smem = p.nst * attn_stage_bytes() + GRP * kHeadDim * sizeof(T) +
+                        (size_t)GRP * p.nsub * kSub * sizeof(float);
     auto fn = p.cl ? attn_decode_kernel<T, GRP, ROPE, true> : attn_decode_kernel<T, GRP, ROPE, false>;
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -651,7 +679,10 @@ int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head
     if (!workspace || workspace_bytes < need) return fail(NQ_ERR_WORKSPACE, "attention workspace needs %zu bytes", need);
     if (((uintptr_t)workspace) & 255) return fail(NQ_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
     if ((((uintptr_t)p.kc) | ((uintptr_t)p.vc)) & 15) return fail(NQ_ERR_INVALID_ARGUMENT, "caches must be 16B aligned");
-    const AttnChunks ch = attn_chunks_for(max_seq, batch * hkv, sm_count());
+    const AttnChunks ch = attn_chunks_for(max_seq, batch * hkv, sm_count(), (int)grp);
+    if (ch.nsub == 0)
+        return fail(NQ_ERR_UNSUPPORTED, "max_seq %lld needs chunks longer than the %zu-byte score buffer allows",
+                    (long long)max_seq, kAttnScoreBytes);
     unsigned char *ws = static_cast<unsigned char *>(workspace);
     p.ctrl = reinterpret_cast<Ctrl *>(ws);
     p.count = reinterpret_cast<unsigned *>(ws + sizeof(Ctrl));
@@ -660,7 +691,7 @@ int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head
     p.max_seq = (int)max_seq;
     p.nchunk = ch.nchunk;
     p.nsub = ch.nsub;
-    p.nst = ch.nsub < kAttnMaxStages ? ch.nsub : kAttnMaxStages;
+    p.nst = 2 * ch.nsub < kAttnMaxStages ? 2 * ch.nsub : kAttnMaxStages;
     p.cl = ch.nchunk <= kClusterChunks ? 1 : 0;
     p.scale = 1.0f / sqrtf((float)head_dim);
     return NQ_OK;
