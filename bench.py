@@ -335,9 +335,7 @@ def run_nq(args, world, rank, local):
     alg_bytes, us_launch, n_lin = gemv_roofline(dec)
     peak, peak_kind = peaks()
     achieved = alg_bytes / (us_launch * 1e-6) / 1e9
-    # per layer: gemv x4 (q/k/v and gate/up grouped), rmsnorm x2, attention (rope + cache write fused), silu;
-    # then the final norm
-    launches_per_step = cfg.layers * (4 + 2 + 1 + 1) + 1
+    launches_per_step = dec.own_launches_per_step()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

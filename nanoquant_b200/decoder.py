@@ -326,6 +326,16 @@ class Decoder:
         return x @ self.lm_head.t()
 
     @torch.no_grad()
+    def own_launches_per_step(self) -> int:
+        """Kernels of this package that one decode step launches (library kernels such as the
+        lm_head GEMM, argmax and the embedding gather are not counted)."""
+        n = self.cfg.layers
+        if self.chain_ws is not None:
+            return 1 + n * 2 + 1        # first q/k/v chain; attention + block chain per layer; final norm
+        if self.fuse_neighbours and self.batch <= 8:
+            return n * 5 + 1            # q/k/v, attention, o, gate/up, down; final norm
+        return n * (4 + 2 + 1 + 1) + 1  # four GEMVs, two norms, attention, SiLU·up; final norm
+
     def step_logits(self) -> torch.Tensor:
         """Logits for the current tokens at the current positions (writes the caches)."""
         if self.chain_ws is not None:
