@@ -261,14 +261,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     const int pos = ROPE ? p.pos[b] : 0;
     int L = ROPE ? pos + 1 : p.seq_len[b];
     L = min(L, p.max_seq);
-    // chunks of equal length for this row's actual sequence (not max_seq): every CTA streams
-    // the same number of rows, so the SMs finish together
-    const int nchunk = (int)gridDim.x;
-    const int clen = L > 0 ? (L + nchunk - 1) / nchunk : 1;
+    const int clen = p.nsub * kSub;
     const int c0 = chunk * clen;
     const int c1 = max(c0, min(c0 + clen, L));
     const bool active = c1 > c0;
-    const int sstride = p.nsub * kSub;  // score-buffer stride: the longest chunk max_seq allows
     T *out = static_cast<T *>(p.out) + ((size_t)b * hq + (size_t)kh * GRP) * D;
     if (!CL) {
         if (L <= 0) {  // nothing to attend to: zeros, written once
@@ -288,7 +284,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     const T *kg = static_cast<const T *>(p.kc) + head_row0 * D;
     const T *vg = static_cast<const T *>(p.vc) + head_row0 * D;
     T *qsm = reinterpret_cast<T *>(smem + nst * attn_stage_bytes());
-    float *sc = reinterpret_cast<float *>(qsm + GRP * D);  // [GRP][sstride]: scores, then P
+    float *sc = reinterpret_cast<float *>(qsm + GRP * D);  // [GRP][clen]: scores, then P
 
     // Copy items 0 .. 2 nsb - 1: the chunk's K sub-blocks, then its V sub-blocks.
     auto issue = [&](int it) {  // thread 0
@@ -393,7 +389,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             float a = acc[g][0] + acc[g][1];
             a += __shfl_xor_sync(0xffffffffu, a, 1);
             a += __shfl_xor_sync(0xffffffffu, a, 2);
-            if (qd == 0 && pp < nv) sc[g * sstride + it * kSub + pp] = a * p.scale;
+            if (qd == 0 && pp < nv) sc[g * clen + it * kSub + pp] = a * p.scale;
         }
         __syncthreads();  // the stage is free again
         if (tid == 0 && it + nst < 2 * nsb) {
@@ -404,7 +400,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     // ---- phase 2: one softmax per head over the whole chunk: P = e^(s - m), l = sum P
     for (int g = 0; g < GRP && nsb > 0; ++g) {
         float mx = -INFINITY;
-        for (int i = tid; i < npos; i += kAttnThreads) mx = fmaxf(mx, sc[g * sstride + i]);
+        for (int i = tid; i < npos; i += kAttnThreads) mx = fmaxf(mx, sc[g * clen + i]);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
         if (lane == 0) red[w] = mx;
@@ -414,8 +410,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         for (int i = 1; i < kAttnThreads / 32; ++i) m = fmaxf(m, red[i]);
         float sm = 0.f;
         for (int i = tid; i < npos; i += kAttnThreads) {
-            const float e = expf(sc[g * sstride + i] - m);
-            sc[g * sstride + i] = e;
+            const float e = expf(sc[g * clen + i] - m);
+            sc[g * clen + i] = e;
             sm += e;
         }
 #pragma unroll
@@ -456,7 +452,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             const float2 v = f2_of<T>(vw[q2 * (D / 2)]);
 #pragma unroll
             for (int g = 0; g < GRP; ++g) {
-                const float pw = pb[g * sstride + q2];
+                const float pw = pb[g * clen + q2];
                 o[g][0] = fmaf(pw, v.x, o[g][0]);
                 o[g][1] = fmaf(pw, v.y, o[g][1]);
             }
@@ -519,7 +515,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         cluster_sync_all();  // the partials stay alive until rank 0 has read them
         return;
     }
-    float *pbase = p.part + ((size_t)b * hq + (size_t)kh * GRP) * nchunk * (D + 2);
+    float *pbase = p.part + ((size_t)b * hq + (size_t)kh * GRP) * p.nchunk * (D + 2);
     if (nact == 1) {  // the whole sequence was this chunk
         if (pg == 0)
 #pragma unroll
@@ -533,7 +529,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     if (pg == 0)
 #pragma unroll
         for (int g = 0; g < GRP; ++g) {
-            float *pc = pbase + ((size_t)g * nchunk + chunk) * (D + 2);
+            float *pc = pbase + ((size_t)g * p.nchunk + chunk) * (D + 2);
             *reinterpret_cast<float2 *>(pc + 2 * dp) = make_float2(o[g][0], o[g][1]);
             if (dp == 0) *reinterpret_cast<float2 *>(pc + D) = make_float2(mrow[g], lrow[g]);
         }
@@ -546,7 +542,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     __threadfence();
     // combine: out = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c  (nact <= kMaxChunks = 64)
     for (int g = 0; g < GRP; ++g) {
-        const float *pg_ = pbase + (size_t)g * nchunk * (D + 2);
+        const float *pg_ = pbase + (size_t)g * p.nchunk * (D + 2);
         float mc = -INFINITY, lc = 0.f;
         if (tid < nact) {
             const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pg_ + (size_t)tid * (D + 2) + D));
@@ -594,21 +590,13 @@ inline AttnChunks attn_chunks(int64_t max_seq) {
 // The chunk's scores stay in shared memory, so a chunk is at most kAttnScoreBytes / (grp x 4 B)
 // positions; nsub = 0 when max_seq needs longer chunks than that (more than kMaxChunks).
 inline AttnChunks attn_chunks_for(int64_t max_seq, int64_t heads_x_batch, int sms, int grp) {
-    // chunks per (batch row, kv head): one cluster of kClusterChunks while that keeps the grid
-    // within two CTAs per SM, else about two CTAs per SM, never more than the workspace holds
-    const int64_t nmax = attn_chunks(max_seq).nchunk;
-    const int64_t hb = std::max<int64_t>(1, heads_x_batch);
-    int64_t nchunk = hb * kClusterChunks <= 2 * (int64_t)sms ? kClusterChunks : (2 * (int64_t)sms) / hb;
-    nchunk = std::max<int64_t>(1, std::min(nchunk, nmax));
-    // the score buffer holds the longest chunk: ceil(max_seq / nchunk) positions
+    const int64_t n64 = (max_seq + kSub - 1) / kSub;
+    const int64_t target = std::max<int64_t>(1, (2 * (int64_t)sms) / std::max<int64_t>(1, heads_x_batch));
     const int64_t nsub_cap = (int64_t)(kAttnScoreBytes / ((size_t)grp * kSub * sizeof(float)));
-    int64_t nsub = ((max_seq + nchunk - 1) / nchunk + kSub - 1) / kSub;
-    while (nsub > nsub_cap && nchunk < nmax) {
-        ++nchunk;
-        nsub = ((max_seq + nchunk - 1) / nchunk + kSub - 1) / kSub;
-    }
-    if (nsub > nsub_cap) return {0, 0};
-    return {(int)nsub, (int)nchunk};
+    const int64_t nsub_min = attn_chunks(max_seq).nsub;
+    if (nsub_min > nsub_cap) return {0, 0};
+    const int64_t nsub = std::min(nsub_cap, std::max<int64_t>(nsub_min, (n64 + target - 1) / target));
+    return {(int)nsub, (int)((n64 + nsub - 1) / nsub)};
 }
 inline size_t attn_count_bytes(int64_t batch, int64_t hq) { return ((size_t)batch * hq * 4 + 255) & ~(size_t)255; }
 
@@ -701,11 +689,10 @@ int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head
     p.part = reinterpret_cast<float *>(ws + sizeof(Ctrl) + attn_count_bytes(batch, hq));
     p.hkv = (int)hkv;
     p.max_seq = (int)max_seq;
+    p.nchunk = ch.nchunk;
+    p.nsub = ch.nsub;
+    p.nst = 2 * ch.nsub < kAttnMaxStages ? 2 * ch.nsub : kAttnMaxStages;
     p.cl = ch.nchunk <= kClusterChunks ? 1 : 0;
-    // a cluster launch always has kClusterChunks chunks per head (the surplus ones stay empty)
-    p.nchunk = p.cl ? kClusterChunks : ch.nchunk;
-    p.nsub = p.cl ? (int)((((max_seq + kClusterChunks - 1) / kClusterChunks) + kSub - 1) / kSub) : ch.nsub;
-    p.nst = 2 * p.nsub < kAttnMaxStages ? 2 * p.nsub : kAttnMaxStages;
     p.scale = 1.0f / sqrtf((float)head_dim);
     return NQ_OK;
 }
