@@ -226,18 +226,35 @@ def run_reference(args, world, rank):
 
 def gemv_roofline(dec, reps: int = 5):
     """Average duration of a fused GEMV launch over one token's worth of launches exactly as
-    the decode step issues them (grouped q/k/v, o, grouped gate/up, down for every layer of
-    this rank, replayed from a CUDA graph), and the algorithmic bytes per launch."""
+    the decode step issues them (for every layer of this rank: q/k/v with RMSNorm(x + residual)
+    in the prologue, o, gate/up with RMSNorm and SiLU on the gate, down with gate * up in the
+    prologue; replayed from a CUDA graph), and the algorithmic bytes per launch: sign planes,
+    scales, the input vectors the launch reads and the vectors it writes."""
+    from nanoquant_b200 import chain as nqchain
     units = []  # (callable, algorithmic bytes)
-    B = dec.batch
+    B, ops, eps = dec.batch, torch.ops.nq_b200, dec.cfg.rms_eps
+    fused = dec.chain_ws is None and dec.fuse_neighbours and B <= 8
     for lay in dec.layers:
         for key in ("qkv", "o", "gate_up", "down"):
             unit = lay[key]
             members = unit.members if hasattr(unit, "members") else (unit,)
-            x = torch.randn(B, members[0].in_features, device=dec.device, dtype=dec.dtype)
-            alg = sum(m.nbytes() + 2 * B * m.out_features for m in members) + 2 * B * members[0].in_features
-            if hasattr(unit, "members"):
-                fn = (lambda u, xx: (lambda: torch.ops.nq_b200.gemv_group(xx, u.s2, u.vb, u.smid, u.ub, u.s1)))(unit, x)
+            n_in = members[0].in_features
+            x = torch.randn(B, n_in, device=dec.device, dtype=dec.dtype)
+            alg = sum(m.nbytes() + 2 * B * m.out_features for m in members) + 2 * B * n_in
+            if fused and key in ("qkv", "gate_up"):
+                x2, res = torch.randn_like(x), torch.empty_like(x)
+                nw = lay["in_norm" if key == "qkv" else "post_norm"]
+                act = 1 if key == "gate_up" else 0
+                alg += 2 * B * n_in * 2 + 2 * n_in  # residual read, sum written, norm weight
+                fn = (lambda u, xx, r, w, o, a: (lambda: ops.gemv_group_ex(xx, r, w, eps, nqchain.RMSNORM, o, a, u.s2, u.vb,
+                                                                            u.smid, u.ub, u.s1)))(unit, x, x2, nw, res, act)
+            elif fused and key == "down":
+                x2 = torch.randn_like(x)
+                alg += 2 * B * n_in  # the second factor (up)
+                fn = (lambda u, xx, yy: (lambda: ops.gemv_group_ex(xx, yy, None, 0.0, nqchain.MUL, None, 0, [u.s2], [u.vb],
+                                                                    [u.smid], [u.ub], [u.s1])))(unit, x, x2)
+            elif hasattr(unit, "members"):
+                fn = (lambda u, xx: (lambda: ops.gemv_group(xx, u.s2, u.vb, u.smid, u.ub, u.s1)))(unit, x)
             else:
                 fn = (lambda u, xx: (lambda: u.gemv(xx)))(unit, x)
             units.append((fn, alg))
