@@ -278,6 +278,11 @@ __device__ __forceinline__ int member_of2(const Params &p, int tile) {
     return l;
 }
 
+// Whether a CTA's stage-1 tile range [t1b, t1e) holds any tile of member mb.
+__device__ __forceinline__ bool owns1(const Member &mb, int t1b, int t1e) {
+    return max(t1b, mb.t1_start) < min(t1e, mb.t1_start + mb.tiles1);
+}
+
 // The part of a CTA's stage-2 tile range [t2b, t2e) that belongs to member l:
 // tiles [a, b) (global indices); a >= b when there is none.
 __device__ __forceinline__ void seg_tiles(const Member &mb, int t2b, int t2e, int &a, int &b) {
@@ -572,6 +577,7 @@ __device__ __forceinline__ void x_transform(const Params &p, T *xs, const T *x2s
                             ? reinterpret_cast<uint4 *>(static_cast<T *>(p.res_out) + (size_t)b * p.in_f)
                             : nullptr;
             float ss = 0.f;
+#pragma unroll 1
             for (int ch = threadIdx.x; ch < n8; ch += kThreads) {
                 float h[8];
                 unpack8<T>(xr[ch], h);
@@ -592,6 +598,7 @@ __device__ __forceinline__ void x_transform(const Params &p, T *xs, const T *x2s
             }
             const float inv = rsqrtf(block_sum_512(ss, sred) / (float)p.in_f + p.eps);
             const uint4 *wr = reinterpret_cast<const uint4 *>(nws);
+#pragma unroll 1
             for (int ch = threadIdx.x; ch < n8; ch += kThreads) {
                 float h[8], w[8];
                 unpack8<T>(xr[ch], h);
@@ -603,6 +610,7 @@ __device__ __forceinline__ void x_transform(const Params &p, T *xs, const T *x2s
             }
         } else {
             const bool silu = p.xmode == kChainSiluMul;
+#pragma unroll 1
             for (int ch = threadIdx.x; ch < n8; ch += kThreads) {
                 float a[8], u[8];
                 unpack8<T>(xr[ch], a);
@@ -678,7 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     }
     __syncthreads();
     bool vec_rows = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 && (p.in_f % 8) == 0;
-    _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) vec_rows = vec_rows && (reinterpret_cast<uintptr_t>(p.m[l].s2) & 15) == 0;
+    _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) vec_rows = vec_rows && (reinterpret_cast<uintptr_t>(p.m[l].s2) & 15) == 0;
     const int warp_id = tid >> 5;
     // Weight-side copies first: they do not depend on the previous kernel, so under programmatic
     // dependent launch they overlap its tail.  Everything that reads the previous kernel's
@@ -686,21 +694,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     if (has1) {
         if ((tid & 31) == 0 && (warp_id == 0 || warp_id == 2)) {
             uint32_t bytes = 0;
-            if (warp_id == 0) {
-                if (vec_rows) bytes = (uint32_t)p.in_f * 2u * (uint32_t)p.nm;
+            if (warp_id == 0) {  // s2 of the members whose stage-1 tiles this CTA owns
+                if (vec_rows)
+                    _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm && owns1(p.m[l], t1b, t1e))
+                        bytes += (uint32_t)p.in_f * 2u;
                 mbar_arrive_expect_tx(&bars[0], bytes);
                 if (vec_rows)
-                    _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm)
+                    _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm && owns1(p.m[l], t1b, t1e))
                         bulk_g2s_pieces(s2s + (size_t)l * in_pad, p.m[l].s2, (uint32_t)p.in_f * 2u, &bars[0]);
             } else {
-                _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+                _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
                     const Member &mb = p.m[l];
                     const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
                     if (a < b)
                         bytes += slab_bulk_bytes(16 * (a - mb.t1_start), min(16 * (b - mb.t1_start), mb.rank), p.wv, false);
                 }
                 mbar_arrive_expect_tx(&bars[0], bytes);
-                _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+                _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
                     const Member &mb = p.m[l];
                     const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
                     if (a < b)
@@ -710,14 +720,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
         }
         // what the copy engine does not carry: slab tails, zero padding, unaligned rows
-        _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+        _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
             const Member &mb = p.m[l];
             const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
             if (a < b)
                 slab_tail(vch + (size_t)16 * (a - t1b) * p.wvs, mb.vbits, 16 * (a - mb.t1_start),
                           min(16 * (b - mb.t1_start), mb.rank), p.wv);
         }
-        _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+        _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm && owns1(p.m[l], t1b, t1e)) {
             if (vec_rows) {
                 zero_tail<T>(s2s + (size_t)l * in_pad, p.in_f, in_pad);
             } else {
@@ -731,7 +741,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         if ((tid & 31) == 0 && (warp_id == kIssuers0 || warp_id == kIssuers0 + 1)) {
             const bool u_side = warp_id == kIssuers0;
             uint32_t bytes = 0;
-            _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+            _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
                 const Member &mb = p.m[l];
                 int a, b;
                 seg_tiles(mb, t2b, t2e, a, b);
@@ -746,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
             mbar_arrive_expect_tx(&bars[1], bytes);
             uint32_t uoff = 0;  // words
-            _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+            _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
                 const Member &mb = p.m[l];
                 int a, b;
                 seg_tiles(mb, t2b, t2e, a, b);
@@ -765,7 +775,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
         }
         uint32_t uoff = 0;  // words
-        _Pragma("unroll") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+        _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
             const Member &mb = p.m[l];
             int a, b;
             seg_tiles(mb, t2b, t2e, a, b);
@@ -833,9 +843,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             // xs2[l][col][k] = bf16 hi (col even) / lo (col odd) of x[col/2][k] * s2_l[k]
             // (members and batch rows outside, 8-value chunks inside: no runtime divisions)
             const int chunks = in_pad / 8;
-#pragma unroll
+#pragma unroll 1
             for (int l = 0; l < kMaxGroup; ++l)
-                if (l < p.nm)
+                if (l < p.nm && owns1(p.m[l], t1b, t1e))
                     for (int b = 0; b < p.batch; ++b)
                         for (int c8 = tid; c8 < chunks; c8 += kThreads) {
                             const int k = 8 * c8;
