@@ -564,7 +564,7 @@ __device__ __forceinline__ void stage2_finish(const Params &p, const float *red,
 // RMSNORM: h = dtype(x + x2) (x alone without x2), res_out = h (by `owner`),
 // x' = dtype(w * dtype(h * rsqrt(mean(h^2) + eps))); MUL: x' = dtype(x * x2);
 // SILU_MUL: x' = dtype(dtype(silu(x)) * x2).  The same roundings as the separate kernels.
-template <typename T>
+template <typename T, bool SILU = true>
 __device__ __forceinline__ void x_transform(const Params &p, T *xs, const T *x2s, const T *nws, int in_pad, bool owner,
                                             float *sred) {
     using E = Elem<T>;
@@ -609,7 +609,7 @@ __device__ __forceinline__ void x_transform(const Params &p, T *xs, const T *x2s
                 xr[ch] = *reinterpret_cast<const uint4 *>(o);
             }
         } else {
-            const bool silu = p.xmode == kChainSiluMul;
+            const bool silu = SILU && p.xmode == kChainSiluMul;
 #pragma unroll 1
             for (int ch = threadIdx.x; ch < n8; ch += kThreads) {
                 float a[8], u[8];
@@ -685,8 +685,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         fence_mbar_init();
     }
     __syncthreads();
-    bool vec_rows = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 && (p.in_f % 8) == 0;
-    _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) vec_rows = vec_rows && (reinterpret_cast<uintptr_t>(p.m[l].s2) & 15) == 0;
+    bool vec_rows = true;  // DECODE: the host checked the alignment
+    if (!DECODE) {
+        vec_rows = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 && (p.in_f % 8) == 0;
+        _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) vec_rows = vec_rows && (reinterpret_cast<uintptr_t>(p.m[l].s2) & 15) == 0;
+    }
     const int warp_id = tid >> 5;
     // Weight-side copies first: they do not depend on the previous kernel, so under programmatic
     // dependent launch they overlap its tail.  Everything that reads the previous kernel's
@@ -835,7 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         ok = mbar_wait(&bars[0], 0, &p.ctrl->status);
         const int nxc = 2 * p.batch;  // folded B columns per member: hi / lo of x*s2 per batch row
         if (p.xmode != kChainPlain) {
-            x_transform<T>(p, xs, reinterpret_cast<const T *>(smem + p.off_x2), reinterpret_cast<const T *>(smem + p.off_nw),
+            x_transform<T, !DECODE>(p, xs, reinterpret_cast<const T *>(smem + p.off_x2), reinterpret_cast<const T *>(smem + p.off_nw),
                            in_pad, t1b == 0, sred);
             __syncthreads();
         }
@@ -1030,7 +1033,12 @@ static int launch(const Plan &plan, cudaStream_t stream) {
     cfg.stream = stream;
     cfg.attrs = attr;
     if (plan.mode == kFused) {
-        const bool decode = plan.prm.fold && plan.prm.x_in_smem && plan.prm.batch <= 4;
+        // the DECODE instantiation: x staged and folded, batch <= 4, 16-byte aligned rows of x
+        // and s2 (no unaligned staging path), no SiLU*up input transform
+        const Params &q = plan.prm;
+        bool vec = (reinterpret_cast<uintptr_t>(q.x) & 15) == 0 && (q.in_f % 8) == 0;
+        for (int l = 0; l < q.nm; ++l) vec = vec && (reinterpret_cast<uintptr_t>(q.m[l].s2) & 15) == 0;
+        const bool decode = q.fold && q.x_in_smem && q.batch <= 4 && vec && q.xmode != kChainSiluMul;
         attr[na].id = cudaLaunchAttributeCooperative;
         attr[na].val.cooperative = 1;
         cfg.numAttrs = na + 1;
