@@ -640,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     const bool fold = DECODE || p.fold;
     const int tid = threadIdx.x;
     const int G = gridDim.x, c = blockIdx.x;
-    const bool do1 = (p.mode & kStage1) != 0, do2 = (p.mode & kStage2) != 0;
+    const bool do1 = DECODE || (p.mode & kStage1) != 0, do2 = DECODE || (p.mode & kStage2) != 0;
     unsigned long long bar_base = 0;  // thread 0 only; read after pdl_wait
     pdl_launch_dependents();
     // First touches of the parameter block miss the parameter cache; lane 0 of eight warps
@@ -722,8 +722,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 }
             }
         }
-        // what the copy engine does not carry: slab tails, zero padding, unaligned rows
-        _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+        // what the copy engine does not carry: slab tails (none in DECODE launches: the host
+        // checked that every slab is a multiple of 16 bytes), zero padding, unaligned rows
+        if (!DECODE) _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
             const Member &mb = p.m[l];
             const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
             if (a < b)
@@ -778,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             }
         }
         uint32_t uoff = 0;  // words
-        _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
+        if (!DECODE) _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm) {
             const Member &mb = p.m[l];
             int a, b;
             seg_tiles(mb, t2b, t2e, a, b);
@@ -797,7 +798,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     __syncthreads();
 
     pdl_wait();  // the previous kernel on the stream has completed; its outputs are visible
-    if (tid == 0 && p.mode == kFused) bar_base = grid_barrier_base(p.ctrl, (unsigned)G);
+    if (tid == 0 && (DECODE || p.mode == kFused)) bar_base = grid_barrier_base(p.ctrl, (unsigned)G);
     if (has1) {
         if (tid == 32) {  // warp 1: x and the transform inputs
             uint32_t bytes = 0;
@@ -872,7 +873,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         stage1_finish<T, DECODE ? 1 : -1>(p, red, t1b, t1e, &wtab);
     }
 
-    if (p.mode == kFused) {
+    if (DECODE || p.mode == kFused) {
         if (!grid_barrier(p.ctrl, bar_base + (unsigned)G)) ok = false;
     } else if (has1 && do2) {
         __syncthreads();
@@ -1038,6 +1039,12 @@ static int launch(const Plan &plan, cudaStream_t stream) {
         const Params &q = plan.prm;
         bool vec = (reinterpret_cast<uintptr_t>(q.x) & 15) == 0 && (q.in_f % 8) == 0;
         for (int l = 0; l < q.nm; ++l) vec = vec && (reinterpret_cast<uintptr_t>(q.m[l].s2) & 15) == 0;
+        // and every V / U slab and s1 slice a whole number of 16-byte pieces (no tail loads)
+        for (int l = 0; l < q.nm; ++l) {
+            const Member &mb = q.m[l];
+            vec = vec && (q.wv % 4 == 0 || mb.rank % 4 == 0) && (mb.wu % 4 == 0 || mb.out_f % 4 == 0) &&
+                  mb.out_f % 8 == 0 && (reinterpret_cast<uintptr_t>(mb.s1) & 15) == 0;
+        }
         const bool decode = q.fold && q.x_in_smem && q.batch <= 4 && vec && q.xmode != kChainSiluMul;
         attr[na].id = cudaLaunchAttributeCooperative;
         attr[na].val.cooperative = 1;
