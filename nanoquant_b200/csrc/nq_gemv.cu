@@ -731,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                 slab_tail(vch + (size_t)16 * (a - t1b) * p.wvs, mb.vbits, 16 * (a - mb.t1_start),
                           min(16 * (b - mb.t1_start), mb.rank), p.wv);
         }
-        _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm && owns1(p.m[l], t1b, t1e)) {
+        if (!DECODE) _Pragma("unroll 1") for (int l = 0; l < kMaxGroup; ++l) if (l < p.nm && owns1(p.m[l], t1b, t1e)) {
             if (vec_rows) {
                 zero_tail<T>(s2s + (size_t)l * in_pad, p.in_f, in_pad);
             } else {
@@ -808,21 +808,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             if (p.xmode == kChainNorm) bytes += (uint32_t)p.in_f * 2u;
             mbar_arrive_expect_tx(&bars[0], bytes);
             if (vec_rows && x_in_smem) {
-                if (in_pad == p.in_f)
+                if (DECODE || in_pad == p.in_f)  // DECODE: in_f is a multiple of 64 (no padding)
                     bulk_g2s_pieces(xs, p.x, (uint32_t)p.batch * (uint32_t)p.in_f * 2u, &bars[0]);
                 else
                     for (int b = 0; b < p.batch; ++b)
                         bulk_g2s_pieces(xs + (size_t)b * in_pad, static_cast<const T *>(p.x) + (size_t)b * p.in_f,
                                         (uint32_t)p.in_f * 2u, &bars[0]);
             }
-            if (p.x2)
+            if (p.x2 && (DECODE || in_pad == p.in_f))
+                bulk_g2s_pieces(smem + p.off_x2, p.x2, (uint32_t)p.batch * (uint32_t)p.in_f * 2u, &bars[0]);
+            else if (p.x2)
                 for (int b = 0; b < p.batch; ++b)
                     bulk_g2s_pieces(smem + p.off_x2 + (size_t)b * in_pad * 2,
                                     static_cast<const T *>(p.x2) + (size_t)b * p.in_f, (uint32_t)p.in_f * 2u,
                                     &bars[0]);
             if (p.xmode == kChainNorm) bulk_g2s_pieces(smem + p.off_nw, p.nw, (uint32_t)p.in_f * 2u, &bars[0]);
         }
-        if (x_in_smem)
+        if (!DECODE && x_in_smem)
             for (int b = 0; b < p.batch; ++b) {
                 if (vec_rows)
                     zero_tail<T>(xs + (size_t)b * in_pad, p.in_f, in_pad);
@@ -1035,7 +1037,7 @@ static int launch(const Plan &plan, cudaStream_t stream) {
     cfg.attrs = attr;
     if (plan.mode == kFused) {
         // the DECODE instantiation: x staged and folded, batch <= 4, 16-byte aligned rows of x
-        // and s2 (no unaligned staging path), no SiLU*up input transform
+        // and s2 that need no K padding (in_f a multiple of 64), no SiLU*up input transform
         const Params &q = plan.prm;
         bool vec = (reinterpret_cast<uintptr_t>(q.x) & 15) == 0 && (q.in_f % 8) == 0;
         for (int l = 0; l < q.nm; ++l) vec = vec && (reinterpret_cast<uintptr_t>(q.m[l].s2) & 15) == 0;
@@ -1045,7 +1047,7 @@ static int launch(const Plan &plan, cudaStream_t stream) {
             vec = vec && (q.wv % 4 == 0 || mb.rank % 4 == 0) && (mb.wu % 4 == 0 || mb.out_f % 4 == 0) &&
                   mb.out_f % 8 == 0 && (reinterpret_cast<uintptr_t>(mb.s1) & 15) == 0;
         }
-        const bool decode = q.fold && q.x_in_smem && q.batch <= 4 && vec && q.xmode != kChainSiluMul;
+        const bool decode = q.fold && q.x_in_smem && q.batch <= 4 && vec && q.xmode != kChainSiluMul && q.in_f % 64 == 0;
         attr[na].id = cudaLaunchAttributeCooperative;
         attr[na].val.cooperative = 1;
         cfg.numAttrs = na + 1;
