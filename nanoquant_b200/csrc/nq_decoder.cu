@@ -220,7 +220,7 @@ __device__ __forceinline__ float2 f2_of<__nv_bfloat16>(uint32_t w) {
 __host__ __device__ constexpr size_t attn_stage_bytes() { return (size_t)kSub * kHeadDim * 2u; }  // K or V, 2-byte types
 
 // Cluster helpers (the chunks of one head combine their partials through distributed shared
-// memory; every CTA of a cluster is resident at once, and all reach both cluster barriers).
+// memory; every CTA of a cluster is resident at once, and all reach the cluster barrier).
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -229,13 +229,15 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float ld_cluster_f32(const float *local, uint32_t rank) {
+// Store v at the address of `local` in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ void st_cluster_f32(float *local, uint32_t rank, float v) {
     uint32_t ra;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-    return v;
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
+// Shared-memory bytes of rank 0's receive buffer for the cluster's partials.
+template <int GRP>
+__host__ __device__ constexpr size_t attn_recv_bytes() { return (size_t)kClusterChunks * GRP * (kHeadDim + 2) * 4u; }
 
 // CL: the kClusterChunks chunks of a head form one cluster and rank 0 combines their partials
 // from distributed shared memory; otherwise partials go to the workspace and the CTA that
@@ -481,38 +483,41 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
                 o[g][1] += osm[(q * GRP + g) * D + 2 * dp + 1];
             }
     if (CL) {
-        // this chunk's partial (unnormalised o, max, sum) in its own shared memory, then rank 0
-        // of the cluster combines all kClusterChunks of them
-        float *part = reinterpret_cast<float *>(smem + 16384);  // [GRP][D + 2], inside stage 0
+        // every chunk stores its partial (unnormalised o, max, sum) straight into rank 0's
+        // receive buffer [kClusterChunks][GRP][D + 2]; one cluster barrier (release / acquire)
+        // publishes them, and rank 0 combines from its own shared memory
+        float *recv = reinterpret_cast<float *>(smem + nst * attn_stage_bytes() + GRP * D * sizeof(T) +
+                                                (size_t)GRP * p.nsub * kSub * sizeof(float));
+        const uint32_t me = cluster_rank();
         if (pg == 0)
 #pragma unroll
             for (int g = 0; g < GRP; ++g) {
-                part[g * (D + 2) + 2 * dp] = o[g][0];
-                part[g * (D + 2) + 2 * dp + 1] = o[g][1];
+                float *dst = recv + ((size_t)me * GRP + g) * (D + 2);
+                st_cluster_f32(dst + 2 * dp, 0, o[g][0]);
+                st_cluster_f32(dst + 2 * dp + 1, 0, o[g][1]);
                 if (dp == 0) {
-                    part[g * (D + 2) + D] = mrow[g];
-                    part[g * (D + 2) + D + 1] = lrow[g];
+                    st_cluster_f32(dst + D, 0, mrow[g]);
+                    st_cluster_f32(dst + D + 1, 0, lrow[g]);
                 }
             }
         cluster_sync_all();
-        if (cluster_rank() == 0 && tid < D) {
+        if (me == 0 && tid < D) {
             for (int g = 0; g < GRP; ++g) {
                 float M = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < kClusterChunks; ++c) M = fmaxf(M, ld_cluster_f32(part + g * (D + 2) + D, c));
+                for (int c = 0; c < kClusterChunks; ++c) M = fmaxf(M, recv[(c * GRP + g) * (D + 2) + D]);
                 float num = 0.f, den = 0.f;
 #pragma unroll
                 for (int c = 0; c < kClusterChunks; ++c) {
-                    const float lc = ld_cluster_f32(part + g * (D + 2) + D + 1, c);
-                    const float mc = ld_cluster_f32(part + g * (D + 2) + D, c);
+                    const float *pc = recv + (c * GRP + g) * (D + 2);
+                    const float lc = pc[D + 1], mc = pc[D];
                     const float wc = lc > 0.f ? expf(mc - M) : 0.f;
                     den = fmaf(wc, lc, den);
-                    num = fmaf(wc, ld_cluster_f32(part + g * (D + 2) + tid, c), num);
+                    num = fmaf(wc, pc[tid], num);
                 }
                 out[g * D + tid] = fromf<T>(den > 0.f ? num / den : 0.f);
             }
         }
-        cluster_sync_all();  // the partials stay alive until rank 0 has read them
         return;
     }
     float *pbase = p.part + ((size_t)b * hq + (size_t)kh * GRP) * p.nchunk * (D + 2);
@@ -612,10 +617,10 @@ __global__ void silu_mul_kernel(const T *__restrict__ gate, const T *__restrict_
 
 template <typename T, int GRP, bool ROPE>
 cudaError_t launch_attn(const AttnParams &p, int batch, cudaStream_t s) {
-    // the ring (>= 2 stages) also holds the final position-group reduction (< 16 KB) and the
-    // cluster partial (at 16 KB) once the chunk is done
+    // the ring (>= 2 stages) also holds the final position-group reduction (< 16 KB) once the
+    // chunk is done; a cluster launch adds rank 0's receive buffer for the chunks' partials
     const size_t smem = p.nst * attn_stage_bytes() + GRP * kHeadDim * sizeof(T) +
-                        (size_t)GRP * p.nsub * kSub * sizeof(float);
+                        (size_t)GRP * p.nsub * kSub * sizeof(float) + (p.cl ? attn_recv_bytes<GRP>() : 0);
     auto fn = p.cl ? attn_decode_kernel<T, GRP, ROPE, true> : attn_decode_kernel<T, GRP, ROPE, false>;
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
