@@ -186,7 +186,8 @@ constexpr int kSub = 64;           // positions per sub-block (one ring stage)
 constexpr int kAttnThreads = 256;  // 8 warps
 constexpr int kMaxChunks = 64;     // chunk length grows with max_seq to keep at most this many
 constexpr int kHeadDim = 128;
-constexpr int kAttnMaxStages = 6;  // copy ring depth (sub-blocks of K or V in flight)
+constexpr int kAttnMaxStages = 12;  // copy ring depth limit (sub-blocks of K or V in flight)
+constexpr int kAttnCtasPerSm = 2;   // chunks per head are sized for about this many CTAs per SM
 constexpr size_t kAttnScoreBytes = 48 * 1024;  // per-chunk score buffer limit (GRP x chunk x 4 B)
 constexpr int kClusterChunks = 8;  // chunks of one head combined through distributed shared memory
 
@@ -203,6 +204,7 @@ struct AttnParams {
     float *part;        // [batch][hq][nchunk][D + 2]
     int hkv, max_seq, nchunk, nsub, nst;
     int cl;             // chunks of a head combined in a cluster (nchunk <= kClusterChunks)
+    int ncl;            // cluster size (a power of two >= nchunk) when cl
     float scale, log2_theta;
 };
 
@@ -239,7 +241,7 @@ __device__ __forceinline__ void st_cluster_f32(float *local, uint32_t rank, floa
 template <int GRP>
 __host__ __device__ constexpr size_t attn_recv_bytes() { return (size_t)kClusterChunks * GRP * (kHeadDim + 2) * 4u; }
 
-// CL: the kClusterChunks chunks of a head form one cluster and rank 0 combines their partials
+// CL: the chunks of a head form one cluster (gridDim.x CTAs) and rank 0 combines their partials
 // from distributed shared memory; otherwise partials go to the workspace and the CTA that
 // finishes last for its head (atomic counter, reset after) combines them.
 template <typename T, int GRP, bool ROPE, bool CL>
@@ -484,7 +486,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             }
     if (CL) {
         // every chunk stores its partial (unnormalised o, max, sum) straight into rank 0's
-        // receive buffer [kClusterChunks][GRP][D + 2]; one cluster barrier (release / acquire)
+        // receive buffer [gridDim.x][GRP][D + 2]; one cluster barrier (release / acquire)
         // publishes them, and rank 0 combines from its own shared memory
         float *recv = reinterpret_cast<float *>(smem + nst * attn_stage_bytes() + GRP * D * sizeof(T) +
                                                 (size_t)GRP * p.nsub * kSub * sizeof(float));
@@ -505,10 +507,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             for (int g = 0; g < GRP; ++g) {
                 float M = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < kClusterChunks; ++c) M = fmaxf(M, recv[(c * GRP + g) * (D + 2) + D]);
+                for (int c = 0; c < (int)gridDim.x; ++c) M = fmaxf(M, recv[(c * GRP + g) * (D + 2) + D]);
                 float num = 0.f, den = 0.f;
 #pragma unroll
-                for (int c = 0; c < kClusterChunks; ++c) {
+                for (int c = 0; c < (int)gridDim.x; ++c) {
                     const float *pc = recv + (c * GRP + g) * (D + 2);
                     const float lc = pc[D + 1], mc = pc[D];
                     const float wc = lc > 0.f ? expf(mc - M) : 0.f;
@@ -596,7 +598,7 @@ inline AttnChunks attn_chunks(int64_t max_seq) {
 // positions; nsub = 0 when max_seq needs longer chunks than that (more than kMaxChunks).
 inline AttnChunks attn_chunks_for(int64_t max_seq, int64_t heads_x_batch, int sms, int grp) {
     const int64_t n64 = (max_seq + kSub - 1) / kSub;
-    const int64_t target = std::max<int64_t>(1, (2 * (int64_t)sms) / std::max<int64_t>(1, heads_x_batch));
+    const int64_t target = std::max<int64_t>(1, (kAttnCtasPerSm * (int64_t)sms) / std::max<int64_t>(1, heads_x_batch));
     const int64_t nsub_cap = (int64_t)(kAttnScoreBytes / ((size_t)grp * kSub * sizeof(float)));
     const int64_t nsub_min = attn_chunks(max_seq).nsub;
     if (nsub_min > nsub_cap) return {0, 0};
@@ -627,7 +629,7 @@ cudaError_t launch_attn(const AttnParams &p, int batch, cudaStream_t s) {
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.cl ? (unsigned)kClusterChunks : (unsigned)p.nchunk, (unsigned)p.hkv, (unsigned)batch);
+    cfg.gridDim = dim3(p.cl ? (unsigned)p.ncl : (unsigned)p.nchunk, (unsigned)p.hkv, (unsigned)batch);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -640,7 +642,7 @@ cudaError_t launch_attn(const AttnParams &p, int batch, cudaStream_t s) {
     }
     if (p.cl) {
         attr[na].id = cudaLaunchAttributeClusterDimension;
-        attr[na].val.clusterDim.x = kClusterChunks;
+        attr[na].val.clusterDim.x = (unsigned)p.ncl;
         attr[na].val.clusterDim.y = 1;
         attr[na].val.clusterDim.z = 1;
         ++na;
@@ -696,8 +698,18 @@ int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head
     p.max_seq = (int)max_seq;
     p.nchunk = ch.nchunk;
     p.nsub = ch.nsub;
-    p.nst = 2 * ch.nsub < kAttnMaxStages ? 2 * ch.nsub : kAttnMaxStages;
     p.cl = ch.nchunk <= kClusterChunks ? 1 : 0;
+    p.ncl = 1;
+    while (p.ncl < ch.nchunk) p.ncl *= 2;
+    // ring depth: every sub-block of the chunk in flight if shared memory allows, keeping room
+    // for two CTAs per SM when the grid needs that many
+    const int64_t ctas = (int64_t)(p.cl ? p.ncl : ch.nchunk) * hkv * batch;
+    const size_t budget = ctas > sm_count() ? 110 * 1024 : 200 * 1024;
+    const size_t fixed = (size_t)grp * kHeadDim * 2 + (size_t)grp * ch.nsub * kSub * sizeof(float) +
+                         (p.cl ? (size_t)kClusterChunks * grp * (kHeadDim + 2) * 4 : 0);
+    int nst = (int)std::min<int64_t>(kAttnMaxStages, 2 * (int64_t)ch.nsub);
+    while (nst > 2 && fixed + (size_t)nst * attn_stage_bytes() > budget) --nst;
+    p.nst = nst;
     p.scale = 1.0f / sqrtf((float)head_dim);
     return NQ_OK;
 }
