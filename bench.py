@@ -27,6 +27,20 @@ import torch  # noqa: E402
 
 METRIC = "batch-1 decode tokens/s (7B shape, 0.55 bpw)"
 
+# Under torchrun, native libraries (NCCL prints its version banner on rank 0) may write to
+# stdout; main() points file descriptor 1 at stderr and keeps the original stdout here for
+# the one JSON line.
+_JSON_FD = None
+
+
+def emit(line: dict) -> None:
+    text = json.dumps(line) + "\n"
+    if _JSON_FD is None:
+        sys.stdout.write(text)
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, text.encode())
+
 
 def parse():
     ap = argparse.ArgumentParser()
@@ -45,6 +59,8 @@ def parse():
     ap.add_argument("--copies", type=int, default=40, help="--layer: distinct weight copies (past L2)")
     ap.add_argument("--chain", action="store_true",
                     help="decode through GEMV chains (one cooperative launch per block besides attention)")
+    ap.add_argument("--peer-allreduce", action="store_true",
+                    help="N > 1: sum the blocks' partial outputs through peer memory (nq_allreduce) instead of NCCL")
     return ap.parse_args()
 
 
@@ -197,6 +213,8 @@ def config_block(cfg, args, world):
             "parallelism": f"tp{world}", "ranks": dict(cfg.ranks),
             "decode_path": "gemv chain per block" if getattr(args, "chain", False) else
                            "grouped GEMV launches with fused RMSNorm / SwiGLU prologues",
+            "tp_allreduce": ("peer memory (nq_allreduce)" if getattr(args, "peer_allreduce", False) else "NCCL")
+                            if world > 1 else None,
             "l2": "working set > L2 (weights + KV cache read per token)"}
 
 
@@ -221,7 +239,7 @@ def run_reference(args, world, rank):
                              "sample": f"per step: one decoder layer (7 dense-factor linears, attention, norms) "
                                        f"timed ~{sample:.1f}s, x{cfg.layers} layers + lm_head"},
             "e2e": {"value": round(val, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def gemv_roofline(dec, reps: int = 5):
@@ -291,7 +309,7 @@ def run_nq(args, world, rank, local):
     group = torch.distributed.group.WORLD if world > 1 else None
     max_seq = args.prompt + args.warmup + 2 * args.steps + 16
     dec = Decoder(cfg, max_seq=max_seq, batch=args.batch, tp_rank=rank, tp=world, group=group, seed=1234,
-                  dtype=torch.float16, device=dev, chain=args.chain)
+                  dtype=torch.float16, device=dev, chain=args.chain, peer_allreduce=args.peer_allreduce)
     g = torch.Generator().manual_seed(42)
     prompt = torch.randint(0, cfg.vocab, (args.prompt,), generator=g)
     torch.cuda.synchronize(dev)
@@ -381,7 +399,7 @@ def run_nq(args, world, rank, local):
                 "clocks": clocks.summary(),
                 "gpu_launches": launches_per_step * args.steps,
                 "prefill_ms": round(prefill_ms, 2), "first_token": int(first[0])}
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         torch.distributed.barrier(device_ids=[local])
         torch.distributed.destroy_process_group()
@@ -425,10 +443,15 @@ def run_layer(args):
 
 
 def main():
+    global _JSON_FD
     args = parse()
     if args.layer:
         run_layer(args)
         return
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         run_reference(args, world, rank)

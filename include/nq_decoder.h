@@ -53,6 +53,26 @@ NQ_API int nq_decode_attention_rope(int dtype, const void *q, const void *k, con
                                     int64_t head_dim, int64_t max_seq, float theta,
                                     void *workspace, size_t workspace_bytes, void *stream);
 
+/* One-shot all-reduce (sum) of a small vector over the GPUs of one node, through peer memory:
+ * the tensor-parallel decoder's per-block sum of the row-parallel layers' partial outputs, which
+ * the reference harness leaves to torch.distributed / NCCL (it has no kernel of its own).
+ * One process per GPU.  Every rank allocates a region with nq_allreduce_region_alloc (zeroed;
+ * nq_allreduce_region_bytes says how large), exports it with nq_ipc_handle (64 bytes), and maps
+ * the other ranks' regions with nq_ipc_open, all before the first call; `regions` lists every
+ * rank's region as mapped in the calling process (its own at index `rank`).  A call sums x over
+ * the ranks into out (may alias x), n a multiple of 8 and <= max_elems, float32 accumulation in
+ * rank order (every rank gets the same bits).  Every rank must make the same sequence of calls;
+ * each call's CTAs wait (bounded, 2 s) for the other ranks and record NQ_ERR_DEVICE_TIMEOUT in
+ * the region's status word (nq_workspace_status) when one does not come. */
+NQ_API size_t nq_allreduce_region_bytes(int world, int64_t max_elems);
+NQ_API int nq_allreduce_region_alloc(int world, int64_t max_elems, void **region_out);
+NQ_API int nq_allreduce_region_free(void *region);
+NQ_API int nq_ipc_handle(const void *region, void *handle_out);
+NQ_API int nq_ipc_open(const void *handle, void **region_out);
+NQ_API int nq_ipc_close(void *region);
+NQ_API int nq_allreduce(int dtype, const void *x, void *out, int64_t n, int rank, int world,
+                        void *const *regions, int64_t max_elems, void *stream);
+
 /* out = dtype(silu(gate)) * up, elementwise over n values. */
 NQ_API int nq_silu_mul(int dtype, const void *gate, const void *up, void *out, int64_t n,
                        void *stream);

@@ -98,6 +98,14 @@ _SIGNATURES = {
                                             _c.c_int64, _c.c_int64, _c.c_int64, _c.c_float, _c.c_void_p,
                                             _c.c_size_t, _c.c_void_p]),
     "nq_silu_mul": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p]),
+    "nq_allreduce_region_bytes": (_c.c_size_t, [_c.c_int, _c.c_int64]),
+    "nq_allreduce_region_alloc": (_c.c_int, [_c.c_int, _c.c_int64, _c.POINTER(_c.c_void_p)]),
+    "nq_allreduce_region_free": (_c.c_int, [_c.c_void_p]),
+    "nq_ipc_handle": (_c.c_int, [_c.c_void_p, _c.c_void_p]),
+    "nq_ipc_open": (_c.c_int, [_c.c_void_p, _c.POINTER(_c.c_void_p)]),
+    "nq_ipc_close": (_c.c_int, [_c.c_void_p]),
+    "nq_allreduce": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int, _c.c_int, _c.c_void_p,
+                                _c.c_int64, _c.c_void_p]),
 }
 
 

@@ -159,12 +159,63 @@ def _make_layer(cfg: DecoderConfig, proj: str, layer: int, seed: int, tp_rank: i
     return QuantLinearShard(vb[:, c0 // 32:c1 // 32].contiguous(), ub, s2[c0:c1].contiguous(), smid, s1)
 
 
+class PeerAllReduce:
+    """Sum of a small tensor over the tensor-parallel ranks of one node through peer memory
+    (nq_allreduce): every rank maps every other rank's region over CUDA IPC once, here; a call
+    is one kernel launch, capturable in the decode graph.  Tensors above `max_elems` elements
+    (prefill) go through torch.distributed instead; the choice depends only on the size, so
+    every rank makes the same sequence of peer calls."""
+
+    def __init__(self, group, rank: int, world: int, max_elems: int, device):
+        import ctypes
+        self.lib, self.rank, self.world, self.group = _lib.cuda_lib(), rank, world, group
+        self.max_elems = max_elems
+        with torch.cuda.device(device):
+            region = ctypes.c_void_p()
+            _lib.check(self.lib.nq_allreduce_region_alloc(world, max_elems, ctypes.byref(region)))
+            self.region = region.value
+            handle = (ctypes.c_char * 64)()
+            _lib.check(self.lib.nq_ipc_handle(self.region, handle))
+            handles = [None] * world
+            torch.distributed.all_gather_object(handles, bytes(handle), group=group)
+            ptrs, self.opened = [], []
+            for r in range(world):
+                if r == rank:
+                    ptrs.append(self.region)
+                    continue
+                peer = ctypes.c_void_p()
+                _lib.check(self.lib.nq_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(peer)))
+                ptrs.append(peer.value)
+                self.opened.append(peer.value)
+            self.ptrs = (ctypes.c_void_p * world)(*ptrs)
+            torch.distributed.barrier(group=group)  # every region zeroed and mapped before any call
+
+    def __call__(self, t: torch.Tensor) -> torch.Tensor:
+        if t.numel() > self.max_elems or t.numel() % 8 or not t.is_contiguous():
+            torch.distributed.all_reduce(t, group=self.group)
+            return t
+        dt = _lib.NQ_DTYPE_F16 if t.dtype == torch.float16 else _lib.NQ_DTYPE_BF16
+        _lib.check(self.lib.nq_allreduce(dt, t.data_ptr(), t.data_ptr(), t.numel(), self.rank, self.world, self.ptrs,
+                                         self.max_elems, torch.cuda.current_stream(t.device).cuda_stream))
+        return t
+
+    def status(self) -> int:
+        """The region's device-side status word (NQ_OK, or NQ_ERR_DEVICE_TIMEOUT if a call gave up
+        waiting for another rank); synchronises the current stream."""
+        import ctypes
+        st = ctypes.c_int(-1)
+        n = self.lib.nq_allreduce_region_bytes(self.world, self.max_elems)
+        _lib.check(self.lib.nq_workspace_status(self.region, n, torch.cuda.current_stream().cuda_stream,
+                                                ctypes.byref(st)))
+        return st.value
+
+
 class Decoder:
     """One TP shard of the decoder plus its KV cache and a graph-capturable decode step."""
 
     def __init__(self, cfg: DecoderConfig, max_seq: int, batch: int = 1, tp_rank: int = 0, tp: int = 1,
                  group=None, seed: int = 0, dtype=torch.float16, device=None, with_mid: bool = False,
-                 chain: bool = False):
+                 chain: bool = False, peer_allreduce: bool = False):
         _lib.load_torch_ops()
         assert cfg.heads % tp == 0 and cfg.kv_heads % tp == 0 and cfg.ffn % tp == 0
         self.cfg, self.max_seq, self.batch, self.tp, self.tp_rank, self.group = cfg, max_seq, batch, tp, tp_rank, group
@@ -199,6 +250,11 @@ class Decoder:
         # RMSNorm / SiLU*up folded into the GEMV prologues and the gate's SiLU into its epilogue
         # (nq_gemv_group_ex); batches above 8 use the separate kernels.
         self.fuse_neighbours = True
+        # tensor parallel: `peer_allreduce` sums the blocks' partial outputs through peer memory
+        # (nq_allreduce) at decode sizes instead of torch.distributed / NCCL
+        self.peer_ar = None
+        if tp > 1 and peer_allreduce:
+            self.peer_ar = PeerAllReduce(group, tp_rank, tp, 8 * cfg.hidden, dev)
         self.chain_ws = None
         if chain and tp == 1:
             h = torch.empty(batch, cfg.hidden, device=dev, dtype=dtype)
@@ -211,6 +267,8 @@ class Decoder:
     # ------------------------------------------------------------------ pieces
     def _all_reduce(self, t: torch.Tensor):
         if self.tp > 1:
+            if self.peer_ar is not None:
+                return self.peer_ar(t)
             torch.distributed.all_reduce(t, group=self.group)
         return t
 
@@ -330,11 +388,12 @@ class Decoder:
         """Kernels of this package that one decode step launches (library kernels such as the
         lm_head GEMM, argmax and the embedding gather are not counted)."""
         n = self.cfg.layers
+        ar = 2 * n if self.peer_ar is not None else 0  # peer all-reduces (o and down of every block)
         if self.chain_ws is not None:
             return 1 + n * 2 + 1        # first q/k/v chain; attention + block chain per layer; final norm
         if self.fuse_neighbours and self.batch <= 8:
-            return n * 5 + 1            # q/k/v, attention, o, gate/up, down; final norm
-        return n * (4 + 2 + 1 + 1) + 1  # four GEMVs, two norms, attention, SiLU·up; final norm
+            return n * 5 + 1 + ar       # q/k/v, attention, o, gate/up, down; final norm
+        return n * (4 + 2 + 1 + 1) + 1 + ar  # four GEMVs, two norms, attention, SiLU·up; final norm
 
     def step_logits(self) -> torch.Tensor:
         """Logits for the current tokens at the current positions (writes the caches)."""

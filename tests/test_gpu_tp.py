@@ -23,7 +23,7 @@ def _port():
     return p
 
 
-def _run(rank, world, port, prompt, steps, q):
+def _run(rank, world, port, prompt, steps, q, peer=False):
     import datetime
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -31,6 +31,7 @@ def _run(rank, world, port, prompt, steps, q):
                                          timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     try:
         dec = Decoder(CFG, max_seq=128, tp_rank=rank, tp=world, group=torch.distributed.group.WORLD, seed=3,
+                      peer_allreduce=peer,
                       device=f"cuda:{rank}")
         first = int(dec.prefill(prompt.cuda())[0])
         logits = dec.step_logits().float().cpu()
@@ -49,7 +50,8 @@ def _run(rank, world, port, prompt, steps, q):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.timeout(600)
-def test_tp2_matches_tp1():
+@pytest.mark.parametrize("peer", [False, True], ids=["nccl", "peer_allreduce"])
+def test_tp2_matches_tp1(peer):
     prompt = torch.randint(0, CFG.vocab, (37,), generator=torch.Generator().manual_seed(9))
     ref = Decoder(CFG, max_seq=128, seed=3, device="cuda:0")
     first = int(ref.prefill(prompt.cuda())[0])
@@ -63,7 +65,7 @@ def test_tp2_matches_tp1():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_run, args=(r, 2, port, prompt, 6, q)) for r in range(2)]
+    procs = [ctx.Process(target=_run, args=(r, 2, port, prompt, 6, q, peer)) for r in range(2)]
     for p in procs:
         p.start()
     got_first, got_logits, got_toks = q.get(timeout=500)
@@ -74,3 +76,68 @@ def test_tp2_matches_tp1():
     rel = float((got_logits - logits).norm() / logits.norm())
     assert rel < 2e-2, rel
     assert got_toks == toks
+
+
+def _ar_run(rank, world, port, q):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
+                                         timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        from nanoquant_b200.decoder import PeerAllReduce
+        dev = torch.device("cuda", rank)
+        ar = PeerAllReduce(torch.distributed.group.WORLD, rank, world, 8192, dev)
+        eager = []
+        for it in range(5):  # consecutive calls alternate the receive buffers
+            x = _ar_input(it, rank).to(dev)
+            ar(x)
+            eager.append(x.cpu())
+        buf = torch.empty(4096, dtype=torch.float16, device=dev)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            ar(buf)
+        graphed = []
+        for it in range(5, 8):  # the same launch replayed: device-side epochs keep the ranks in step
+            buf.copy_(_ar_input(it, rank).to(dev))
+            g.replay()
+            graphed.append(buf.cpu())
+        torch.cuda.synchronize(dev)
+        status = ar.status()
+        del g
+        torch.distributed.barrier(device_ids=[rank])
+        q.put((rank, eager, graphed, status))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def _ar_input(it: int, rank: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(1000 * it + rank)
+    return torch.randn(4096, generator=g).half()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.timeout(600)
+def test_peer_allreduce_two_gpus():
+    """nq_allreduce over 2 GPUs: exactly the float32 rank-order sum rounded once, the same bits on
+    both ranks, for eager calls and for replays of a captured launch, and no device timeout."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_ar_run, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    out.sort(key=lambda t: t[0])
+    for it in range(8):
+        want = sum(_ar_input(it, r).float() for r in range(world)).half()
+        for rank, eager, graphed, status in out:
+            got = eager[it] if it < 5 else graphed[it - 5]
+            assert torch.equal(got, want), f"rank {rank} call {it}"
+    assert all(st == 0 for _, _, _, st in out)
