@@ -266,7 +266,7 @@ def gemv_roofline(dec, reps: int = 5):
                 alg += 2 * B * n_in * 2 + 2 * n_in  # residual read, sum written, norm weight
                 fn = (lambda u, xx, r, w, o, a: (lambda: ops.gemv_group_ex(xx, r, w, eps, nqchain.RMSNORM, o, a, u.s2, u.vb,
                                                                             u.smid, u.ub, u.s1)))(unit, x, x2, nw, res, act)
-            elif fused and key == "down":
+            elif fused and key == "down" and dec.fuse_down:
                 x2 = torch.randn_like(x)
                 alg += 2 * B * n_in  # the second factor (up)
                 fn = (lambda u, xx, yy: (lambda: ops.gemv_group_ex(xx, yy, None, 0.0, nqchain.MUL, None, 0, [u.s2], [u.vb],

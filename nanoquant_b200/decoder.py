@@ -250,6 +250,10 @@ class Decoder:
         # RMSNorm / SiLU*up folded into the GEMV prologues and the gate's SiLU into its epilogue
         # (nq_gemv_group_ex); batches above 8 use the separate kernels.
         self.fuse_neighbours = True
+        # gate * up in the down GEMV's prologue needs both FFN vectors staged in shared memory;
+        # for wide FFN shards (Llama-3-70B on one GPU) no plan fits, and the block uses the
+        # SiLU*up kernel and a plain down GEMV instead
+        self.fuse_down = self._down_prologue_fits()
         # tensor parallel: `peer_allreduce` sums the blocks' partial outputs through peer memory
         # (nq_allreduce) at decode sizes instead of torch.distributed / NCCL
         self.peer_ar = None
@@ -265,6 +269,19 @@ class Decoder:
                 self.chain_ws = torch.zeros(n, dtype=torch.uint8, device=dev)
 
     # ------------------------------------------------------------------ pieces
+    def _down_prologue_fits(self) -> bool:
+        dn = self.layers[0]["down"]
+        g = torch.zeros(self.batch, dn.in_features, device=self.device, dtype=self.dtype)
+        try:
+            torch.ops.nq_b200.gemv_group_ex(g, g, None, 0.0, nqchain.MUL, None, 0, [dn.s2], [dn.vb], [dn.smid], [dn.ub],
+                                            [dn.s1])
+        except RuntimeError as e:
+            if "shared-memory budget" in str(e):
+                return False
+            raise
+        torch.cuda.synchronize(self.device)
+        return True
+
     def _all_reduce(self, t: torch.Tensor):
         if self.tp > 1:
             if self.peer_ar is not None:
@@ -374,12 +391,15 @@ class Decoder:
             o = self._all_reduce(lay["o"](a.view(B, self.hq * D)))
             g = lay["gate_up"]
             res = torch.empty_like(o)
-            gate, up = ops.gemv_group_ex(o, residual, lay["post_norm"], eps, nqchain.RMSNORM, res, 1, g.s2, g.vb,
-                                         g.smid, g.ub, g.s1)
+            gate, up = ops.gemv_group_ex(o, residual, lay["post_norm"], eps, nqchain.RMSNORM, res,
+                                         1 if self.fuse_down else 0, g.s2, g.vb, g.smid, g.ub, g.s1)
             residual = res
             dn = lay["down"]
-            d = self._all_reduce(ops.gemv_group_ex(gate, up, None, 0.0, nqchain.MUL, None, 0, [dn.s2], [dn.vb],
-                                                   [dn.smid], [dn.ub], [dn.s1])[0])
+            if self.fuse_down:
+                d = self._all_reduce(ops.gemv_group_ex(gate, up, None, 0.0, nqchain.MUL, None, 0, [dn.s2], [dn.vb],
+                                                       [dn.smid], [dn.ub], [dn.s1])[0])
+            else:
+                d = self._all_reduce(dn.gemv(ops.silu_mul(gate, up)))
         x, _ = ops.rmsnorm(d, residual, self.final_norm, eps)
         return x @ self.lm_head.t()
 
@@ -392,7 +412,7 @@ class Decoder:
         if self.chain_ws is not None:
             return 1 + n * 2 + 1        # first q/k/v chain; attention + block chain per layer; final norm
         if self.fuse_neighbours and self.batch <= 8:
-            return n * 5 + 1 + ar       # q/k/v, attention, o, gate/up, down; final norm
+            return n * (5 if self.fuse_down else 6) + 1 + ar  # q/k/v, attention, o, gate/up, (SiLU*up,) down; final norm
         return n * (4 + 2 + 1 + 1) + 1 + ar  # four GEMVs, two norms, attention, SiLU·up; final norm
 
     def step_logits(self) -> torch.Tensor:
