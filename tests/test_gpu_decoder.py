@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from nanoquant_b200.decoder import TINY, Decoder
+from nanoquant_b200.decoder import TINY, Decoder, DecoderConfig
 from oracle import decoder_ref as ref
 from oracle import oracle as orc
 
@@ -148,3 +148,29 @@ def test_rmsnorm_and_silu_against_torch():
     a = torch.ops.nq_b200.silu_mul(x, r)
     want = (torch.nn.functional.silu(x.float()).half().float() * r.float())
     assert orc.rel_l2(a.float().cpu().numpy(), want.cpu().numpy()) < 1e-3
+
+
+# A block whose FFN is too wide for gate * up in the down GEMV's prologue (the staged vectors
+# exceed shared memory, as for Llama-3-70B on one GPU): the decoder must detect that and run the
+# SiLU*up kernel and a plain down GEMV, with the same logits as the reference.
+WIDE_FFN = DecoderConfig("wide-ffn", 256, 256, 1, 2, 2, 128, 28672,
+                         {"q": 96, "k": 96, "v": 96, "o": 96, "gate": 160, "up": 160, "down": 160})
+
+
+def test_wide_ffn_falls_back_and_matches_reference():
+    dec = Decoder(WIDE_FFN, max_seq=64, batch=1, seed=11, dtype=torch.float16, device="cuda")
+    assert not dec.fuse_down
+    assert dec.own_launches_per_step() == 6 * WIDE_FFN.layers + 1
+    W = ref.extract(dec)
+    prompt = torch.randint(0, WIDE_FFN.vocab, (21,), generator=torch.Generator().manual_seed(5))
+    first = dec.prefill(prompt.cuda())
+    seq = prompt.tolist() + [int(first[0])]
+    for _ in range(3):
+        got = dec.step_logits().float().cpu()[0]
+        want = ref.logits(WIDE_FFN, W, seq)[-1]
+        assert orc.rel_l2(got.numpy(), want.numpy()) <= TOL
+        nxt = int(torch.argmax(got))
+        seq.append(nxt)
+        dec.tokens.fill_(nxt)
+        dec.pos.add_(1)
+        dec.seq_len.add_(1)
