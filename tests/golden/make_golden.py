@@ -22,7 +22,8 @@ os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")  # the reference packers are @
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
-sys.path.insert(0, os.environ.get("NQ_REFERENCE_SRC", "/root/reference/src"))
+# the reference checkout sits beside this repository unless NQ_REFERENCE_SRC says otherwise
+sys.path.insert(0, os.environ.get("NQ_REFERENCE_SRC", os.path.join(os.path.dirname(REPO), "reference", "src")))
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
