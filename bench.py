@@ -57,6 +57,9 @@ def parse():
                     help="per-layer GEMV instead of whole-model decode: out,in,rank (e.g. 11008,4096,2054); "
                          "prints that layer's GB/s over --copies weight copies cycled through the timed loop")
     ap.add_argument("--copies", type=int, default=40, help="--layer: distinct weight copies (past L2)")
+    ap.add_argument("--attention", type=int, default=None, metavar="L",
+                    help="the fused decode attention (RoPE + cache write + split-KV attention) of --model at "
+                         "sequence length L instead of whole-model decode: KV-cache GB/s over 8 caches cycled")
     ap.add_argument("--chain", action="store_true",
                     help="decode through GEMV chains (one cooperative launch per block besides attention)")
     ap.add_argument("--peer-allreduce", action="store_true",
@@ -442,11 +445,60 @@ def run_layer(args):
                       "dtype": "f16", "data": "synthetic"}), flush=True)
 
 
+def run_attention(args):
+    """The decode attention of one layer of --model (one new token per batch row at position
+    L - 1, every head): 8 distinct KV caches (more bytes than L2 holds) cycled so every launch
+    reads its cache from HBM; KV bytes read per launch / device time per launch."""
+    from nanoquant_b200.decoder import CONFIGS
+    _lib_load()
+    cfg = CONFIGS[args.model]
+    L, B, D = args.attention, args.batch, cfg.head_dim
+    dev = torch.device("cuda", 0)
+    max_seq = L + 64
+    caches = [(torch.randn(B, cfg.kv_heads, max_seq, D, device=dev).half(),
+               torch.randn(B, cfg.kv_heads, max_seq, D, device=dev).half()) for _ in range(8)]
+    q = torch.randn(B, cfg.heads, D, device=dev).half()
+    k = torch.randn(B, cfg.kv_heads, D, device=dev).half()
+    v = torch.randn(B, cfg.kv_heads, D, device=dev).half()
+    pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
+    ops = torch.ops.nq_b200
+    for i in range(max(args.warmup, 3)):
+        kc, vc = caches[i % 8]
+        ops.decode_attention_rope(q, k, v, pos, kc, vc, cfg.rope_theta)
+    torch.cuda.synchronize(dev)
+    n = args.steps * 8
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(n):
+        kc, vc = caches[i % 8]
+        ops.decode_attention_rope(q, k, v, pos, kc, vc, cfg.rope_theta)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / n
+    kv = 2 * B * cfg.kv_heads * L * D * 2
+    peak, kind = peaks()
+    gbs = kv / (us * 1e-6) / 1e9
+    print(json.dumps({"metric": "decode attention GB/s (KV-cache bytes)", "value": round(gbs, 2), "unit": "GB/s",
+                      "attention": {"model": cfg.name, "seq_len": L, "batch": B, "heads": cfg.heads,
+                                    "kv_heads": cfg.kv_heads}, "us_per_launch": round(us, 3), "bytes_per_launch": kv,
+                      "launches": n, "roofline": {"bound": "hbm", "peak": peak, "frac": round(gbs / peak, 5),
+                                                  "peak_source": kind},
+                      "dtype": "f16", "data": "synthetic"}), flush=True)
+
+
+def _lib_load():
+    from nanoquant_b200 import _lib
+    _lib.load_torch_ops()
+
+
 def main():
     global _JSON_FD
     args = parse()
     if args.layer:
         run_layer(args)
+        return
+    if args.attention:
+        run_attention(args)
         return
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         sys.stdout.flush()
