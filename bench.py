@@ -221,9 +221,33 @@ def config_block(cfg, args, world):
             "l2": "working set > L2 (weights + KV cache read per token)"}
 
 
+def _configs_module():
+    """nanoquant_b200/configs.py loaded by path: importing it through the package would run the
+    package __init__, which maps this repository's native libraries into the process."""
+    import importlib.util
+    name = "nq_b200_configs"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, "nanoquant_b200", "configs.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod  # dataclasses resolve their module through sys.modules
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def repo_libraries_mapped():
+    """The product's native libraries (nanoquant_b200/*.so) mapped into this process."""
+    pkg = os.path.join(ROOT, "nanoquant_b200") + os.sep
+    try:
+        with open("/proc/self/maps") as f:
+            paths = {line.split()[-1] for line in f if ".so" in line}
+    except OSError:
+        return []
+    return sorted(p for p in paths if p.startswith(pkg))
+
+
 def run_reference(args, world, rank):
-    from nanoquant_b200.decoder import CONFIGS
-    cfg = CONFIGS[args.model]
+    cfg = _configs_module().CONFIGS[args.model]
     if rank != 0:
         return
     sample = max(1.0, args.cpu_seconds / max(1, args.steps + args.warmup))
@@ -242,6 +266,9 @@ def run_reference(args, world, rank):
                              "sample": f"per step: one decoder layer (7 dense-factor linears, attention, norms) "
                                        f"timed ~{sample:.1f}s, x{cfg.layers} layers + lm_head"},
             "e2e": {"value": round(val, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    mapped = repo_libraries_mapped()
+    if mapped:  # the reference arm must run without this repository's kernels
+        raise SystemExit(f"reference arm mapped repository libraries: {mapped}")
     emit(line)
 
 

@@ -165,6 +165,12 @@ NQ_API int nq_gemv_static(int dtype, const void *x, int64_t batch, int64_t in_fe
                           const void *scale_pre, const int32_t *v_bits, int64_t rank,
                           const void *scale_mid, const int32_t *u_bits, int64_t out_features,
                           const void *scale_post, void *y, void *stream);
+/* Device-side status of the last nq_gemv_static call on the current device: synchronises
+ * `stream`, then reads the static scratch's status word (NQ_OK, or NQ_ERR_DEVICE_TIMEOUT when
+ * a bounded wait inside the kernel gave up and y is not valid).  The next nq_gemv_static call
+ * clears the word, so read it before that call.  Neither function may be used after a
+ * cudaDeviceReset in the same process (the cached scratch address would be stale). */
+NQ_API int nq_gemv_static_status(void *stream, int *status_out);
 
 /* ---------------------------------------------------------------------------------
  * GEMV chain: up to NQ_CHAIN_MAX_PHASES grouped decode GEMVs run back to back in ONE

@@ -72,6 +72,7 @@ _SIGNATURES = {
     "nq_gemv_static": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p,
                                   _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p,
                                   _c.c_void_p]),
+    "nq_gemv_static_status": (_c.c_int, [_c.c_void_p, _c.POINTER(_c.c_int)]),
     "nq_gemv_group_ex": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_void_p, _c.c_int,
                                     _c.c_void_p, _c.c_size_t, _c.c_void_p]),
     "nq_gemv_chain_workspace_bytes": (_c.c_size_t, [_c.c_int, _c.c_int64, _c.c_int, _c.c_void_p]),

@@ -40,15 +40,23 @@ def _run(cmd, verbose):
 
 
 def build_cuda(force=False, verbose=False) -> str:
+    """Compile every csrc/*.cu into libnq_b200.so.  NQ_NVCC_EXTRA (space-separated nvcc flags,
+    e.g. -DNQ_GEMV_TRACE for the GEMV phase timeline) makes a debug build; the flags are
+    recorded beside the library, so changing them triggers a rebuild."""
     cu = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     deps = cu + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
-    if force or _stale(CUDA_LIB, deps):
+    extra = os.environ.get("NQ_NVCC_EXTRA", "").split()
+    stamp = CUDA_LIB + ".flags"
+    prev = open(stamp).read() if os.path.exists(stamp) else ""
+    if force or _stale(CUDA_LIB, deps) or prev != " ".join(extra):
         os.makedirs(OUT, exist_ok=True)
         cmd = [NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
-               "-Xcompiler", "-fvisibility=hidden", "-shared", "-cudart", "static", "-I", INCLUDE, *cu, "-o",
+               "-Xcompiler", "-fvisibility=hidden", "-shared", "-cudart", "static", "-I", INCLUDE, *extra, *cu, "-o",
                CUDA_LIB + ".tmp"]
         _run(cmd, verbose)
         os.replace(CUDA_LIB + ".tmp", CUDA_LIB)
+        with open(stamp, "w") as f:
+            f.write(" ".join(extra))
     return CUDA_LIB
 
 

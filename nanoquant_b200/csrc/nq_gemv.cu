@@ -44,6 +44,20 @@ constexpr int kFoldMaxBatch = 2;         // batch rows for which stage 1 folds s
 
 enum Mode : int { kStage1 = 1, kStage2 = 2, kFused = 3 };
 
+// Phase timeline of the fused kernel, compiled only into debug builds (-DNQ_GEMV_TRACE):
+// thread 0 of every CTA keeps globaltimer stamps at the phase boundaries in registers and
+// stores them at the end into the launch's slot of g_trace (slot = launches seen so far,
+// read after griddepcontrol.wait, advanced by CTA 0 after the grid barrier).
+// nq_debug_gemv_trace copies the stamps out.  Release builds compile none of this.
+#ifdef NQ_GEMV_TRACE
+constexpr int kTraceLaunches = 512, kTraceCtas = 160, kTraceStamps = 12;
+__device__ unsigned long long g_trace[kTraceLaunches][kTraceCtas][kTraceStamps];
+__device__ unsigned int g_trace_launch;
+#define NQ_STAMP(i) do { if (threadIdx.x == 0) tr_[i] = globaltimer_ns(); } while (0)
+#else
+#define NQ_STAMP(i) do { } while (0)
+#endif
+
 __device__ __forceinline__ void tile_range(int tiles, int c, int G, int &b, int &e) {
     b = (tiles * c) / G;  // tiles <= 2^16 and G <= 2^10 keep this within 32 bits
     e = (tiles * (c + 1)) / G;
@@ -642,6 +656,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     const int G = gridDim.x, c = blockIdx.x;
     const bool do1 = DECODE || (p.mode & kStage1) != 0, do2 = DECODE || (p.mode & kStage2) != 0;
     unsigned long long bar_base = 0;  // thread 0 only; read after pdl_wait
+#ifdef NQ_GEMV_TRACE
+    unsigned long long tr_[kTraceStamps] = {};
+    unsigned int tr_slot = 0;
+#endif
+    NQ_STAMP(0);
     pdl_launch_dependents();
     // First touches of the parameter block miss the parameter cache; lane 0 of eight warps
     // reads one field each from different parts of it so that those misses overlap (the
@@ -796,8 +815,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         }
     }
     __syncthreads();
+    NQ_STAMP(1);
 
     pdl_wait();  // the previous kernel on the stream has completed; its outputs are visible
+    NQ_STAMP(2);
+#ifdef NQ_GEMV_TRACE
+    if (tid == 0) tr_slot = *reinterpret_cast<volatile unsigned int *>(&g_trace_launch);
+#endif
     if (tid == 0 && (DECODE || p.mode == kFused)) bar_base = grid_barrier_base(p.ctrl, (unsigned)G);
     if (has1) {
         if (tid == 32) {  // warp 1: x and the transform inputs
@@ -839,12 +863,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     // ------------------------------------------------------------------ stage 1
     if (has1) {
         ok = mbar_wait(&bars[0], 0, &p.ctrl->status);
+        NQ_STAMP(3);
         const int nxc = 2 * p.batch;  // folded B columns per member: hi / lo of x*s2 per batch row
         if (p.xmode != kChainPlain) {
             x_transform<T, !DECODE>(p, xs, reinterpret_cast<const T *>(smem + p.off_x2), reinterpret_cast<const T *>(smem + p.off_nw),
                            in_pad, t1b == 0, sred);
             __syncthreads();
         }
+        NQ_STAMP(4);
         if (fold) {
             // xs2[l][col][k] = bf16 hi (col even) / lo (col odd) of x[col/2][k] * s2_l[k]
             // (members and batch rows outside, 8-value chunks inside: no runtime divisions)
@@ -870,27 +896,40 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
                         }
             __syncthreads();
         }
+        NQ_STAMP(5);
         stage1_items<T, DECODE ? 1 : -1>(p, vch, s2s, xs, xs2, red, t1b, t1e, ok, &wtab);
         __syncthreads();
+        NQ_STAMP(6);
         stage1_finish<T, DECODE ? 1 : -1>(p, red, t1b, t1e, &wtab);
     }
+    NQ_STAMP(7);
 
     if (DECODE || p.mode == kFused) {
         if (!grid_barrier(p.ctrl, bar_base + (unsigned)G)) ok = false;
     } else if (has1 && do2) {
         __syncthreads();
     }
+    NQ_STAMP(8);
 
     // ------------------------------------------------------------------ stage 2
     if (has2) {
         if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
+        NQ_STAMP(9);
         if (DECODE || p.batch <= 4)
             stage2_items<T, 1>(p, uch, red, t2b, t2e, ok, nullptr, &wtab);
         else
             stage2_items<T, 2>(p, uch, red, t2b, t2e, ok, nullptr, &wtab);
         __syncthreads();
+        NQ_STAMP(10);
         stage2_finish<T>(p, red, s1s, t2b, t2e, nullptr, p.act, &wtab);
     }
+    NQ_STAMP(11);
+#ifdef NQ_GEMV_TRACE
+    if (tid == 0 && tr_slot < kTraceLaunches && c < kTraceCtas) {
+        for (int i = 0; i < kTraceStamps; ++i) g_trace[tr_slot][c][i] = tr_[i];
+        if (c == 0) atomicAdd(&g_trace_launch, 1u);
+    }
+#endif
 }
 
 struct Plan {
@@ -1800,7 +1839,9 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 
 // Device address of g_static_scratch on the current device.  In host code the array's name
 // is only a host-side stand-in, so the address comes from cudaGetSymbolAddress, once per
-// device, with that device current.
+// device, with that device current.  The cached address belongs to the device's primary
+// context: after cudaDeviceReset the library's module is loaded anew and the entry point
+// must not be used again in that process.
 static int static_scratch(void **out) {
     static std::mutex mu;
     static void *addr[64] = {};
@@ -1844,4 +1885,33 @@ int nq_gemv_static(int dtype, const void *x, int64_t batch, int64_t in_features,
                    y, scratch, kStaticScratchBytes, stream);
 }
 
+int nq_gemv_static_status(void *stream, int *status_out) {
+    using namespace nq;
+    using namespace nq::gemv;
+    if (!status_out) return fail(NQ_ERR_INVALID_ARGUMENT, "null status_out");
+    void *scratch = nullptr;
+    int st = static_scratch(&scratch);
+    if (st) return st;
+    return nq_workspace_status(scratch, kStaticScratchBytes, stream, status_out);
+}
+
 }  // extern "C"
+
+#ifdef NQ_GEMV_TRACE
+// Debug builds only: copy the phase stamps of up to `max_launches` fused launches
+// ([launch][kTraceCtas][kTraceStamps] u64, host memory) and return how many were recorded;
+// `reset` != 0 then clears the launch counter.
+extern "C" NQ_API int nq_debug_gemv_trace(unsigned long long *host, int max_launches, int reset) {
+    using namespace nq::gemv;
+    unsigned int n = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    if (cudaMemcpyFromSymbol(&n, g_trace_launch, sizeof(n)) != cudaSuccess) return -1;
+    const int m = (int)std::min<unsigned int>(n, (unsigned)std::min(max_launches, kTraceLaunches));
+    if (m > 0 && cudaMemcpyFromSymbol(host, g_trace, (size_t)m * kTraceCtas * kTraceStamps * 8) != cudaSuccess) return -1;
+    if (reset) {
+        const unsigned int z = 0;
+        if (cudaMemcpyToSymbol(g_trace_launch, &z, sizeof(z)) != cudaSuccess) return -1;
+    }
+    return (int)n;
+}
+#endif

@@ -56,6 +56,44 @@ def rmsnorm(x, w, eps):
     return w * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps))
 
 
+class Incremental:
+    """The same float32 decoder fed a few tokens at a time with a KV cache, as HF's generate
+    loop runs it: ``feed(tokens)`` appends tokens and returns the logits of the last one.
+    Equal to ``logits(...)[-1]`` of the whole sequence up to float32 summation order."""
+
+    def __init__(self, cfg, W: dict):
+        self.cfg, self.W = cfg, W
+        self.k = [None] * len(W["layers"])
+        self.v = [None] * len(W["layers"])
+        self.n = 0
+
+    @torch.no_grad()
+    def feed(self, tokens) -> torch.Tensor:
+        cfg, W = self.cfg, self.W
+        t = torch.as_tensor(tokens, dtype=torch.long).reshape(-1)
+        T, D, n = t.numel(), cfg.head_dim, self.n
+        pos = torch.arange(n, n + T)
+        # query i (position n + i) sees keys 0 .. n + i
+        mask = torch.arange(n + T)[None, :] <= pos[:, None]
+        rep = cfg.heads // cfg.kv_heads
+        h = W["embed"][t]
+        for li, L in enumerate(W["layers"]):
+            x = rmsnorm(h, L["in_norm"], cfg.rms_eps)
+            q = rope(linear(x, L["q"]).view(T, cfg.heads, D), pos, cfg.rope_theta)
+            k = rope(linear(x, L["k"]).view(T, cfg.kv_heads, D), pos, cfg.rope_theta)
+            v = linear(x, L["v"]).view(T, cfg.kv_heads, D)
+            self.k[li] = k if self.k[li] is None else torch.cat([self.k[li], k])
+            self.v[li] = v if self.v[li] is None else torch.cat([self.v[li], v])
+            a = F.scaled_dot_product_attention(q.transpose(0, 1),
+                                               self.k[li].transpose(0, 1).repeat_interleave(rep, 0),
+                                               self.v[li].transpose(0, 1).repeat_interleave(rep, 0), attn_mask=mask)
+            h = h + linear(a.transpose(0, 1).reshape(T, -1), L["o"])
+            x = rmsnorm(h, L["post_norm"], cfg.rms_eps)
+            h = h + linear(F.silu(linear(x, L["gate"])) * linear(x, L["up"]), L["down"])
+        self.n += T
+        return (rmsnorm(h[-1:], W["final_norm"], cfg.rms_eps) @ W["lm_head"].t())[0]
+
+
 @torch.no_grad()
 def logits(cfg, W: dict, tokens) -> torch.Tensor:
     """float32 logits [T, vocab] of the whole token sequence."""

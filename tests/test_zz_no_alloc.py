@@ -42,6 +42,49 @@ def test_static_entry_point_matches_workspace_entry_point_twice():
         assert_close_to_oracle(y_static, d.oracle(), d.dtype)
 
 
+def static_status() -> int:
+    lib = _lib.cuda_lib()
+    out = ctypes.c_int(-1)
+    _lib.check(lib.nq_gemv_static_status(stream_ptr(), ctypes.byref(out)))
+    return out.value
+
+
+def device_free_bytes() -> int:
+    free, _total = torch.cuda.mem_get_info()
+    return free
+
+
+def test_static_entry_point_at_rank_limit_and_beyond_eight_rows():
+    # rank == NQ_GEMV_STATIC_MAX_RANK fills the scratch exactly; batch 9 runs two launches that
+    # share the one control block (cleared once per call, monotonic barrier counter after that)
+    for d in (DeviceLayer(orc.make_layer(33, 1024, 2048, MAX_RANK, 1, "bf16"), "bf16"),
+              DeviceLayer(orc.make_layer(34, 2048, 1024, 700, 9, "f16", with_mid=True), "f16")):
+        y = capi_gemv_static(d)
+        torch.cuda.synchronize()
+        assert static_status() == _lib.NQ_OK
+        assert_close_to_oracle(y, d.oracle(), d.dtype)
+
+
+def test_static_entry_point_allocates_nothing():
+    d = DeviceLayer(orc.make_layer(35, 4096, 4096, 1126, 1, "f16"), "f16")
+    y = torch.empty(1, 4096, dtype=torch.float16, device="cuda")
+    lib = _lib.cuda_lib()
+    args = (NQ_DT["f16"], ptr(d.x), 1, 4096, ptr(d.s2), ptr(d.vb), 1126, None, ptr(d.ub), 4096, ptr(d.s1), ptr(y),
+            stream_ptr())
+    _lib.check(lib.nq_gemv_static(*args))  # the first call on the device looks up the scratch address
+    torch.cuda.synchronize()
+    stats0 = torch.cuda.memory_stats()
+    free0 = device_free_bytes()
+    for _ in range(3):
+        _lib.check(lib.nq_gemv_static(*args))
+    torch.cuda.synchronize()
+    assert device_free_bytes() == free0, "device memory changed across nq_gemv_static calls"
+    stats1 = torch.cuda.memory_stats()
+    assert stats1.get("allocation.all.allocated", 0) == stats0.get("allocation.all.allocated", 0)
+    assert static_status() == _lib.NQ_OK
+    assert_close_to_oracle(y, d.oracle(), "f16")
+
+
 def test_static_entry_point_rejects_rank_above_limit():
     lib = _lib.cuda_lib()
     fake = ctypes.c_void_p(0x10000)  # never dereferenced: the size check comes first
