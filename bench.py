@@ -60,6 +60,11 @@ def parse():
     ap.add_argument("--attention", type=int, default=None, metavar="L",
                     help="the fused decode attention (RoPE + cache write + split-KV attention) of --model at "
                          "sequence length L instead of whole-model decode: KV-cache GB/s over 8 caches cycled")
+    ap.add_argument("--gemm", default=None, metavar="M,OUT,IN,RANK",
+                    help="the prefill GEMM of one layer instead of whole-model decode (e.g. 2048,11008,4096,2054): "
+                         "TFLOP/s counting the two rank-r contractions, 2*M*r*(in+out), over --copies weight copies")
+    ap.add_argument("--fast-gemm", action="store_true",
+                    help="--gemm: the reference-rounding mode (T rounded once to bf16) instead of precise")
     ap.add_argument("--chain", action="store_true",
                     help="decode through GEMV chains (one cooperative launch per block besides attention)")
     ap.add_argument("--peer-allreduce", action="store_true",
@@ -113,14 +118,19 @@ class ClockSampler:
 
     def __init__(self, gpu: int):
         self.gpu, self.lines, self.proc = gpu, [], None
+        self.first = threading.Event()
 
     def __enter__(self):
+        """Start nvidia-smi and wait (up to 5 s) for its first sample, so that samples cover the
+        timed region even when it lasts well under a second (nvidia-smi takes a while to start,
+        longer when several ranks start one each)."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                          "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            self.first.wait(timeout=5.0)
         except OSError:
             self.proc = None
         return self
@@ -128,9 +138,13 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+            self.first.set()
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            n0, t0 = len(self.lines), time.time()
+            while len(self.lines) <= n0 and time.time() - t0 < 1.0:  # one sample at the end of the region
+                time.sleep(0.02)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -349,6 +363,13 @@ def run_nq(args, world, rank, local):
     e1.record()
     torch.cuda.synchronize(dev)
     prefill_ms = e0.elapsed_time(e1)
+    # a second, warm prefill of the same prompt (first-call costs -- library loading, cuDNN and
+    # cuBLAS heuristics, kernel attribute setup -- are paid by the first one)
+    e0.record()
+    dec.prefill(prompt.to(dev))
+    e1.record()
+    torch.cuda.synchronize(dev)
+    prefill_warm_ms = e0.elapsed_time(e1)
     graphed = dec.capture(warmup=2)
     cur = torch.cuda.current_stream(dev)
 
@@ -428,7 +449,8 @@ def run_nq(args, world, rank, local):
                 "cpu_baseline": cpu,
                 "clocks": clocks.summary(),
                 "gpu_launches": launches_per_step * args.steps,
-                "prefill_ms": round(prefill_ms, 2), "first_token": int(first[0])}
+                "prefill_ms": round(prefill_ms, 2), "prefill_warm_ms": round(prefill_warm_ms, 2),
+                "first_token": int(first[0])}
         emit(line)
     if world > 1:
         torch.distributed.barrier(device_ids=[local])
@@ -470,6 +492,63 @@ def run_layer(args):
                       "bytes_per_launch": alg, "copies": args.copies, "launches": n,
                       "roofline": {"bound": "hbm", "peak": peak, "frac": round(gbs / peak, 5), "peak_source": kind},
                       "dtype": "f16", "data": "synthetic"}), flush=True)
+
+
+def run_gemm(args):
+    """One NanoQuant layer's prefill GEMM (tcgen05): --copies distinct seeded weight sets cycled,
+    bf16 activations N(0,1) [M, in], bf16 output; TFLOP/s counts the algorithmic flops of the two
+    rank-r contractions, 2*M*r*(in+out), per device time per launch (CUDA events)."""
+    from nanoquant_b200.decoder import QuantLinearShard, _random_planes
+    m, out_f, in_f, r = (int(v) for v in args.gemm.split(","))
+    dev = torch.device("cuda", 0)
+    copies = max(2, min(args.copies, 8))
+    layers = []
+    for c in range(copies):
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(2000 + c)
+        vb, ub = _random_planes(gen, r, in_f, dev), _random_planes(gen, out_f, r, dev)
+        s2 = (torch.rand(in_f, generator=gen, device=dev) + 0.5).bfloat16()
+        s1 = (torch.rand(out_f, generator=gen, device=dev) * 0.02).bfloat16()
+        layers.append(QuantLinearShard(vb, ub, s2, None, s1))
+    x = torch.randn(m, in_f, device=dev).bfloat16()
+    precise = not args.fast_gemm
+    ops = torch.ops.nq_b200
+
+    def call(i):
+        q = layers[i % copies]
+        return ops.gemm(x, q.s2, q.vb, q.smid, q.ub, q.s1, precise)
+
+    for i in range(max(args.warmup, 3)):
+        call(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(args.steps, 1) * copies
+    with ClockSampler(0) as clocks:
+        e0.record()
+        for i in range(n):
+            call(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / n
+    flops = 2.0 * m * r * (in_f + out_f)
+    tflops = flops / (us * 1e-6) / 1e12
+    pk = _peak_tflops()
+    print(json.dumps({"metric": "prefill GEMM TFLOP/s (two rank-r contractions)", "value": round(tflops, 2),
+                      "unit": "TFLOP/s", "layer": {"m": m, "out": out_f, "in": in_f, "rank": r,
+                                                   "mode": "precise" if precise else "fast"},
+                      "us_per_launch": round(us, 3), "flops_per_launch": flops, "copies": copies, "launches": n,
+                      "roofline": {"bound": "tensor", "peak": pk[0], "frac": round(tflops / pk[0], 5),
+                                   "peak_source": pk[1], "unit": "TFLOP/s"},
+                      "clocks": clocks.summary(), "dtype": "bf16", "data": "synthetic"}), flush=True)
+
+
+def _peak_tflops():
+    """Dense bf16 burst TFLOP/s of MEASURED_PEAKS.json, else the recipe's fallback (1590)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
 
 
 def run_attention(args):
@@ -526,6 +605,10 @@ def main():
         return
     if args.attention:
         run_attention(args)
+        return
+    if args.gemm:
+        _lib_load()
+        run_gemm(args)
         return
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         sys.stdout.flush()
