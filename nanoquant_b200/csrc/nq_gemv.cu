@@ -33,11 +33,6 @@
 
 #include "nq_common.cuh"
 
-// The two-kernel decode GEMV for batch <= 2 (nq_gemv2.cu).
-int nq_gemv2_try(int dtype, const void *x, int64_t batch, int64_t in_features, int n, const nq_gemv_layer *layers,
-                 int xmode, const void *x2, const void *nw, void *res_out, float eps, int act, void *workspace,
-                 size_t workspace_bytes, void *stream);
-
 namespace nq {
 namespace gemv {
 
@@ -1217,14 +1212,6 @@ static int group_impl(int dtype, const GroupInput &in, int64_t batch, int64_t in
         t2 += mb.tiles2;
         mb.tb = reinterpret_cast<__nv_bfloat16 *>(tbp);
         tbp += tb_bytes(L.rank);
-    }
-    // batch <= 2 with the common alignments: the two-kernel path (nq_gemv2.cu), which lets the
-    // next kernel's weight copies overlap this one; it declines (NQ_ERR_UNSUPPORTED, nothing
-    // launched) what it does not cover, and the single-launch kernel below runs instead
-    if (batch <= 2) {
-        const int st2 = nq_gemv2_try(dtype, x, batch, in_features, n, layers, in.xmode, in.x2, in.nw, in.res_out,
-                                     in.eps, in.act, workspace, workspace_bytes, stream);
-        if (st2 != NQ_ERR_UNSUPPORTED) return st2;
     }
     base.tiles1 = t1;
     base.tiles2 = t2;

@@ -96,6 +96,67 @@ def unpack(packed: np.ndarray, shape, method: str = "lsb_first") -> np.ndarray:
     return out
 
 
+# ---------------------------------------------------------------------------------------------
+# Marlin layout (kernel/utils.py:186-284): the reference's prefill-GEMM packing.
+# For a weight [n_out, k_red] (output rows, reduction columns), element (o, r) with
+#   o = ((tile_out * 4 + o16) * 2 + o8) * 8 + o1,  r = ((tile_red * 2 + r8) * 4 + r2) * 2 + r1
+# sits in word [tile_red, tile_out * 32 + o1 * 4 + r2] at bit 15 - (2 * o8 + r8) + 16 * r1 - 4 * o16
+# (utils.py:191-205: the reshape / permute and the exponent table), bit set for -1.
+def marlin_positions(n_out: int, k_red: int):
+    """(word row, word column, bit) of every element of an [n_out, k_red] weight."""
+    if n_out % 64 or k_red % 16:
+        raise ValueError("the Marlin layout needs n_out % 64 == 0 and k_red % 16 == 0")
+    o = np.arange(n_out)[:, None]
+    r = np.arange(k_red)[None, :]
+    tile_out, o16, o8, o1 = o // 64, (o % 64) // 16, (o % 16) // 8, o % 8
+    tile_red, r8, r2, r1 = r // 16, (r % 16) // 8, (r % 8) // 2, r % 2
+    row = np.broadcast_to(tile_red, (n_out, k_red))
+    col = tile_out * 32 + o1 * 4 + r2
+    bit = 15 - (2 * o8 + r8) + 16 * r1 - 4 * o16
+    return row, np.broadcast_to(col, (n_out, k_red)), bit
+
+
+def pack_marlin(signs: np.ndarray) -> np.ndarray:
+    """int8 +-1 weight [n_out, k_red] -> int32 Marlin words [k_red / 16, n_out / 2]."""
+    n_out, k_red = signs.shape
+    row, col, bit = marlin_positions(n_out, k_red)
+    words = np.zeros((k_red // 16, n_out // 2), dtype=np.uint64)
+    vals = (signs < 0).astype(np.uint64) << bit.astype(np.uint64)
+    np.add.at(words, (row.ravel(), col.ravel()), vals.ravel())
+    return words.astype(np.uint32).view(np.int32)
+
+
+def unpack_marlin(words: np.ndarray, n_out: int, k_red: int) -> np.ndarray:
+    """Inverse of pack_marlin: int32 words -> int8 +-1 [n_out, k_red]."""
+    row, col, bit = marlin_positions(n_out, k_red)
+    w = np.asarray(words).view(np.uint32).astype(np.uint64)
+    b = (w[row, col] >> bit.astype(np.uint64)) & np.uint64(1)
+    return (1 - 2 * b.astype(np.int8)).astype(np.int8)
+
+
+def marlin_perm_in(s: np.ndarray) -> np.ndarray:
+    """Input-scale order of the Marlin GEMM (utils.py:207-208)."""
+    return np.asarray(s).reshape(-1, 2, 4, 2).transpose(0, 2, 1, 3).reshape(-1)
+
+
+def marlin_perm_out(s: np.ndarray) -> np.ndarray:
+    """Output-scale order of the Marlin GEMM (utils.py:209-210)."""
+    return np.asarray(s).reshape(-1, 4, 4, 2).transpose(0, 2, 1, 3).reshape(-1)
+
+
+def pack_marlin_fused(V: np.ndarray, U: np.ndarray, sg, sl, sh):
+    """pack_binary_marlin_fused (utils.py:217-284) for a module's V [rank, in] and U [out, rank]
+    (the reference passes V.T and U.T): rank padded to a multiple of 256 with +1 signs and zero
+    scale_mid; returns (V words, U words, s1, s2, s3, workspace elements)."""
+    r = V.shape[0]
+    rp = (r + 255) // 256 * 256
+    Vp = np.concatenate([V, np.ones((rp - r, V.shape[1]), dtype=np.int8)], 0)
+    Up = np.concatenate([U, np.ones((U.shape[0], rp - r), dtype=np.int8)], 1)
+    slp = np.concatenate([np.asarray(sl, dtype=np.float32), np.zeros(rp - r, dtype=np.float32)])
+    ws = max(rp // 128 * 32, U.shape[0] // 128 * 32)
+    return (pack_marlin(Vp), pack_marlin(Up), marlin_perm_in(sg), marlin_perm_out(slp), marlin_perm_out(sh), ws)
+
+
 def forward(x, s2, v_bits, rank, smid, u_bits, s1, method: str = "lsb_first", return_interm=False):
     """float64 y = s1 * (U (smid * (V (s2 * x)))) from packed planes (linear.py:282-291).
 
