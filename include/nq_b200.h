@@ -218,8 +218,9 @@ NQ_API int nq_gemv_chain(int dtype, int64_t batch, int n_phases, const nq_chain_
  * Prefill GEMM: replaces marlin_nanoquant_cuda (src/nanoquant/kernel/cuda/gemm.cpp:112-122,
  * schema src/nanoquant/kernel/pybind.cpp:99-104) on the same HALF2 planes the GEMV uses.
  * tcgen05 tensor-core contraction in two stages, T = (x*s2) V^T * smid then y = (T U^T) * s1.
- * `precise` = 1 keeps T as a bf16 hi/lo pair (float32-grade intermediate); 0 rounds T
- * once to bf16 like the reference's fp16/bf16 intermediate (gemm.cpp:119).
+ * `precise` = 1 keeps T as a bf16 hi/lo pair (float32-grade intermediate); 0 rounds T once to
+ * the layer dtype, as the reference's fp16/bf16 intermediate `imm` (gemm.cpp:119), and runs one
+ * MMA per K step in stage 2 instead of two.
  * Requires in_features % 8 == 0 and 16-byte aligned x / y.
  * ------------------------------------------------------------------------------- */
 NQ_API size_t nq_gemm_workspace_bytes(int64_t m, int64_t rank);
@@ -227,6 +228,35 @@ NQ_API int nq_gemm(int dtype, const void *x, int64_t m, int64_t in_features, con
             const int32_t *v_bits, int64_t rank, const void *scale_mid, const int32_t *u_bits,
             int64_t out_features, const void *scale_post, int precise, void *y, void *workspace,
             size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * Single-stage GEMM y = ((x * scale_in) W^T) * scale_out with W [n, k] in +-1 (HALF2 planes
+ * [n, ceil(k/32)]): replaces marlin_onebit_cuda (src/nanoquant/kernel/cuda/gemm.cpp:58-93,
+ * schema pybind.cpp:93-98) on this build's planes.  scale_in [k] must be given (pass ones for
+ * none); scale_out [n] may be NULL.  Requires k % 8 == 0 and 16-byte aligned x, y, scale_in.
+ * The workspace holds only the status word (nq_gemm_onebit_workspace_bytes()).
+ * ------------------------------------------------------------------------------- */
+NQ_API size_t nq_gemm_onebit_workspace_bytes(void);
+NQ_API int nq_gemm_onebit(int dtype, const void *x, int64_t m, int64_t k, const void *scale_in,
+                          const int32_t *w_bits, int64_t n, const void *scale_out, void *y,
+                          void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * The reference's Marlin sign layout (its prefill-GEMM kernel type's packing).
+ * nq_pack_marlin replaces the sign packing of pack_binary_marlin (src/nanoquant/kernel/
+ * utils.py:186-206): int8 +-1 weight [n_out, k_red] -> int32 words [k_red/16, n_out/2], element
+ * (o, r) at word [r/16][(o/64)*32 + (o%8)*4 + (r%8)/2], bit 15 - (2*((o%16)/8) + (r%16)/8)
+ * + 16*(r%2) - 4*((o%64)/16), set for -1; needs n_out % 64 == 0 and k_red % 16 == 0.
+ * `invalid_count` as in nq_pack_signs.  nq_unpack_marlin is its inverse (no reference
+ * counterpart).  nq_marlin_to_half2 converts Marlin words to HALF2 planes [n_out, ceil(k_red/32)]
+ * on the device (no reference counterpart: it lets the marlin_* ops run this build's GEMM).
+ * ------------------------------------------------------------------------------- */
+NQ_API int nq_pack_marlin(const int8_t *signs, int64_t n_out, int64_t k_red, int32_t *words,
+                          int32_t *invalid_count, void *stream);
+NQ_API int nq_unpack_marlin(const int32_t *words, int64_t n_out, int64_t k_red, int8_t *signs,
+                            void *stream);
+NQ_API int nq_marlin_to_half2(const int32_t *words, int64_t n_out, int64_t k_red, int32_t *planes,
+                              void *stream);
 
 /* ---------------------------------------------------------------------------------
  * Workspace status word (no reference counterpart: the reference kernels have no

@@ -79,6 +79,12 @@ _SIGNATURES = {
     "nq_gemv_chain": (_c.c_int, [_c.c_int, _c.c_int64, _c.c_int, _c.c_void_p, _c.c_void_p, _c.c_size_t,
                                  _c.c_void_p]),
     "nq_gemm_workspace_bytes": (_c.c_size_t, [_c.c_int64, _c.c_int64]),
+    "nq_gemm_onebit_workspace_bytes": (_c.c_size_t, []),
+    "nq_gemm_onebit": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p,
+                                  _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t, _c.c_void_p]),
+    "nq_pack_marlin": (_c.c_int, [_c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p]),
+    "nq_unpack_marlin": (_c.c_int, [_c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p]),
+    "nq_marlin_to_half2": (_c.c_int, [_c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p]),
     "nq_gemm": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64,
                            _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_void_p,
                            _c.c_size_t, _c.c_void_p]),

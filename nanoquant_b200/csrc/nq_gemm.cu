@@ -140,11 +140,13 @@ struct Layout {
     static constexpr uint32_t kTotal = (kAbort + 4 + 127) & ~127u;
 };
 
-// TA: MMA operand type (stage 1: the layer dtype, stage 2: bf16).  TOut: the layer dtype,
-// which is the type of the column scale (smid / s1) and of the stage-2 output y; stage 1
-// always writes T as bf16 (hi, and lo when kHiLo).  kS2: fold the s2 slice into the weight
-// operand (stage 1).  kTwoA: two activation tiles (T_hi, T_lo) per K step (stage 2, precise).
-template <typename TA, typename TOut, bool kS2, bool kTwoA, bool kHiLo>
+// TA: MMA operand type (stage 1: the layer dtype; stage 2: bf16 in precise mode, the layer dtype
+// otherwise).  TOut: the layer dtype, the type of the column scale (smid / s1) and of what the
+// epilogue stores unless kStoreT.  kS2: fold the s2 slice into the weight operand (stage 1, and
+// the single-stage GEMM).  kTwoA: two activation tiles (T_hi, T_lo) per K step (stage 2, precise).
+// kStoreT: the epilogue stores T as bf16 (hi, and lo when kHiLo) -- stage 1 of precise mode; else
+// it stores TOut (stage 1 of fast mode: T in the layer dtype; stage 2; the single-stage GEMM).
+template <typename TA, typename TOut, bool kS2, bool kTwoA, bool kHiLo, bool kStoreT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
                 const __grid_constant__ CUtensorMap map_s2, const Params p) {
@@ -304,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             const int ncols = min(32, p.N - (n0 + c));
-            if (kS2) {
+            if (kStoreT) {
                 // stage 1: T (bf16) and optionally T_lo
                 __nv_bfloat16 *hi = static_cast<__nv_bfloat16 *>(p.out_hi) + (size_t)m * p.ldo + n0 + c;
                 __nv_bfloat16 *lo = static_cast<__nv_bfloat16 *>(p.out_lo) + (size_t)m * p.ldo + n0 + c;
@@ -407,10 +409,10 @@ static int make_map_1d(CUtensorMap *map, const void *base, CUtensorMapDataType d
     return NQ_OK;
 }
 
-template <typename TA, typename TOut, bool kS2, bool kTwoA, bool kHiLo>
+template <typename TA, typename TOut, bool kS2, bool kTwoA, bool kHiLo, bool kStoreT>
 static int launch_stage(const CUtensorMap &a, const CUtensorMap &a2, const CUtensorMap &s2, const Params &p,
                         cudaStream_t stream) {
-    auto kern = gemm_kernel<TA, TOut, kS2, kTwoA, kHiLo>;
+    auto kern = gemm_kernel<TA, TOut, kS2, kTwoA, kHiLo, kStoreT>;
     const size_t smem = Layout<kTwoA, kS2>::kTotal + 1024;
     static bool attr_set[64] = {};
     int dev = 0;
@@ -482,7 +484,8 @@ int nq_gemm(int dtype, const void *x, int64_t m, int64_t in_features, const void
     CUtensorMap mx, ms2, mth, mtl;
     int st = make_map_2d(&mx, x, in_dt, m, in_features, in_features);
     if (!st) st = make_map_1d(&ms2, scale_pre, in_dt, in_features);
-    if (!st) st = make_map_2d(&mth, t_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, m, rank, (int64_t)ldt);
+    // precise: T as bf16 hi / lo planes; fast: T in the layer dtype (one plane)
+    if (!st) st = make_map_2d(&mth, t_hi, precise ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : in_dt, m, rank, (int64_t)ldt);
     if (!st) st = make_map_2d(&mtl, t_lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, m, rank, (int64_t)ldt);
     if (st) return st;
 
@@ -513,19 +516,64 @@ int nq_gemm(int dtype, const void *x, int64_t m, int64_t in_features, const void
     p2.status = &ctrl->status;
 
     if (dtype == NQ_DTYPE_F16) {
-        st = precise ? launch_stage<__half, __half, true, false, true>(mx, mx, ms2, p1, s)
-                     : launch_stage<__half, __half, true, false, false>(mx, mx, ms2, p1, s);
+        st = precise ? launch_stage<__half, __half, true, false, true, true>(mx, mx, ms2, p1, s)
+                     : launch_stage<__half, __half, true, false, false, false>(mx, mx, ms2, p1, s);
         if (st) return st;
-        st = precise ? launch_stage<__nv_bfloat16, __half, false, true, false>(mth, mtl, ms2, p2, s)
-                     : launch_stage<__nv_bfloat16, __half, false, false, false>(mth, mth, ms2, p2, s);
+        st = precise ? launch_stage<__nv_bfloat16, __half, false, true, false, false>(mth, mtl, ms2, p2, s)
+                     : launch_stage<__half, __half, false, false, false, false>(mth, mth, ms2, p2, s);
     } else {
-        st = precise ? launch_stage<__nv_bfloat16, __nv_bfloat16, true, false, true>(mx, mx, ms2, p1, s)
-                     : launch_stage<__nv_bfloat16, __nv_bfloat16, true, false, false>(mx, mx, ms2, p1, s);
+        st = precise ? launch_stage<__nv_bfloat16, __nv_bfloat16, true, false, true, true>(mx, mx, ms2, p1, s)
+                     : launch_stage<__nv_bfloat16, __nv_bfloat16, true, false, false, false>(mx, mx, ms2, p1, s);
         if (st) return st;
-        st = precise ? launch_stage<__nv_bfloat16, __nv_bfloat16, false, true, false>(mth, mtl, ms2, p2, s)
-                     : launch_stage<__nv_bfloat16, __nv_bfloat16, false, false, false>(mth, mth, ms2, p2, s);
+        st = precise ? launch_stage<__nv_bfloat16, __nv_bfloat16, false, true, false, false>(mth, mtl, ms2, p2, s)
+                     : launch_stage<__nv_bfloat16, __nv_bfloat16, false, false, false, false>(mth, mth, ms2, p2, s);
     }
     return st;
+}
+
+size_t nq_gemm_onebit_workspace_bytes(void) { return sizeof(nq::Ctrl); }
+
+int nq_gemm_onebit(int dtype, const void *x, int64_t m, int64_t k, const void *scale_in, const int32_t *w_bits,
+                   int64_t n, const void *scale_out, void *y, void *workspace, size_t workspace_bytes, void *stream) {
+    using namespace nq;
+    using namespace nq::gemm;
+    if (dtype != NQ_DTYPE_F16 && dtype != NQ_DTYPE_BF16)
+        return fail(NQ_ERR_UNSUPPORTED, "dtype must be NQ_DTYPE_F16 or NQ_DTYPE_BF16 (got %d)", dtype);
+    if (!x || !scale_in || !w_bits || !y) return fail(NQ_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (m <= 0 || k <= 0 || n <= 0) return fail(NQ_ERR_INVALID_ARGUMENT, "sizes must be positive");
+    if (k % 8 != 0) return fail(NQ_ERR_UNSUPPORTED, "k must be a multiple of 8 for the GEMM");
+    if (m > (1 << 24) || k > (1 << 24) || n > (1 << 24)) return fail(NQ_ERR_UNSUPPORTED, "sizes beyond the supported range");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(scale_in)) & 15)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "x, y and scale_in must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(scale_out) & 1) return fail(NQ_ERR_INVALID_ARGUMENT, "scale_out must be 2-byte aligned");
+    if (reinterpret_cast<uintptr_t>(w_bits) & 3) return fail(NQ_ERR_INVALID_ARGUMENT, "sign planes must be 4-byte aligned");
+    if (!workspace || workspace_bytes < sizeof(Ctrl))
+        return fail(NQ_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", sizeof(Ctrl), workspace_bytes);
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+    if (device_info(dev).cc_major != 10) return fail(NQ_ERR_UNSUPPORTED, "this build targets sm_100a");
+    const CUtensorMapDataType in_dt =
+        dtype == NQ_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap mx, ms;
+    int st = make_map_2d(&mx, x, in_dt, m, k, k);
+    if (!st) st = make_map_1d(&ms, scale_in, in_dt, k);
+    if (st) return st;
+    Params p{};
+    p.bits = reinterpret_cast<const uint32_t *>(w_bits);
+    p.W = (int)((k + 31) / 32);
+    p.M = (int)m;
+    p.N = (int)n;
+    p.K = (int)k;
+    p.nk = (int)((k + BK - 1) / BK);
+    p.col_scale = scale_out;
+    p.out_hi = y;
+    p.out_lo = nullptr;
+    p.ldo = (int)n;
+    p.status = &static_cast<Ctrl *>(workspace)->status;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return dtype == NQ_DTYPE_F16 ? launch_stage<__half, __half, true, false, false, false>(mx, mx, ms, p, s)
+                                 : launch_stage<__nv_bfloat16, __nv_bfloat16, true, false, false, false>(mx, mx, ms, p, s);
 }
 
 }  // extern "C"

@@ -155,9 +155,105 @@ bool gemm_ok(const LayerArgs &a) {
            (reinterpret_cast<uintptr_t>(a.x.data_ptr()) & 15) == 0;
 }
 
+// GEMM precision: bf16 layers keep T as a bf16 hi/lo pair (rounding T to bf16 alone costs about
+// 2e-3 rel-L2); fp16 layers round T once to fp16, the reference's own intermediate (gemm.cpp:119),
+// well inside 1e-3, with one stage-2 MMA per K step instead of two.
 at::Tensor forward_auto(const LayerArgs &a) {
-    at::Tensor y = gemm_ok(a) ? run_gemm(a, true) : run_gemv(a);
+    at::Tensor y = gemm_ok(a) ? run_gemm(a, a.x.scalar_type() == at::kBFloat16) : run_gemv(a);
     return a.x.dim() == 1 ? y.squeeze(0) : y;
+}
+
+// ------------------------------------------------------------------ Marlin layout (reference gemm kernel type)
+// Inverses of the reference's scale permutations (src/nanoquant/kernel/utils.py:207-210).
+at::Tensor marlin_unperm_in(const at::Tensor &s) { return s.reshape({-1, 4, 2, 2}).permute({0, 2, 1, 3}).reshape({-1}); }
+at::Tensor marlin_unperm_out(const at::Tensor &s) { return s.reshape({-1, 4, 4, 2}).permute({0, 2, 1, 3}).reshape({-1}); }
+
+at::Tensor marlin_to_half2_t(const at::Tensor &words, int64_t n_out, int64_t k_red) {
+    CHECK_CUDA_CONT(words, at::kInt);
+    TORCH_CHECK(words.dim() == 2 && words.size(0) * 16 == k_red && words.size(1) * 2 == n_out,
+                "Marlin words must be [k_red/16, n_out/2]");
+    c10::cuda::CUDAGuard guard(words.device());
+    auto planes = at::empty({n_out, (k_red + 31) / 32}, words.options());
+    NQ_TORCH_CHECK(nq_marlin_to_half2(words.data_ptr<int32_t>(), n_out, k_red, planes.data_ptr<int32_t>(),
+                                      cur_stream(words)));
+    return planes;
+}
+
+// The reference's marlin_onebit_check_and_alloc (gemm.cpp:37-56): same checks, same messages.
+void marlin_check(const at::Tensor &A, const at::Tensor &B, const std::optional<at::Tensor> &s_in,
+                  const std::optional<at::Tensor> &s_out, const at::Tensor &workspace) {
+    constexpr int64_t kMinMaxPar = 32;  // MARLIN_MIN_MAX_PAR
+    TORCH_CHECK(A.scalar_type() == at::kHalf || A.scalar_type() == at::kBFloat16,
+                "Unsupported dtype: Marlin only supports Half and BFloat16");
+    TORCH_CHECK(A.dim() == 2 && B.dim() == 2, "x and the weight must be 2-D");
+    const int64_t prob_n = B.size(1) * 2, prob_k = A.size(1);
+    TORCH_CHECK(prob_k == B.size(0) * 16, "k dimension mismatch");
+    TORCH_CHECK(!s_in.has_value() || s_in->size(0) == prob_k, "s_in size mismatch");
+    TORCH_CHECK(!s_out.has_value() || s_out->size(0) == prob_n, "s_out size mismatch");
+    TORCH_CHECK(workspace.numel() >= prob_n / 128 * kMinMaxPar, "workspace too small");
+}
+
+at::Tensor marlin_onebit_forward_cuda(const at::Tensor &x, const at::Tensor &weight,
+                                      const std::optional<at::Tensor> &scale_g,
+                                      const std::optional<at::Tensor> &scale_h, at::Tensor &workspace) {
+    marlin_check(x, weight, scale_g, scale_h, workspace);
+    CHECK_CUDA_CONT(x, x.scalar_type());
+    c10::cuda::CUDAGuard guard(x.device());
+    const int64_t m = x.size(0), k = x.size(1), n = weight.size(1) * 2;
+    at::Tensor planes = marlin_to_half2_t(weight, n, k);
+    at::Tensor s_in = scale_g.has_value() ? marlin_unperm_in(scale_g->to(x.scalar_type())).contiguous()
+                                          : at::ones({k}, x.options());
+    at::Tensor s_out;
+    if (scale_h.has_value()) s_out = marlin_unperm_out(scale_h->to(x.scalar_type())).contiguous();
+    auto y = at::empty({m, n}, x.options());
+    if (m == 0) return y;
+    at::Tensor ws = at::zeros({(int64_t)nq_gemm_onebit_workspace_bytes()}, x.options().dtype(at::kByte));
+    NQ_TORCH_CHECK(nq_gemm_onebit(dtype_code(x.scalar_type()), x.data_ptr(), m, k, s_in.data_ptr(),
+                                  planes.data_ptr<int32_t>(), n, s_out.defined() ? s_out.data_ptr() : nullptr,
+                                  y.data_ptr(), ws.data_ptr(), (size_t)ws.numel(), cur_stream(x)));
+    return y;
+}
+
+at::Tensor marlin_onebit_forward_meta(const at::Tensor &x, const at::Tensor &weight,
+                                      const std::optional<at::Tensor> &scale_g,
+                                      const std::optional<at::Tensor> &scale_h, at::Tensor &workspace) {
+    marlin_check(x, weight, scale_g, scale_h, workspace);
+    return at::empty({x.size(0), weight.size(1) * 2}, x.options());
+}
+
+// marlin_nanoquant_cuda (gemm.cpp:112-122) is two marlin_onebit calls: imm = x V (s_in = scale_g,
+// s_out = scale_l), y = imm U (s_out = scale_h).  Here the two factors are converted to HALF2
+// planes and the layer runs as one NanoQuant layer of rank = the padded rank: the GEMV for up to
+// 32 rows, the tcgen05 GEMM above (fp16: T rounded once to fp16 like the reference's imm).
+at::Tensor marlin_nanoquant_forward_cuda(const at::Tensor &x, const at::Tensor &weight_u, const at::Tensor &weight_v,
+                                         const std::optional<at::Tensor> &scale_g,
+                                         const std::optional<at::Tensor> &scale_l,
+                                         const std::optional<at::Tensor> &scale_h, at::Tensor &workspace) {
+    marlin_check(x, weight_u, scale_g, scale_l, workspace);
+    const int64_t rank = weight_u.size(1) * 2;
+    TORCH_CHECK(rank == weight_v.size(0) * 16, "k dimension mismatch");
+    TORCH_CHECK(!scale_h.has_value() || scale_h->size(0) == weight_v.size(1) * 2, "s_out size mismatch");
+    TORCH_CHECK(workspace.numel() >= weight_v.size(1) * 2 / 128 * 32, "workspace too small");
+    CHECK_CUDA_CONT(x, x.scalar_type());
+    c10::cuda::CUDAGuard guard(x.device());
+    const int64_t in_f = x.size(1), out_f = weight_v.size(1) * 2;
+    at::Tensor vb = marlin_to_half2_t(weight_u, rank, in_f);
+    at::Tensor ub = marlin_to_half2_t(weight_v, out_f, rank);
+    const auto dt = x.scalar_type();
+    at::Tensor s2 = scale_g.has_value() ? marlin_unperm_in(scale_g->to(dt)).contiguous() : at::ones({in_f}, x.options());
+    at::Tensor s1 = scale_h.has_value() ? marlin_unperm_out(scale_h->to(dt)).contiguous() : at::ones({out_f}, x.options());
+    std::optional<at::Tensor> smid;
+    if (scale_l.has_value()) smid = marlin_unperm_out(scale_l->to(dt)).contiguous();
+    if (x.size(0) == 0) return at::empty({0, out_f}, x.options());
+    return forward_auto(check_layer(x, s2, vb, smid, ub, s1));
+}
+
+at::Tensor marlin_nanoquant_forward_meta(const at::Tensor &x, const at::Tensor &weight_u, const at::Tensor &weight_v,
+                                         const std::optional<at::Tensor> &scale_g,
+                                         const std::optional<at::Tensor> &scale_l,
+                                         const std::optional<at::Tensor> &scale_h, at::Tensor &workspace) {
+    marlin_check(x, weight_u, scale_g, scale_l, workspace);
+    return at::empty({x.size(0), weight_v.size(1) * 2}, x.options());
 }
 
 // ------------------------------------------------------------------ binary_kernels (reference schemas)
@@ -214,6 +310,55 @@ at::Tensor pack_signs_cuda(const at::Tensor &signs, const std::string &method, b
         TORCH_CHECK_VALUE(n == 0, "Cannot pack: factors must contain only -1 and +1 (", n, " other values)");
     }
     return out;
+}
+
+at::Tensor pack_marlin_cuda(const at::Tensor &signs, bool check) {
+    TORCH_CHECK_TYPE(signs.scalar_type() == at::kChar, "Input tensor must be int8.");
+    TORCH_CHECK(signs.is_cuda(), "signs must be a CUDA tensor");
+    TORCH_CHECK(signs.dim() == 2, "signs must be 2-D [n_out, k_red]");
+    c10::cuda::CUDAGuard guard(signs.device());
+    at::Tensor s = signs.contiguous();
+    const int64_t n = s.size(0), k = s.size(1);
+    TORCH_CHECK_VALUE(n % 64 == 0 && k % 16 == 0, "the Marlin layout needs n_out % 64 == 0 and k_red % 16 == 0, got ",
+                      s.sizes());
+    auto out = at::empty({k / 16, n / 2}, s.options().dtype(at::kInt));
+    if (n == 0 || k == 0) return out;
+    at::Tensor bad;
+    if (check) bad = at::zeros({1}, s.options().dtype(at::kInt));
+    NQ_TORCH_CHECK(nq_pack_marlin(s.data_ptr<int8_t>(), n, k, out.data_ptr<int32_t>(),
+                                  check ? bad.data_ptr<int32_t>() : nullptr, cur_stream(s)));
+    if (check) {
+        const int nb = bad.item<int>();
+        TORCH_CHECK_VALUE(nb == 0, "Cannot pack: factors must contain only -1 and +1 (", nb, " other values)");
+    }
+    return out;
+}
+
+at::Tensor pack_marlin_meta(const at::Tensor &signs, bool) {
+    return at::empty({signs.size(1) / 16, signs.size(0) / 2}, signs.options().dtype(at::kInt));
+}
+
+at::Tensor unpack_marlin_cuda(const at::Tensor &words, int64_t n_out, int64_t k_red) {
+    CHECK_CUDA_CONT(words, at::kInt);
+    TORCH_CHECK_VALUE(words.dim() == 2 && words.size(0) * 16 == k_red && words.size(1) * 2 == n_out,
+                      "Marlin words must be [k_red/16, n_out/2]");
+    c10::cuda::CUDAGuard guard(words.device());
+    auto out = at::empty({n_out, k_red}, words.options().dtype(at::kChar));
+    if (n_out == 0 || k_red == 0) return out;
+    NQ_TORCH_CHECK(nq_unpack_marlin(words.data_ptr<int32_t>(), n_out, k_red, out.data_ptr<int8_t>(), cur_stream(words)));
+    return out;
+}
+
+at::Tensor unpack_marlin_meta(const at::Tensor &words, int64_t n_out, int64_t k_red) {
+    return at::empty({n_out, k_red}, words.options().dtype(at::kChar));
+}
+
+at::Tensor marlin_to_half2_cuda(const at::Tensor &words, int64_t n_out, int64_t k_red) {
+    return marlin_to_half2_t(words, n_out, k_red);
+}
+
+at::Tensor marlin_to_half2_meta(const at::Tensor &words, int64_t n_out, int64_t k_red) {
+    return at::empty({n_out, (k_red + 31) / 32}, words.options());
 }
 
 at::Tensor pack_signs_meta(const at::Tensor &signs, const std::string &method, bool check) {
@@ -593,14 +738,25 @@ TORCH_LIBRARY(binary_kernels, m) {
         "Tensor(a!) workspace) -> Tensor");
 }
 
-TORCH_LIBRARY_IMPL(binary_kernels, CUDA, m) { m.impl("nanoquant_dyn_forward", &nanoquant_dyn_forward_cuda); }
+TORCH_LIBRARY_IMPL(binary_kernels, CUDA, m) {
+    m.impl("nanoquant_dyn_forward", &nanoquant_dyn_forward_cuda);
+    m.impl("marlin_onebit_forward", &marlin_onebit_forward_cuda);
+    m.impl("marlin_nanoquant_forward", &marlin_nanoquant_forward_cuda);
+}
 
-TORCH_LIBRARY_IMPL(binary_kernels, Meta, m) { m.impl("nanoquant_dyn_forward", &nanoquant_dyn_forward_meta); }
+TORCH_LIBRARY_IMPL(binary_kernels, Meta, m) {
+    m.impl("nanoquant_dyn_forward", &nanoquant_dyn_forward_meta);
+    m.impl("marlin_onebit_forward", &marlin_onebit_forward_meta);
+    m.impl("marlin_nanoquant_forward", &marlin_nanoquant_forward_meta);
+}
 
 TORCH_LIBRARY(nq_b200, m) {
     m.def("pack_signs(Tensor signs, str method='lsb_first', bool check=False) -> Tensor");
     m.def("unpack_signs(Tensor packed, int rows, int cols, str method='lsb_first') -> Tensor");
     m.def("repack_signs(Tensor packed, int cols, str src_method, str dst_method) -> Tensor");
+    m.def("pack_marlin(Tensor signs, bool check=False) -> Tensor");
+    m.def("unpack_marlin(Tensor words, int n_out, int k_red) -> Tensor");
+    m.def("marlin_to_half2(Tensor words, int n_out, int k_red) -> Tensor");
     m.def(
         "gemv(Tensor x, Tensor scale_pre, Tensor v_bits, Tensor? scale_mid, Tensor u_bits, Tensor scale_post) -> "
         "Tensor");
@@ -634,6 +790,9 @@ TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
     m.impl("pack_signs", &pack_signs_cuda);
     m.impl("unpack_signs", &unpack_signs_cuda);
     m.impl("repack_signs", &repack_signs_cuda);
+    m.impl("pack_marlin", &pack_marlin_cuda);
+    m.impl("unpack_marlin", &unpack_marlin_cuda);
+    m.impl("marlin_to_half2", &marlin_to_half2_cuda);
     m.impl("gemv", &gemv_cuda);
     m.impl("gemm", &gemm_cuda);
     m.impl("linear", &linear_cuda);
@@ -651,6 +810,9 @@ TORCH_LIBRARY_IMPL(nq_b200, Meta, m) {
     m.impl("pack_signs", &pack_signs_meta);
     m.impl("unpack_signs", &unpack_signs_meta);
     m.impl("repack_signs", &repack_signs_meta);
+    m.impl("pack_marlin", &pack_marlin_meta);
+    m.impl("unpack_marlin", &unpack_marlin_meta);
+    m.impl("marlin_to_half2", &marlin_to_half2_meta);
     m.impl("gemv", &layer_meta);
     m.impl("gemm", &gemm_meta);
     m.impl("linear", &layer_meta);

@@ -6,7 +6,10 @@ Mirrors the names, argument meaning and error behaviour of
 * ``pack_binary_gemv``   (utils.py:51-113)  -> nq_pack_signs CUDA kernel
 * ``unpack_binary_gemv`` (utils.py:116-183) -> nq_unpack_signs CUDA kernel
 * ``get_kernel_function`` (utils.py:33-48)  -> resolves ``torch.ops.binary_kernels.*``
-* ``binary_packer`` / ``binary_unpacker`` aliases (utils.py:503-507)
+* ``pack_binary_marlin`` (utils.py:186-214), ``pack_binary_marlin_fused`` (utils.py:217-284)
+  -> nq_pack_marlin CUDA kernel + the reference's scale permutations
+* ``binary_packer`` / ``binary_unpacker`` / ``marlin_onebit_packer`` / ``marlin_nanoquant_packer``
+  aliases (utils.py:503-507)
 
 The kernels need CUDA tensors; a CPU tensor raises instead of being packed on the host.
 """
@@ -73,8 +76,75 @@ def repack_binary(packed: torch.Tensor, n_cols: int, src_method: str, dst_method
     return _ops().repack_signs(packed.contiguous(), int(n_cols), src_method, dst_method)
 
 
+MARLIN_MIN_MAX_PAR = 32  # the reference's lower bound for parallel column slices (kernel/utils.py:21)
+
+
+def _perm_in(s: torch.Tensor) -> torch.Tensor:
+    return s.reshape(s.numel() // 16, 2, 4, 2).permute(0, 2, 1, 3).reshape(-1).contiguous()
+
+
+def _perm_out(s: torch.Tensor) -> torch.Tensor:
+    return s.reshape(s.numel() // 32, 4, 4, 2).permute(0, 2, 1, 3).reshape(-1).contiguous()
+
+
+def pack_binary_marlin(weight: torch.Tensor, scale_in: torch.Tensor, scale_out: torch.Tensor):
+    """Marlin packing of a {-1,+1} weight [n_out, k_red] (kernel/utils.py:186-214), on the GPU.
+
+    Returns (words int32 [k_red/16, n_out/2], scale_in permuted, scale_out permuted,
+    workspace size) exactly as the reference; the sign words come from the nq_pack_marlin
+    CUDA kernel, the scale permutations are the reference's reshape / permute."""
+    _require_cuda(weight, "pack_binary_marlin")
+    n_out, k_red = weight.shape
+    if n_out % 64 or k_red % 16:
+        raise RuntimeError(f"shape {tuple(weight.shape)} is invalid for the Marlin layout "
+                           "(needs rows % 64 == 0 and columns % 16 == 0)")
+    words = _ops().pack_marlin(weight.to(torch.int8).contiguous(), False)
+    workspace_size = scale_out.numel() // 128 * MARLIN_MIN_MAX_PAR
+    return words, _perm_in(scale_in), _perm_out(scale_out), workspace_size
+
+
+def pack_binary_marlin_fused(V_sign: torch.Tensor, U_sign: torch.Tensor, scale_g: torch.Tensor,
+                             scale_l: torch.Tensor, scale_h: torch.Tensor):
+    """Both factors of a layer for the Marlin GEMM (kernel/utils.py:217-284), on the GPU.
+
+    V_sign [N, R] and U_sign [R, M] are the module's V.T and U.T; the rank is padded to a
+    multiple of 256 with +1 signs (V columns, U rows) and zero scale_l, as the reference does
+    (which, like it, needs R % 32 == 0: utils.py:251-262 rounds only a local copy of R).
+    Returns (V_bits, U_bits, scale_g_marlin, scale_l_marlin, scale_h_marlin, workspace)."""
+    dev = V_sign.device
+    N = scale_g.shape[0]
+    R = scale_l.shape[0] if scale_l is not None else U_sign.shape[0]
+    M = scale_h.shape[0]
+    p = 32
+    if N % p != 0:
+        N = ((N // p) + 1) * p
+    if R % p != 0:
+        R = ((R // p) + 1) * p
+    if M % p != 0:
+        M = ((M // p) + 1) * p
+    rank_marlin = (R + 255) // 256 * 256
+    if rank_marlin > R:
+        pad = rank_marlin - R
+        V_sign = torch.cat([V_sign, torch.ones(N, pad, device=dev, dtype=torch.int8)], dim=1)
+        U_sign = torch.cat([U_sign, torch.ones(pad, M, device=dev, dtype=torch.int8)], dim=0)
+        if scale_l is not None:
+            scale_l = torch.cat([scale_l, torch.zeros(pad, device=dev, dtype=scale_l.dtype)], dim=0)
+    V_bits, scale_g_m, scale_l_m, ws_v = pack_binary_marlin(V_sign.T, scale_g, scale_l)
+    U_bits, _, scale_h_m, ws_u = pack_binary_marlin(U_sign.T, scale_l, scale_h)
+    workspace = torch.zeros(max(ws_v, ws_u), device=dev, dtype=torch.int32)
+    return V_bits.contiguous(), U_bits.contiguous(), scale_g_m, scale_l_m, scale_h_m, workspace
+
+
+def unpack_binary_marlin(words: torch.Tensor, n_out: int, k_red: int) -> torch.Tensor:
+    """Inverse of the Marlin sign packing: int32 words -> int8 +-1 [n_out, k_red] (GPU)."""
+    _require_cuda(words, "unpack_binary_marlin")
+    return _ops().unpack_marlin(words.contiguous(), int(n_out), int(k_red))
+
+
 binary_packer = pack_binary_gemv
 binary_unpacker = unpack_binary_gemv
+marlin_onebit_packer = pack_binary_marlin
+marlin_nanoquant_packer = pack_binary_marlin_fused
 
 
 def get_kernel_function(namespace: str, dtype: torch.dtype, kernel_type: str):

@@ -136,7 +136,9 @@ class NanoQuantLinear(nn.Module):
         """Convert scales to 1-D ``dtype`` and the factors to half2 planes (linear.py:186-238).
 
         kernel_type: "gemv" -> torch.ops.binary_kernels.nanoquant_dyn_forward (reference op);
-        "gemm" -> torch.ops.nq_b200.gemm (tcgen05 prefill GEMM on the same planes);
+        "gemm" -> the reference's Marlin path: marlin_nanoquant_packer on V.T / U.T (rank padded
+        to 256) and torch.ops.binary_kernels.marlin_nanoquant_forward (linear.py:220-236), whose
+        CUDA implementation here runs the tcgen05 GEMM (the GEMV for <= 32 rows);
         "b200" -> torch.ops.nq_b200.linear (GEMV for <= 32 rows, GEMM above).
         The reference's "gemlite" backend (third-party Triton) is not provided.
         """
@@ -150,6 +152,9 @@ class NanoQuantLinear(nn.Module):
             raise RuntimeError("move the module to a CUDA device before _prepare_kernel")
         _lib.load_torch_ops()
         v, u = self._planes_half2()
+        if kernel_type == "gemm":
+            self._prepare_marlin(v, u, dtype)
+            return
         self.V_int8, self.U_int8 = v.contiguous(), u.contiguous()
         for name in ("V", "U", "V_packed", "U_packed"):
             if name in self._parameters or name in self._buffers:
@@ -164,12 +169,31 @@ class NanoQuantLinear(nn.Module):
         if kernel_type == "gemv":
             self.kernel_forward = get_kernel_function("nanoquant", dtype, kernel_type="dynamic")
             self.kernel_kwargs = dict(REFERENCE_GEMV_KWARGS)
-        elif kernel_type == "gemm":
-            self.kernel_forward = torch.ops.nq_b200.gemm
-            self.kernel_kwargs = {}
         else:
             self.kernel_forward = torch.ops.nq_b200.linear
             self.kernel_kwargs = {}
+
+    def _prepare_marlin(self, v_planes: torch.Tensor, u_planes: torch.Tensor, dtype: torch.dtype):
+        """The reference's gemm branch (linear.py:220-236): scales in ``dtype`` (scale_mid ones if
+        absent), marlin_nanoquant_packer(V.T, U.T, ...), the op marlin_nanoquant_forward."""
+        from .kernel_utils import marlin_nanoquant_packer
+        V = unpack_binary_gemv(v_planes, (self.rank, self.in_features), "half2")
+        U = unpack_binary_gemv(u_planes, (self.out_features, self.rank), "half2")
+        s_pre = self.scale_pre.detach().to(dtype).reshape(-1)
+        s_post = self.scale_post.detach().to(dtype).reshape(-1)
+        s_mid = (self.scale_mid.detach().to(dtype).reshape(-1) if self.scale_mid is not None
+                 else torch.ones(self.rank, device=s_pre.device, dtype=dtype))
+        (self.V_int8, self.U_int8, self.s1, self.s2, self.s3,
+         self.workspace) = marlin_nanoquant_packer(V.T, U.T, s_pre, s_mid, s_post)
+        for name in ("V", "U", "V_packed", "U_packed", "scale_pre", "scale_mid", "scale_post"):
+            if name in self._parameters or name in self._buffers or hasattr(self, name):
+                delattr(self, name)
+        self.scale_mid = None
+        self.dtype = dtype
+        self.kernel_type = "gemm"
+        self.do_kernel_inference = True
+        self.kernel_forward = getattr(torch.ops.binary_kernels, "marlin_nanoquant_forward")
+        self.kernel_kwargs = {}
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not getattr(self, "do_kernel_inference", False):
@@ -185,8 +209,11 @@ class NanoQuantLinear(nn.Module):
             x = x.contiguous()
         else:
             raise ValueError(f"Expected 2D or 3D input tensor, got {x.ndim}D")
-        y = self.kernel_forward(x, self.scale_pre, self.V_int8, self.scale_mid, self.U_int8, self.scale_post,
-                                **self.kernel_kwargs)
+        if self.kernel_type == "gemm":
+            y = self.kernel_forward(x, self.V_int8, self.U_int8, self.s1, self.s2, self.s3, self.workspace)
+        else:
+            y = self.kernel_forward(x, self.scale_pre, self.V_int8, self.scale_mid, self.U_int8, self.scale_post,
+                                    **self.kernel_kwargs)
         if self.bias is not None:
             y = y + self.bias.to(y.dtype)
         if original_shape is not None:

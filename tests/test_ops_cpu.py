@@ -35,6 +35,30 @@ def test_meta_shapes():
     assert p.shape == (5, 2) and p.dtype == torch.int32
 
 
+def test_marlin_meta_shapes_and_checks():
+    """The Marlin ops' Meta kernels: output shapes and the reference's argument checks
+    (gemm.cpp:37-56) without a GPU."""
+    x = torch.empty(7, 512, device="meta", dtype=torch.float16)
+    vb = torch.empty(32, 128, device="meta", dtype=torch.int32)   # in 512, padded rank 256
+    ub = torch.empty(16, 64, device="meta", dtype=torch.int32)    # rank 256, out 128
+    ws = torch.empty(64, device="meta", dtype=torch.int32)
+    y = torch.ops.binary_kernels.marlin_nanoquant_forward(x, vb, ub, None, None, None, ws)
+    assert y.shape == (7, 128) and y.dtype == torch.float16
+    y1 = torch.ops.binary_kernels.marlin_onebit_forward(x, vb, None, None, ws)
+    assert y1.shape == (7, 256)
+    with pytest.raises(RuntimeError, match="k dimension mismatch"):
+        torch.ops.binary_kernels.marlin_onebit_forward(x, ub, None, None, ws)
+    p = torch.ops.nq_b200.pack_marlin(torch.empty(128, 64, device="meta", dtype=torch.int8), False)
+    assert p.shape == (4, 64) and p.dtype == torch.int32
+
+
+def test_marlin_packer_aliases_match_reference_names():
+    from nanoquant_b200 import kernel_utils as ku
+    assert ku.marlin_onebit_packer is ku.pack_binary_marlin
+    assert ku.marlin_nanoquant_packer is ku.pack_binary_marlin_fused
+    assert ku.MARLIN_MIN_MAX_PAR == 32
+
+
 def test_get_kernel_function_resolves_reference_op():
     f = nq.get_kernel_function("nanoquant", torch.float16, "dynamic")
     assert f is torch.ops.binary_kernels.nanoquant_dyn_forward
