@@ -67,6 +67,8 @@ def parse():
                     help="--gemm: the reference-rounding mode (T rounded once to bf16) instead of precise")
     ap.add_argument("--chain", action="store_true",
                     help="decode through GEMV chains (one cooperative launch per block besides attention)")
+    ap.add_argument("--no-exchange", action="store_true",
+                    help="N > 1: per-block sums through NCCL instead of inside the GEMVs (the default exchange)")
     ap.add_argument("--peer-allreduce", action="store_true",
                     help="N > 1: sum the blocks' partial outputs through peer memory (nq_allreduce) instead of NCCL")
     return ap.parse_args()
@@ -230,7 +232,9 @@ def config_block(cfg, args, world):
             "parallelism": f"tp{world}", "ranks": dict(cfg.ranks),
             "decode_path": "gemv chain per block" if getattr(args, "chain", False) else
                            "grouped GEMV launches with fused RMSNorm / SwiGLU prologues",
-            "tp_allreduce": ("peer memory (nq_allreduce)" if getattr(args, "peer_allreduce", False) else "NCCL")
+            "tp_allreduce": ("peer memory (nq_allreduce)" if getattr(args, "peer_allreduce", False) else
+                             "NCCL" if getattr(args, "no_exchange", False) else
+                             "inside the GEMVs (push from o / down, pull in the next RMSNorm prologue)")
                             if world > 1 else None,
             "l2": "working set > L2 (weights + KV cache read per token)"}
 
@@ -353,9 +357,10 @@ def run_nq(args, world, rank, local):
     group = torch.distributed.group.WORLD if world > 1 else None
     max_seq = args.prompt + args.warmup + 2 * args.steps + 16
     dec = Decoder(cfg, max_seq=max_seq, batch=args.batch, tp_rank=rank, tp=world, group=group, seed=1234,
-                  dtype=torch.float16, device=dev, chain=args.chain, peer_allreduce=args.peer_allreduce)
+                  dtype=torch.float16, device=dev, chain=args.chain, peer_allreduce=args.peer_allreduce,
+                  tp_exchange=not args.no_exchange)
     g = torch.Generator().manual_seed(42)
-    prompt = torch.randint(0, cfg.vocab, (args.prompt,), generator=g)
+    prompt = torch.randint(0, cfg.vocab, (args.batch, args.prompt), generator=g)  # one random-id prompt per row
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()

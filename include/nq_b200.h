@@ -144,6 +144,40 @@ NQ_API int nq_gemv_group_ex(int dtype, const nq_gemv_input *input, int64_t batch
                             void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---------------------------------------------------------------------------------
+ * Tensor-parallel exchange fused into the decode GEMVs.  No reference counterpart: the reference
+ * is single-GPU.  The decoder's per-block sum of the row-parallel layers' partial outputs (o and
+ * down) runs inside the GEMVs themselves, over peer memory (one process per GPU, CUDA IPC):
+ *   NQ_TP_PUSH  (one layer) the output rows, rounded to dtype, are also stored into every rank's
+ *               receive buffer (NVLink stores), two values per 8-byte word together with the
+ *               exchange's epoch as a flag, so no fence or separate signal is needed;
+ *   NQ_TP_PULL  (x_mode NQ_CHAIN_X_RMSNORM) x is not read: the launch polls (bounded, 2 s) the
+ *               ranks' words until their flags show the epoch and uses x = dtype(sum over ranks, in
+ *               rank order, of their pushed rows), float32 accumulation -- the same bits on every rank.
+ * Every rank allocates a zeroed region with nq_tp_region_alloc (nq_tp_region_bytes; free it with
+ * nq_allreduce_region_free), exports it with nq_ipc_handle and maps the others with nq_ipc_open
+ * (include/nq_decoder.h); `regions` lists every rank's region as mapped in the calling process.
+ * Every rank must make the same sequence of calls, PUSH and PULL alternating (nq_tp_pull counts
+ * as a PULL); batch <= 8; the GEMV must run as its single cooperative launch; a timed-out wait
+ * records NQ_ERR_DEVICE_TIMEOUT in the region's status word (nq_workspace_status).
+ * ------------------------------------------------------------------------------- */
+#define NQ_TP_PULL 1
+#define NQ_TP_PUSH 2
+typedef struct {
+    void *regions[8];          /* every rank's region as mapped in this process (own at `rank`) */
+    int rank;
+    int world;                 /* <= 8 */
+    int64_t max_elems;         /* values per source buffer (>= batch * hidden), multiple of 8 */
+} nq_tp_exchange;
+NQ_API size_t nq_tp_region_bytes(int world, int64_t max_elems);
+NQ_API int nq_tp_region_alloc(int world, int64_t max_elems, void **region_out);
+NQ_API int nq_gemv_group_tp(int dtype, const nq_gemv_input *input, int64_t batch, int64_t in_features,
+                            int n_layers, const nq_gemv_layer *layers, int act,
+                            const nq_tp_exchange *tp, int tp_mode, void *workspace,
+                            size_t workspace_bytes, void *stream);
+/* A PULL on its own: out [n] = the summed vector (the final norm's input after the last layer). */
+NQ_API int nq_tp_pull(int dtype, const nq_tp_exchange *tp, int64_t n, void *out, void *stream);
+
+/* ---------------------------------------------------------------------------------
  * Allocation-free decode GEMV.  No counterpart in the reference: its kernels allocate their
  * intermediate with the torch caching allocator on every call (gemv_kernel.cu:345-346).
  * For callers that cannot allocate device memory -- a plugin or custom-op interface that

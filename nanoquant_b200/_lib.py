@@ -42,6 +42,12 @@ class GemvInput(ctypes.Structure):
                 ("norm_weight", ctypes.c_void_p), ("residual_out", ctypes.c_void_p)]
 
 
+class TpExchange(ctypes.Structure):
+    """nq_tp_exchange of include/nq_b200.h."""
+    _fields_ = [("regions", ctypes.c_void_p * 8), ("rank", ctypes.c_int), ("world", ctypes.c_int),
+                ("max_elems", ctypes.c_int64)]
+
+
 class ChainPhase(ctypes.Structure):
     """nq_chain_phase of include/nq_b200.h."""
     _fields_ = [("n_layers", ctypes.c_int), ("x_mode", ctypes.c_int), ("act", ctypes.c_int), ("eps", ctypes.c_float),
@@ -73,6 +79,11 @@ _SIGNATURES = {
                                   _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p,
                                   _c.c_void_p]),
     "nq_gemv_static_status": (_c.c_int, [_c.c_void_p, _c.POINTER(_c.c_int)]),
+    "nq_tp_region_bytes": (_c.c_size_t, [_c.c_int, _c.c_int64]),
+    "nq_tp_region_alloc": (_c.c_int, [_c.c_int, _c.c_int64, _c.POINTER(_c.c_void_p)]),
+    "nq_gemv_group_tp": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_void_p, _c.c_int,
+                                    _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_size_t, _c.c_void_p]),
+    "nq_tp_pull": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p]),
     "nq_gemv_group_ex": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_void_p, _c.c_int,
                                     _c.c_void_p, _c.c_size_t, _c.c_void_p]),
     "nq_gemv_chain_workspace_bytes": (_c.c_size_t, [_c.c_int, _c.c_int64, _c.c_int, _c.c_void_p]),

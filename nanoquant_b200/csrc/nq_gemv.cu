@@ -44,6 +44,79 @@ constexpr int kFoldMaxBatch = 2;         // batch rows for which stage 1 folds s
 
 enum Mode : int { kStage1 = 1, kStage2 = 2, kFused = 3 };
 
+// Tensor-parallel exchange fused into the GEMVs (nq_gemv_group_tp).  A PUSH launch (the
+// row-parallel o / down projection) stores its rounded output rows into every rank's receive
+// buffer over NVLink; the next PULL launch (q/k/v or gate/up, whose RMSNorm prologue needs the
+// summed vector) sums the ranks' buffers in rank order (float32, rounded once: the same bits on
+// every rank) in place of reading x.  The messages are a few kilobytes, so the protocol is built
+// for latency: every 8-byte store carries two values and the exchange's epoch as a flag
+// ({2 x 16-bit values, u32 epoch}, single-copy atomic), so the producer needs no fence and no
+// separate signal, and the consumer polls the words it sums until their flags show the epoch.
+// Region of each rank (mapped by every other rank over CUDA IPC), bytes:
+//   [Ctrl 256][push epochs kTpMaxCtas x u32][pull epochs kTpMaxCtas x u32][reserved]
+//   [data 2 parities x world x max_elems / 2 words of 8 B]
+// Epochs are per-CTA counters advanced by every launch of their kind (push / pull), so graph
+// replays stay in step on all ranks as long as every rank makes the same sequence of calls,
+// pushes and pulls alternating.  Receive buffers alternate by epoch parity: a rank runs at most one
+// exchange ahead of another (its next push needs its own pull, which needs every rank's push),
+// so a buffer is rewritten only after every rank has read it, and a flag equals the epoch only
+// once that exchange's word has landed.
+constexpr int kTpMaxWorld = 8;
+constexpr int kTpMaxCtas = 256;
+enum TpMode : int { kTpPull = NQ_TP_PULL, kTpPush = NQ_TP_PUSH };
+constexpr size_t kTpOffPush = sizeof(Ctrl);
+constexpr size_t kTpOffPull = kTpOffPush + 4 * kTpMaxCtas;
+constexpr size_t kTpOffFlags = kTpOffPull + 4 * kTpMaxCtas;
+constexpr size_t kTpOffData = kTpOffFlags + 4 * (size_t)kTpMaxWorld * kTpMaxCtas;
+static_assert(kTpOffData % 256 == 0, "exchange data starts 256-byte aligned");
+
+struct TpX {
+    unsigned char *region[kTpMaxWorld];  // every rank's region as mapped in this process
+    int rank, world, mode, gprod;        // gprod: CTAs of the PUSH launches (one flag each)
+    long long max_elems;                 // values per source buffer
+};
+
+// One receive buffer of rank `dst`: source `src`'s words for exchange e (max_elems / 2 words).
+__device__ __forceinline__ uint2 *tp_words(const TpX &tp, int dst, unsigned e, int src) {
+    const size_t plane = (size_t)tp.max_elems * 4;
+    return reinterpret_cast<uint2 *>(tp.region[dst] + kTpOffData + ((size_t)(e & 1u) * tp.world + src) * plane);
+}
+__device__ __forceinline__ void tp_st_word(uint2 *p, uint32_t vals, unsigned e) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(vals), "r"(e) : "memory");
+}
+__device__ __forceinline__ uint4 tp_ld_words(const uint2 *p) {  // two 8-byte words
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
+// 8 values (4 words) of source src for exchange e, polled (bounded) until every word carries e.
+// Returns false (and records NQ_ERR_DEVICE_TIMEOUT) when the source did not come within the limit.
+__device__ __forceinline__ bool tp_read8(const TpX &tp, unsigned e, int src, int64_t word0, uint32_t (&v)[4],
+                                         int *status) {
+    const uint2 *w = tp_words(tp, tp.rank, e, src) + word0;
+    uint4 a = tp_ld_words(w), b = tp_ld_words(w + 2);
+    if (a.y != e || a.w != e || b.y != e || b.w != e) {
+        const uint64_t t0 = globaltimer_ns();
+        while (a.y != e || a.w != e || b.y != e || b.w != e) {
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+                record_status(status, NQ_ERR_DEVICE_TIMEOUT);
+                return false;
+            }
+            a = tp_ld_words(w);
+            b = tp_ld_words(w + 2);
+        }
+    }
+    v[0] = a.x;
+    v[1] = a.z;
+    v[2] = b.x;
+    v[3] = b.z;
+    return true;
+}
+
 // Phase timeline of the fused kernel, compiled only into debug builds (-DNQ_GEMV_TRACE):
 // thread 0 of every CTA keeps globaltimer stamps at the phase boundaries in registers and
 // stores them at the end into the launch's slot of g_trace (slot = launches seen so far,
@@ -544,7 +617,8 @@ __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uc
 // Stage 2, second half: reduce, scale by s1, round, and store y (optionally y = y + res).
 template <typename T>
 __device__ __forceinline__ void stage2_finish(const Params &p, const float *red, const T *s1s, int t2b, int t2e,
-                                              const void *res, int act, const WarpTab *wt) {
+                                              const void *res, int act, const WarpTab *wt, const TpX *push = nullptr,
+                                              unsigned push_e = 0, T *stage = nullptr) {
     using E = Elem<T>;
     const int tid = threadIdx.x;
     const int ntiles = t2e - t2b;
@@ -570,6 +644,23 @@ __device__ __forceinline__ void stage2_finish(const Params &p, const float *red,
                 out = E::rn(E::to_f(out) + E::to_f(*reinterpret_cast<const T *>(&rb)));
             }
             static_cast<T *>(mb.y)[o] = out;
+            if (push) stage[i] = out;  // staged for the flagged pair stores below
+        }
+    }
+    if (push) {  // every rank's receive buffer for this source: one flagged word per row pair
+        __syncthreads();
+        const int n = ntiles * 16 * p.batch;
+        for (int i = 2 * tid; i < n; i += 2 * kThreads) {
+            const int lt = i / (16 * p.batch), rem = i - lt * 16 * p.batch;
+            const int b = rem >> 4, row = rem & 15;  // row is even: pairs never straddle a tile
+            const int tile = t2b + lt;
+            const Member &mb = p.m[member_of2(p, tile)];
+            const int m = 16 * (tile - mb.t2_start) + row;
+            if (m >= mb.out_f) continue;
+            const uint32_t vals = (uint32_t)*reinterpret_cast<const uint16_t *>(&stage[i]) |
+                                  ((uint32_t)*reinterpret_cast<const uint16_t *>(&stage[i + 1]) << 16);
+            const int64_t word = ((int64_t)b * mb.out_f + m) >> 1;
+            for (int d = 0; d < push->world; ++d) tp_st_word(tp_words(*push, d, push_e, push->rank) + word, vals, push_e);
         }
     }
 }
@@ -644,11 +735,12 @@ __device__ __forceinline__ void x_transform(const Params &p, T *xs, const T *x2s
 // DECODE = true: the instantiation for fused launches with x staged and folded (batch <= 2,
 // the decode case) -- only that path is compiled, which keeps its code small enough for the
 // instruction cache; DECODE = false decides every variant at run time.
-template <typename T, bool DECODE>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
+template <typename T, bool DECODE, bool TP>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p, const TpX tp) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float sred[kWarps];
     __shared__ WarpTab wtab;
+    __shared__ unsigned s_tp_epoch;
     using E = Elem<T>;
     const bool x_in_smem = DECODE || p.x_in_smem;
     const bool fold = DECODE || p.fold;
@@ -819,6 +911,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
 
     pdl_wait();  // the previous kernel on the stream has completed; its outputs are visible
     NQ_STAMP(2);
+    if (TP && tp.mode && tid == 0) {  // this launch's exchange epoch (after pdl_wait: earlier launches are done)
+        unsigned *ep = reinterpret_cast<unsigned *>(tp.region[tp.rank] +
+                                                    ((tp.mode & kTpPush) ? kTpOffPush : kTpOffPull)) + c;
+        s_tp_epoch = *ep + 1u;
+        *ep = s_tp_epoch;
+    }
+    const bool pull = TP && (tp.mode & kTpPull) != 0;
 #ifdef NQ_GEMV_TRACE
     if (tid == 0) tr_slot = *reinterpret_cast<volatile unsigned int *>(&g_trace_launch);
 #endif
@@ -827,11 +926,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         if (tid == 32) {  // warp 1: x and the transform inputs
             uint32_t bytes = 0;
             // transform inputs: the host guarantees vec_rows and x in shared memory for them
-            if (vec_rows && x_in_smem) bytes += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
+            // (a PULL launch forms x from the ranks' receive buffers instead)
+            if (vec_rows && x_in_smem && !pull) bytes += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
             if (p.x2) bytes += (uint32_t)p.in_f * 2u * (uint32_t)p.batch;
             if (p.xmode == kChainNorm) bytes += (uint32_t)p.in_f * 2u;
             mbar_arrive_expect_tx(&bars[0], bytes);
-            if (vec_rows && x_in_smem) {
+            if (vec_rows && x_in_smem && !pull) {
                 if (DECODE || in_pad == p.in_f)  // DECODE: in_f is a multiple of 64 (no padding)
                     bulk_g2s_pieces(xs, p.x, (uint32_t)p.batch * (uint32_t)p.in_f * 2u, &bars[0]);
                 else
@@ -863,6 +963,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     // ------------------------------------------------------------------ stage 1
     if (has1) {
         ok = mbar_wait(&bars[0], 0, &p.ctrl->status);
+        if (pull) {  // x = sum over ranks (rank order) of their pushed partials, rounded once
+            __syncthreads();  // s_tp_epoch
+            const unsigned e = s_tp_epoch;
+            const int n8 = p.in_f / 8;
+            for (int i = tid; i < p.batch * n8; i += kThreads) {
+                const int b = i / n8, ch = i - b * n8;
+                float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                for (int src = 0; src < tp.world; ++src) {
+                    uint32_t w4[4];
+                    if (!tp_read8(tp, e, src, (int64_t)i * 4, w4, &p.ctrl->status)) ok = false;
+                    float v[8];
+                    unpack8<T>(make_uint4(w4[0], w4[1], w4[2], w4[3]), v);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) acc[q] += v[q];
+                }
+                T o[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) o[q] = E::rn(acc[q]);
+                reinterpret_cast<uint4 *>(xs + (size_t)b * in_pad)[ch] = *reinterpret_cast<const uint4 *>(o);
+            }
+            __syncthreads();
+        }
         NQ_STAMP(3);
         const int nxc = 2 * p.batch;  // folded B columns per member: hi / lo of x*s2 per batch row
         if (p.xmode != kChainPlain) {
@@ -921,7 +1043,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
             stage2_items<T, 2>(p, uch, red, t2b, t2e, ok, nullptr, &wtab);
         __syncthreads();
         NQ_STAMP(10);
-        stage2_finish<T>(p, red, s1s, t2b, t2e, nullptr, p.act, &wtab);
+        // a PUSH stages its rows in the x region (stage 1 is over; the host checked its size)
+        stage2_finish<T>(p, red, s1s, t2b, t2e, nullptr, p.act, &wtab, (TP && (tp.mode & kTpPush)) ? &tp : nullptr,
+                         s_tp_epoch, xs);
     }
     NQ_STAMP(11);
 #ifdef NQ_GEMV_TRACE
@@ -1050,15 +1174,19 @@ static int make_plan(int dev, const Params &base, Plan &plan) {
 }
 
 template <typename T>
-static int launch(const Plan &plan, cudaStream_t stream) {
+static int launch(const Plan &plan, cudaStream_t stream, const TpX &tp) {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
         const int cap = device_info(dev).max_smem_optin - kStaticSmemReserve;
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<T, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemv_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+            e = cudaFuncSetAttribute(gemv_kernel<T, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemv_kernel<T, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemv_kernel<T, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
         attr_set[dev] = true;
     }
@@ -1092,18 +1220,23 @@ static int launch(const Plan &plan, cudaStream_t stream) {
         cfg.numAttrs = na + 1;
         cfg.gridDim = dim3(plan.grid);
         cfg.dynamicSmemBytes = plan.smem;
-        cudaError_t e = decode ? cudaLaunchKernelEx(&cfg, gemv_kernel<T, true>, plan.prm)
-                               : cudaLaunchKernelEx(&cfg, gemv_kernel<T, false>, plan.prm);
+        // the exchange code is compiled only into the TP instantiations (single-GPU code stays small)
+        cudaError_t e = tp.mode ? (decode ? cudaLaunchKernelEx(&cfg, gemv_kernel<T, true, true>, plan.prm, tp)
+                                          : cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, true>, plan.prm, tp))
+                                : (decode ? cudaLaunchKernelEx(&cfg, gemv_kernel<T, true, false>, plan.prm, tp)
+                                          : cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, false>, plan.prm, tp));
         return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv fused launch");
     }
+    if (tp.mode) return fail(NQ_ERR_UNSUPPORTED, "the tensor-parallel exchange needs the single-launch GEMV");
+    const TpX none{};
     cfg.numAttrs = na;
     cfg.gridDim = dim3(plan.grid1);
     cfg.dynamicSmemBytes = plan.smem1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<T, false>, plan.prm1);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, false>, plan.prm1, none);
     if (e != cudaSuccess) return cuda_fail(e, "gemv stage-1 launch");
     cfg.gridDim = dim3(plan.grid2);
     cfg.dynamicSmemBytes = plan.smem2;
-    e = cudaLaunchKernelEx(&cfg, gemv_kernel<T, false>, plan.prm2);
+    e = cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, false>, plan.prm2, none);
     return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv stage-2 launch");
 }
 
@@ -1120,7 +1253,9 @@ struct GroupInput {
 };
 
 static int group_impl(int dtype, const GroupInput &in, int64_t batch, int64_t in_features, int n,
-                      const nq_gemv_layer *layers, void *workspace, size_t workspace_bytes, void *stream) {
+                      const nq_gemv_layer *layers, void *workspace, size_t workspace_bytes, void *stream,
+                      const TpX *tpx = nullptr) {
+    const TpX tp = tpx ? *tpx : TpX{};
     const void *x = in.x;
     if (n >= 1 && n <= kMaxGroup) {
         if (in.act & ~((1 << n) - 1)) return fail(NQ_ERR_INVALID_ARGUMENT, "act bit beyond the %d layers", n);
@@ -1231,7 +1366,20 @@ static int group_impl(int dtype, const GroupInput &in, int64_t batch, int64_t in
         Plan plan;
         int st = make_plan(dev, p, plan);
         if (st) return st;
-        st = (dtype == NQ_DTYPE_F16) ? launch<__half>(plan, s) : launch<__nv_bfloat16>(plan, s);
+        if (tp.mode) {
+            if (batch > kMaxBatch) return fail(NQ_ERR_UNSUPPORTED, "the exchange supports batch <= %d", kMaxBatch);
+            if (plan.mode != kFused || plan.grid != tp.gprod || ((tp.mode & kTpPull) && !plan.prm.x_in_smem))
+                return fail(NQ_ERR_UNSUPPORTED, "the exchange needs the single-launch GEMV on %d CTAs", tp.gprod);
+            if ((tp.mode & kTpPull) && (p.in_f % 8 || (long long)p.batch * p.in_f > tp.max_elems))
+                return fail(NQ_ERR_UNSUPPORTED, "pull: batch * in_features must fit the exchange buffers");
+            if ((tp.mode & kTpPush) && (n != 1 || (long long)p.batch * p.m[0].out_f > tp.max_elems ||
+                                         p.m[0].out_f % 8 != 0))
+                return fail(NQ_ERR_UNSUPPORTED, "push: one layer, out_features % 8 == 0, batch * out within the buffers");
+            if ((tp.mode & kTpPush) &&
+                (!plan.prm.x_in_smem || (size_t)plan.prm.kb1 * 64 < (size_t)16 * ((p.tiles2 + plan.grid - 1) / plan.grid)))
+                return fail(NQ_ERR_UNSUPPORTED, "push: the rows of a CTA must fit its staged-x region");
+        }
+        st = (dtype == NQ_DTYPE_F16) ? launch<__half>(plan, s, tp) : launch<__nv_bfloat16>(plan, s, tp);
         if (st) return st;
     }
     return NQ_OK;
@@ -1748,10 +1896,129 @@ static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *pha
     return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv chain launch");
 }
 
+// Standalone PULL (the final norm after the last row-parallel layer): one CTA sums the ranks'
+// buffers into `out` and advances every GEMV CTA's pull epoch, keeping them in step.
+template <typename T>
+__global__ void __launch_bounds__(512) tp_pull_kernel(const TpX tp, int64_t n, T *out) {
+    __shared__ unsigned se;
+    Ctrl *ctrl = reinterpret_cast<Ctrl *>(tp.region[tp.rank]);
+    if ((int)threadIdx.x < tp.gprod) {
+        unsigned *ep = reinterpret_cast<unsigned *>(tp.region[tp.rank] + kTpOffPull) + threadIdx.x;
+        const unsigned v = *ep + 1u;
+        *ep = v;
+        if (threadIdx.x == 0) se = v;
+    }
+    __syncthreads();
+    const unsigned e = se;
+    for (int64_t i = threadIdx.x; i < n / 8; i += blockDim.x) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int src = 0; src < tp.world; ++src) {
+            uint32_t w4[4];
+            tp_read8(tp, e, src, i * 4, w4, &ctrl->status);
+            float v[8];
+            unpack8<T>(make_uint4(w4[0], w4[1], w4[2], w4[3]), v);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc[q] += v[q];
+        }
+        T o[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) o[q] = Elem<T>::rn(acc[q]);
+        reinterpret_cast<uint4 *>(out)[i] = *reinterpret_cast<const uint4 *>(o);
+    }
+}
+
+static int make_tpx(const nq_tp_exchange *x, int mode, TpX &tp) {
+    if (!x) return fail(NQ_ERR_INVALID_ARGUMENT, "null exchange descriptor");
+    if (x->world < 1 || x->world > kTpMaxWorld || x->rank < 0 || x->rank >= x->world)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "exchange: rank %d of world %d (at most %d)", x->rank, x->world, kTpMaxWorld);
+    if (x->max_elems <= 0 || x->max_elems % 8)
+        return fail(NQ_ERR_INVALID_ARGUMENT, "exchange: max_elems must be a positive multiple of 8");
+    tp = TpX{};
+    for (int r = 0; r < x->world; ++r) {
+        if (!x->regions[r] || (reinterpret_cast<uintptr_t>(x->regions[r]) & 255))
+            return fail(NQ_ERR_INVALID_ARGUMENT, "exchange: region %d missing or not 256-byte aligned", r);
+        tp.region[r] = static_cast<unsigned char *>(x->regions[r]);
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    tp.rank = x->rank;
+    tp.world = x->world;
+    tp.mode = mode;
+    tp.gprod = device_info(dev).sms;  // the single-launch GEMV runs one CTA per SM
+    tp.max_elems = x->max_elems;
+    if (tp.gprod > kTpMaxCtas) return fail(NQ_ERR_UNSUPPORTED, "exchange: more than %d SMs", kTpMaxCtas);
+    return NQ_OK;
+}
+
 }  // namespace gemv
 }  // namespace nq
 
 extern "C" {
+
+size_t nq_tp_region_bytes(int world, int64_t max_elems) {
+    if (world < 1 || world > nq::gemv::kTpMaxWorld || max_elems <= 0) return 0;
+    return nq::gemv::kTpOffData + 2 * (size_t)world * (size_t)max_elems * 4;  // 8-byte words per value pair
+}
+
+int nq_tp_region_alloc(int world, int64_t max_elems, void **region_out) {
+    const size_t bytes = nq_tp_region_bytes(world, max_elems);
+    if (!bytes || !region_out)
+        return nq::fail(NQ_ERR_INVALID_ARGUMENT, "exchange region: world %d, max_elems %lld", world, (long long)max_elems);
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);  // its own allocation: an IPC handle maps whole allocations
+    if (e != cudaSuccess) return nq::cuda_fail(e, "cudaMalloc(exchange region)");
+    e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return nq::cuda_fail(e, "cudaMemset(exchange region)");
+    }
+    *region_out = p;
+    return NQ_OK;
+}
+
+int nq_gemv_group_tp(int dtype, const nq_gemv_input *input, int64_t batch, int64_t in_features, int n_layers,
+                     const nq_gemv_layer *layers, int act, const nq_tp_exchange *tp, int tp_mode, void *workspace,
+                     size_t workspace_bytes, void *stream) {
+    using namespace nq::gemv;
+    if (!input) return nq::fail(NQ_ERR_INVALID_ARGUMENT, "null input descriptor");
+    if (tp_mode & ~(kTpPull | kTpPush)) return nq::fail(NQ_ERR_INVALID_ARGUMENT, "unknown exchange mode %d", tp_mode);
+    if ((tp_mode & kTpPull) && input->x_mode != NQ_CHAIN_X_RMSNORM)
+        return nq::fail(NQ_ERR_UNSUPPORTED, "a PULL launch forms its input with RMSNORM");
+    TpX tpx{};
+    if (tp_mode) {
+        const int st = make_tpx(tp, tp_mode, tpx);
+        if (st) return st;
+    }
+    GroupInput in;
+    in.x = input->x;
+    in.xmode = input->x_mode;
+    in.x2 = input->x2;
+    in.nw = input->norm_weight;
+    in.res_out = input->residual_out;
+    in.eps = input->eps;
+    in.act = act;
+    return group_impl(dtype, in, batch, in_features, n_layers, layers, workspace, workspace_bytes, stream,
+                      tp_mode ? &tpx : nullptr);
+}
+
+int nq_tp_pull(int dtype, const nq_tp_exchange *tp, int64_t n, void *out, void *stream) {
+    using namespace nq::gemv;
+    if (dtype != NQ_DTYPE_F16 && dtype != NQ_DTYPE_BF16) return nq::fail(NQ_ERR_UNSUPPORTED, "exchange dtype");
+    TpX tpx{};
+    int st = make_tpx(tp, kTpPull, tpx);
+    if (st) return st;
+    if (!out || n <= 0 || n % 8 || n > tpx.max_elems || (reinterpret_cast<uintptr_t>(out) & 15))
+        return nq::fail(NQ_ERR_INVALID_ARGUMENT, "pull: n must be a multiple of 8 <= max_elems, out 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == NQ_DTYPE_F16)
+        tp_pull_kernel<__half><<<1, 512, 0, s>>>(tpx, n, static_cast<__half *>(out));
+    else
+        tp_pull_kernel<__nv_bfloat16><<<1, 512, 0, s>>>(tpx, n, static_cast<__nv_bfloat16 *>(out));
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? NQ_OK : nq::cuda_fail(e, "exchange pull launch");
+}
 
 size_t nq_gemv_chain_workspace_bytes(int dtype, int64_t batch, int n_phases, const nq_chain_phase *phases) {
     size_t need = 0;

@@ -597,7 +597,8 @@ std::vector<at::Tensor> run_group(const at::Tensor &x, const std::vector<LayerAr
 // SiLU on chosen outputs: one launch for what the decoder otherwise runs as 2-3.
 std::vector<at::Tensor> run_group_ex(const at::Tensor &x, const std::vector<LayerArgs> &ls, int64_t x_mode,
                                      const std::optional<at::Tensor> &x2, const std::optional<at::Tensor> &nw,
-                                     double eps, const std::optional<at::Tensor> &res_out, int64_t act) {
+                                     double eps, const std::optional<at::Tensor> &res_out, int64_t act,
+                                     const nq_tp_exchange *tp = nullptr, int tp_mode = 0) {
     c10::cuda::CUDAGuard guard(x.device());
     const auto st = x.scalar_type();
     nq_gemv_input in{};
@@ -637,9 +638,23 @@ std::vector<at::Tensor> run_group_ex(const at::Tensor &x, const std::vector<Laye
     }
     const size_t wsb = nq_gemv_group_workspace_bytes((int)ls.size(), ranks.data());
     at::Tensor ws = workspace_for(x, wsb);
-    NQ_TORCH_CHECK(nq_gemv_group_ex(dtype_code(st), &in, ls[0].rows, ls[0].in_f, (int)ls.size(), desc.data(),
-                                    (int)act, ws.data_ptr(), (size_t)ws.numel(), cur_stream(x)));
+    if (tp_mode)
+        NQ_TORCH_CHECK(nq_gemv_group_tp(dtype_code(st), &in, ls[0].rows, ls[0].in_f, (int)ls.size(), desc.data(),
+                                        (int)act, tp, tp_mode, ws.data_ptr(), (size_t)ws.numel(), cur_stream(x)));
+    else
+        NQ_TORCH_CHECK(nq_gemv_group_ex(dtype_code(st), &in, ls[0].rows, ls[0].in_f, (int)ls.size(), desc.data(),
+                                        (int)act, ws.data_ptr(), (size_t)ws.numel(), cur_stream(x)));
     return ys;
+}
+
+nq_tp_exchange make_exchange(at::IntArrayRef regions, int64_t rank, int64_t max_elems) {
+    TORCH_CHECK(regions.size() >= 1 && regions.size() <= 8, "1..8 exchange regions");
+    nq_tp_exchange x{};
+    for (size_t r = 0; r < regions.size(); ++r) x.regions[r] = reinterpret_cast<void *>(regions[r]);
+    x.rank = (int)rank;
+    x.world = (int)regions.size();
+    x.max_elems = max_elems;
+    return x;
 }
 
 std::vector<LayerArgs> check_group(const at::Tensor &x, const std::vector<at::Tensor> &s2,
@@ -664,6 +679,31 @@ std::vector<at::Tensor> gemv_group_cuda(const at::Tensor &x, at::TensorList s2, 
     if (x.dim() == 1)
         for (auto &y : ys) y = y.squeeze(0);
     return ys;
+}
+
+std::vector<at::Tensor> gemv_group_tp_cuda(const at::Tensor &x, const std::optional<at::Tensor> &x2,
+                                           const std::optional<at::Tensor> &norm_weight, double eps, int64_t x_mode,
+                                           const std::optional<at::Tensor> &residual_out, int64_t act,
+                                           at::TensorList s2, at::TensorList vbits,
+                                           const c10::List<std::optional<at::Tensor>> &smid, at::TensorList ubits,
+                                           at::TensorList s1, at::IntArrayRef regions, int64_t rank,
+                                           int64_t max_elems, int64_t tp_mode) {
+    std::vector<std::optional<at::Tensor>> sm(smid.begin(), smid.end());
+    auto ls = check_group(x, s2.vec(), vbits.vec(), sm, ubits.vec(), s1.vec());
+    const nq_tp_exchange ex = make_exchange(regions, rank, max_elems);
+    auto ys = run_group_ex(x, ls, x_mode, x2, norm_weight, eps, residual_out, act, &ex, (int)tp_mode);
+    if (x.dim() == 1)
+        for (auto &y : ys) y = y.squeeze(0);
+    return ys;
+}
+
+at::Tensor tp_pull_cuda(const at::Tensor &like, at::IntArrayRef regions, int64_t rank, int64_t max_elems) {
+    CHECK_CUDA_CONT(like, like.scalar_type());
+    c10::cuda::CUDAGuard guard(like.device());
+    auto out = at::empty_like(like);
+    const nq_tp_exchange ex = make_exchange(regions, rank, max_elems);
+    NQ_TORCH_CHECK(nq_tp_pull(dtype_code(like.scalar_type()), &ex, like.numel(), out.data_ptr(), cur_stream(like)));
+    return out;
 }
 
 std::vector<at::Tensor> gemv_group_ex_cuda(const at::Tensor &x, const std::optional<at::Tensor> &x2,
@@ -784,6 +824,11 @@ TORCH_LIBRARY(nq_b200, m) {
         "gemv_group_ex(Tensor x, Tensor? x2, Tensor? norm_weight, float eps, int x_mode, Tensor(a!)? residual_out, "
         "int act, Tensor[] scale_pre, Tensor[] v_bits, Tensor?[] scale_mid, Tensor[] u_bits, Tensor[] scale_post) "
         "-> Tensor[]");
+    m.def(
+        "gemv_group_tp(Tensor x, Tensor? x2, Tensor? norm_weight, float eps, int x_mode, Tensor(a!)? residual_out, "
+        "int act, Tensor[] scale_pre, Tensor[] v_bits, Tensor?[] scale_mid, Tensor[] u_bits, Tensor[] scale_post, "
+        "int[] regions, int rank, int max_elems, int tp_mode) -> Tensor[]");
+    m.def("tp_pull(Tensor like, int[] regions, int rank, int max_elems) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
@@ -803,6 +848,8 @@ TORCH_LIBRARY_IMPL(nq_b200, CUDA, m) {
     m.impl("silu_mul", &silu_mul_cuda);
     m.impl("gemv_group", &gemv_group_cuda);
     m.impl("gemv_group_ex", &gemv_group_ex_cuda);
+    m.impl("gemv_group_tp", &gemv_group_tp_cuda);
+    m.impl("tp_pull", &tp_pull_cuda);
     m.impl("linear_group", &linear_group_cuda);
 }
 

@@ -113,6 +113,59 @@ def _make_layer(cfg: DecoderConfig, proj: str, layer: int, seed: int, tp_rank: i
     return QuantLinearShard(vb[:, c0 // 32:c1 // 32].contiguous(), ub, s2[c0:c1].contiguous(), smid, s1)
 
 
+def _map_peer_regions(lib, region: int, group, rank: int, world: int):
+    """Exchange CUDA IPC handles of every rank's region (all_gather over `group`) and map the
+    others' here: returns (every rank's region as mapped in this process, the ones opened)."""
+    import ctypes
+    handle = (ctypes.c_char * 64)()
+    _lib.check(lib.nq_ipc_handle(region, handle))
+    handles = [None] * world
+    torch.distributed.all_gather_object(handles, bytes(handle), group=group)
+    ptrs, opened = [], []
+    for r in range(world):
+        if r == rank:
+            ptrs.append(region)
+            continue
+        peer = ctypes.c_void_p()
+        _lib.check(lib.nq_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(peer)))
+        ptrs.append(peer.value)
+        opened.append(peer.value)
+    return ptrs, opened
+
+
+class TPExchange:
+    """The tensor-parallel sum fused into the decode GEMVs (nq_gemv_group_tp, include/nq_b200.h):
+    the row-parallel o / down GEMVs PUSH their rounded output rows into every rank's receive buffer
+    over NVLink, and the next GEMV's RMSNorm prologue PULLs (waits for every rank, sums in rank
+    order).  One region per rank, mapped by every other rank over CUDA IPC here, once."""
+
+    PULL, PUSH = 1, 2
+
+    def __init__(self, group, rank: int, world: int, max_elems: int, device):
+        import ctypes
+        self.lib, self.rank, self.world = _lib.cuda_lib(), rank, world
+        self.max_elems = (max_elems + 7) // 8 * 8
+        with torch.cuda.device(device):
+            region = ctypes.c_void_p()
+            _lib.check(self.lib.nq_tp_region_alloc(world, self.max_elems, ctypes.byref(region)))
+            self.region = region.value
+            self.regions, self.opened = _map_peer_regions(self.lib, self.region, group, rank, world)
+            torch.distributed.barrier(group=group)  # every region zeroed and mapped before any call
+
+    def args(self, mode: int):
+        return self.regions, self.rank, self.max_elems, mode
+
+    def status(self) -> int:
+        """The region's status word (NQ_OK, or NQ_ERR_DEVICE_TIMEOUT if a wait for another rank gave
+        up); synchronises the current stream."""
+        import ctypes
+        st = ctypes.c_int(-1)
+        n = self.lib.nq_tp_region_bytes(self.world, self.max_elems)
+        _lib.check(self.lib.nq_workspace_status(self.region, n, torch.cuda.current_stream().cuda_stream,
+                                                ctypes.byref(st)))
+        return st.value
+
+
 class PeerAllReduce:
     """Sum of a small tensor over the tensor-parallel ranks of one node through peer memory
     (nq_allreduce): every rank maps every other rank's region over CUDA IPC once, here; a call
@@ -128,19 +181,7 @@ class PeerAllReduce:
             region = ctypes.c_void_p()
             _lib.check(self.lib.nq_allreduce_region_alloc(world, max_elems, ctypes.byref(region)))
             self.region = region.value
-            handle = (ctypes.c_char * 64)()
-            _lib.check(self.lib.nq_ipc_handle(self.region, handle))
-            handles = [None] * world
-            torch.distributed.all_gather_object(handles, bytes(handle), group=group)
-            ptrs, self.opened = [], []
-            for r in range(world):
-                if r == rank:
-                    ptrs.append(self.region)
-                    continue
-                peer = ctypes.c_void_p()
-                _lib.check(self.lib.nq_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(peer)))
-                ptrs.append(peer.value)
-                self.opened.append(peer.value)
+            ptrs, self.opened = _map_peer_regions(self.lib, self.region, group, rank, world)
             self.ptrs = (ctypes.c_void_p * world)(*ptrs)
             torch.distributed.barrier(group=group)  # every region zeroed and mapped before any call
 
@@ -169,7 +210,7 @@ class Decoder:
 
     def __init__(self, cfg: DecoderConfig, max_seq: int, batch: int = 1, tp_rank: int = 0, tp: int = 1,
                  group=None, seed: int = 0, dtype=torch.float16, device=None, with_mid: bool = False,
-                 chain: bool = False, peer_allreduce: bool = False):
+                 chain: bool = False, peer_allreduce: bool = False, tp_exchange: bool = True):
         _lib.load_torch_ops()
         assert cfg.heads % tp == 0 and cfg.kv_heads % tp == 0 and cfg.ffn % tp == 0
         self.cfg, self.max_seq, self.batch, self.tp, self.tp_rank, self.group = cfg, max_seq, batch, tp, tp_rank, group
@@ -213,6 +254,11 @@ class Decoder:
         self.peer_ar = None
         if tp > 1 and peer_allreduce:
             self.peer_ar = PeerAllReduce(group, tp_rank, tp, 8 * cfg.hidden, dev)
+        # `tp_exchange` (the default for tp > 1): the decode step's per-block sums run inside the
+        # GEMVs (push from o / down, pull in the next RMSNorm prologue); NCCL stays for prefill
+        self.tpx = None
+        if tp > 1 and tp_exchange and not peer_allreduce and batch <= 8:
+            self.tpx = TPExchange(group, tp_rank, tp, batch * cfg.hidden, dev)
         self.chain_ws = None
         if chain and tp == 1:
             h = torch.empty(batch, cfg.hidden, device=dev, dtype=dtype)
@@ -255,30 +301,36 @@ class Decoder:
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
     def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
-        """Run the prompt (batch 1, [T] token ids) through the model, fill the caches and
-        return the first generated token (greedy).  Sets the decode state."""
-        assert self.batch == 1 and prompt.dim() == 1
-        cfg, T = self.cfg, prompt.numel()
+        """Run the prompt through the model, fill the caches and return the first generated token
+        of every batch row (greedy).  ``prompt``: token ids [T] (batch 1) or [batch, T] (every row
+        the same length).  All rows go through each projection as one GEMM of batch * T rows;
+        attention is causal per row.  Sets the decode state."""
+        if prompt.dim() == 1:
+            prompt = prompt[None]
+        B, T = prompt.shape
+        assert B == self.batch, f"prompt has {B} rows, the decoder was built for batch {self.batch}"
         assert T < self.max_seq
-        D = cfg.head_dim
-        pos = torch.arange(T, dtype=torch.int32, device=self.device)
-        bidx = torch.zeros(T, dtype=torch.int32, device=self.device)
-        h = F.embedding(prompt.to(self.device), self.embed)
+        cfg, D = self.cfg, self.cfg.head_dim
+        pos = torch.arange(T, dtype=torch.int32, device=self.device).repeat(B)
+        bidx = torch.arange(B, dtype=torch.int32, device=self.device).repeat_interleave(T)
+        h = F.embedding(prompt.reshape(-1).to(self.device), self.embed)
         residual = None
         for li, lay in enumerate(self.layers):
             x, residual = torch.ops.nq_b200.rmsnorm(h, residual, lay["in_norm"], cfg.rms_eps)
             q, k, v = lay["qkv"](x)
-            q, k, v = q.view(T, self.hq, D), k.view(T, self.hkv, D), v.view(T, self.hkv, D)
+            q, k, v = q.view(B * T, self.hq, D), k.view(B * T, self.hkv, D), v.view(B * T, self.hkv, D)
             torch.ops.nq_b200.rope_cache(q, k, v, pos, bidx, self.k_cache[li], self.v_cache[li], cfg.rope_theta)
-            a = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0),
-                                               v.transpose(0, 1).unsqueeze(0), is_causal=True,
+            a = F.scaled_dot_product_attention(q.view(B, T, self.hq, D).transpose(1, 2),
+                                               k.view(B, T, self.hkv, D).transpose(1, 2),
+                                               v.view(B, T, self.hkv, D).transpose(1, 2), is_causal=True,
                                                enable_gqa=self.hq != self.hkv)
-            a = a.squeeze(0).transpose(0, 1).reshape(T, self.hq * D).contiguous()
+            a = a.transpose(1, 2).reshape(B * T, self.hq * D).contiguous()
             o = self._all_reduce(lay["o"](a))
             x, residual = torch.ops.nq_b200.rmsnorm(o, residual, lay["post_norm"], cfg.rms_eps)
             act = torch.ops.nq_b200.silu_mul(*lay["gate_up"](x))
             h = self._all_reduce(lay["down"](act))
-        x, _ = torch.ops.nq_b200.rmsnorm(h[-1:].contiguous(), residual[-1:].contiguous(), self.final_norm,
+        last = torch.arange(B, device=self.device) * T + (T - 1)
+        x, _ = torch.ops.nq_b200.rmsnorm(h[last].contiguous(), residual[last].contiguous(), self.final_norm,
                                          cfg.rms_eps)
         nxt = torch.argmax(x @ self.lm_head.t(), dim=-1)
         self.tokens.copy_(nxt)
@@ -332,6 +384,8 @@ class Decoder:
         SiLU on the gate in its epilogue, down with gate * up in its prologue."""
         cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
         ops, eps = torch.ops.nq_b200, cfg.rms_eps
+        if self.tpx is not None:
+            return self._step_logits_exchange()
         d = F.embedding(self.tokens, self.embed)  # the first block's input; no residual yet
         residual = None
         for li, lay in enumerate(self.layers):
@@ -358,11 +412,54 @@ class Decoder:
         return x @ self.lm_head.t()
 
     @torch.no_grad()
+    def _step_logits_exchange(self) -> torch.Tensor:
+        """The fused step with the tensor-parallel sums inside the GEMVs: o and down PUSH their
+        partial rows to every rank; the next q/k/v or gate/up launch PULLs (its RMSNorm prologue
+        sums the ranks' rows and adds the residual); a standalone pull feeds the final norm."""
+        cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
+        ops, eps, ex = torch.ops.nq_b200, cfg.rms_eps, self.tpx
+        d = F.embedding(self.tokens, self.embed)  # replicated on every rank: the first block does not pull
+        residual = None
+        for li, lay in enumerate(self.layers):
+            g = lay["qkv"]
+            res = torch.empty_like(d)
+            if li == 0:
+                q, k, v = ops.gemv_group_ex(d, residual, lay["in_norm"], eps, nqchain.RMSNORM, res, 0, g.s2, g.vb,
+                                            g.smid, g.ub, g.s1)
+            else:
+                q, k, v = ops.gemv_group_tp(d, residual, lay["in_norm"], eps, nqchain.RMSNORM, res, 0, g.s2, g.vb,
+                                            g.smid, g.ub, g.s1, *ex.args(ex.PULL))
+            residual = res
+            a = ops.decode_attention_rope(q.view(B, self.hq, D), k.view(B, self.hkv, D), v.view(B, self.hkv, D),
+                                          self.pos, self.k_cache[li], self.v_cache[li], cfg.rope_theta)
+            ol = lay["o"]
+            o = ops.gemv_group_tp(a.view(B, self.hq * D), None, None, 0.0, nqchain.PLAIN, None, 0, [ol.s2], [ol.vb],
+                                  [ol.smid], [ol.ub], [ol.s1], *ex.args(ex.PUSH))[0]
+            g = lay["gate_up"]
+            res = torch.empty_like(o)
+            gate, up = ops.gemv_group_tp(o, residual, lay["post_norm"], eps, nqchain.RMSNORM, res,
+                                         1 if self.fuse_down else 0, g.s2, g.vb, g.smid, g.ub, g.s1,
+                                         *ex.args(ex.PULL))
+            residual = res
+            dn = lay["down"]
+            if self.fuse_down:
+                d = ops.gemv_group_tp(gate, up, None, 0.0, nqchain.MUL, None, 0, [dn.s2], [dn.vb], [dn.smid],
+                                      [dn.ub], [dn.s1], *ex.args(ex.PUSH))[0]
+            else:
+                d = ops.gemv_group_tp(ops.silu_mul(gate, up), None, None, 0.0, nqchain.PLAIN, None, 0, [dn.s2],
+                                      [dn.vb], [dn.smid], [dn.ub], [dn.s1], *ex.args(ex.PUSH))[0]
+        d = ops.tp_pull(d, *ex.args(ex.PULL)[:3])
+        x, _ = ops.rmsnorm(d, residual, self.final_norm, eps)
+        return x @ self.lm_head.t()
+
+    @torch.no_grad()
     def own_launches_per_step(self) -> int:
         """Kernels of this package that one decode step launches (library kernels such as the
         lm_head GEMM, argmax and the embedding gather are not counted)."""
         n = self.cfg.layers
         ar = 2 * n if self.peer_ar is not None else 0  # peer all-reduces (o and down of every block)
+        if self.tpx is not None:  # sums inside the GEMVs; one standalone pull before the final norm
+            return n * (5 if self.fuse_down else 6) + 1 + 1
         if self.chain_ws is not None:
             return 1 + n * 2 + 1        # first q/k/v chain; attention + block chain per layer; final norm
         if self.fuse_neighbours and self.batch <= 8:

@@ -1,7 +1,9 @@
-"""Tensor-parallel decode on 2 GPUs (NCCL): the sharded model must produce the same greedy
-tokens and nearly the same logits as the unsharded one.  Skipped with fewer than 2 GPUs."""
+"""Tensor-parallel decode on 2 GPUs: the sharded model must produce the same greedy tokens and
+nearly the same logits as the unsharded one, with the per-block sums fused into the GEMVs (the
+default exchange), through NCCL, or through the standalone peer all-reduce.  Skipped with fewer
+than 2 GPUs."""
 import os
-import socket
+import tempfile
 
 import pytest
 import torch
@@ -15,24 +17,26 @@ CFG = DecoderConfig("tp-small", 1024, 512, 2, 4, 2, 128, 1024,
                     {"q": 160, "k": 96, "v": 96, "o": 160, "gate": 200, "up": 200, "down": 200})
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def _rendezvous():
+    """A fresh file for torch.distributed's file rendezvous (no TCP port that another process
+    could hold)."""
+    fd, path = tempfile.mkstemp(prefix="nq_tp_rdzv_")
+    os.close(fd)
+    os.unlink(path)
+    return "file://" + path
 
 
-def _run(rank, world, port, prompt, steps, q, peer=False):
+def _run(rank, world, rdzv, prompt, steps, q, mode="exchange"):
     import datetime
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
+    torch.distributed.init_process_group("nccl", init_method=rdzv, rank=rank, world_size=world,
                                          timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     try:
         dec = Decoder(CFG, max_seq=128, tp_rank=rank, tp=world, group=torch.distributed.group.WORLD, seed=3,
-                      peer_allreduce=peer,
+                      peer_allreduce=mode == "peer_allreduce", tp_exchange=mode == "exchange",
                       device=f"cuda:{rank}")
+        assert (dec.tpx is not None) == (mode == "exchange")
         first = int(dec.prefill(prompt.cuda())[0])
         logits = dec.step_logits().float().cpu()
         dec.tokens.fill_(int(torch.argmax(logits[0])))
@@ -41,17 +45,17 @@ def _run(rank, world, port, prompt, steps, q, peer=False):
         g = dec.capture(warmup=2)
         toks = [int(g.replay()[0]) for _ in range(steps)]
         g.release()
+        status = dec.tpx.status() if dec.tpx is not None else 0
         torch.distributed.barrier(device_ids=[rank])
-        if rank == 0:
-            q.put((first, logits, toks))
+        q.put((rank, first, logits, toks, status))
     finally:
         torch.distributed.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.timeout(600)
-@pytest.mark.parametrize("peer", [False, True], ids=["nccl", "peer_allreduce"])
-def test_tp2_matches_tp1(peer):
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("mode", ["exchange", "nccl", "peer_allreduce"])
+def test_tp2_matches_tp1(mode):
     prompt = torch.randint(0, CFG.vocab, (37,), generator=torch.Generator().manual_seed(9))
     ref = Decoder(CFG, max_seq=128, seed=3, device="cuda:0")
     first = int(ref.prefill(prompt.cuda())[0])
@@ -64,25 +68,29 @@ def test_tp2_matches_tp1(peer):
     torch.cuda.empty_cache()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_run, args=(r, 2, port, prompt, 6, q, peer)) for r in range(2)]
+    rdzv = _rendezvous()
+    procs = [ctx.Process(target=_run, args=(r, 2, rdzv, prompt, 6, q, mode)) for r in range(2)]
     for p in procs:
         p.start()
-    got_first, got_logits, got_toks = q.get(timeout=500)
+    outs = sorted([q.get(timeout=240) for _ in range(2)], key=lambda t: t[0])
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert got_first == first
-    rel = float((got_logits - logits).norm() / logits.norm())
-    assert rel < 2e-2, rel
-    assert got_toks == toks
+    for rank, got_first, got_logits, got_toks, status in outs:
+        assert got_first == first
+        rel = float((got_logits - logits).norm() / logits.norm())
+        assert rel < 2e-2, rel
+        assert got_toks == toks
+        assert status == 0, f"rank {rank}: device-side timeout in the exchange"
+    # the ranks' residual streams are bit-identical, so are their logits
+    assert torch.equal(outs[0][2], outs[1][2])
 
 
-def _ar_run(rank, world, port, q):
+def _ar_run(rank, world, rdzv, q):
     import datetime
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
+    torch.distributed.init_process_group("nccl", init_method=rdzv, rank=rank, world_size=world,
                                          timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     try:
         from nanoquant_b200.decoder import PeerAllReduce
@@ -119,18 +127,18 @@ def _ar_input(it: int, rank: int) -> torch.Tensor:
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.timeout(600)
+@pytest.mark.timeout(300)
 def test_peer_allreduce_two_gpus():
     """nq_allreduce over 2 GPUs: exactly the float32 rank-order sum rounded once, the same bits on
     both ranks, for eager calls and for replays of a captured launch, and no device timeout."""
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_ar_run, args=(r, world, port, q)) for r in range(world)]
+    rdzv = _rendezvous()
+    procs = [ctx.Process(target=_ar_run, args=(r, world, rdzv, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = [q.get(timeout=300) for _ in range(world)]
+    out = [q.get(timeout=240) for _ in range(world)]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
