@@ -100,8 +100,16 @@ def _make_layer(cfg: DecoderConfig, proj: str, layer: int, seed: int, tp_rank: i
     s2 = (torch.randn(in_f, generator=gen, device=device).abs() / math.sqrt(in_f)).to(dtype)
     s1 = (torch.randn(out_f, generator=gen, device=device).abs() / math.sqrt(r)).to(dtype)
     smid = (torch.randn(r, generator=gen, device=device).abs() + 0.5).to(dtype) if with_mid else None
+    return shard_layer(proj, vb, ub, s2, smid, s1, tp_rank, tp)
+
+
+def shard_layer(proj: str, vb, ub, s2, smid, s1, tp_rank: int, tp: int) -> QuantLinearShard:
+    """This rank's shard of a whole layer given as half2 planes and 1-D scales: column-parallel
+    projections (q/k/v/gate/up) keep the U rows of their outputs, row-parallel ones (o/down) the V
+    columns of their input slice (a multiple of 32 columns, whole words)."""
     if tp == 1:
         return QuantLinearShard(vb, ub, s2, smid, s1)
+    out_f, in_f = s1.numel(), s2.numel()
     if proj in ("q", "k", "v", "gate", "up"):  # column-parallel: U rows of this rank's outputs
         n = out_f // tp
         sl = slice(tp_rank * n, (tp_rank + 1) * n)
@@ -210,7 +218,12 @@ class Decoder:
 
     def __init__(self, cfg: DecoderConfig, max_seq: int, batch: int = 1, tp_rank: int = 0, tp: int = 1,
                  group=None, seed: int = 0, dtype=torch.float16, device=None, with_mid: bool = False,
-                 chain: bool = False, peer_allreduce: bool = False, tp_exchange: bool = True):
+                 chain: bool = False, peer_allreduce: bool = False, tp_exchange: bool = True,
+                 weights: Optional[dict] = None):
+        """``weights`` (from nanoquant_b200.loader) replaces the seeded random weights: "embed",
+        "lm_head", "final_norm" tensors and "layers", one dict per layer with "in_norm",
+        "post_norm" and, per projection, (V planes, U planes, scale_pre, scale_mid, scale_post) --
+        planes in half2 order, scales 1-D -- all on this rank's device, unsharded."""
         _lib.load_torch_ops()
         assert cfg.heads % tp == 0 and cfg.kv_heads % tp == 0 and cfg.ffn % tp == 0
         self.cfg, self.max_seq, self.batch, self.tp, self.tp_rank, self.group = cfg, max_seq, batch, tp, tp_rank, group
@@ -218,19 +231,34 @@ class Decoder:
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         dev = self.device
         self.hq, self.hkv = cfg.heads // tp, cfg.kv_heads // tp
-        gen = torch.Generator(device=dev)
-        gen.manual_seed(seed * 7919 + 1)
-        self.embed = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=dev) * 0.02).to(dtype)
-        self.lm_head = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=dev) * 0.02).to(dtype)
-        self.final_norm = torch.ones(cfg.hidden, device=dev, dtype=dtype)
         self.layers = []
-        for li in range(cfg.layers):
-            lay = {p: _make_layer(cfg, p, li, seed, tp_rank, tp, dtype, dev, with_mid) for p in PROJ}
+        if weights is not None:
+            cast = lambda t: None if t is None else t.to(device=dev, dtype=dtype).reshape(-1).contiguous()  # noqa: E731
+            self.embed = weights["embed"].to(device=dev, dtype=dtype).contiguous()
+            self.lm_head = weights["lm_head"].to(device=dev, dtype=dtype).contiguous()
+            self.final_norm = cast(weights["final_norm"])
+            for w in weights["layers"]:
+                lay = {}
+                for p in PROJ:
+                    vb, ub, s2, smid, s1 = w[p]
+                    lay[p] = shard_layer(p, vb.to(dev), ub.to(dev), cast(s2), cast(smid), cast(s1), tp_rank, tp)
+                lay["in_norm"] = cast(w["in_norm"])
+                lay["post_norm"] = cast(w["post_norm"])
+                self.layers.append(lay)
+        else:
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(seed * 7919 + 1)
+            self.embed = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=dev) * 0.02).to(dtype)
+            self.lm_head = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=dev) * 0.02).to(dtype)
+            self.final_norm = torch.ones(cfg.hidden, device=dev, dtype=dtype)
+            for li in range(cfg.layers):
+                lay = {p: _make_layer(cfg, p, li, seed, tp_rank, tp, dtype, dev, with_mid) for p in PROJ}
+                lay["in_norm"] = torch.ones(cfg.hidden, device=dev, dtype=dtype)
+                lay["post_norm"] = torch.ones(cfg.hidden, device=dev, dtype=dtype)
+                self.layers.append(lay)
+        for lay in self.layers:
             lay["qkv"] = QuantGroup(lay["q"], lay["k"], lay["v"])
             lay["gate_up"] = QuantGroup(lay["gate"], lay["up"])
-            lay["in_norm"] = torch.ones(cfg.hidden, device=dev, dtype=dtype)
-            lay["post_norm"] = torch.ones(cfg.hidden, device=dev, dtype=dtype)
-            self.layers.append(lay)
         self.k_cache = torch.zeros(cfg.layers, batch, self.hkv, max_seq, cfg.head_dim, device=dev, dtype=dtype)
         self.v_cache = torch.zeros_like(self.k_cache)
         # decode-step state, all on the device

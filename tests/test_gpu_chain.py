@@ -58,6 +58,12 @@ def test_single_plain_phase_matches_gemv_bitwise(shape, dt):
 @pytest.mark.parametrize("gate_act", [False, True])
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
 def test_decoder_block_chain_matches_separate_launches(dt, gate_act):
+    _block_chain(dt, gate_act)
+
+
+def _block_chain(dt, gate_act):
+    """Runs the o / MLP / next-q/k/v chain against the separate launches (asserting as it goes)
+    and returns the residual stream and the next block's q/k/v."""
     hid, ffn, ra, rm = 4096, 11008, 1126, 2054
     o = layer(hid, hid, ra, dt, 1)
     gate, up = layer(ffn, hid, rm, dt, 2), layer(ffn, hid, rm, dt, 3)
@@ -109,8 +115,8 @@ def test_decoder_block_chain_matches_separate_launches(dt, gate_act):
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
 def test_gate_silu_then_mul_equals_silu_mul_bitwise(dt):
     """act on the gate + MUL computes the same bits as SILU_MUL on the raw gate."""
-    h_a, qkv_a = test_decoder_block_chain_matches_separate_launches(dt, False)
-    h_b, qkv_b = test_decoder_block_chain_matches_separate_launches(dt, True)
+    h_a, qkv_a = _block_chain(dt, False)
+    h_b, qkv_b = _block_chain(dt, True)
     assert torch.equal(h_a, h_b)
     for a, b in zip(qkv_a, qkv_b):
         assert torch.equal(a, b)
