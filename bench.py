@@ -65,6 +65,10 @@ def parse():
                          "TFLOP/s counting the two rank-r contractions, 2*M*r*(in+out), over --copies weight copies")
     ap.add_argument("--fast-gemm", action="store_true",
                     help="--gemm: the reference-rounding mode (T rounded once to bf16) instead of precise")
+    ap.add_argument("--gemv-trace", action="store_true",
+                    help="phase timeline of every fused GEMV launch of one decode step (rank 0; needs the library "
+                         "built with NQ_NVCC_EXTRA=-DNQ_GEMV_TRACE): per launch kind, the median over the step's "
+                         "launches of the median and slowest CTA's time at each phase boundary")
     ap.add_argument("--chain", action="store_true",
                     help="decode through GEMV chains (one cooperative launch per block besides attention)")
     ap.add_argument("--no-exchange", action="store_true",
@@ -462,6 +466,76 @@ def run_nq(args, world, rank, local):
         torch.distributed.destroy_process_group()
 
 
+GEMV_PHASES = ["start", "copies issued", "pdl wait", "x landed", "x transformed", "x folded", "stage-1 MMA",
+               "stage-1 reduce", "grid barrier", "U landed", "stage-2 MMA", "end"]
+
+
+def run_gemv_trace(args, world, rank, local):
+    """One decode step's fused GEMV launches, phase by phase, from the debug build's globaltimer
+    stamps (nq_debug_gemv_trace).  Prints a table of microseconds from each launch's first CTA."""
+    import ctypes
+    import numpy as np
+    from nanoquant_b200 import _lib
+    from nanoquant_b200.decoder import CONFIGS, Decoder
+    lib = _lib.cuda_lib()
+    if not hasattr(lib, "nq_debug_gemv_trace"):
+        raise SystemExit("--gemv-trace needs the library built with NQ_NVCC_EXTRA=-DNQ_GEMV_TRACE")
+    fn = lib.nq_debug_gemv_trace
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+    cfg = CONFIGS[args.model]
+    dev = torch.device("cuda", local)
+    group = torch.distributed.group.WORLD if world > 1 else None
+    dec = Decoder(cfg, max_seq=args.prompt + 64, batch=args.batch, tp_rank=rank, tp=world, group=group, seed=1234,
+                  dtype=torch.float16, device=dev, tp_exchange=not args.no_exchange)
+    prompt = torch.randint(0, cfg.vocab, (args.batch, args.prompt), generator=torch.Generator().manual_seed(42))
+    dec.prefill(prompt.to(dev))
+    g = dec.capture(warmup=2)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    buf = np.zeros((512, 160, 12), dtype=np.uint64)
+    fn(buf.ctypes.data, 512, 1)
+    if world > 1:
+        torch.distributed.barrier(device_ids=[local])
+    g.replay()
+    torch.cuda.synchronize(dev)
+    n = fn(buf.ctypes.data, 512, 1)
+    if world > 1:
+        torch.distributed.barrier(device_ids=[local])
+    g.release()
+    if rank != 0:
+        return
+    G = torch.cuda.get_device_properties(dev).multi_processor_count
+    kinds = ["q/k/v", "o", "gate/up", "down"]
+    lines = [f"{cfg.name} tp{world} batch {args.batch}: {n} fused GEMV launches in one decode step; microseconds "
+             f"from the launch's first CTA start, median CTA / slowest CTA (median over the step's launches)",
+             "| phase | " + " | ".join(kinds) + " |", "|---" * (len(kinds) + 1) + "|"]
+    per = {k: [] for k in kinds}
+    for li in range(n):
+        st = buf[li, :G, :].astype(np.int64)
+        active = st[:, 11] > 0
+        rel = (st[active] - st[active, 0].min()) / 1000.0
+        rel[rel < 0] = np.nan  # a phase this CTA skips (no stage-1 tiles) has no stamp
+        per[kinds[li % 4]].append(rel)
+    cols = {}
+    for k in kinds:
+        arr = per[k]
+        med = np.median(np.stack([np.nanmedian(a, axis=0) for a in arr]), axis=0)
+        mx = np.median(np.stack([np.nanmax(a, axis=0) for a in arr]), axis=0)
+        cols[k] = (med, mx)
+    for i, ph in enumerate(GEMV_PHASES):
+        lines.append(f"| {ph} | " + " | ".join(f"{cols[k][0][i]:.2f} / {cols[k][1][i]:.2f}" for k in kinds) + " |")
+    starts = [buf[li, :G, 0].astype(np.int64).min() for li in range(n)]
+    ends = [buf[li, :G, 11].astype(np.int64).max() for li in range(n)]
+    gaps = [(starts[i + 1] - ends[i]) / 1000 for i in range(n - 1)]
+    for j, k in enumerate(kinds):
+        sel = [gaps[i] for i in range(len(gaps)) if i % 4 == j]
+        lines.append(f"gap from the end of a {k} launch to the next GEMV launch: median {np.median(sel):.2f} us")
+    lines.append(f"first GEMV start to last GEMV end: {(ends[-1] - starts[0]) / 1000:.1f} us")
+    print("\n".join(lines), flush=True)
+
+
 def run_layer(args):
     """One NanoQuant layer's fused decode GEMV (the per-layer measurement): --copies distinct
     seeded weight sets, more bytes than L2 holds, cycled so every launch reads its weights
@@ -620,6 +694,12 @@ def main():
         _JSON_FD = os.dup(1)
         os.dup2(2, 1)
     world, rank, local = dist_setup(args)
+    if args.gemv_trace:
+        _lib_load()
+        run_gemv_trace(args, world, rank, local)
+        if world > 1 and torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+        return
     if args.impl == "reference":
         run_reference(args, world, rank)
     else:

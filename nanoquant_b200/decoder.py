@@ -273,10 +273,15 @@ class Decoder:
         # RMSNorm / SiLU*up folded into the GEMV prologues and the gate's SiLU into its epilogue
         # (nq_gemv_group_ex); batches above 8 use the separate kernels.
         self.fuse_neighbours = True
+        # the fused prologues stage their inputs in shared memory: where the RMSNorm one has no plan
+        # (wide hidden sizes at large batches: Llama-3-70B at batch 8), the step uses separate
+        # RMSNorm / SiLU*up kernels and plain GEMVs (and NCCL for tensor-parallel sums)
+        if batch > 8 or not self._norm_prologue_fits():
+            self.fuse_neighbours = False
         # gate * up in the down GEMV's prologue needs both FFN vectors staged in shared memory;
         # for wide FFN shards (Llama-3-70B on one GPU) no plan fits, and the block uses the
         # SiLU*up kernel and a plain down GEMV instead
-        self.fuse_down = self._down_prologue_fits()
+        self.fuse_down = self.fuse_neighbours and self._down_prologue_fits()
         # tensor parallel: `peer_allreduce` sums the blocks' partial outputs through peer memory
         # (nq_allreduce) at decode sizes instead of torch.distributed / NCCL
         self.peer_ar = None
@@ -285,7 +290,7 @@ class Decoder:
         # `tp_exchange` (the default for tp > 1): the decode step's per-block sums run inside the
         # GEMVs (push from o / down, pull in the next RMSNorm prologue); NCCL stays for prefill
         self.tpx = None
-        if tp > 1 and tp_exchange and not peer_allreduce and batch <= 8:
+        if tp > 1 and tp_exchange and not peer_allreduce and batch <= 8 and self.fuse_neighbours:
             self.tpx = TPExchange(group, tp_rank, tp, batch * cfg.hidden, dev)
         self.chain_ws = None
         if chain and tp == 1:
@@ -297,6 +302,20 @@ class Decoder:
                 self.chain_ws = torch.zeros(n, dtype=torch.uint8, device=dev)
 
     # ------------------------------------------------------------------ pieces
+    def _norm_prologue_fits(self) -> bool:
+        """Whether the q/k/v launch with RMSNorm(x + residual) in its prologue has a plan."""
+        g = self.layers[0]["qkv"]
+        x = torch.zeros(self.batch, self.cfg.hidden, device=self.device, dtype=self.dtype)
+        try:
+            torch.ops.nq_b200.gemv_group_ex(x, x, self.layers[0]["in_norm"], 1e-5, nqchain.RMSNORM, None, 0, g.s2, g.vb,
+                                            g.smid, g.ub, g.s1)
+        except RuntimeError as e:
+            if "shared-memory budget" in str(e):
+                return False
+            raise
+        torch.cuda.synchronize(self.device)
+        return True
+
     def _down_prologue_fits(self) -> bool:
         dn = self.layers[0]["down"]
         g = torch.zeros(self.batch, dn.in_features, device=self.device, dtype=self.dtype)
