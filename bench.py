@@ -621,6 +621,123 @@ def run_gemm(args):
                       "clocks": clocks.summary(), "dtype": "bf16", "data": "synthetic"}), flush=True)
 
 
+def _ref_ops(what: str):
+    """The reference's own CUDA kernels (oracle/_ref, built from its sources), or None after
+    printing the reference arm's `unavailable` line."""
+    from oracle import ref_kernels as rk
+    if not rk.available():
+        emit({"impl": "reference", "unavailable": f"{what}: the reference kernels are not built "
+                                                  "(python oracle/build_ref.py needs the reference sources)"})
+        return None, rk
+    return rk.load(), rk
+
+
+def run_reference_layer(args):
+    """--impl reference --layer OUT,IN,RANK: the reference's own decode GEMV
+    (binary_kernels::nanoquant_dyn_forward, gemv_kernel.cu:308-429, with the reference module's
+    launch configuration) on this GPU, timed exactly like run_layer: --copies distinct random
+    weight sets cycled past L2, CUDA events, algorithmic bytes per launch."""
+    out_f, in_f, r = (int(v) for v in args.layer.split(","))
+    ops, rk = _ref_ops("--layer")
+    if ops is None:
+        return
+    if not rk.gemv_shape_ok(out_f, in_f, r):
+        emit({"impl": "reference", "unavailable": f"the reference GEMV reads and writes out of bounds at rank {r} / "
+                                                  f"in {in_f} / out {out_f} (needs multiples of 32 and 8)"})
+        return
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000)
+    # uniformly random words are uniformly random +-1 planes (no padding bits at these shapes)
+    words = lambda rows, cols: torch.randint(-2**31, 2**31 - 1, (rows, cols // 32), generator=gen,  # noqa: E731
+                                             device=dev, dtype=torch.int32)
+    layers = [(words(r, in_f), words(out_f, r), (torch.rand(in_f, generator=gen, device=dev) + 0.5).half(),
+               (torch.rand(out_f, generator=gen, device=dev) * 0.02).half()) for _ in range(args.copies)]
+    x = torch.randn(args.batch, in_f, device=dev).half()
+    alg = 4 * r * (in_f // 32) + 4 * out_f * (r // 32) + 2 * (in_f + out_f) + 2 * args.batch * (in_f + out_f)
+
+    def call(i):
+        vb, ub, s2, s1 = layers[i % args.copies]
+        return rk.gemv(ops, x, s2, vb, None, ub, s1)
+
+    for i in range(max(args.warmup, 3)):
+        call(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = args.steps * args.copies
+    with ClockSampler(0) as clocks:
+        e0.record()
+        for i in range(n):
+            call(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / n
+    peak, kind = peaks()
+    gbs = alg / (us * 1e-6) / 1e9
+    emit({"impl": "reference", "metric": "decode GEMV GB/s (algorithmic bytes)", "value": round(gbs, 2),
+          "unit": "GB/s", "kernel": "reference nanoquant_dyn_forward (two launches, fp16 accumulation)",
+          "layer": {"out": out_f, "in": in_f, "rank": r, "batch": args.batch}, "us_per_launch": round(us, 3),
+          "bytes_per_launch": alg, "copies": args.copies, "launches": n,
+          "roofline": {"bound": "hbm", "peak": peak, "frac": round(gbs / peak, 5), "peak_source": kind},
+          "clocks": clocks.summary(), "dtype": "f16", "data": "synthetic"})
+
+
+def run_reference_gemm(args):
+    """--impl reference --gemm M,OUT,IN,RANK: the reference's own prefill GEMM
+    (binary_kernels::marlin_nanoquant_forward, gemm.cpp:112-122: two Marlin launches) on this
+    GPU with the Marlin operands of the same layer (rank padded to a multiple of 256 as the
+    reference packer pads it), timed like run_gemm; TFLOP/s counts the unpadded rank's flops."""
+    m, out_f, in_f, r = (int(v) for v in args.gemm.split(","))
+    ops, rk = _ref_ops("--gemm")
+    if ops is None:
+        return
+    rp = (r + 255) // 256 * 256
+    dtype = torch.bfloat16  # the prefill config's activation type
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2000)
+    copies = max(2, min(args.copies, 8))
+    words = lambda k, n: torch.randint(-2**31, 2**31 - 1, (k // 16, n // 2), generator=gen, device=dev,  # noqa: E731
+                                       dtype=torch.int32)
+    layers = [(words(in_f, rp), words(rp, out_f), (torch.rand(in_f, generator=gen, device=dev) + 0.5).to(dtype),
+               torch.ones(rp, device=dev, dtype=dtype), (torch.rand(out_f, generator=gen, device=dev) * 0.02).to(dtype))
+              for _ in range(copies)]
+    ws = torch.zeros(max(rp // 128, out_f // 128) * 32, dtype=torch.int32, device=dev)
+    x = torch.randn(m, in_f, device=dev).to(dtype)
+
+    def call(i):
+        vw, uw, s1, s2, s3 = layers[i % copies]
+        return ops.marlin_nanoquant_forward(x, vw, uw, s1, s2, s3, ws)
+
+    try:
+        for i in range(max(args.warmup, 3)):
+            call(i)
+    except RuntimeError as err:  # the reference's own host-side shape checks (gemm.cpp:91-95)
+        emit({"impl": "reference", "unavailable": f"marlin_nanoquant_forward rejects M={m} {out_f}x{in_f} "
+                                                  f"r={r}: {str(err).splitlines()[0]}"})
+        return
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(args.steps, 1) * copies
+    with ClockSampler(0) as clocks:
+        e0.record()
+        for i in range(n):
+            call(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / n
+    flops = 2.0 * m * r * (in_f + out_f)
+    tflops = flops / (us * 1e-6) / 1e12
+    pk = _peak_tflops()
+    emit({"impl": "reference", "metric": "prefill GEMM TFLOP/s (two rank-r contractions)", "value": round(tflops, 2),
+          "unit": "TFLOP/s", "kernel": "reference marlin_nanoquant_forward (two Marlin launches, mma.sync)",
+          "layer": {"m": m, "out": out_f, "in": in_f, "rank": r, "rank_padded": rp},
+          "us_per_launch": round(us, 3), "flops_per_launch": flops, "copies": copies, "launches": n,
+          "roofline": {"bound": "tensor", "peak": pk[0], "frac": round(tflops / pk[0], 5), "peak_source": pk[1],
+                       "unit": "TFLOP/s"},
+          "clocks": clocks.summary(), "dtype": "bf16", "data": "synthetic"})
+
+
 def _peak_tflops():
     """Dense bf16 burst TFLOP/s of MEASURED_PEAKS.json, else the recipe's fallback (1590)."""
     try:
@@ -679,6 +796,10 @@ def _lib_load():
 def main():
     global _JSON_FD
     args = parse()
+    if args.impl == "reference" and (args.layer or args.gemm):
+        if int(os.environ.get("RANK", "0")) == 0:
+            run_reference_layer(args) if args.layer else run_reference_gemm(args)
+        return
     if args.layer:
         run_layer(args)
         return

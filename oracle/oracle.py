@@ -117,13 +117,23 @@ def marlin_positions(n_out: int, k_red: int):
 
 
 def pack_marlin(signs: np.ndarray) -> np.ndarray:
-    """int8 +-1 weight [n_out, k_red] -> int32 Marlin words [k_red / 16, n_out / 2]."""
+    """int8 +-1 weight [n_out, k_red] -> int32 Marlin words [k_red / 16, n_out / 2].
+
+    The 32 bits of word [tile_red, tile_out * 32 + o1 * 4 + r2] are the elements with
+    (o16, o8, r8, r1) running over 4 x 2 x 2 x 2 (marlin_positions), so the weight is viewed as
+    [tile_out, o16, o8, o1, tile_red, r8, r2, r1] and each word is a weighted sum over those axes."""
     n_out, k_red = signs.shape
-    row, col, bit = marlin_positions(n_out, k_red)
-    words = np.zeros((k_red // 16, n_out // 2), dtype=np.uint64)
-    vals = (signs < 0).astype(np.uint64) << bit.astype(np.uint64)
-    np.add.at(words, (row.ravel(), col.ravel()), vals.ravel())
-    return words.astype(np.uint32).view(np.int32)
+    if n_out % 64 or k_red % 16:
+        raise ValueError("the Marlin layout needs n_out % 64 == 0 and k_red % 16 == 0")
+    neg = (np.asarray(signs) < 0).astype(np.uint64).reshape(n_out // 64, 4, 2, 8, k_red // 16, 2, 4, 2)
+    o16 = np.arange(4).reshape(1, 4, 1, 1, 1, 1, 1, 1)
+    o8 = np.arange(2).reshape(1, 1, 2, 1, 1, 1, 1, 1)
+    r8 = np.arange(2).reshape(1, 1, 1, 1, 1, 2, 1, 1)
+    r1 = np.arange(2).reshape(1, 1, 1, 1, 1, 1, 1, 2)
+    weight = np.left_shift(np.uint64(1), (15 - (2 * o8 + r8) + 16 * r1 - 4 * o16).astype(np.uint64))
+    w = (neg * weight).sum(axis=(1, 2, 5, 7))              # [tile_out, o1, tile_red, r2]
+    w = w.transpose(2, 0, 1, 3).reshape(k_red // 16, n_out // 2)
+    return w.astype(np.uint32).view(np.int32)
 
 
 def unpack_marlin(words: np.ndarray, n_out: int, k_red: int) -> np.ndarray:

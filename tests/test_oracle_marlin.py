@@ -37,3 +37,13 @@ def test_marlin_fused_pack_matches_reference(key):
 def test_marlin_rejects_unaligned_shapes():
     with pytest.raises(ValueError):
         orc.pack_marlin(np.ones((32, 16), dtype=np.int8))
+
+
+def test_reference_kernels_refuse_a_process_with_this_package():
+    """The reference extension registers the same op namespace: it never loads beside this package."""
+    import nanoquant_b200  # noqa: F401
+    from oracle import ref_kernels as rk
+    if not rk._repo_libraries_mapped():
+        pytest.skip("this package's libraries are not mapped in this process")
+    with pytest.raises(RuntimeError, match="binary_kernels namespace"):
+        rk.load()
