@@ -683,59 +683,13 @@ def run_reference_layer(args):
 
 
 def run_reference_gemm(args):
-    """--impl reference --gemm M,OUT,IN,RANK: the reference's own prefill GEMM
-    (binary_kernels::marlin_nanoquant_forward, gemm.cpp:112-122: two Marlin launches) on this
-    GPU with the Marlin operands of the same layer (rank padded to a multiple of 256 as the
-    reference packer pads it), timed like run_gemm; TFLOP/s counts the unpadded rank's flops."""
-    m, out_f, in_f, r = (int(v) for v in args.gemm.split(","))
-    ops, rk = _ref_ops("--gemm")
-    if ops is None:
-        return
-    rp = (r + 255) // 256 * 256
-    dtype = torch.bfloat16  # the prefill config's activation type
-    dev = torch.device("cuda", 0)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(2000)
-    copies = max(2, min(args.copies, 8))
-    words = lambda k, n: torch.randint(-2**31, 2**31 - 1, (k // 16, n // 2), generator=gen, device=dev,  # noqa: E731
-                                       dtype=torch.int32)
-    layers = [(words(in_f, rp), words(rp, out_f), (torch.rand(in_f, generator=gen, device=dev) + 0.5).to(dtype),
-               torch.ones(rp, device=dev, dtype=dtype), (torch.rand(out_f, generator=gen, device=dev) * 0.02).to(dtype))
-              for _ in range(copies)]
-    ws = torch.zeros(max(rp // 128, out_f // 128) * 32, dtype=torch.int32, device=dev)
-    x = torch.randn(m, in_f, device=dev).to(dtype)
-
-    def call(i):
-        vw, uw, s1, s2, s3 = layers[i % copies]
-        return ops.marlin_nanoquant_forward(x, vw, uw, s1, s2, s3, ws)
-
-    try:
-        for i in range(max(args.warmup, 3)):
-            call(i)
-    except RuntimeError as err:  # the reference's own host-side shape checks (gemm.cpp:91-95)
-        emit({"impl": "reference", "unavailable": f"marlin_nanoquant_forward rejects M={m} {out_f}x{in_f} "
-                                                  f"r={r}: {str(err).splitlines()[0]}"})
-        return
-    torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n = max(args.steps, 1) * copies
-    with ClockSampler(0) as clocks:
-        e0.record()
-        for i in range(n):
-            call(i)
-        e1.record()
-        torch.cuda.synchronize(dev)
-    us = e0.elapsed_time(e1) * 1e3 / n
-    flops = 2.0 * m * r * (in_f + out_f)
-    tflops = flops / (us * 1e-6) / 1e12
-    pk = _peak_tflops()
-    emit({"impl": "reference", "metric": "prefill GEMM TFLOP/s (two rank-r contractions)", "value": round(tflops, 2),
-          "unit": "TFLOP/s", "kernel": "reference marlin_nanoquant_forward (two Marlin launches, mma.sync)",
-          "layer": {"m": m, "out": out_f, "in": in_f, "rank": r, "rank_padded": rp},
-          "us_per_launch": round(us, 3), "flops_per_launch": flops, "copies": copies, "launches": n,
-          "roofline": {"bound": "tensor", "peak": pk[0], "frac": round(tflops / pk[0], 5), "peak_source": pk[1],
-                       "unit": "TFLOP/s"},
-          "clocks": clocks.summary(), "dtype": "bf16", "data": "synthetic"})
+    """--impl reference --gemm: the reference's own prefill GEMM (marlin_nanoquant_forward,
+    gemm.cpp:112-122) is not run on this GPU.  Built for sm_100a from its sources it stopped with
+    "an illegal instruction was encountered" on a B200, on shapes its host checks accept
+    (M = 128 / 2048 at 4096x4096 r1088 and 4096x11008 r1600, bf16), so this arm reports it as
+    unavailable instead of running it again."""
+    emit({"impl": "reference", "unavailable": "the reference Marlin GEMM (marlin_nanoquant_forward) built for "
+                                              "sm_100a faults on B200 with an illegal instruction; not run"})
 
 
 def _peak_tflops():

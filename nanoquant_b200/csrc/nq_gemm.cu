@@ -21,6 +21,8 @@
 // Stages rotate through a 4-deep shared-memory ring guarded by mbarriers; every wait is
 // bounded (globaltimer) and an abort flag stops the pipeline if one gives up.  No TMA
 // multicast is used.
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <type_traits>
 
@@ -44,6 +46,13 @@ struct Params {
     void *out_lo;          // stage 1 precise: T_lo bf16 [M, ldo]
     int ldo;
     int *status;
+    // split-K (small M, too few output tiles to fill the GPU): CTA z of the grid's third
+    // dimension runs K steps [z * kbs, min((z + 1) * kbs, nk)) and, when `partial` is set,
+    // stores its raw float32 accumulator tile in partial[z][M][ldp]; splitk_finalize sums the
+    // slots in order and applies the column scale and the output format.
+    int kbs;
+    float *partial;
+    int ldp;
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -125,17 +134,19 @@ __host__ __device__ constexpr uint32_t f16_idesc(int n) {
 }
 
 // Shared-memory layout (offsets from a 1024-byte aligned base).  Stage i holds the
-// activation tile(s) and the expanded weight tile, each 128 rows x 128 bytes, so every
-// operand buffer is 1024-byte aligned as SWIZZLE_128B requires; the s2 slices follow.
-template <bool kTwoA, bool kS2>
+// activation tile(s) (128 rows x 128 bytes each) and the expanded weight tile (kBN rows x 128
+// bytes), so every operand buffer is 1024-byte aligned as SWIZZLE_128B requires; the s2 slices
+// follow.  Four stages when they fit in 200 KB, else three.
+template <bool kTwoA, bool kS2, int kBN>
 struct Layout {
-    static constexpr uint32_t kStageBytes = (kTwoA ? 3 : 2) * kTileBytes;
+    static constexpr uint32_t kStageBytes = (kTwoA ? 2 : 1) * kTileBytes + kBN * 128;
+    static constexpr int kStg = kStageBytes * 4 <= 200 * 1024 ? 4 : 3;
     __host__ __device__ static constexpr uint32_t a_hi(int s) { return s * kStageBytes; }
     __host__ __device__ static constexpr uint32_t a_lo(int s) { return s * kStageBytes + (kTwoA ? kTileBytes : 0); }
     __host__ __device__ static constexpr uint32_t b(int s) { return s * kStageBytes + (kTwoA ? 2 : 1) * kTileBytes; }
-    __host__ __device__ static constexpr uint32_t s2(int s) { return kStages * kStageBytes + 128 * s; }
-    static constexpr uint32_t kBars = kStages * kStageBytes + (kS2 ? 128 * kStages : 0);
-    static constexpr uint32_t kTmemSlot = kBars + (3 * kStages + 1) * 8;
+    __host__ __device__ static constexpr uint32_t s2(int s) { return kStg * kStageBytes + 128 * s; }
+    static constexpr uint32_t kBars = kStg * kStageBytes + (kS2 ? 128 * kStg : 0);
+    static constexpr uint32_t kTmemSlot = kBars + (3 * kStg + 1) * 8;
     static constexpr uint32_t kAbort = kTmemSlot + 4;
     static constexpr uint32_t kTotal = (kAbort + 4 + 127) & ~127u;
 };
@@ -146,14 +157,18 @@ struct Layout {
 // the single-stage GEMM).  kTwoA: two activation tiles (T_hi, T_lo) per K step (stage 2, precise).
 // kStoreT: the epilogue stores T as bf16 (hi, and lo when kHiLo) -- stage 1 of precise mode; else
 // it stores TOut (stage 1 of fast mode: T in the layer dtype; stage 2; the single-stage GEMM).
-template <typename TA, typename TOut, bool kS2, bool kTwoA, bool kHiLo, bool kStoreT>
+// kBN: output columns per CTA (128 or 256; the MMA is M=128 N=kBN K=16, each expander thread
+// owns kBN / 128 weight rows).  A 256-wide tile reads the activation tile once per two weight
+// row blocks, which lowers the shared-memory traffic per MMA.
+template <typename TA, typename TOut, bool kS2, bool kTwoA, bool kHiLo, bool kStoreT, int kBN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
                 const __grid_constant__ CUtensorMap map_s2, const Params p) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte align the working area (the launch reserves the slack)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    using L = Layout<kTwoA, kS2>;
+    using L = Layout<kTwoA, kS2, kBN>;
+    constexpr int kStages = L::kStg;
     uint64_t *full_a = reinterpret_cast<uint64_t *>(smem + L::kBars);
     uint64_t *full_b = full_a + kStages;
     uint64_t *empty = full_b + kStages;
@@ -162,7 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::kAbort);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * BM;
+    const int kb_begin = blockIdx.z * p.kbs;
+    const int nk = min(p.nk - kb_begin, p.kbs);  // this CTA's K steps (>= 1, the host checks)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -174,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 1) tmem_alloc(const_cast<uint32_t *>(tmem_slot), BN);
+    if (warp == 1) tmem_alloc(const_cast<uint32_t *>(tmem_slot), kBN);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -194,13 +211,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t bytes = kTileBytes * (kTwoA ? 2 : 1) + (kS2 ? 128 : 0);
             int issued_until = 0;
-            for (int kb = 0; kb < p.nk; ++kb) {
+            for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % kStages;
+                const int kx = (kb_begin + kb) * BK;
                 if (kb >= kStages && !wait(&empty[s], ((kb / kStages) - 1) & 1)) break;
                 mbar_arrive_expect_tx(&full_a[s], bytes);
-                tma_load_2d(smem + L::a_hi(s), &map_a, &full_a[s], kb * BK, m0);
-                if (kTwoA) tma_load_2d(smem + L::a_lo(s), &map_a2, &full_a[s], kb * BK, m0);
-                if (kS2) tma_load_1d(smem + L::s2(s), &map_s2, &full_a[s], kb * BK);
+                tma_load_2d(smem + L::a_hi(s), &map_a, &full_a[s], kx, m0);
+                if (kTwoA) tma_load_2d(smem + L::a_lo(s), &map_a2, &full_a[s], kx, m0);
+                if (kS2) tma_load_1d(smem + L::s2(s), &map_s2, &full_a[s], kx);
                 issued_until = kb + 1;
             }
             // on abort, let copies already in flight land before the CTA exits
@@ -211,10 +229,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = f16_idesc<TA>(BN);
+            constexpr uint32_t idesc = f16_idesc<TA>(kBN);
             const uint32_t sbase = smem_u32(smem);
             uint32_t acc = 0;
-            for (int kb = 0; kb < p.nk; ++kb) {
+            for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % kStages;
                 const uint32_t par = (kb / kStages) & 1;
                 if (!wait(&full_a[s], par) || !wait(&full_b[s], par)) break;
@@ -232,52 +250,66 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------------------------------------------------- weight expanders
-        const int e = threadIdx.x - 64;  // 0..127: one weight row per thread
-        const int n = n0 + e;
-        const bool row_ok = n < p.N;
-        const uint32_t *row = p.bits + (size_t)(row_ok ? n : 0) * p.W;
-        // words for the next steps are fetched ahead (4-deep register queue)
-        uint32_t q0[kStages], q1[kStages];
+        constexpr int kRows = kBN / 128;  // weight rows per thread: e, e + 128, ...
+        const int e = threadIdx.x - 64;   // 0..127
+        const uint32_t *row[kRows];
+        bool row_ok[kRows];
+        // this CTA's K range starts at word 2 * kb_begin of each row (two words per K step)
+        const int wl = p.W - 2 * kb_begin;
 #pragma unroll
-        for (int i = 0; i < kStages; ++i) {
-            const int w = 2 * i;
-            q0[i] = (row_ok && i < p.nk && w < p.W) ? __ldg(row + w) : 0u;
-            q1[i] = (row_ok && i < p.nk && w + 1 < p.W) ? __ldg(row + w + 1) : 0u;
+        for (int rr = 0; rr < kRows; ++rr) {
+            const int n = n0 + e + 128 * rr;
+            row_ok[rr] = n < p.N;
+            row[rr] = p.bits + (size_t)(row_ok[rr] ? n : 0) * p.W + 2 * kb_begin;
         }
+        // words for the next steps are fetched ahead (a register queue as deep as the ring)
+        uint32_t q0[kRows][kStages], q1[kRows][kStages];
+#pragma unroll
+        for (int rr = 0; rr < kRows; ++rr)
+#pragma unroll
+            for (int i = 0; i < kStages; ++i) {
+                const int w = 2 * i;
+                q0[rr][i] = (row_ok[rr] && i < nk && w < wl) ? __ldg(row[rr] + w) : 0u;
+                q1[rr][i] = (row_ok[rr] && i < nk && w + 1 < wl) ? __ldg(row[rr] + w + 1) : 0u;
+            }
         uint8_t *const brow_base = smem;
-        for (int kb0 = 0; kb0 < p.nk; kb0 += kStages) {
+        for (int kb0 = 0; kb0 < nk; kb0 += kStages) {
 #pragma unroll
             for (int i = 0; i < kStages; ++i) {
                 const int kb = kb0 + i;
-                if (kb < p.nk) {
+                if (kb < nk) {
                     const int s = i;  // kb % kStages == i because kb0 is a multiple of kStages
-                    const uint32_t w0 = q0[i], w1 = q1[i];
-                    const int nxt = kb + kStages, wn = 2 * nxt;
-                    q0[i] = (row_ok && nxt < p.nk && wn < p.W) ? __ldg(row + wn) : 0u;
-                    q1[i] = (row_ok && nxt < p.nk && wn + 1 < p.W) ? __ldg(row + wn + 1) : 0u;
                     // slot s is free once this step's activation tile is in flight-complete:
                     // the producer only re-arms full_a[s] after empty[s] fired
                     const bool ok = wait(&full_a[s], (kb / kStages) & 1);
-                    uint8_t *brow = brow_base + L::b(s) + e * 128;
                     const uint32_t *s2w = reinterpret_cast<const uint32_t *>(smem + L::s2(s));
+                    const int nxt = kb + kStages, wn = 2 * nxt;
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint32_t w = h ? w1 : w0;
+                    for (int rr = 0; rr < kRows; ++rr) {
+                        const uint32_t w0 = q0[rr][i], w1 = q1[rr][i];
+                        q0[rr][i] = (row_ok[rr] && nxt < nk && wn < wl) ? __ldg(row[rr] + wn) : 0u;
+                        q1[rr][i] = (row_ok[rr] && nxt < nk && wn + 1 < wl) ? __ldg(row[rr] + wn + 1) : 0u;
+                        uint8_t *brow = brow_base + L::b(s) + (e + 128 * rr) * 128;
 #pragma unroll
-                        for (int qc = 0; qc < 4; ++qc) {
-                            uint32_t v[4];
+                        for (int h = 0; h < 2; ++h) {
+                            const uint32_t w = h ? w1 : w0;
 #pragma unroll
-                            for (int pp = 0; pp < 4; ++pp) {
-                                const int P = 4 * qc + pp;  // pair index inside the word
-                                uint32_t val;
-                                if (kS2)
-                                    val = s2w[16 * h + P];
-                                else
-                                    val = std::is_same<TA, __nv_bfloat16>::value ? 0x3F803F80u : 0x3C003C00u;
-                                v[pp] = row_ok && ok ? lop_sign(w << P, val) : 0u;
+                            for (int qc = 0; qc < 4; ++qc) {
+                                uint32_t v[4];
+#pragma unroll
+                                for (int pp = 0; pp < 4; ++pp) {
+                                    const int P = 4 * qc + pp;  // pair index inside the word
+                                    uint32_t val;
+                                    if (kS2)
+                                        val = s2w[16 * h + P];
+                                    else
+                                        val = std::is_same<TA, __nv_bfloat16>::value ? 0x3F803F80u : 0x3C003C00u;
+                                    v[pp] = row_ok[rr] && ok ? lop_sign(w << P, val) : 0u;
+                                }
+                                const int chunk = 4 * h + qc;  // rows e and e + 128 share the swizzle phase
+                                *reinterpret_cast<uint4 *>(brow + ((chunk ^ (e & 7)) << 4)) =
+                                    make_uint4(v[0], v[1], v[2], v[3]);
                             }
-                            const int chunk = 4 * h + qc;
-                            *reinterpret_cast<uint4 *>(brow + ((chunk ^ (e & 7)) << 4)) = make_uint4(v[0], v[1], v[2], v[3]);
                         }
                     }
                     fence_proxy_async_smem();
@@ -292,10 +324,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3;  // TMEM lanes this warp may access
         const int m = m0 + quarter * 32 + lane;
         const TOut *sc = static_cast<const TOut *>(p.col_scale);
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = 0; c < kBN; c += 32) {
             uint32_t r[32];
             tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, r);
             if (!ok || m >= p.M || n0 + c >= p.N) continue;
+            if (p.partial) {  // split-K: the raw accumulator row segment, scaled and converted later
+                float *dst = p.partial + ((size_t)blockIdx.z * p.M + m) * p.ldp + n0 + c;
+                const int nc = min(32, p.N - (n0 + c));
+                if (nc == 32) {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        reinterpret_cast<uint4 *>(dst)[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+                } else {  // unrolled with a predicate: constant indices keep r in registers
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < nc) dst[j] = __uint_as_float(r[j]);
+                }
+                continue;
+            }
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -329,7 +375,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                             reinterpret_cast<uint4 *>(lo)[q] = make_uint4(pl[4 * q], pl[4 * q + 1], pl[4 * q + 2], pl[4 * q + 3]);
                     }
                 } else {
-                    for (int j = 0; j < ncols; ++j) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (j >= ncols) continue;
                         hi[j] = __ushort_as_bfloat16((uint16_t)(ph[j >> 1] >> (16 * (j & 1))));
                         if (kHiLo) lo[j] = __ushort_as_bfloat16((uint16_t)(pl[j >> 1] >> (16 * (j & 1))));
                     }
@@ -349,7 +397,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         reinterpret_cast<uint4 *>(o)[q] = make_uint4(po[4 * q], po[4 * q + 1], po[4 * q + 2], po[4 * q + 3]);
                 } else {
                     uint16_t *o16 = reinterpret_cast<uint16_t *>(o);
-                    for (int j = 0; j < ncols; ++j) o16[j] = (uint16_t)(po[j >> 1] >> (16 * (j & 1)));
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < ncols) o16[j] = (uint16_t)(po[j >> 1] >> (16 * (j & 1)));
                 }
             }
         }
@@ -358,7 +408,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, kBN);
+    }
+}
+
+// Split-K epilogue: out[m][n] = format(scale[n] * sum_z partial[z][m][n]), the slots summed in
+// order (deterministic).  Four columns per thread; formats as gemm_kernel's epilogue.
+template <typename TOut, bool kStoreT, bool kHiLo>
+__global__ void __launch_bounds__(256) splitk_finalize(const float *__restrict__ part, int splits, int M, int N,
+                                                       int ldp, const TOut *__restrict__ scale, void *out_hi,
+                                                       void *out_lo, int ldo) {
+    const int q = (N + 3) >> 2;
+    const int64_t total = (int64_t)M * q;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / q), n = (int)(i % q) * 4;
+        const float *src = part + (size_t)m * ldp + n;
+        float4 acc = *reinterpret_cast<const float4 *>(src);
+        for (int z = 1; z < splits; ++z) {
+            const float4 v = *reinterpret_cast<const float4 *>(src + (size_t)z * M * ldp);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+        for (int j = 0; j < 4 && n + j < N; ++j) {
+            const float v = scale ? a[j] * Elem<TOut>::to_f(scale[n + j]) : a[j];
+            const size_t o = (size_t)m * ldo + n + j;
+            if (kStoreT) {
+                const __nv_bfloat16 h = __float2bfloat16_rn(v);
+                static_cast<__nv_bfloat16 *>(out_hi)[o] = h;
+                if (kHiLo) static_cast<__nv_bfloat16 *>(out_lo)[o] = __float2bfloat16_rn(v - __bfloat162float(h));
+            } else {
+                static_cast<TOut *>(out_hi)[o] = Elem<TOut>::out(v);
+            }
+        }
     }
 }
 
@@ -409,11 +493,31 @@ static int make_map_1d(CUtensorMap *map, const void *base, CUtensorMapDataType d
     return NQ_OK;
 }
 
-template <typename TA, typename TOut, bool kS2, bool kTwoA, bool kHiLo, bool kStoreT>
-static int launch_stage(const CUtensorMap &a, const CUtensorMap &a2, const CUtensorMap &s2, const Params &p,
-                        cudaStream_t stream) {
-    auto kern = gemm_kernel<TA, TOut, kS2, kTwoA, kHiLo, kStoreT>;
-    const size_t smem = Layout<kTwoA, kS2>::kTotal + 1024;
+// Most CTAs a split-K launch may use; the workspace reserves kMaxSplitCtas * BM * BN float32
+// partial values (the tiles x splits of one launch never exceed it).
+constexpr int kMaxSplitCtas = 160;
+constexpr int64_t kSplitMaxM = 1024;  // split-K only for M up to this many rows
+constexpr int kMinStepsPerSplit = 4;
+
+// K splits for a launch of `tiles` output tiles and nk K steps on `sms` SMs: enough CTAs for
+// about one wave when the tiles alone leave more than half of the SMs idle.
+static int choose_splits(int64_t m, int tiles, int nk, int sms) {
+    const int cap = std::min(sms, kMaxSplitCtas);
+    if (m > kSplitMaxM || tiles * 2 > cap) return 1;
+    int splits = std::min(cap / tiles, nk / kMinStepsPerSplit);
+    return splits < 2 ? 1 : splits;
+}
+
+template <typename TA, typename TOut, bool kS2, bool kTwoA, bool kHiLo, bool kStoreT, int kBN>
+static int launch_stage(const CUtensorMap &a, const CUtensorMap &a2, const CUtensorMap &s2, const Params &p_in,
+                        cudaStream_t stream, float *partial = nullptr, int splits = 1) {
+    Params p = p_in;
+    p.kbs = (p.nk + splits - 1) / splits;
+    splits = (p.nk + p.kbs - 1) / p.kbs;  // no empty split
+    p.partial = splits > 1 ? partial : nullptr;
+    p.ldp = (p.N + 3) & ~3;
+    auto kern = gemm_kernel<TA, TOut, kS2, kTwoA, kHiLo, kStoreT, kBN>;
+    const size_t smem = Layout<kTwoA, kS2, kBN>::kTotal + 1024;
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -422,10 +526,40 @@ static int launch_stage(const CUtensorMap &a, const CUtensorMap &a2, const CUten
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
         attr_set[dev] = true;
     }
-    dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM);
+    dim3 grid((p.N + kBN - 1) / kBN, (p.M + BM - 1) / BM, p.partial ? splits : 1);
     kern<<<grid, kThreads, smem, stream>>>(a, a2, s2, p);
     cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemm launch");
+    if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+    if (p.partial) {
+        const int64_t work = (int64_t)p.M * ((p.N + 3) / 4);
+        const int blocks = (int)std::min<int64_t>((work + 255) / 256, 4 * 148);
+        splitk_finalize<TOut, kStoreT, kHiLo><<<blocks, 256, 0, stream>>>(
+            p.partial, splits, p.M, p.N, p.ldp, static_cast<const TOut *>(p.col_scale), p.out_hi, p.out_lo, p.ldo);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e, "gemm split-K finalize launch");
+    }
+    return NQ_OK;
+}
+
+// 256-wide tiles when they alone give most SMs a CTA (or NQ_GEMM_TILE_N=128 / 256 forces a
+// width); otherwise 128-wide tiles, split along K when M is small.
+static int tile_width(int64_t m, int64_t n, int sms) {
+    static const int forced = [] {
+        const char *v = getenv("NQ_GEMM_TILE_N");
+        return v ? atoi(v) : 0;
+    }();
+    if (forced == 128 || forced == 256) return forced;
+    const int64_t t256 = (m + BM - 1) / BM * ((n + 255) / 256);
+    return t256 * 4 >= (int64_t)sms * 3 ? 256 : 128;
+}
+
+template <typename TA, typename TOut, bool kS2, bool kTwoA, bool kHiLo, bool kStoreT>
+static int launch_tiled(int64_t m, int sms, const CUtensorMap &a, const CUtensorMap &a2, const CUtensorMap &s2,
+                        const Params &p, cudaStream_t stream, float *partial) {
+    if (tile_width(m, p.N, sms) == 256)
+        return launch_stage<TA, TOut, kS2, kTwoA, kHiLo, kStoreT, 256>(a, a2, s2, p, stream);
+    const int splits = partial ? choose_splits(m, (int)((m + BM - 1) / BM * ((p.N + 127) / 128)), p.nk, sms) : 1;
+    return launch_stage<TA, TOut, kS2, kTwoA, kHiLo, kStoreT, 128>(a, a2, s2, p, stream, partial, splits);
 }
 
 static inline size_t t_ld(int64_t rank) { return (size_t)((rank + 7) / 8 * 8); }
@@ -436,10 +570,13 @@ static inline size_t t_ld(int64_t rank) { return (size_t)((rank + 7) / 8 * 8); }
 extern "C" {
 
 size_t nq_gemm_workspace_bytes(int64_t m, int64_t rank) {
+    using namespace nq::gemm;
     if (m <= 0 || rank <= 0) return 0;
-    const size_t plane = (size_t)m * nq::gemm::t_ld(rank) * 2;
+    const size_t plane = (size_t)m * t_ld(rank) * 2;
     const size_t planeal = (plane + 255) & ~size_t(255);
-    return sizeof(nq::Ctrl) + 2 * planeal;
+    // split-K partial slots for small M (both stages use them in turn)
+    const size_t part = m <= kSplitMaxM ? (size_t)kMaxSplitCtas * BM * BN * sizeof(float) : 0;
+    return sizeof(nq::Ctrl) + 2 * planeal + part;
 }
 
 int nq_gemm(int dtype, const void *x, int64_t m, int64_t in_features, const void *scale_pre, const int32_t *v_bits,
@@ -479,6 +616,7 @@ int nq_gemm(int dtype, const void *x, int64_t m, int64_t in_features, const void
     Ctrl *ctrl = static_cast<Ctrl *>(workspace);
     void *t_hi = static_cast<char *>(workspace) + sizeof(Ctrl);
     void *t_lo = static_cast<char *>(t_hi) + planeal;
+    float *partial = m <= kSplitMaxM ? reinterpret_cast<float *>(static_cast<char *>(t_lo) + planeal) : nullptr;
     const CUtensorMapDataType in_dt =
         dtype == NQ_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     CUtensorMap mx, ms2, mth, mtl;
@@ -515,18 +653,21 @@ int nq_gemm(int dtype, const void *x, int64_t m, int64_t in_features, const void
     p2.ldo = (int)out_features;
     p2.status = &ctrl->status;
 
+    const int sms = device_info(dev).sms;
+    using H = __half;
+    using B = __nv_bfloat16;
     if (dtype == NQ_DTYPE_F16) {
-        st = precise ? launch_stage<__half, __half, true, false, true, true>(mx, mx, ms2, p1, s)
-                     : launch_stage<__half, __half, true, false, false, false>(mx, mx, ms2, p1, s);
+        st = precise ? launch_tiled<H, H, true, false, true, true>(m, sms, mx, mx, ms2, p1, s, partial)
+                     : launch_tiled<H, H, true, false, false, false>(m, sms, mx, mx, ms2, p1, s, partial);
         if (st) return st;
-        st = precise ? launch_stage<__nv_bfloat16, __half, false, true, false, false>(mth, mtl, ms2, p2, s)
-                     : launch_stage<__half, __half, false, false, false, false>(mth, mth, ms2, p2, s);
+        st = precise ? launch_tiled<B, H, false, true, false, false>(m, sms, mth, mtl, ms2, p2, s, partial)
+                     : launch_tiled<H, H, false, false, false, false>(m, sms, mth, mth, ms2, p2, s, partial);
     } else {
-        st = precise ? launch_stage<__nv_bfloat16, __nv_bfloat16, true, false, true, true>(mx, mx, ms2, p1, s)
-                     : launch_stage<__nv_bfloat16, __nv_bfloat16, true, false, false, false>(mx, mx, ms2, p1, s);
+        st = precise ? launch_tiled<B, B, true, false, true, true>(m, sms, mx, mx, ms2, p1, s, partial)
+                     : launch_tiled<B, B, true, false, false, false>(m, sms, mx, mx, ms2, p1, s, partial);
         if (st) return st;
-        st = precise ? launch_stage<__nv_bfloat16, __nv_bfloat16, false, true, false, false>(mth, mtl, ms2, p2, s)
-                     : launch_stage<__nv_bfloat16, __nv_bfloat16, false, false, false, false>(mth, mth, ms2, p2, s);
+        st = precise ? launch_tiled<B, B, false, true, false, false>(m, sms, mth, mtl, ms2, p2, s, partial)
+                     : launch_tiled<B, B, false, false, false, false>(m, sms, mth, mth, ms2, p2, s, partial);
     }
     return st;
 }
@@ -572,8 +713,8 @@ int nq_gemm_onebit(int dtype, const void *x, int64_t m, int64_t k, const void *s
     p.ldo = (int)n;
     p.status = &static_cast<Ctrl *>(workspace)->status;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    return dtype == NQ_DTYPE_F16 ? launch_stage<__half, __half, true, false, false, false>(mx, mx, ms, p, s)
-                                 : launch_stage<__nv_bfloat16, __nv_bfloat16, true, false, false, false>(mx, mx, ms, p, s);
+    return dtype == NQ_DTYPE_F16 ? launch_stage<__half, __half, true, false, false, false, 128>(mx, mx, ms, p, s)
+                                 : launch_stage<__nv_bfloat16, __nv_bfloat16, true, false, false, false, 128>(mx, mx, ms, p, s);
 }
 
 }  // extern "C"

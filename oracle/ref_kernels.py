@@ -1,14 +1,16 @@
 """The reference's own CUDA kernels, built from its sources by oracle/build_ref.py.
 
-Test and measurement infrastructure, not product.  Two uses:
+Test and measurement infrastructure, not product.  Two uses of its decode GEMV
+(``binary_kernels::nanoquant_dyn_forward``, kernel/cuda/gemv_kernel.cu:308-429):
 
-* a checker: ``python -m oracle.ref_kernels <in.npz> <out.npz>`` runs the reference's
-  ``binary_kernels::nanoquant_dyn_forward`` (kernel/cuda/gemv_kernel.cu:308-429) and
-  ``marlin_nanoquant_forward`` (kernel/cuda/gemm.cpp:112-122) on the packed inputs of the file and
-  writes their outputs, so the GPU tests compare this package's kernels with the reference's on
-  identical words;
-* the reference arm of ``bench.py --impl reference --layer / --gemm``, which times those kernels
-  on the same GPU.
+* a checker: ``python -m oracle.ref_kernels <in.npz> <out.npz>`` runs it on the packed inputs of
+  the file and writes its outputs, so the GPU tests compare this package's GEMV with the
+  reference's on identical words;
+* the reference arm of ``bench.py --impl reference --layer``, which times it on the same GPU.
+
+The reference's Marlin GEMM (``marlin_nanoquant_forward``, gemm.cpp:112-122) is built into the
+same library but never run: compiled for sm_100a it stopped with "an illegal instruction was
+encountered" on a B200 on inputs that satisfy its host-side shape checks, so it stays off the GPU.
 
 The library registers the op namespace ``binary_kernels``, which this package registers too, so
 ``load()`` refuses to run in a process that has this package's libraries mapped: callers run it in
@@ -71,7 +73,7 @@ def gemv(ops, x, s2, v_half2, smid, u_half2, s1):
 
 
 def run_file(src: str, dst: str) -> None:
-    """Run every case of ``src`` (gemv_<k>_* and marlin_<k>_* arrays) and save the outputs."""
+    """Run every GEMV case of ``src`` (gemv_<k>_* arrays) and save the outputs."""
     import torch
     ops = load()
     d = dict(np.load(src))
@@ -84,16 +86,12 @@ def run_file(src: str, dst: str) -> None:
 
     for key in sorted({k.split("_")[1] for k in d if k.startswith("gemv_")}):
         p = f"gemv_{key}_"
+        out_f, in_f = int(d[p + "s1"].size), int(d[p + "s2"].size)
+        if not gemv_shape_ok(out_f, in_f, int(d[p + "vb"].shape[0])):
+            raise ValueError(f"case {key}: a shape the reference GEMV does not handle in bounds")
         td = torch.float16 if int(d[p + "dtype"][0]) == 0 else torch.bfloat16
         smid = t(d[p + "smid"], td) if p + "smid" in d else None
         y = gemv(ops, t(d[p + "x"], td), t(d[p + "s2"], td), t(d[p + "vb"]), smid, t(d[p + "ub"]), t(d[p + "s1"], td))
-        out[p + "y"] = y.float().cpu().numpy()
-    for key in sorted({k.split("_")[1] for k in d if k.startswith("marlin_")}):
-        p = f"marlin_{key}_"
-        td = torch.float16 if int(d[p + "dtype"][0]) == 0 else torch.bfloat16
-        ws = torch.zeros(int(d[p + "ws"][0]), dtype=torch.int32, device=dev)
-        y = ops.marlin_nanoquant_forward(t(d[p + "x"], td), t(d[p + "vw"]), t(d[p + "uw"]), t(d[p + "s1"], td),
-                                         t(d[p + "s2"], td), t(d[p + "s3"], td), ws)
         out[p + "y"] = y.float().cpu().numpy()
     torch.cuda.synchronize(dev)
     np.savez(dst, **out)

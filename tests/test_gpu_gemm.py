@@ -69,7 +69,8 @@ def test_gemm_fast_mode_matches_dtype_intermediate(dtype):
 
 
 @pytest.mark.parametrize("shape", [(7, 8, 3, 1), (100, 64, 33, 5), (130, 96, 47, 130), (1000, 200, 96, 77),
-                                   (33, 1024, 300, 257), (4096, 11008, 2054, 1)])
+                                   (33, 1024, 300, 257), (4096, 11008, 2054, 1),
+                                   (1000, 2000, 300, 77)])  # split-K over a ragged K tail
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
 def test_gemm_ragged_shapes(shape, dtype):
     out_f, in_f, rank, m = shape
@@ -77,6 +78,20 @@ def test_gemm_ragged_shapes(shape, dtype):
     d = DeviceLayer(L, dtype)
     y, ws = capi_gemm(d, precise=True)
     assert_close_to_oracle(y, dense_ref(d), dtype)
+    assert workspace_status(ws) == 0
+
+
+@pytest.mark.parametrize("shape,dtype,precise", [((4096, 4096, 2054, 2048), "bf16", True),
+                                                 ((4096, 4096, 2054, 2048), "f16", False),
+                                                 ((4000, 4096, 2050, 2000), "bf16", True)])
+def test_gemm_wide_tiles(shape, dtype, precise):
+    """Shapes whose output tiles fill the GPU run 256-column tiles in both stages (ragged M and N
+    included)."""
+    out_f, in_f, rank, m = shape
+    L = orc.make_layer(m + rank, out_f, in_f, rank, m, dtype, with_mid=True)
+    d = DeviceLayer(L, dtype)
+    y, ws = capi_gemm(d, precise=precise)
+    assert_close_to_oracle(y, dense_ref(d, round_t=None if precise else dtype), dtype)
     assert workspace_status(ws) == 0
 
 
