@@ -69,8 +69,6 @@ def parse():
                     help="phase timeline of every fused GEMV launch of one decode step (rank 0; needs the library "
                          "built with NQ_NVCC_EXTRA=-DNQ_GEMV_TRACE): per launch kind, the median over the step's "
                          "launches of the median and slowest CTA's time at each phase boundary")
-    ap.add_argument("--chain", action="store_true",
-                    help="decode through GEMV chains (one cooperative launch per block besides attention)")
     ap.add_argument("--no-exchange", action="store_true",
                     help="N > 1: per-block sums through NCCL instead of inside the GEMVs (the default exchange)")
     ap.add_argument("--peer-allreduce", action="store_true",
@@ -234,8 +232,7 @@ def config_block(cfg, args, world):
                         f"random-id prompt",
             "model": cfg.name, "global_batch": args.batch, "seq_len": args.prompt,
             "parallelism": f"tp{world}", "ranks": dict(cfg.ranks),
-            "decode_path": "gemv chain per block" if getattr(args, "chain", False) else
-                           "grouped GEMV launches with fused RMSNorm / SwiGLU prologues",
+            "decode_path": "grouped GEMV launches with fused RMSNorm / SwiGLU prologues",
             "tp_allreduce": ("peer memory (nq_allreduce)" if getattr(args, "peer_allreduce", False) else
                              "NCCL" if getattr(args, "no_exchange", False) else
                              "inside the GEMVs (push from o / down, pull in the next RMSNorm prologue)")
@@ -303,7 +300,7 @@ def gemv_roofline(dec, reps: int = 5):
     from nanoquant_b200 import chain as nqchain
     units = []  # (callable, algorithmic bytes)
     B, ops, eps = dec.batch, torch.ops.nq_b200, dec.cfg.rms_eps
-    fused = dec.chain_ws is None and dec.fuse_neighbours and B <= 8
+    fused = dec.fuse_neighbours and B <= 8
     for lay in dec.layers:
         for key in ("qkv", "o", "gate_up", "down"):
             unit = lay[key]
@@ -361,7 +358,7 @@ def run_nq(args, world, rank, local):
     group = torch.distributed.group.WORLD if world > 1 else None
     max_seq = args.prompt + args.warmup + 2 * args.steps + 16
     dec = Decoder(cfg, max_seq=max_seq, batch=args.batch, tp_rank=rank, tp=world, group=group, seed=1234,
-                  dtype=torch.float16, device=dev, chain=args.chain, peer_allreduce=args.peer_allreduce,
+                  dtype=torch.float16, device=dev, peer_allreduce=args.peer_allreduce,
                   tp_exchange=not args.no_exchange)
     g = torch.Generator().manual_seed(42)
     prompt = torch.randint(0, cfg.vocab, (args.batch, args.prompt), generator=g)  # one random-id prompt per row

@@ -131,8 +131,9 @@ NQ_API int nq_gemv_group(int dtype, const void *x, int64_t batch, int64_t in_fea
  * Transformed inputs need batch <= 8, in_features % 8 == 0 and 16-byte aligned x, x2,
  * norm_weight, residual_out and scale_pre.  Workspace as nq_gemv_group.
  * ------------------------------------------------------------------------------- */
+enum { NQ_CHAIN_X_PLAIN = 0, NQ_CHAIN_X_RMSNORM = 1, NQ_CHAIN_X_SILU_MUL = 2, NQ_CHAIN_X_MUL = 3 };
 typedef struct {
-    int x_mode;                /* NQ_CHAIN_X_* (defined below) */
+    int x_mode;                /* NQ_CHAIN_X_* */
     float eps;                 /* NQ_CHAIN_X_RMSNORM */
     const void *x;             /* [batch, in] */
     const void *x2;            /* residual [batch, in] (RMSNORM, may be NULL) or second factor */
@@ -205,48 +206,6 @@ NQ_API int nq_gemv_static(int dtype, const void *x, int64_t batch, int64_t in_fe
  * clears the word, so read it before that call.  Neither function may be used after a
  * cudaDeviceReset in the same process (the cached scratch address would be stale). */
 NQ_API int nq_gemv_static_status(void *stream, int *status_out);
-
-/* ---------------------------------------------------------------------------------
- * GEMV chain: up to NQ_CHAIN_MAX_PHASES grouped decode GEMVs run back to back in ONE
- * cooperative launch, each phase's input formed on the fly from earlier outputs -- the
- * o-projection, MLP and next q/k/v of a decoder block with the RMSNorm, SwiGLU and residual
- * adds between them folded in.  No reference counterpart: the reference runs each linear as
- * its own nanoquant_dyn_forward call (src/nanoquant/modules/linear.py:155-164) and the
- * neighbours as HF modules (src/nanoquant/kernel/test_decode.py).  Every phase's layers
- * compute exactly what nq_gemv computes on the phase input x', which is
- *   NQ_CHAIN_X_PLAIN     x' = x
- *   NQ_CHAIN_X_RMSNORM   x' = dtype(norm_weight * dtype(x * rsqrt(mean(x^2) + eps)))
- *   NQ_CHAIN_X_SILU_MUL  x' = dtype(dtype(silu(x)) * x2)
- *   NQ_CHAIN_X_MUL       x' = dtype(x * x2)
- * and with `residual` set (single-layer phases) the output is dtype(dtype(y) + residual),
- * stored to y, which may be the residual buffer itself; bit l of `act` stores layer l's
- * output as dtype(silu(dtype(y))) instead (a gate whose SiLU is then applied once per value,
- * not once per consumer: SILU_MUL on (gate, up) equals MUL on (act gate, up), bit for bit).  Phases run in order; a phase may
- * read what earlier phases wrote.  Limits: batch <= 2; in_features % 8 == 0; x, x2,
- * norm_weight and every scale_pre 16-byte aligned; RMSNorm rows <= 16384 values; and the
- * weight slabs of two consecutive phases must fit one SM's shared memory.
- * nq_gemv_chain_workspace_bytes() plans the chain without launching: 0 means it cannot run
- * (nq_last_error_message() says why).  The workspace must start zeroed and serves one chain
- * at a time, as for nq_gemv.
- * ------------------------------------------------------------------------------- */
-#define NQ_CHAIN_MAX_PHASES 4
-enum { NQ_CHAIN_X_PLAIN = 0, NQ_CHAIN_X_RMSNORM = 1, NQ_CHAIN_X_SILU_MUL = 2, NQ_CHAIN_X_MUL = 3 };
-typedef struct {
-    int n_layers;              /* 1..3 layers reading the same x' */
-    int x_mode;                /* NQ_CHAIN_X_* */
-    int act;                   /* bit l: layer l's output goes through SiLU */
-    float eps;                 /* NQ_CHAIN_X_RMSNORM */
-    int64_t in_features;
-    const void *x;             /* [batch, in]: the input, the stream to normalise, or the gate */
-    const void *x2;            /* NQ_CHAIN_X_SILU_MUL / NQ_CHAIN_X_MUL: up [batch, in] */
-    const void *norm_weight;   /* NQ_CHAIN_X_RMSNORM: [in] */
-    const void *residual;      /* NULL, or [batch, out] added to the output (n_layers == 1) */
-    nq_gemv_layer layers[3];
-} nq_chain_phase;
-NQ_API size_t nq_gemv_chain_workspace_bytes(int dtype, int64_t batch, int n_phases,
-                                            const nq_chain_phase *phases);
-NQ_API int nq_gemv_chain(int dtype, int64_t batch, int n_phases, const nq_chain_phase *phases,
-                         void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---------------------------------------------------------------------------------
  * Prefill GEMM: replaces marlin_nanoquant_cuda (src/nanoquant/kernel/cuda/gemm.cpp:112-122,

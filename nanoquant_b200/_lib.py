@@ -48,13 +48,6 @@ class TpExchange(ctypes.Structure):
                 ("max_elems", ctypes.c_int64)]
 
 
-class ChainPhase(ctypes.Structure):
-    """nq_chain_phase of include/nq_b200.h."""
-    _fields_ = [("n_layers", ctypes.c_int), ("x_mode", ctypes.c_int), ("act", ctypes.c_int), ("eps", ctypes.c_float),
-                ("in_features", ctypes.c_int64), ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p),
-                ("norm_weight", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("layers", GemvLayer * 3)]
-
-
 _lock = threading.Lock()
 _cuda = None
 _torch_loaded = False
@@ -86,9 +79,6 @@ _SIGNATURES = {
     "nq_tp_pull": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p]),
     "nq_gemv_group_ex": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_void_p, _c.c_int,
                                     _c.c_void_p, _c.c_size_t, _c.c_void_p]),
-    "nq_gemv_chain_workspace_bytes": (_c.c_size_t, [_c.c_int, _c.c_int64, _c.c_int, _c.c_void_p]),
-    "nq_gemv_chain": (_c.c_int, [_c.c_int, _c.c_int64, _c.c_int, _c.c_void_p, _c.c_void_p, _c.c_size_t,
-                                 _c.c_void_p]),
     "nq_gemm_workspace_bytes": (_c.c_size_t, [_c.c_int64, _c.c_int64]),
     "nq_gemm_onebit_workspace_bytes": (_c.c_size_t, []),
     "nq_gemm_onebit": (_c.c_int, [_c.c_int, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_void_p,

@@ -331,7 +331,6 @@ struct Member {
     int tiles1, tiles2;        // 16-row tiles of this layer in stage 1 / stage 2
     int t1_start, t2_start;    // its first tile in the group's concatenated tile lists
     int u_rows, wus;           // U slab copied row by row (wu % 4 == 0) and its smem row stride
-    int tbs, ldis;             // chain: staged t columns in shared memory (element offset, column stride)
 };
 
 struct Params {
@@ -397,8 +396,8 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
 }
 
 // ------------------------------------------------------------------ stage bodies
-// Shared by the single-group kernel and the chain kernel.  Stage 1: this CTA's tiles
-// [t1b, t1e) split over the warps by K-block units (warp_units), partial 16x8 tiles into `red`.
+// Stage 1: this CTA's tiles [t1b, t1e) split over the warps by K-block units (warp_units),
+// partial 16x8 tiles into `red`.
 // FOLD: 1 compiles only the folded-operand path, -1 decides at run time (p.fold).
 template <typename T, int FOLD = -1>
 __device__ __forceinline__ void stage1_items(const Params &p, const uint32_t *vch, const T *s2s, const T *xs,
@@ -525,12 +524,11 @@ __device__ __forceinline__ void stage1_finish(const Params &p, const float *red,
 }
 
 // Stage 2: this CTA's tiles [t2b, t2e) of U against t, split like stage 1; partials into `red`.
-// NT = 8-column B tiles: (hi, lo) of 4 batch rows each, so 1 for batch <= 4.  `tsm`: the
-// members' t columns staged in shared memory (member l at mb.tbs, column stride mb.ldis), or
-// null to read them from global memory (L2).
+// NT = 8-column B tiles: (hi, lo) of 4 batch rows each, so 1 for batch <= 4; the members' t
+// columns are read from global memory (L2), where stage 1 left them.
 template <typename T, int NT>
 __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uch, float *red, int t2b, int t2e,
-                                             bool ok, const __nv_bfloat16 *tsm, WarpTab *wt) {
+                                             bool ok, WarpTab *wt) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int sh0 = 8 * (t & 1);
@@ -564,7 +562,7 @@ __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uc
         const bool vA = ok && (row0 + g < mb.out_f), vB = ok && (row0 + g + 8 < mb.out_f);
         const uint32_t *rowA = uch + uoff + (size_t)(16 * (tile - a0) + g) * mb.wus;
         const uint32_t *rowB = rowA + (size_t)8 * mb.wus;
-        const __nv_bfloat16 *trow0 = tsm ? tsm + mb.tbs + (size_t)g * mb.ldis : mb.tb + (size_t)g * mb.ldi;
+        const __nv_bfloat16 *trow0 = mb.tb + (size_t)g * mb.ldi;
         const __nv_bfloat16 *trow1 = mb.tb + (size_t)(8 + g) * mb.ldi;
         float acc0[4][4] = {}, acc1[NT][4][4] = {};
         for (int kb0 = kbeg; kb0 < kend; kb0 += kChunkKb) {
@@ -573,16 +571,7 @@ __device__ __forceinline__ void stage2_items(const Params &p, const uint32_t *uc
             for (int q = 0; q < kChunkKb; ++q) {
                 const int kc = 64 * (kb0 + q) + 16 * t;
                 const bool in = kb0 + q < kend;
-                if (tsm) {
-                    if (in && v0) {
-                        load16_smem(trow0 + kc, bp0[q]);
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) bp0[q][e] = 0u;
-                    }
-                } else {
-                    load_t_pairs(trow0 + kc, in && v0, bp0[q]);
-                }
+                load_t_pairs(trow0 + kc, in && v0, bp0[q]);
                 if (NT == 2) load_t_pairs(trow1 + kc, in && v1, bp1[NT - 1][q]);
             }
 #pragma unroll
@@ -1038,9 +1027,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p, const
         if (!mbar_wait(&bars[1], 0, &p.ctrl->status)) ok = false;
         NQ_STAMP(9);
         if (DECODE || p.batch <= 4)
-            stage2_items<T, 1>(p, uch, red, t2b, t2e, ok, nullptr, &wtab);
+            stage2_items<T, 1>(p, uch, red, t2b, t2e, ok, &wtab);
         else
-            stage2_items<T, 2>(p, uch, red, t2b, t2e, ok, nullptr, &wtab);
+            stage2_items<T, 2>(p, uch, red, t2b, t2e, ok, &wtab);
         __syncthreads();
         NQ_STAMP(10);
         // a PUSH stages its rows in the x region (stage 1 is over; the host checked its size)
@@ -1385,517 +1374,6 @@ static int group_impl(int dtype, const GroupInput &in, int64_t batch, int64_t in
     return NQ_OK;
 }
 
-// ------------------------------------------------------------------ GEMV chain
-// Up to kMaxPhases grouped GEMVs in one cooperative launch.  Every weight byte of phase k
-// (V rows, s2, U rows, s1 of this CTA's tiles) is put in flight one phase ahead: phases 0
-// and 1 at kernel start, phase k+1 right after the grid barrier that opens phase k.  Two
-// shared-memory regions alternate (phase k uses region k & 1), each with its own pair of
-// mbarriers (V side, U side).  Within a phase: x' is formed from global memory (L2) and folded
-// with each member's s2 into the bf16 (hi, lo) B operand, stage 1 runs, a grid barrier, stage 2
-// with the optional residual add, then a grid barrier before the next phase reads the output.
-constexpr int kMaxPhases = NQ_CHAIN_MAX_PHASES;
-constexpr int kNormMaxChunks = 4;  // RMSNorm rows up to kNormMaxChunks * 8 * kThreads values
-
-struct ChainPhase {
-    Params g;           // the phase's grouped GEMV (fold mode, offsets into this phase's region)
-    const void *x2;     // SiLU-mul: up
-    const void *nw;     // RMSNorm weight
-    const void *res;    // residual added to the output, or null
-    float eps;
-    int xmode;
-    int act;            // bit l: SiLU on member l's output
-};
-
-struct alignas(16) ChainParams {
-    ChainPhase ph[kMaxPhases];
-    int nph;
-};
-static_assert(sizeof(ChainParams) % 16 == 0, "copied to shared memory in 16-byte pieces");
-
-// Issue phase p's weight copies for this CTA: V rows and s2 rows on bv[0], U rows and s1
-// on bv[1].  Each barrier gets exactly one arrival per phase (zero bytes when the CTA has
-// no tile in that stage), so a barrier's k-th completion always belongs to its k-th phase.
-template <typename T>
-__device__ __forceinline__ void chain_issue(const Params &p, uint8_t *smem, uint64_t *bv) {
-    const int tid = threadIdx.x;
-    int t1b, t1e, t2b, t2e;
-    tile_range(p.tiles1, blockIdx.x, gridDim.x, t1b, t1e);
-    tile_range(p.tiles2, blockIdx.x, gridDim.x, t2b, t2e);
-    const bool has1 = t1e > t1b, has2 = t2e > t2b;
-    const int in_pad = p.kb1 * 64;
-    T *s2s = reinterpret_cast<T *>(smem + p.off_s2);
-    uint32_t *vch = reinterpret_cast<uint32_t *>(smem + p.off_v);
-    uint32_t *uch = reinterpret_cast<uint32_t *>(smem + p.off_u);
-    T *s1s = reinterpret_cast<T *>(smem + p.off_s1);
-    if (tid == 0) {
-        uint32_t bytes0 = 0;
-        if (has1) {
-            for (int l = 0; l < p.nm; ++l) {
-                const Member &mb = p.m[l];
-                const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
-                if (a < b)
-                    bytes0 += slab_bulk_bytes(16 * (a - mb.t1_start), min(16 * (b - mb.t1_start), mb.rank), p.wv,
-                                              p.v_rows);
-            }
-            bytes0 += (uint32_t)p.in_f * 2u * (uint32_t)p.nm;
-        }
-        mbar_arrive_expect_tx(&bv[0], bytes0);
-        if (has1)
-            for (int l = 0; l < p.nm; ++l)
-                bulk_g2s_pieces(s2s + (size_t)l * in_pad, p.m[l].s2, (uint32_t)p.in_f * 2u, &bv[0]);
-    }
-    if (tid == 32) {
-        uint32_t bytes1 = 0;
-        if (has2)
-            for (int l = 0; l < p.nm; ++l) {
-                const Member &mb = p.m[l];
-                int a, b;
-                seg_tiles(mb, t2b, t2e, a, b);
-                if (a >= b) continue;
-                const int r0 = 16 * (a - mb.t2_start), r1 = min(16 * (b - mb.t2_start), mb.out_f);
-                bytes1 += slab_bulk_bytes(r0, r1, mb.wu, mb.u_rows);
-                const T *s1src = static_cast<const T *>(mb.s1) + r0;
-                if ((reinterpret_cast<uintptr_t>(s1src) & 15) == 0) bytes1 += ((uint32_t)(r1 - r0) * 2u) & ~15u;
-            }
-        mbar_arrive_expect_tx(&bv[1], bytes1);
-    }
-    __syncwarp();
-    if (has1) {
-        for (int l = 0; l < p.nm; ++l) {
-            const Member &mb = p.m[l];
-            const int a = max(t1b, mb.t1_start), b = min(t1e, mb.t1_start + mb.tiles1);
-            if (a < b)
-                copy_slab(vch + (size_t)16 * (a - t1b) * p.wvs, mb.vbits, 16 * (a - mb.t1_start),
-                          min(16 * (b - mb.t1_start), mb.rank), p.wv, p.wvs, p.v_rows, &bv[0], 0);
-        }
-        for (int l = 0; l < p.nm; ++l) zero_tail<T>(s2s + (size_t)l * in_pad, p.in_f, in_pad);
-    }
-    if (has2) {
-        uint32_t uoff = 0;  // words; same segment layout stage2_items assumes
-        for (int l = 0; l < p.nm; ++l) {
-            const Member &mb = p.m[l];
-            int a, b;
-            seg_tiles(mb, t2b, t2e, a, b);
-            if (a >= b) continue;
-            const int r0 = 16 * (a - mb.t2_start), r1 = min(16 * (b - mb.t2_start), mb.out_f);
-            copy_slab(uch + uoff, mb.ubits, r0, r1, mb.wu, mb.wus, mb.u_rows, &bv[1], 1);
-            uoff += (uint32_t)(16 * (b - a)) * (uint32_t)mb.wus;
-            uoff = (uoff + 3u) & ~3u;
-            const T *s1src = static_cast<const T *>(mb.s1) + r0;
-            T *s1dst = s1s + 16 * (a - t2b);
-            const uint32_t s1_bulk =
-                (reinterpret_cast<uintptr_t>(s1src) & 15) == 0 ? ((uint32_t)(r1 - r0) * 2u) & ~15u : 0u;
-            if (tid == 32 && s1_bulk) bulk_g2s(s1dst, s1src, s1_bulk, &bv[1]);
-            for (int i = (int)(s1_bulk / 2) + tid; i < r1 - r0; i += kThreads) s1dst[i] = s1src[i];
-        }
-    }
-}
-
-// xs2[l][2b (+1)][k] = bf16 hi (lo) of x'[b][k] * s2_l[k], x' formed per ph.xmode from global
-// memory written by earlier phases (read through L2: __ldcg).
-template <typename T>
-__device__ __forceinline__ void chain_fold(const ChainPhase &ph, uint8_t *smem, float *sred) {
-    using E = Elem<T>;
-    const Params &p = ph.g;
-    const int tid = threadIdx.x;
-    const int in_pad = p.kb1 * 64, chunks = in_pad / 8, nxc = 2 * p.batch;
-    const int nfull = p.in_f / 8;  // in_f % 8 == 0
-    const T *s2s = reinterpret_cast<const T *>(smem + p.off_s2);
-    __nv_bfloat16 *xs2 = reinterpret_cast<__nv_bfloat16 *>(smem + p.off_xs2);
-    auto emit = [&](int b, int ch, const float (&xf)[8]) {
-        for (int l = 0; l < p.nm; ++l) {
-            float sf[8];
-            unpack8<T>(*reinterpret_cast<const uint4 *>(s2s + (size_t)l * in_pad + 8 * ch), sf);
-            uint32_t hi[4], lo[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) split_pair(xf[2 * j] * sf[2 * j], xf[2 * j + 1] * sf[2 * j + 1], hi[j], lo[j]);
-            __nv_bfloat16 *dst = xs2 + ((size_t)l * nxc + 2 * b) * in_pad + 8 * ch;
-            *reinterpret_cast<uint4 *>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4 *>(dst + in_pad) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        }
-    };
-    // every global load of a pass is issued before the first use (one L2 round trip per pass)
-    for (int b = 0; b < p.batch; ++b) {
-        const uint4 *xr = reinterpret_cast<const uint4 *>(static_cast<const T *>(p.x) + (size_t)b * p.in_f);
-        if (ph.xmode == kChainNorm) {
-            const uint4 *wr = reinterpret_cast<const uint4 *>(ph.nw);
-            uint4 hv[kNormMaxChunks], wv[kNormMaxChunks];
-#pragma unroll
-            for (int j = 0; j < kNormMaxChunks; ++j) {
-                const int ch = tid + j * kThreads;
-                if (ch < nfull) {
-                    hv[j] = __ldcg(xr + ch);
-                    wv[j] = __ldg(wr + ch);
-                }
-            }
-            float ss = 0.f;
-#pragma unroll
-            for (int j = 0; j < kNormMaxChunks; ++j) {
-                if (tid + j * kThreads < nfull) {
-                    float f[8];
-                    unpack8<T>(hv[j], f);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
-                }
-            }
-            const float inv = rsqrtf(block_sum_512(ss, sred) / (float)p.in_f + ph.eps);
-#pragma unroll
-            for (int j = 0; j < kNormMaxChunks; ++j) {
-                const int ch = tid + j * kThreads;
-                if (ch >= chunks) continue;
-                float xf[8];
-                if (ch < nfull) {
-                    float h[8], w[8];
-                    unpack8<T>(hv[j], h);
-                    unpack8<T>(wv[j], w);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) xf[e] = E::to_f(E::rn(w[e] * E::to_f(E::rn(h[e] * inv))));
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) xf[e] = 0.f;
-                }
-                emit(b, ch, xf);
-            }
-        } else {
-            const bool two = ph.xmode == kChainSiluMul || ph.xmode == kChainMul;
-            const bool silu = ph.xmode == kChainSiluMul;
-            const uint4 *ur =
-                two ? reinterpret_cast<const uint4 *>(static_cast<const T *>(ph.x2) + (size_t)b * p.in_f) : nullptr;
-            constexpr int J = 4;
-            for (int base = 0; base < chunks; base += J * kThreads) {
-                uint4 av[J], uv[J];
-#pragma unroll
-                for (int j = 0; j < J; ++j) {
-                    const int ch = base + tid + j * kThreads;
-                    if (ch < nfull) {
-                        av[j] = __ldcg(xr + ch);
-                        if (ur) uv[j] = __ldcg(ur + ch);
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < J; ++j) {
-                    const int ch = base + tid + j * kThreads;
-                    if (ch >= chunks) continue;
-                    float xf[8];
-                    if (ch >= nfull) {
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) xf[e] = 0.f;
-                    } else if (ur) {
-                        float gt[8], up[8];
-                        unpack8<T>(av[j], gt);
-                        unpack8<T>(uv[j], up);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            const float sg = silu ? E::to_f(E::rn(gt[e] / (1.f + expf(-gt[e])))) : gt[e];
-                            xf[e] = E::to_f(E::rn(sg * up[e]));
-                        }
-                    } else {
-                        unpack8<T>(av[j], xf);
-                    }
-                    emit(b, ch, xf);
-                }
-            }
-        }
-    }
-}
-
-// The stage bodies as the chain kernel runs them (inlined: out of line, the shared-memory
-// pointers would become generic ones).
-template <typename T>
-__device__ __forceinline__ void chain_stage1(const Params &p, uint8_t *smem, int t1b, int t1e, bool ok, WarpTab *wt) {
-    const __nv_bfloat16 *xs2 = reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2);
-    float *red = reinterpret_cast<float *>(smem + p.off_red);
-    stage1_items<T, 1>(p, reinterpret_cast<const uint32_t *>(smem + p.off_v), reinterpret_cast<const T *>(smem + p.off_s2),
-                    reinterpret_cast<const T *>(xs2), xs2, red, t1b, t1e, ok, wt);
-    __syncthreads();
-    stage1_finish<T, 1>(p, red, t1b, t1e, wt);
-}
-template <typename T>
-__device__ __forceinline__ void chain_stage2(const Params &p, uint8_t *smem, int t2b, int t2e, bool ok, const void *res,
-                                             int act, WarpTab *wt) {
-    float *red = reinterpret_cast<float *>(smem + p.off_red);
-    stage2_items<T, 1>(p, reinterpret_cast<const uint32_t *>(smem + p.off_u), red, t2b, t2e, ok,
-                       reinterpret_cast<const __nv_bfloat16 *>(smem + p.off_xs2), wt);
-    __syncthreads();
-    stage2_finish<T>(p, red, reinterpret_cast<const T *>(smem + p.off_s1), t2b, t2e, res, act, wt);
-}
-
-// Phase k of the chain.  One copy of the code serves every phase (a copy per phase would not
-// stay in the instruction cache); the runtime index into the parameter block becomes indexed
-// constant-bank loads.
-template <typename T>
-__device__ __forceinline__ void chain_phase(const ChainParams &cp, int k, uint8_t *smem, float *sred, WarpTab *wt,
-                                            bool &ok, unsigned long long bar_base) {
-    const ChainPhase &ph = cp.ph[k];
-    const Params &p = ph.g;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // [region][V side, U side]
-    uint64_t *bv = &bars[2 * (k & 1)];
-    const uint32_t par = (uint32_t)(k >> 1) & 1u;
-    Ctrl *ctrl = p.ctrl;
-    const unsigned G = gridDim.x;
-    if (k > 0) {
-        if (!grid_barrier(ctrl, bar_base + (unsigned long long)(2 * k) * G)) ok = false;  // phase k-1's outputs
-        if (k + 1 < cp.nph) {  // region (k+1)&1 is free: phase k-1 is done
-            fence_proxy_async_smem();
-            chain_issue<T>(cp.ph[k + 1].g, smem, &bars[2 * ((k + 1) & 1)]);
-        }
-    }
-    int t1b, t1e, t2b, t2e;
-    tile_range(p.tiles1, blockIdx.x, G, t1b, t1e);
-    tile_range(p.tiles2, blockIdx.x, G, t2b, t2e);
-    if (t1e > t1b) {
-        if (!mbar_wait(&bv[0], par, &ctrl->status)) ok = false;
-        chain_fold<T>(ph, smem, sred);
-        __syncthreads();
-        chain_stage1<T>(p, smem, t1b, t1e, ok, wt);
-    }
-    if (!grid_barrier(ctrl, bar_base + (unsigned long long)(2 * k + 1) * G)) ok = false;  // t is complete
-    // The t columns of the members this CTA serves go to the (now idle) fold buffer, one bulk
-    // copy per member and column; the barrier completes once per phase (zero bytes if no tile).
-    uint64_t *tbar = &bars[4];
-    if (threadIdx.x == 0) {
-        fence_proxy_async_global();  // t was written through the generic proxy by other CTAs
-        fence_proxy_async_smem();    // the fold buffer was written and read through it here
-        uint32_t bytes = 0;
-        for (int l = 0; l < p.nm && t2e > t2b; ++l) {
-            int a, b;
-            seg_tiles(p.m[l], t2b, t2e, a, b);
-            if (a < b) bytes += (uint32_t)(2 * p.batch) * (uint32_t)p.m[l].ldi * 2u;
-        }
-        mbar_arrive_expect_tx(tbar, bytes);
-        __nv_bfloat16 *tsm = reinterpret_cast<__nv_bfloat16 *>(smem + p.off_xs2);
-        for (int l = 0; l < p.nm && t2e > t2b; ++l) {
-            const Member &mb = p.m[l];
-            int a, b;
-            seg_tiles(mb, t2b, t2e, a, b);
-            if (a >= b) continue;
-            for (int c = 0; c < 2 * p.batch; ++c)
-                bulk_g2s(tsm + mb.tbs + (size_t)c * mb.ldis, mb.tb + (size_t)c * mb.ldi, (uint32_t)mb.ldi * 2u, tbar);
-        }
-    }
-    if (t2e > t2b) {
-        if (!mbar_wait(tbar, (uint32_t)k & 1u, &ctrl->status)) ok = false;
-        if (!mbar_wait(&bv[1], par, &ctrl->status)) ok = false;
-        chain_stage2<T>(p, smem, t2b, t2e, ok, ph.res, ph.act, wt);
-    }
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) chain_kernel(const ChainParams cp) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float sred[kWarps];
-    __shared__ WarpTab wtab;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-    unsigned long long bar_base = 0;  // thread 0 only
-    if (threadIdx.x == 0) {
-        bar_base = grid_barrier_base(cp.ph[0].g.ctrl, gridDim.x);
-#pragma unroll
-        for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);  // 2 regions x (V, U), staged t
-        fence_mbar_init();
-    }
-    __syncthreads();
-    chain_issue<T>(cp.ph[0].g, smem, &bars[0]);
-    if (cp.nph > 1) chain_issue<T>(cp.ph[1].g, smem, &bars[2]);
-    bool ok = true;
-    for (int k = 0; k < cp.nph; ++k) chain_phase<T>(cp, k, smem, sred, &wtab, ok, bar_base);
-}
-
-// Host: validate the phases, build their Params, lay out shared memory.  `launch` = false
-// plans only (the workspace query).
-static int chain_impl(int dtype, int64_t batch, int n, const nq_chain_phase *phases, void *workspace,
-                      size_t workspace_bytes, void *stream, bool launch, size_t *ws_need) {
-    if (dtype != NQ_DTYPE_F16 && dtype != NQ_DTYPE_BF16)
-        return fail(NQ_ERR_UNSUPPORTED, "dtype must be NQ_DTYPE_F16 or NQ_DTYPE_BF16 (got %d)", dtype);
-    if (n < 1 || n > kMaxPhases) return fail(NQ_ERR_INVALID_ARGUMENT, "a chain holds 1..%d phases (got %d)", kMaxPhases, n);
-    if (!phases) return fail(NQ_ERR_INVALID_ARGUMENT, "null phase array");
-    if (batch < 1 || batch > kFoldMaxBatch)
-        return fail(NQ_ERR_UNSUPPORTED, "a chain runs batch 1..%d (got %lld)", kFoldMaxBatch, (long long)batch);
-    // Planning needs no GPU: without one it assumes a B200 (148 SMs, 227 KiB of shared memory
-    // per block), so the workspace query also works on a build machine.
-    int dev = 0;
-    DeviceInfo di;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) {
-        di = device_info(dev);
-    } else {
-        if (launch) return cuda_fail(e, "cudaGetDevice");
-        cudaGetLastError();
-    }
-    if (launch && di.cc_major != 10)
-        return fail(NQ_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", dev, di.cc_major, di.cc_minor);
-    const int G = di.sms > 0 ? di.sms : 148;
-    const int smem_optin = di.max_smem_optin > 0 ? di.max_smem_optin : 232448;
-    ChainParams cp{};
-    cp.nph = n;
-    size_t need = sizeof(Ctrl);
-    int max_slots = kWarps;
-    size_t xs2_bytes = 0, region[2] = {0, 0};
-    const uintptr_t ws_base = reinterpret_cast<uintptr_t>(workspace);
-    for (int k = 0; k < n; ++k) {
-        const nq_chain_phase &P = phases[k];
-        ChainPhase &ph = cp.ph[k];
-        Params &p = ph.g;
-        if (P.n_layers < 1 || P.n_layers > kMaxGroup)
-            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: 1..%d layers (got %d)", k, kMaxGroup, P.n_layers);
-        if (P.x_mode != kChainPlain && P.x_mode != kChainNorm && P.x_mode != kChainSiluMul && P.x_mode != kChainMul)
-            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: unknown x_mode %d", k, P.x_mode);
-        if (P.act & ~((1 << P.n_layers) - 1))
-            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: act bit beyond its %d layers", k, P.n_layers);
-        if (P.in_features <= 0 || P.in_features % 8 || P.in_features > (1 << 20))
-            return fail(NQ_ERR_UNSUPPORTED, "phase %d: in_features must be a positive multiple of 8 (got %lld)", k,
-                        (long long)P.in_features);
-        if (!P.x || ((P.x_mode == kChainSiluMul || P.x_mode == kChainMul) && !P.x2) ||
-            (P.x_mode == kChainNorm && !P.norm_weight))
-            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: missing input tensor", k);
-        if ((reinterpret_cast<uintptr_t>(P.x) | reinterpret_cast<uintptr_t>(P.x2) |
-             reinterpret_cast<uintptr_t>(P.norm_weight)) & 15)
-            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: x, x2 and norm_weight must be 16-byte aligned", k);
-        if (P.x_mode == kChainNorm && P.in_features > (int64_t)kNormMaxChunks * 8 * kThreads)
-            return fail(NQ_ERR_UNSUPPORTED, "phase %d: RMSNorm rows are limited to %d values", k,
-                        kNormMaxChunks * 8 * kThreads);
-        if (P.residual && P.n_layers != 1)
-            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: a residual needs a single-layer phase", k);
-        if (reinterpret_cast<uintptr_t>(P.residual) & 1)
-            return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d: residual must be 2-byte aligned", k);
-        p.ctrl = static_cast<Ctrl *>(workspace);
-        p.x = P.x;
-        p.batch = (int)batch;
-        p.in_f = (int)P.in_features;
-        p.wv = (int)((P.in_features + 31) / 32);
-        p.kb1 = (p.wv + 1) / 2;
-        p.nm = P.n_layers;
-        p.mode = kFused;
-        p.fold = 1;
-        p.x_in_smem = 0;
-        ph.x2 = P.x2;
-        ph.nw = P.norm_weight;
-        ph.res = P.residual;
-        ph.eps = P.eps;
-        ph.xmode = P.x_mode;
-        ph.act = P.act;
-        int t1 = 0, t2 = 0;
-        for (int l = 0; l < P.n_layers; ++l) {
-            const nq_gemv_layer &L = P.layers[l];
-            if (!L.scale_pre || !L.v_bits || !L.u_bits || !L.scale_post || !L.y)
-                return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d layer %d: null tensor pointer", k, l);
-            if (L.rank <= 0 || L.out_features <= 0 || L.rank > (1 << 20) || L.out_features > (1 << 24))
-                return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d layer %d: bad sizes (rank=%lld out=%lld)", k, l,
-                            (long long)L.rank, (long long)L.out_features);
-            if (reinterpret_cast<uintptr_t>(L.scale_pre) & 15)
-                return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d layer %d: scale_pre must be 16-byte aligned", k, l);
-            if ((reinterpret_cast<uintptr_t>(L.scale_post) | reinterpret_cast<uintptr_t>(L.y) |
-                 reinterpret_cast<uintptr_t>(L.scale_mid)) & 1)
-                return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d layer %d: 16-bit tensors must be 2-byte aligned", k, l);
-            if ((reinterpret_cast<uintptr_t>(L.v_bits) | reinterpret_cast<uintptr_t>(L.u_bits)) & 15)
-                return fail(NQ_ERR_INVALID_ARGUMENT, "phase %d layer %d: sign planes must be 16-byte aligned", k, l);
-            Member &mb = p.m[l];
-            mb.s2 = L.scale_pre;
-            mb.vbits = reinterpret_cast<const uint32_t *>(L.v_bits);
-            mb.smid = L.scale_mid;
-            mb.ubits = reinterpret_cast<const uint32_t *>(L.u_bits);
-            mb.s1 = L.scale_post;
-            mb.y = L.y;
-            mb.rank = (int)L.rank;
-            mb.out_f = (int)L.out_features;
-            mb.wu = (int)((L.rank + 31) / 32);
-            mb.kb2 = (mb.wu + 1) / 2;
-            mb.ldi = mb.kb2 * 64;
-            mb.tiles1 = (int)((L.rank + 15) / 16);
-            mb.tiles2 = (int)((L.out_features + 15) / 16);
-            mb.t1_start = t1;
-            mb.t2_start = t2;
-            t1 += mb.tiles1;
-            t2 += mb.tiles2;
-            mb.tb = reinterpret_cast<__nv_bfloat16 *>(ws_base + need);  // tb regions follow the control block
-            need += tb_bytes(L.rank);
-            mb.u_rows = 0;
-            mb.wus = mb.u_rows ? padded_stride(mb.wu) : mb.wu;
-        }
-        if (t1 > 65536 || t2 > 65536) return fail(NQ_ERR_UNSUPPORTED, "phase %d: layer group too large", k);
-        p.tiles1 = t1;
-        p.tiles2 = t2;
-        p.v_rows = 0;  // one contiguous copy per slab (see layout())
-        p.wvs = p.v_rows ? padded_stride(p.wv) : p.wv;
-        const int tpc1 = (t1 + G - 1) / G, tpc2 = (t2 + G - 1) / G;
-        p.kbu2 = 1;
-        for (int l = 0; l < p.nm; ++l) p.kbu2 = std::max(p.kbu2, p.m[l].kb2);
-        p.seg1 = seg_bound(tpc1, p.kb1);
-        p.seg2 = seg_bound(tpc2, p.kbu2);
-        max_slots = std::max(max_slots, kWarps * std::max(p.seg1, p.seg2));
-        const size_t in_pad = (size_t)p.kb1 * 64;
-        xs2_bytes = std::max(xs2_bytes, (size_t)p.nm * 2 * (size_t)batch * in_pad * 2);
-        // stage 2 reuses the fold buffer for the members' t columns, column stride ldi + 8
-        // (16 bytes of padding keep the columns on different banks)
-        size_t staged = 0;
-        for (int l = 0; l < p.nm; ++l) {
-            p.m[l].ldis = p.m[l].ldi + 8;
-            p.m[l].tbs = (int)staged;
-            staged += (size_t)2 * batch * p.m[l].ldis;
-        }
-        xs2_bytes = std::max(xs2_bytes, staged * 2);
-        int max_wus = 0;
-        for (int l = 0; l < p.nm; ++l) max_wus = std::max(max_wus, p.m[l].wus);
-        // region-relative offsets; made absolute below
-        size_t off = 0;
-        p.off_s2 = (uint32_t)off;
-        off = align128(off + (size_t)p.nm * in_pad * 2);
-        p.off_v = (uint32_t)off;
-        off = align128(off + (size_t)16 * tpc1 * p.wvs * 4 + 16);
-        p.off_u = (uint32_t)off;
-        off = align128(off + ((size_t)16 * tpc2 * max_wus + 4 * (size_t)p.nm) * 4 + 16);
-        p.off_s1 = (uint32_t)off;
-        off = align128(off + (size_t)16 * tpc2 * 2 + 16);
-        region[k & 1] = std::max(region[k & 1], off);
-    }
-    const size_t off_red = 128;  // four mbarriers first
-    const size_t off_xs2 = align128(off_red + (size_t)max_slots * 256 * sizeof(float));
-    const size_t off_r0 = align128(off_xs2 + xs2_bytes);
-    const size_t off_r1 = align128(off_r0 + region[0]);
-    const size_t smem = off_r1 + region[1];
-    const size_t cap = (size_t)smem_optin - kStaticSmemReserve;
-    if (ws_need) *ws_need = need;
-    if (smem > cap)
-        return fail(NQ_ERR_UNSUPPORTED, "chain needs %zu bytes of shared memory per SM (limit %zu)", smem, cap);
-    if (!launch) return NQ_OK;
-    if (!di.coop) return fail(NQ_ERR_UNSUPPORTED, "device %d lacks cooperative launch", dev);
-    if (!workspace || workspace_bytes < need)
-        return fail(NQ_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
-    if (reinterpret_cast<uintptr_t>(workspace) & 255)
-        return fail(NQ_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
-    for (int k = 0; k < n; ++k) {
-        Params &p = cp.ph[k].g;
-        const size_t base = (k & 1) ? off_r1 : off_r0;
-        p.off_red = (uint32_t)off_red;
-        p.off_xs2 = (uint32_t)off_xs2;
-        p.off_x = (uint32_t)off_xs2;
-        p.off_s2 += (uint32_t)base;
-        p.off_v += (uint32_t)base;
-        p.off_u += (uint32_t)base;
-        p.off_s1 += (uint32_t)base;
-    }
-    static bool attr_set[2][64] = {};
-    const int ti = dtype == NQ_DTYPE_F16 ? 0 : 1;
-    if (dev >= 0 && dev < 64 && !attr_set[ti][dev]) {
-        e = ti == 0 ? cudaFuncSetAttribute(chain_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cap)
-                    : cudaFuncSetAttribute(chain_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)cap);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain)");
-        attr_set[ti][dev] = true;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)G);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = static_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = ti == 0 ? cudaLaunchKernelEx(&cfg, chain_kernel<__half>, cp) : cudaLaunchKernelEx(&cfg, chain_kernel<__nv_bfloat16>, cp);
-    return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv chain launch");
-}
-
 // Standalone PULL (the final norm after the last row-parallel layer): one CTA sums the ranks'
 // buffers into `out` and advances every GEMV CTA's pull epoch, keeping them in step.
 template <typename T>
@@ -2018,17 +1496,6 @@ int nq_tp_pull(int dtype, const nq_tp_exchange *tp, int64_t n, void *out, void *
         tp_pull_kernel<__nv_bfloat16><<<1, 512, 0, s>>>(tpx, n, static_cast<__nv_bfloat16 *>(out));
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? NQ_OK : nq::cuda_fail(e, "exchange pull launch");
-}
-
-size_t nq_gemv_chain_workspace_bytes(int dtype, int64_t batch, int n_phases, const nq_chain_phase *phases) {
-    size_t need = 0;
-    const int st = nq::gemv::chain_impl(dtype, batch, n_phases, phases, nullptr, 0, nullptr, false, &need);
-    return st == NQ_OK ? need : 0;
-}
-
-int nq_gemv_chain(int dtype, int64_t batch, int n_phases, const nq_chain_phase *phases, void *workspace,
-                  size_t workspace_bytes, void *stream) {
-    return nq::gemv::chain_impl(dtype, batch, n_phases, phases, workspace, workspace_bytes, stream, true, nullptr);
 }
 
 size_t nq_gemv_workspace_bytes(int64_t batch, int64_t rank) {

@@ -218,7 +218,7 @@ class Decoder:
 
     def __init__(self, cfg: DecoderConfig, max_seq: int, batch: int = 1, tp_rank: int = 0, tp: int = 1,
                  group=None, seed: int = 0, dtype=torch.float16, device=None, with_mid: bool = False,
-                 chain: bool = False, peer_allreduce: bool = False, tp_exchange: bool = True,
+                 peer_allreduce: bool = False, tp_exchange: bool = True,
                  weights: Optional[dict] = None):
         """``weights`` (from nanoquant_b200.loader) replaces the seeded random weights: "embed",
         "lm_head", "final_norm" tensors and "layers", one dict per layer with "in_norm",
@@ -266,10 +266,6 @@ class Decoder:
         self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.seq_len = torch.ones(batch, dtype=torch.int32, device=dev)
         self.next_tokens = torch.zeros(batch, dtype=torch.long, device=dev)
-        # `chain`: decode through GEMV chains (one launch per block besides attention) where the
-        # block's chain can run: one GPU (the chain has no all-reduce), batch <= 2, and the
-        # weight slabs of consecutive phases fit shared memory.  Off by default: on B200 the
-        # chain is still slower than the separate launches it replaces.
         # RMSNorm / SiLU*up folded into the GEMV prologues and the gate's SiLU into its epilogue
         # (nq_gemv_group_ex); batches above 8 use the separate kernels.
         self.fuse_neighbours = True
@@ -292,14 +288,6 @@ class Decoder:
         self.tpx = None
         if tp > 1 and tp_exchange and not peer_allreduce and batch <= 8 and self.fuse_neighbours:
             self.tpx = TPExchange(group, tp_rank, tp, batch * cfg.hidden, dev)
-        self.chain_ws = None
-        if chain and tp == 1:
-            h = torch.empty(batch, cfg.hidden, device=dev, dtype=dtype)
-            a = torch.empty(batch, self.hq * cfg.head_dim, device=dev, dtype=dtype)
-            phases, _ = self._block_phases(0, a, h, alloc=False)
-            n = nqchain.workspace_bytes(phases, batch)
-            if n:
-                self.chain_ws = torch.zeros(n, dtype=torch.uint8, device=dev)
 
     # ------------------------------------------------------------------ pieces
     def _norm_prologue_fits(self) -> bool:
@@ -386,44 +374,6 @@ class Decoder:
         return nxt
 
     # ------------------------------------------------------------------ decode
-    def _qkv_phase(self, li: int, h: torch.Tensor, alloc: bool = True):
-        """Block li's q/k/v from RMSNorm(h) (the block's input norm)."""
-        lay, B, dev, dt = self.layers[li], self.batch, self.device, self.dtype
-        outs = [torch.empty(B, m.s1.numel(), device=dev, dtype=dt) for m in lay["qkv"].members] if alloc else None
-        return nqchain.Phase(lay["qkv"].members, h, nqchain.RMSNORM, norm_weight=lay["in_norm"], eps=self.cfg.rms_eps,
-                             out=outs)
-
-    def _block_phases(self, li: int, a: torch.Tensor, h: torch.Tensor, alloc: bool = True):
-        """Chain of block li after attention: o (+ residual into h), gate/up from RMSNorm(h)
-        (SiLU on the gate), down from silu(gate) * up (+ residual into h), then block li+1's q/k/v."""
-        cfg, lay, B = self.cfg, self.layers[li], self.batch
-        gate = torch.empty(B, cfg.ffn // self.tp, device=self.device, dtype=self.dtype)
-        up = torch.empty_like(gate)
-        # the gate's SiLU is applied once per value in its own epilogue; down multiplies by up
-        phases = [nqchain.Phase([lay["o"]], a, residual=h, out=[h]),
-                  nqchain.Phase([lay["gate"], lay["up"]], h, nqchain.RMSNORM, norm_weight=lay["post_norm"],
-                                eps=cfg.rms_eps, out=[gate, up], act=1),
-                  nqchain.Phase([lay["down"]], gate, nqchain.MUL, x2=up, residual=h, out=[h])]
-        if li + 1 < cfg.layers:
-            phases.append(self._qkv_phase(li + 1, h, alloc))
-        return phases, (gate, up)
-
-    @torch.no_grad()
-    def _step_logits_chain(self) -> torch.Tensor:
-        cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
-        h = F.embedding(self.tokens, self.embed)  # the residual stream; the chains update it in place
-        q, k, v = nqchain.run([self._qkv_phase(0, h)], self.chain_ws)[0]
-        for li in range(cfg.layers):
-            a = torch.ops.nq_b200.decode_attention_rope(q.view(B, self.hq, D), k.view(B, self.hkv, D),
-                                                        v.view(B, self.hkv, D), self.pos, self.k_cache[li],
-                                                        self.v_cache[li], cfg.rope_theta)
-            phases, _ = self._block_phases(li, a.view(B, self.hq * D), h)
-            outs = nqchain.run(phases, self.chain_ws)
-            if li + 1 < cfg.layers:
-                q, k, v = outs[3]
-        x, _ = torch.ops.nq_b200.rmsnorm(h, None, self.final_norm, cfg.rms_eps)
-        return x @ self.lm_head.t()
-
     @torch.no_grad()
     def _step_logits_fused(self) -> torch.Tensor:
         """Five launches per block: q/k/v with RMSNorm(x + residual) in its prologue, attention
@@ -507,16 +457,12 @@ class Decoder:
         ar = 2 * n if self.peer_ar is not None else 0  # peer all-reduces (o and down of every block)
         if self.tpx is not None:  # sums inside the GEMVs; one standalone pull before the final norm
             return n * (5 if self.fuse_down else 6) + 1 + 1
-        if self.chain_ws is not None:
-            return 1 + n * 2 + 1        # first q/k/v chain; attention + block chain per layer; final norm
         if self.fuse_neighbours and self.batch <= 8:
             return n * (5 if self.fuse_down else 6) + 1 + ar  # q/k/v, attention, o, gate/up, (SiLU*up,) down; final norm
         return n * (4 + 2 + 1 + 1) + 1 + ar  # four GEMVs, two norms, attention, SiLU·up; final norm
 
     def step_logits(self) -> torch.Tensor:
         """Logits for the current tokens at the current positions (writes the caches)."""
-        if self.chain_ws is not None:
-            return self._step_logits_chain()
         if self.fuse_neighbours and self.batch <= 8:
             return self._step_logits_fused()
         cfg, B, D = self.cfg, self.batch, self.cfg.head_dim

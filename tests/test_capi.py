@@ -114,39 +114,6 @@ def test_pack_rejects_bad_arguments_on_host():
         _lib.check(_lib.NQ_ERR_INVALID_ARGUMENT)
 
 
-def _fake_layer(out_f, in_f, r):
-    import torch
-    from types import SimpleNamespace as NS
-    return NS(s2=torch.empty(in_f, dtype=torch.float16), vb=torch.empty(r, (in_f + 31) // 32, dtype=torch.int32),
-              smid=None, ub=torch.empty(out_f, (r + 31) // 32, dtype=torch.int32),
-              s1=torch.empty(out_f, dtype=torch.float16))
-
-
-def test_chain_planning_without_a_gpu():
-    """The chain workspace query plans on the host only: the 7B decoder-block chain fits one
-    SM's shared memory at batch 1; unsupported chains return 0 with a reason."""
-    import torch
-    from nanoquant_b200 import chain
-    h, a = torch.empty(1, 4096, dtype=torch.float16), torch.empty(1, 4096, dtype=torch.float16)
-    g, u = torch.empty(1, 11008, dtype=torch.float16), torch.empty(1, 11008, dtype=torch.float16)
-    nw = torch.empty(4096, dtype=torch.float16)
-    attn, mlp_in, mlp_out = _fake_layer(4096, 4096, 1126), _fake_layer(11008, 4096, 2054), _fake_layer(4096, 11008, 2054)
-    block = [chain.Phase([attn], a, residual=h, out=[h]),
-             chain.Phase([mlp_in, mlp_in], h, chain.RMSNORM, norm_weight=nw, out=[g, u]),
-             chain.Phase([mlp_out], g, chain.SILU_MUL, x2=u, residual=h, out=[h]),
-             chain.Phase([attn] * 3, h, chain.RMSNORM, norm_weight=nw)]
-    # control block + each member's stage-2 operand: 16 x round_up(rank, 64) bf16
-    tb = lambda r: 16 * ((r + 63) // 64) * 64 * 2
-    assert chain.workspace_bytes(block, 1) == 256 + 4 * tb(1126) + 3 * tb(2054)
-    assert chain.workspace_bytes(block, 3) == 0 and "batch" in chain.why_not()
-    bad = [chain.Phase([mlp_in, mlp_in], h, residual=h)]
-    assert chain.workspace_bytes(bad, 1) == 0 and "residual" in chain.why_not()
-    wide = torch.empty(1, 20480, dtype=torch.float16)
-    big = [chain.Phase([_fake_layer(64, 20480, 64)], wide, chain.RMSNORM, norm_weight=torch.empty(20480))]
-    assert chain.workspace_bytes(big, 1) == 0 and "RMSNorm" in chain.why_not()
-    assert chain.workspace_bytes(block * 2, 1) == 0  # more than NQ_CHAIN_MAX_PHASES
-
-
 @pytest.mark.parametrize("case", ["mode", "no_x2", "no_weight", "unaligned", "act", "batch"])
 def test_group_ex_rejects_bad_input_descriptors_on_host(case):
     lib = _lib.cuda_lib()
