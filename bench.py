@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--attention", type=int, default=None, metavar="L",
                     help="the fused decode attention (RoPE + cache write + split-KV attention) of --model at "
                          "sequence length L instead of whole-model decode: KV-cache GB/s over 8 caches cycled")
+    ap.add_argument("--max-seq", type=int, default=None,
+                    help="--attention: KV-cache capacity in positions (default L + 64 rounded up to a multiple of 64); "
+                         "the kernel's chunking and the cache layout follow it")
     ap.add_argument("--gemm", default=None, metavar="M,OUT,IN,RANK",
                     help="the prefill GEMM of one layer instead of whole-model decode (e.g. 2048,11008,4096,2054): "
                          "TFLOP/s counting the two rank-r contractions, 2*M*r*(in+out), over --copies weight copies")
@@ -707,7 +710,7 @@ def run_attention(args):
     cfg = CONFIGS[args.model]
     L, B, D = args.attention, args.batch, cfg.head_dim
     dev = torch.device("cuda", 0)
-    max_seq = L + 64
+    max_seq = args.max_seq if args.max_seq else (L + 64 + 63) // 64 * 64
     caches = [(torch.randn(B, cfg.kv_heads, max_seq, D, device=dev).half(),
                torch.randn(B, cfg.kv_heads, max_seq, D, device=dev).half()) for _ in range(8)]
     q = torch.randn(B, cfg.heads, D, device=dev).half()
@@ -732,8 +735,8 @@ def run_attention(args):
     peak, kind = peaks()
     gbs = kv / (us * 1e-6) / 1e9
     print(json.dumps({"metric": "decode attention GB/s (KV-cache bytes)", "value": round(gbs, 2), "unit": "GB/s",
-                      "attention": {"model": cfg.name, "seq_len": L, "batch": B, "heads": cfg.heads,
-                                    "kv_heads": cfg.kv_heads}, "us_per_launch": round(us, 3), "bytes_per_launch": kv,
+                      "attention": {"model": cfg.name, "seq_len": L, "max_seq": max_seq, "batch": B,
+                                    "heads": cfg.heads, "kv_heads": cfg.kv_heads}, "us_per_launch": round(us, 3), "bytes_per_launch": kv,
                       "launches": n, "roofline": {"bound": "hbm", "peak": peak, "frac": round(gbs / peak, 5),
                                                   "peak_source": kind},
                       "dtype": "f16", "data": "synthetic"}), flush=True)

@@ -32,7 +32,7 @@ namespace nq {
 namespace gemm {
 
 constexpr int BM = 128, BN = 128, BK = 64;
-constexpr int kStages = 4;
+
 constexpr int kThreads = 192;
 constexpr int kTileBytes = 128 * 128;  // 128 rows x 128 bytes (64 16-bit values)
 
