@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--attention", type=int, default=None, metavar="L",
                     help="the fused decode attention (RoPE + cache write + split-KV attention) of --model at "
                          "sequence length L instead of whole-model decode: KV-cache GB/s over 8 caches cycled")
+    ap.add_argument("--attention-tp", type=int, default=1,
+                    help="--attention: the heads of one tensor-parallel rank of --model (heads / N, kv heads / N)")
     ap.add_argument("--max-seq", type=int, default=None,
                     help="--attention: KV-cache capacity in positions (default L + 64 rounded up to a multiple of 64); "
                          "the kernel's chunking and the cache layout follow it")
@@ -709,13 +711,15 @@ def run_attention(args):
     _lib_load()
     cfg = CONFIGS[args.model]
     L, B, D = args.attention, args.batch, cfg.head_dim
+    tp = max(1, args.attention_tp)
+    hq, hkv = cfg.heads // tp, cfg.kv_heads // tp
     dev = torch.device("cuda", 0)
     max_seq = args.max_seq if args.max_seq else (L + 64 + 63) // 64 * 64
-    caches = [(torch.randn(B, cfg.kv_heads, max_seq, D, device=dev).half(),
-               torch.randn(B, cfg.kv_heads, max_seq, D, device=dev).half()) for _ in range(8)]
-    q = torch.randn(B, cfg.heads, D, device=dev).half()
-    k = torch.randn(B, cfg.kv_heads, D, device=dev).half()
-    v = torch.randn(B, cfg.kv_heads, D, device=dev).half()
+    caches = [(torch.randn(B, hkv, max_seq, D, device=dev).half(),
+               torch.randn(B, hkv, max_seq, D, device=dev).half()) for _ in range(8)]
+    q = torch.randn(B, hq, D, device=dev).half()
+    k = torch.randn(B, hkv, D, device=dev).half()
+    v = torch.randn(B, hkv, D, device=dev).half()
     pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
     ops = torch.ops.nq_b200
     for i in range(max(args.warmup, 3)):
@@ -731,12 +735,12 @@ def run_attention(args):
     e1.record()
     torch.cuda.synchronize(dev)
     us = e0.elapsed_time(e1) * 1e3 / n
-    kv = 2 * B * cfg.kv_heads * L * D * 2
+    kv = 2 * B * hkv * L * D * 2
     peak, kind = peaks()
     gbs = kv / (us * 1e-6) / 1e9
     print(json.dumps({"metric": "decode attention GB/s (KV-cache bytes)", "value": round(gbs, 2), "unit": "GB/s",
                       "attention": {"model": cfg.name, "seq_len": L, "max_seq": max_seq, "batch": B,
-                                    "heads": cfg.heads, "kv_heads": cfg.kv_heads}, "us_per_launch": round(us, 3), "bytes_per_launch": kv,
+                                    "heads": hq, "kv_heads": hkv, "tp": tp}, "us_per_launch": round(us, 3), "bytes_per_launch": kv,
                       "launches": n, "roofline": {"bound": "hbm", "peak": peak, "frac": round(gbs / peak, 5),
                                                   "peak_source": kind},
                       "dtype": "f16", "data": "synthetic"}), flush=True)

@@ -205,6 +205,7 @@ struct AttnParams {
     int hkv, max_seq, nchunk, nsub, nst;
     int cl;             // chunks of a head combined in a cluster (nchunk <= kClusterChunks)
     int ncl;            // cluster size (a power of two >= nchunk) when cl
+    int qsplit;         // CTAs sharing one kv head's chunk, each with GRP of its hq / hkv query heads
     float scale, log2_theta;
 };
 
@@ -250,12 +251,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kAttnMaxStages];
     __shared__ float mrow[GRP], lrow[GRP];
-    __shared__ float wts[kMaxChunks];
     __shared__ float red[kAttnThreads / 32];
     __shared__ int last;
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-    const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
-    const int hq = p.hkv * GRP;
+    const int chunk = blockIdx.x, b = blockIdx.z;
+    const int kh = blockIdx.y / p.qsplit, qsub = blockIdx.y - kh * p.qsplit;  // kv head, query-head subgroup
+    const int hq = p.hkv * GRP * p.qsplit;
+    const int qh0 = (kh * p.qsplit + qsub) * GRP;  // this CTA's first query head
     pdl_launch_dependents();
     // Programmatic dependent launch: the RoPE variant (one decode step) reads the positions and
     // issues its cache copies before waiting for the previous kernel -- the positions change
@@ -265,11 +267,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     const int pos = ROPE ? p.pos[b] : 0;
     int L = ROPE ? pos + 1 : p.seq_len[b];
     L = min(L, p.max_seq);
-    const int clen = p.nsub * kSub;
+    // Chunks of whole 64-position blocks sized from this row's actual length: the CTAs along x
+    // share the row's blocks evenly, so none idles while L is below the capacity (the score
+    // buffer holds p.nsub blocks, and ceil(blocks / CTAs) never exceeds it), and every block of
+    // a chunk starts on a 64-row (16 KB) boundary of the cache.
+    const int nch = (int)gridDim.x;
+    const int spc = max(1, ((L + kSub - 1) / kSub + nch - 1) / nch);
+    const int clen = spc * kSub;
     const int c0 = chunk * clen;
     const int c1 = max(c0, min(c0 + clen, L));
     const bool active = c1 > c0;
-    T *out = static_cast<T *>(p.out) + ((size_t)b * hq + (size_t)kh * GRP) * D;
+    T *out = static_cast<T *>(p.out) + ((size_t)b * hq + (size_t)qh0) * D;
     if (!CL) {
         if (L <= 0) {  // nothing to attend to: zeros, written once
             if (ROPE) pdl_wait();
@@ -313,7 +321,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     // q (rotated here when ROPE) into shared memory; the owner of the new row rotates k too.
     const bool owner = ROPE && L > 0 && pos >= 0 && pos < p.max_seq && (L - 1) / clen == chunk;
     T knew_a = fromf<T>(0.f), knew_b = knew_a, vnew_a = knew_a, vnew_b = knew_a;
-    const T *qg = static_cast<const T *>(p.q) + ((size_t)b * hq + (size_t)kh * GRP) * D;
+    const T *qg = static_cast<const T *>(p.q) + ((size_t)b * hq + (size_t)qh0) * D;
     if (ROPE) {
         if (tid < D / 2) {
             const int j = tid;
@@ -336,12 +344,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
                 knew_b = fromf<T>(bb * c + a * s);
                 vnew_a = vn[j];
                 vnew_b = vn[j + D / 2];
-                T *kd = static_cast<T *>(p.kc) + (head_row0 + pos) * D;
-                T *vd = static_cast<T *>(p.vc) + (head_row0 + pos) * D;
-                kd[j] = knew_a;
-                kd[j + D / 2] = knew_b;
-                vd[j] = vnew_a;
-                vd[j + D / 2] = vnew_b;
+                if (qsub == 0) {  // one writer per kv head; every subgroup patches its own copy
+                    T *kd = static_cast<T *>(p.kc) + (head_row0 + pos) * D;
+                    T *vd = static_cast<T *>(p.vc) + (head_row0 + pos) * D;
+                    kd[j] = knew_a;
+                    kd[j + D / 2] = knew_b;
+                    vd[j] = vnew_a;
+                    vd[j + D / 2] = vnew_b;
+                }
             }
         }
     } else {
@@ -522,7 +532,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         }
         return;
     }
-    float *pbase = p.part + ((size_t)b * hq + (size_t)kh * GRP) * p.nchunk * (D + 2);
+    float *pbase = p.part + ((size_t)b * hq + (size_t)qh0) * p.nchunk * (D + 2);
     if (nact == 1) {  // the whole sequence was this chunk
         if (pg == 0)
 #pragma unroll
@@ -542,42 +552,60 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         }
     __threadfence();
     __syncthreads();
-    unsigned *cnt = p.count + (size_t)b * p.hkv + kh;
+    unsigned *cnt = p.count + (size_t)b * p.hkv * p.qsplit + blockIdx.y;
     if (tid == 0) last = atomicAdd(cnt, 1u) == (unsigned)(nact - 1);
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // combine: out = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c  (nact <= kMaxChunks = 64)
-    for (int g = 0; g < GRP; ++g) {
+    // combine: out = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c  (nact <= kMaxChunks = 64).
+    // One warp per head forms the chunk weights (lanes hold chunks lane and lane + 32); then every
+    // thread takes output values (head, dim) and sums the chunks' partials with independent loads,
+    // so the heads of a GQA group are combined at once rather than one after another.
+    float *cw = reinterpret_cast<float *>(smem);  // [GRP][kMaxChunks] weights (the copy ring is idle)
+    float *cden = cw + GRP * kMaxChunks;          // [GRP] sum_c e^(m_c - M) l_c
+    for (int g = w; g < GRP; g += kAttnThreads / 32) {
         const float *pg_ = pbase + (size_t)g * p.nchunk * (D + 2);
-        float mc = -INFINITY, lc = 0.f;
-        if (tid < nact) {
-            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pg_ + (size_t)tid * (D + 2) + D));
-            mc = ml.x;
-            lc = ml.y;
+        float mc[2], lc[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int ci = lane + 32 * j;
+            mc[j] = -INFINITY;
+            lc[j] = 0.f;
+            if (ci < nact) {
+                const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pg_ + (size_t)ci * (D + 2) + D));
+                mc[j] = ml.x;
+                lc[j] = ml.y;
+            }
         }
-        float mx = mc;
+        float mx = fmaxf(mc[0], mc[1]);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        if (lane == 0 && w < 2) red[w] = mx;
-        __syncthreads();
-        const float M = fmaxf(red[0], red[1]);
-        const float wc = tid < nact ? expf(mc - M) : 0.f;
-        if (tid < nact) wts[tid] = wc;
-        float den = wc * lc;
+        float den = 0.f;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const float wc = lane + 32 * j < nact ? expf(mc[j] - mx) : 0.f;
+            cw[g * kMaxChunks + lane + 32 * j] = wc;
+            den = fmaf(wc, lc[j], den);
+        }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-        __syncthreads();
-        if (lane == 0 && w < 2) red[w] = den;
-        __syncthreads();
-        den = red[0] + red[1];
-        if (tid < D) {
-            float num = 0.f;
-#pragma unroll 8
-            for (int c = 0; c < nact; ++c) num = fmaf(wts[c], __ldcg(pg_ + (size_t)c * (D + 2) + tid), num);
-            out[g * D + tid] = fromf<T>(num / den);
+        if (lane == 0) cden[g] = den;
+    }
+    __syncthreads();
+    for (int i = tid; i < GRP * D; i += kAttnThreads) {
+        const int g = i / D, d = i - g * D;
+        const float *src = pbase + (size_t)g * p.nchunk * (D + 2) + d;
+        const float *wg = cw + g * kMaxChunks;
+        float n0 = 0.f, n1 = 0.f, n2 = 0.f, n3 = 0.f;
+        int ci = 0;
+        for (; ci + 4 <= nact; ci += 4) {
+            n0 = fmaf(wg[ci], __ldcg(src + (size_t)ci * (D + 2)), n0);
+            n1 = fmaf(wg[ci + 1], __ldcg(src + (size_t)(ci + 1) * (D + 2)), n1);
+            n2 = fmaf(wg[ci + 2], __ldcg(src + (size_t)(ci + 2) * (D + 2)), n2);
+            n3 = fmaf(wg[ci + 3], __ldcg(src + (size_t)(ci + 3) * (D + 2)), n3);
         }
-        __syncthreads();  // red / wts reused by the next head
+        for (; ci < nact; ++ci) n0 = fmaf(wg[ci], __ldcg(src + (size_t)ci * (D + 2)), n0);
+        out[g * D + d] = fromf<T>(((n0 + n1) + (n2 + n3)) / cden[g]);
     }
     if (tid == 0) *cnt = 0u;
 }
@@ -629,7 +657,7 @@ cudaError_t launch_attn(const AttnParams &p, int batch, cudaStream_t s) {
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.cl ? (unsigned)p.ncl : (unsigned)p.nchunk, (unsigned)p.hkv, (unsigned)batch);
+    cfg.gridDim = dim3(p.cl ? (unsigned)p.ncl : (unsigned)p.nchunk, (unsigned)(p.hkv * p.qsplit), (unsigned)batch);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -701,12 +729,19 @@ int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head
     p.cl = ch.nchunk <= kClusterChunks ? 1 : 0;
     p.ncl = 1;
     while (p.ncl < ch.nchunk) p.ncl *= 2;
+    // GQA with few kv heads (a tensor-parallel shard): the query heads of a kv head are split
+    // over up to `grp` CTAs per chunk (each reads the chunk's K / V; the second and later reads
+    // hit L2) until the grid reaches about one CTA per SM
+    int64_t ctas = (int64_t)(p.cl ? p.ncl : ch.nchunk) * hkv * batch;
+    p.qsplit = 1;
+    while (p.qsplit < grp && ctas * p.qsplit * 2 <= sm_count()) p.qsplit *= 2;
+    ctas *= p.qsplit;
+    const int64_t gcta = grp / p.qsplit;  // query heads per CTA
     // ring depth: every sub-block of the chunk in flight if shared memory allows, keeping room
     // for two CTAs per SM when the grid needs that many
-    const int64_t ctas = (int64_t)(p.cl ? p.ncl : ch.nchunk) * hkv * batch;
     const size_t budget = ctas > sm_count() ? 110 * 1024 : 200 * 1024;
-    const size_t fixed = (size_t)grp * kHeadDim * 2 + (size_t)grp * ch.nsub * kSub * sizeof(float) +
-                         (p.cl ? (size_t)kClusterChunks * grp * (kHeadDim + 2) * 4 : 0);
+    const size_t fixed = (size_t)gcta * kHeadDim * 2 + (size_t)gcta * ch.nsub * kSub * sizeof(float) +
+                         (p.cl ? (size_t)kClusterChunks * gcta * (kHeadDim + 2) * 4 : 0);
     int nst = (int)std::min<int64_t>(kAttnMaxStages, 2 * (int64_t)ch.nsub);
     while (nst > 2 && fixed + (size_t)nst * attn_stage_bytes() > budget) --nst;
     p.nst = nst;
@@ -815,7 +850,8 @@ int nq_decode_attention(int dtype, const void *q, const void *k_cache, const voi
     p.out = out;
     const int st = attn_prepare(dtype, batch, hq, hkv, head_dim, max_seq, workspace, workspace_bytes, p);
     if (st != NQ_OK) return st;
-    const cudaError_t e = dispatch_attn<false>(dtype, (int)(hq / hkv), p, (int)batch, static_cast<cudaStream_t>(stream));
+    const cudaError_t e =
+        dispatch_attn<false>(dtype, (int)(hq / hkv) / p.qsplit, p, (int)batch, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? NQ_OK : cuda_fail(e, "decode attention launch");
 }
 
@@ -839,7 +875,8 @@ int nq_decode_attention_rope(int dtype, const void *q, const void *k, const void
     p.log2_theta = log2f(theta);
     const int st = attn_prepare(dtype, batch, hq, hkv, head_dim, max_seq, workspace, workspace_bytes, p);
     if (st != NQ_OK) return st;
-    const cudaError_t e = dispatch_attn<true>(dtype, (int)(hq / hkv), p, (int)batch, static_cast<cudaStream_t>(stream));
+    const cudaError_t e =
+        dispatch_attn<true>(dtype, (int)(hq / hkv) / p.qsplit, p, (int)batch, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? NQ_OK : cuda_fail(e, "decode attention (rope) launch");
 }
 

@@ -77,6 +77,8 @@ ATTN_CASES = [  # (hq, hkv, max_seq, lengths, dtype): groups 1/2/4/8, one and se
     (4, 2, 200, [0, 5], torch.float16),             # an empty sequence (zeros),
     (16, 2, 9000, [9000, 4097], torch.float16),     # 3 sub-blocks per chunk (two-stage ring)
     (32, 32, 2400, [2049], torch.bfloat16),         # the 7B decode shape
+    (8, 1, 2176, [2048], torch.float16),            # one kv head (a 70B TP8 shard): query heads split over CTAs
+    (4, 1, 512, [500, 77], torch.bfloat16),         # query heads split over CTAs of a cluster
 ]
 
 
@@ -108,6 +110,7 @@ def test_decode_attention_against_reference(case):
     (8, 2, 300, [299, 64], torch.float16),
     (32, 32, 2400, [2048], torch.bfloat16),
     (16, 2, 9000, [8999, 130], torch.float16),
+    (8, 1, 2176, [2047], torch.float16),
 ])
 def test_decode_attention_rope_matches_rope_cache_then_attention(hq, hkv, S, pos, dt):
     """The fused entry point: caches bit-identical to rope_cache's writes, output bit-identical
