@@ -411,32 +411,37 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             issue(it + nst);
         }
     }
-    // ---- phase 2: one softmax per head over the whole chunk: P = e^(s - m), l = sum P
-    for (int g = 0; g < GRP && nsb > 0; ++g) {
+    // ---- phase 2: one softmax per head over the whole chunk: P = e^(s - m), l = sum P.  The
+    // heads run side by side, kAttnThreads / 32 / GRP warps each, so a GQA group costs three
+    // block barriers in all rather than four per head.
+    {
+        constexpr int kWph = kAttnThreads / 32 / GRP;  // warps per head
+        const int g = w / kWph, wi = w - g * kWph;
+        const int tl = wi * 32 + lane;
         float mx = -INFINITY;
-        for (int i = tid; i < npos; i += kAttnThreads) mx = fmaxf(mx, sc[g * clen + i]);
+        for (int i = tl; i < npos; i += kWph * 32) mx = fmaxf(mx, sc[g * clen + i]);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
         if (lane == 0) red[w] = mx;
         __syncthreads();
-        float m = red[0];
+        float m = red[g * kWph];
 #pragma unroll
-        for (int i = 1; i < kAttnThreads / 32; ++i) m = fmaxf(m, red[i]);
+        for (int j = 1; j < kWph; ++j) m = fmaxf(m, red[g * kWph + j]);
         float sm = 0.f;
-        for (int i = tid; i < npos; i += kAttnThreads) {
+        for (int i = tl; i < npos; i += kWph * 32) {
             const float e = expf(sc[g * clen + i] - m);
             sc[g * clen + i] = e;
             sm += e;
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
-        __syncthreads();  // everyone has read red (the max) before it is reused
+        __syncthreads();  // every warp has read the maxima before red is reused
         if (lane == 0) red[w] = sm;
         __syncthreads();
-        if (tid == 0) {
+        if (wi == 0 && lane == 0 && npos > 0) {  // an empty chunk keeps m = -inf, l = 0
             float l = 0.f;
 #pragma unroll
-            for (int i = 0; i < kAttnThreads / 32; ++i) l += red[i];
+            for (int j = 0; j < kWph; ++j) l += red[g * kWph + j];
             mrow[g] = m;
             lrow[g] = l;
         }
@@ -596,16 +601,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         const int g = i / D, d = i - g * D;
         const float *src = pbase + (size_t)g * p.nchunk * (D + 2) + d;
         const float *wg = cw + g * kMaxChunks;
-        float n0 = 0.f, n1 = 0.f, n2 = 0.f, n3 = 0.f;
-        int ci = 0;
-        for (; ci + 4 <= nact; ci += 4) {
-            n0 = fmaf(wg[ci], __ldcg(src + (size_t)ci * (D + 2)), n0);
-            n1 = fmaf(wg[ci + 1], __ldcg(src + (size_t)(ci + 1) * (D + 2)), n1);
-            n2 = fmaf(wg[ci + 2], __ldcg(src + (size_t)(ci + 2) * (D + 2)), n2);
-            n3 = fmaf(wg[ci + 3], __ldcg(src + (size_t)(ci + 3) * (D + 2)), n3);
+        // 16 loads in flight per round trip (the weights of chunks >= nact are 0)
+        float num = 0.f;
+        for (int c0 = 0; c0 < nact; c0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = c0 + j < nact ? __ldcg(src + (size_t)(c0 + j) * (D + 2)) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) num = fmaf(wg[c0 + j], v[j], num);
         }
-        for (; ci < nact; ++ci) n0 = fmaf(wg[ci], __ldcg(src + (size_t)ci * (D + 2)), n0);
-        out[g * D + d] = fromf<T>(((n0 + n1) + (n2 + n3)) / cden[g]);
+        out[g * D + d] = fromf<T>(num / cden[g]);
     }
     if (tid == 0) *cnt = 0u;
 }
