@@ -160,9 +160,14 @@ NQ_API int nq_gemv_group_ex(int dtype, const nq_gemv_input *input, int64_t batch
  * Every rank must make the same sequence of calls, PUSH and PULL alternating (nq_tp_pull counts
  * as a PULL); batch <= 8; the GEMV must run as its single cooperative launch; a timed-out wait
  * records NQ_ERR_DEVICE_TIMEOUT in the region's status word (nq_workspace_status).
+ * NQ_TP_CHECK added to tp_mode plans the call without launching it (and without reading the
+ * regions, which may be NULL): NQ_OK when the exchange can run at these shapes, otherwise the
+ * error the launch would return (for instance a layer group whose weight slabs need the
+ * two-launch GEMV), so a caller can fall back to a separate all-reduce before it starts.
  * ------------------------------------------------------------------------------- */
 #define NQ_TP_PULL 1
 #define NQ_TP_PUSH 2
+#define NQ_TP_CHECK 4
 typedef struct {
     void *regions[8];          /* every rank's region as mapped in this process (own at `rank`) */
     int rank;

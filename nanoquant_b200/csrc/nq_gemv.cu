@@ -1243,7 +1243,7 @@ struct GroupInput {
 
 static int group_impl(int dtype, const GroupInput &in, int64_t batch, int64_t in_features, int n,
                       const nq_gemv_layer *layers, void *workspace, size_t workspace_bytes, void *stream,
-                      const TpX *tpx = nullptr) {
+                      const TpX *tpx = nullptr, bool plan_only = false) {
     const TpX tp = tpx ? *tpx : TpX{};
     const void *x = in.x;
     if (n >= 1 && n <= kMaxGroup) {
@@ -1368,6 +1368,7 @@ static int group_impl(int dtype, const GroupInput &in, int64_t batch, int64_t in
                 (!plan.prm.x_in_smem || (size_t)plan.prm.kb1 * 64 < (size_t)16 * ((p.tiles2 + plan.grid - 1) / plan.grid)))
                 return fail(NQ_ERR_UNSUPPORTED, "push: the rows of a CTA must fit its staged-x region");
         }
+        if (plan_only) continue;
         st = (dtype == NQ_DTYPE_F16) ? launch<__half>(plan, s, tp) : launch<__nv_bfloat16>(plan, s, tp);
         if (st) return st;
     }
@@ -1405,14 +1406,15 @@ __global__ void __launch_bounds__(512) tp_pull_kernel(const TpX tp, int64_t n, T
     }
 }
 
-static int make_tpx(const nq_tp_exchange *x, int mode, TpX &tp) {
+// `need_regions` false: the descriptor of a plan-only check (NQ_TP_CHECK), regions not read.
+static int make_tpx(const nq_tp_exchange *x, int mode, TpX &tp, bool need_regions = true) {
     if (!x) return fail(NQ_ERR_INVALID_ARGUMENT, "null exchange descriptor");
     if (x->world < 1 || x->world > kTpMaxWorld || x->rank < 0 || x->rank >= x->world)
         return fail(NQ_ERR_INVALID_ARGUMENT, "exchange: rank %d of world %d (at most %d)", x->rank, x->world, kTpMaxWorld);
     if (x->max_elems <= 0 || x->max_elems % 8)
         return fail(NQ_ERR_INVALID_ARGUMENT, "exchange: max_elems must be a positive multiple of 8");
     tp = TpX{};
-    for (int r = 0; r < x->world; ++r) {
+    for (int r = 0; r < x->world && need_regions; ++r) {
         if (!x->regions[r] || (reinterpret_cast<uintptr_t>(x->regions[r]) & 255))
             return fail(NQ_ERR_INVALID_ARGUMENT, "exchange: region %d missing or not 256-byte aligned", r);
         tp.region[r] = static_cast<unsigned char *>(x->regions[r]);
@@ -1461,12 +1463,15 @@ int nq_gemv_group_tp(int dtype, const nq_gemv_input *input, int64_t batch, int64
                      size_t workspace_bytes, void *stream) {
     using namespace nq::gemv;
     if (!input) return nq::fail(NQ_ERR_INVALID_ARGUMENT, "null input descriptor");
-    if (tp_mode & ~(kTpPull | kTpPush)) return nq::fail(NQ_ERR_INVALID_ARGUMENT, "unknown exchange mode %d", tp_mode);
+    if (tp_mode & ~(kTpPull | kTpPush | NQ_TP_CHECK))
+        return nq::fail(NQ_ERR_INVALID_ARGUMENT, "unknown exchange mode %d", tp_mode);
+    const bool check = (tp_mode & NQ_TP_CHECK) != 0;
+    tp_mode &= kTpPull | kTpPush;
     if ((tp_mode & kTpPull) && input->x_mode != NQ_CHAIN_X_RMSNORM)
         return nq::fail(NQ_ERR_UNSUPPORTED, "a PULL launch forms its input with RMSNORM");
     TpX tpx{};
     if (tp_mode) {
-        const int st = make_tpx(tp, tp_mode, tpx);
+        const int st = make_tpx(tp, tp_mode, tpx, !check);
         if (st) return st;
     }
     GroupInput in;
@@ -1478,7 +1483,7 @@ int nq_gemv_group_tp(int dtype, const nq_gemv_input *input, int64_t batch, int64
     in.eps = input->eps;
     in.act = act;
     return group_impl(dtype, in, batch, in_features, n_layers, layers, workspace, workspace_bytes, stream,
-                      tp_mode ? &tpx : nullptr);
+                      tp_mode ? &tpx : nullptr, check);
 }
 
 int nq_tp_pull(int dtype, const nq_tp_exchange *tp, int64_t n, void *out, void *stream) {

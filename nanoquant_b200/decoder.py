@@ -288,8 +288,10 @@ class Decoder:
             self.peer_ar = PeerAllReduce(group, tp_rank, tp, 8 * cfg.hidden, dev)
         # `tp_exchange` (the default for tp > 1): the decode step's per-block sums run inside the
         # GEMVs (push from o / down, pull in the next RMSNorm prologue); NCCL stays for prefill
+        # (every rank holds shards of the same shapes, so every rank makes the same choice)
         self.tpx = None
-        if tp > 1 and tp_exchange and not peer_allreduce and batch <= 8 and self.fuse_neighbours:
+        if (tp > 1 and tp_exchange and not peer_allreduce and batch <= 8 and self.fuse_neighbours
+                and self._exchange_fits()):
             self.tpx = TPExchange(group, tp_rank, tp, batch * cfg.hidden, dev)
 
     # ------------------------------------------------------------------ pieces
@@ -318,6 +320,38 @@ class Decoder:
                 return False
             raise
         torch.cuda.synchronize(self.device)
+        return True
+
+    def _exchange_fits(self) -> bool:
+        """Whether the four exchange GEMVs of a decoder block (q/k/v and gate/up pulling, o and
+        down pushing) have their single-launch plan at this shard's shapes: planned with
+        NQ_TP_CHECK, nothing launched.  Wide shards (Llama-3-70B at TP2) whose weight slabs need
+        the two-launch GEMV keep the NCCL sums instead."""
+        ops, lay, B, dev, dt = torch.ops.nq_b200, self.layers[0], self.batch, self.device, self.dtype
+        check, mx = 4, (B * self.cfg.hidden + 7) // 8 * 8
+        ex = ([0] * self.tp, self.tp_rank, mx)
+        h = torch.zeros(B, self.cfg.hidden, device=dev, dtype=dt)
+        a = torch.zeros(B, self.hq * self.cfg.head_dim, device=dev, dtype=dt)
+        f = torch.zeros(B, lay["down"].in_features, device=dev, dtype=dt)
+        g, gu, ol, dn = lay["qkv"], lay["gate_up"], lay["o"], lay["down"]
+        try:
+            ops.gemv_group_tp(h, h, lay["in_norm"], 1e-5, nqchain.RMSNORM, torch.empty_like(h), 0, g.s2, g.vb, g.smid,
+                              g.ub, g.s1, *ex, TPExchange.PULL | check)
+            ops.gemv_group_tp(a, None, None, 0.0, nqchain.PLAIN, None, 0, [ol.s2], [ol.vb], [ol.smid], [ol.ub],
+                              [ol.s1], *ex, TPExchange.PUSH | check)
+            ops.gemv_group_tp(h, h, lay["post_norm"], 1e-5, nqchain.RMSNORM, torch.empty_like(h),
+                              1 if self.fuse_down else 0, gu.s2, gu.vb, gu.smid, gu.ub, gu.s1, *ex,
+                              TPExchange.PULL | check)
+            if self.fuse_down:
+                ops.gemv_group_tp(f, f, None, 0.0, nqchain.MUL, None, 0, [dn.s2], [dn.vb], [dn.smid], [dn.ub],
+                                  [dn.s1], *ex, TPExchange.PUSH | check)
+            else:
+                ops.gemv_group_tp(f, None, None, 0.0, nqchain.PLAIN, None, 0, [dn.s2], [dn.vb], [dn.smid], [dn.ub],
+                                  [dn.s1], *ex, TPExchange.PUSH | check)
+        except RuntimeError as e:
+            if "unsupported" in str(e) or "shared-memory budget" in str(e):
+                return False
+            raise
         return True
 
     def _all_reduce(self, t: torch.Tensor):

@@ -70,3 +70,16 @@ def test_gemm_llama3_70b_shapes_m2048_sampled_rows(proj):
     ref = orc.forward_dense(d.xr[rows], d.s2r, L.V, d.smidr, L.U, d.s1r)
     assert_close_to_oracle(y[torch.as_tensor(rows, device=y.device)], ref, "bf16")
     assert workspace_status(ws) == 0
+
+
+@pytest.mark.parametrize("tp,fits", [(2, False), (8, True)])
+def test_exchange_plan_check_on_70b_shards(tp, fits):
+    """NQ_TP_CHECK plans the exchange launches without running them (no peers, no regions): every
+    exchange GEMV of a TP8 shard has its single-launch plan; at TP2 some shard's weight slabs need
+    the two-launch GEMV, which the check reports, so the decoder keeps NCCL sums there."""
+    import dataclasses
+
+    from nanoquant_b200.decoder import Decoder
+    cfg = dataclasses.replace(LLAMA3_70B, layers=1)
+    dec = Decoder(cfg, max_seq=64, tp_rank=0, tp=tp, tp_exchange=False, dtype=torch.float16, device="cuda")
+    assert dec._exchange_fits() is fits
