@@ -1,8 +1,8 @@
 """Benchmark: batch-1 greedy decode tokens/s of a Llama-2-7B-architecture decoder whose
 every linear is a NanoQuant layer at the benchmark ranks (~0.55 bpw), after a 2048-token
-random-id prompt, tensor-parallel over N GPUs (one process per GPU, NCCL all-reduce per
-attention / MLP block).  Also reports the fused decode GEMV against the HBM roofline and
-the reference's CPU path on this host.
+random-id prompt, tensor-parallel over N GPUs (one process per GPU; the per-block sums run
+inside the GEMVs over NVLink, or through NCCL where a shard cannot).  Also reports the fused
+decode GEMV against the HBM roofline and the reference's CPU path on this host.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nq|reference] [--model NAME]
 
@@ -232,14 +232,17 @@ def cpu_reference_token_time(cfg, context: int, seconds: float):
     return cfg.layers * t_layer + t_head, threads, n
 
 
-def config_block(cfg, args, world):
+def config_block(cfg, args, world, dec=None):
+    """The line's config; with the decoder, the tensor-parallel sum it actually runs (the fused
+    exchange falls back to NCCL where a shard's GEMV has no single-launch plan)."""
+    exchange = not getattr(args, "no_exchange", False) if dec is None else dec.tpx is not None
     return {"workload": f"{cfg.name} 0.55bpw batch-{args.batch} greedy decode after a {args.prompt}-token "
                         f"random-id prompt",
             "model": cfg.name, "global_batch": args.batch, "seq_len": args.prompt,
             "parallelism": f"tp{world}", "ranks": dict(cfg.ranks),
             "decode_path": "grouped GEMV launches with fused RMSNorm / SwiGLU prologues",
             "tp_allreduce": ("peer memory (nq_allreduce)" if getattr(args, "peer_allreduce", False) else
-                             "NCCL" if getattr(args, "no_exchange", False) else
+                             "NCCL" if not exchange else
                              "inside the GEMVs (push from o / down, pull in the next RMSNorm prologue)")
                             if world > 1 else None,
             "l2": "working set > L2 (weights + KV cache read per token)"}
@@ -449,7 +452,7 @@ def run_nq(args, world, rank, local):
                 "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "f16",
                 "data": "synthetic (seeded random +-1 factors, fp16 scales, random token ids)",
-                "config": config_block(cfg, args, world),
+                "config": config_block(cfg, args, world, dec),
                 "e2e": {"value": round(e2e, 3), "unit": "tokens/s", "h2d_bytes_per_step": 8 * args.batch,
                         "d2h_bytes_per_step": 8 * args.batch},
                 "roofline": {"bound": "hbm", "kernel": "gemv_kernel (fused decode GEMV)",
