@@ -139,32 +139,35 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T *__restrict__ x, c
 
 // ------------------------------------------------------------------ rotary + cache write
 // q [n, hq, D], k [n, hkv, D] rotated in place (pairs (i, i + D/2), angle = pos * theta^(-2i/D));
-// k, v written to cache[batch][kv head][pos][D].
+// k, v written to cache[batch][kv head][pos][D].  One CTA per token: thread (i, g) computes the
+// angle of pair i once and rotates that pair in heads g, g + G, ... (G = blockDim.x / (D/2)).
 template <typename T>
 __global__ void rope_cache_kernel(T *__restrict__ q, T *__restrict__ k, const T *__restrict__ v,
                                   const int *__restrict__ pos, const int *__restrict__ batch_of, T *__restrict__ kc,
                                   T *__restrict__ vc, int hq, int hkv, int D, int max_seq, float log2_theta) {
-    const int tok = blockIdx.y, head = blockIdx.x, i = threadIdx.x;  // i < D/2
-    const int p = pos[tok];
     const int half = D / 2;
+    const int tok = blockIdx.x, i = threadIdx.x % half, g0 = threadIdx.x / half, G = blockDim.x / half;
+    const int p = pos[tok];
     const float inv_freq = exp2f(-(2.f * i / (float)D) * log2_theta);
     float sn, cs;
     sincosf((float)p * inv_freq, &sn, &cs);
     const float c = tof(fromf<T>(cs)), s = tof(fromf<T>(sn));
-    T *row = head < hq ? q + ((size_t)tok * hq + head) * D : k + ((size_t)tok * hkv + (head - hq)) * D;
-    const float a = tof(row[i]), b = tof(row[i + half]);
-    const T ra = fromf<T>(a * c - b * s), rb = fromf<T>(b * c + a * s);
-    row[i] = ra;
-    row[i + half] = rb;
-    if (head >= hq && p >= 0 && p < max_seq) {
-        const int kh = head - hq;
-        const int bb = batch_of ? batch_of[tok] : tok;
-        const size_t off = (((size_t)bb * hkv + kh) * max_seq + p) * D;
-        kc[off + i] = ra;
-        kc[off + i + half] = rb;
-        const T *vr = v + ((size_t)tok * hkv + kh) * D;
-        vc[off + i] = vr[i];
-        vc[off + i + half] = vr[i + half];
+    const int bb = batch_of ? batch_of[tok] : tok;
+    for (int head = g0; head < hq + hkv; head += G) {
+        T *row = head < hq ? q + ((size_t)tok * hq + head) * D : k + ((size_t)tok * hkv + (head - hq)) * D;
+        const float a = tof(row[i]), b = tof(row[i + half]);
+        const T ra = fromf<T>(a * c - b * s), rb = fromf<T>(b * c + a * s);
+        row[i] = ra;
+        row[i + half] = rb;
+        if (head >= hq && p >= 0 && p < max_seq) {
+            const int kh = head - hq;
+            const size_t off = (((size_t)bb * hkv + kh) * max_seq + p) * D;
+            kc[off + i] = ra;
+            kc[off + i + half] = rb;
+            const T *vr = v + ((size_t)tok * hkv + kh) * D;
+            vc[off + i] = vr[i];
+            vc[off + i + half] = vr[i + half];
+        }
     }
 }
 
@@ -643,11 +646,33 @@ inline size_t attn_count_bytes(int64_t batch, int64_t hq) { return ((size_t)batc
 // ------------------------------------------------------------------ SwiGLU
 template <typename T>
 __global__ void silu_mul_kernel(const T *__restrict__ gate, const T *__restrict__ up, T *__restrict__ out, size_t n) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    auto one = [&](size_t i) {
         const float g = tof(gate[i]);
         const T s = fromf<T>(g / (1.f + expf(-g)));
         out[i] = fromf<T>(tof(s) * tof(up[i]));
+    };
+    const size_t stride = (size_t)gridDim.x * blockDim.x, t0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    const bool vec = ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) |
+                       reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+    size_t done = 0;
+    if (vec) {  // eight values per 16-byte access, the same arithmetic per value
+        const size_t n8 = n / 8;
+        for (size_t c = t0; c < n8; c += stride) {
+            const uint4 gv = reinterpret_cast<const uint4 *>(gate)[c], uv = reinterpret_cast<const uint4 *>(up)[c];
+            const T *ge = reinterpret_cast<const T *>(&gv), *ue = reinterpret_cast<const T *>(&uv);
+            uint4 ov;
+            T *oe = reinterpret_cast<T *>(&ov);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float g = tof(ge[j]);
+                const T s = fromf<T>(g / (1.f + expf(-g)));
+                oe[j] = fromf<T>(tof(s) * tof(ue[j]));
+            }
+            reinterpret_cast<uint4 *>(out)[c] = ov;
+        }
+        done = n8 * 8;
     }
+    for (size_t i = done + t0; i < n; i += stride) one(i);
 }
 
 template <typename T, int GRP, bool ROPE>
@@ -818,14 +843,17 @@ int nq_rope_cache(int dtype, void *q, void *k, const void *v, const int32_t *pos
         return fail(NQ_ERR_INVALID_ARGUMENT, "bad rope_cache args");
     if (head_dim % 2 || head_dim > 1024) return fail(NQ_ERR_UNSUPPORTED, "head_dim must be even and <= 1024");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    dim3 grid((unsigned)(hq + hkv), (unsigned)n_tokens);
+    if (n_tokens > INT32_MAX) return fail(NQ_ERR_UNSUPPORTED, "too many tokens");
+    // one CTA per token; as many head groups as fit 256 threads (at least one)
+    const unsigned block = (unsigned)(head_dim / 2) * (unsigned)std::max<int64_t>(1, 256 / (head_dim / 2));
+    const unsigned grid = (unsigned)n_tokens;
     const float l2t = log2f(theta);
     if (dtype == NQ_DTYPE_F16)
-        dec::rope_cache_kernel<__half><<<grid, (unsigned)(head_dim / 2), 0, s>>>(
+        dec::rope_cache_kernel<__half><<<grid, block, 0, s>>>(
             (__half *)q, (__half *)k, (const __half *)v, positions, batch_of, (__half *)k_cache, (__half *)v_cache,
             (int)hq, (int)hkv, (int)head_dim, (int)max_seq, l2t);
     else if (dtype == NQ_DTYPE_BF16)
-        dec::rope_cache_kernel<__nv_bfloat16><<<grid, (unsigned)(head_dim / 2), 0, s>>>(
+        dec::rope_cache_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
             (__nv_bfloat16 *)q, (__nv_bfloat16 *)k, (const __nv_bfloat16 *)v, positions, batch_of,
             (__nv_bfloat16 *)k_cache, (__nv_bfloat16 *)v_cache, (int)hq, (int)hkv, (int)head_dim, (int)max_seq, l2t);
     else
