@@ -13,12 +13,15 @@ decode with the step captured as a CUDA graph), rebuilt around the kernels of th
 * the decode step reads token ids / positions from device buffers and advances them itself,
   so a captured graph replays one autoregressive step with no host work.
 
-Tensor parallelism (one all-reduce per attention block and per MLP block):
+Tensor parallelism (one sum over the ranks per attention block and per MLP block):
 * q/k/v and gate/up are column-parallel: each rank holds the U rows of its heads / FFN
   columns (U split by output rows) and the full V;
 * o and down receive their input sharded by heads / FFN columns, so each rank holds the V
   columns of its shard (V split by input columns) and the full U; by linearity the ranks'
-  outputs s1 * U(smid * V_shard (s2 * x_shard)) sum to the full layer, which the all-reduce does.
+  outputs s1 * U(smid * V_shard (s2 * x_shard)) sum to the full layer;
+* in decode the sum runs inside the GEMVs (TPExchange: o / down push their rows to every rank
+  over NVLink, the next RMSNorm prologue pulls and sums them) where every exchange launch has
+  its single-launch plan, otherwise through torch.distributed (NCCL), as in prefill.
 Weights are random (seeded) with the per-layer ranks of the benchmark configs; every rank
 draws the same global planes and keeps its slice, so any TP degree computes the same model.
 """
