@@ -33,7 +33,8 @@ namespace gemm {
 
 constexpr int BM = 128, BN = 128, BK = 64;
 
-constexpr int kThreads = 192;
+constexpr int kExpWarps = 8;                  // weight expanders (and epilogue warps)
+constexpr int kThreads = 64 + 32 * kExpWarps;  // + the TMA producer and the MMA issuer
 constexpr int kTileBytes = 128 * 128;  // 128 rows x 128 bytes (64 16-bit values)
 
 struct Params {
@@ -184,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&full_a[i], 1);
-            mbar_init(&full_b[i], 4);
+            mbar_init(&full_b[i], kExpWarps);
             mbar_init(&empty[i], 1);
         }
         mbar_init(accum, 1);
@@ -250,27 +251,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------------------------------------------------- weight expanders
-        constexpr int kRows = kBN / 128;  // weight rows per thread: e, e + 128, ...
-        const int e = threadIdx.x - 64;   // 0..127
-        const uint32_t *row[kRows];
-        bool row_ok[kRows];
+        // 32 * kExpWarps threads over the tile's kBN rows x 2 sign words per K step: kTpr threads
+        // per row, each expanding kWords of the row's words (kBN 256: one row, both words;
+        // kBN 128: half a row, one word)
+        constexpr int kExp = 32 * kExpWarps;
+        constexpr int kTpr = kExp / kBN;
+        constexpr int kWords = 2 / kTpr;
+        static_assert(kTpr * kBN == kExp && kWords * kTpr == 2, "expander split");
+        const int ex = threadIdx.x - 64;
+        const int e = ex % kBN, h0 = (ex / kBN) * kWords;  // row in the tile, first word of the two
+        const int n = n0 + e;
+        const bool row_ok = n < p.N;
         // this CTA's K range starts at word 2 * kb_begin of each row (two words per K step)
         const int wl = p.W - 2 * kb_begin;
-#pragma unroll
-        for (int rr = 0; rr < kRows; ++rr) {
-            const int n = n0 + e + 128 * rr;
-            row_ok[rr] = n < p.N;
-            row[rr] = p.bits + (size_t)(row_ok[rr] ? n : 0) * p.W + 2 * kb_begin;
-        }
+        const uint32_t *row = p.bits + (size_t)(row_ok ? n : 0) * p.W + 2 * kb_begin + h0;
+        const int wl_h = wl - h0;
         // words for the next steps are fetched ahead (a register queue as deep as the ring)
-        uint32_t q0[kRows][kStages], q1[kRows][kStages];
+        uint32_t q[kWords][kStages];
 #pragma unroll
-        for (int rr = 0; rr < kRows; ++rr)
+        for (int j = 0; j < kWords; ++j)
 #pragma unroll
             for (int i = 0; i < kStages; ++i) {
-                const int w = 2 * i;
-                q0[rr][i] = (row_ok[rr] && i < nk && w < wl) ? __ldg(row[rr] + w) : 0u;
-                q1[rr][i] = (row_ok[rr] && i < nk && w + 1 < wl) ? __ldg(row[rr] + w + 1) : 0u;
+                const int w = 2 * i + j;
+                q[j][i] = (row_ok && i < nk && w < wl_h) ? __ldg(row + w) : 0u;
             }
         uint8_t *const brow_base = smem;
         for (int kb0 = 0; kb0 < nk; kb0 += kStages) {
@@ -283,33 +286,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // the producer only re-arms full_a[s] after empty[s] fired
                     const bool ok = wait(&full_a[s], (kb / kStages) & 1);
                     const uint32_t *s2w = reinterpret_cast<const uint32_t *>(smem + L::s2(s));
-                    const int nxt = kb + kStages, wn = 2 * nxt;
+                    const int nxt = kb + kStages;
+                    uint8_t *brow = brow_base + L::b(s) + e * 128;
 #pragma unroll
-                    for (int rr = 0; rr < kRows; ++rr) {
-                        const uint32_t w0 = q0[rr][i], w1 = q1[rr][i];
-                        q0[rr][i] = (row_ok[rr] && nxt < nk && wn < wl) ? __ldg(row[rr] + wn) : 0u;
-                        q1[rr][i] = (row_ok[rr] && nxt < nk && wn + 1 < wl) ? __ldg(row[rr] + wn + 1) : 0u;
-                        uint8_t *brow = brow_base + L::b(s) + (e + 128 * rr) * 128;
+                    for (int j = 0; j < kWords; ++j) {
+                        const uint32_t w = q[j][i];
+                        const int wn = 2 * nxt + j;
+                        q[j][i] = (row_ok && nxt < nk && wn < wl_h) ? __ldg(row + wn) : 0u;
+                        const int h = h0 + j;  // word of the K step: columns 32 h .. 32 h + 31
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const uint32_t w = h ? w1 : w0;
+                        for (int qc = 0; qc < 4; ++qc) {
+                            uint32_t v[4];
 #pragma unroll
-                            for (int qc = 0; qc < 4; ++qc) {
-                                uint32_t v[4];
-#pragma unroll
-                                for (int pp = 0; pp < 4; ++pp) {
-                                    const int P = 4 * qc + pp;  // pair index inside the word
-                                    uint32_t val;
-                                    if (kS2)
-                                        val = s2w[16 * h + P];
-                                    else
-                                        val = std::is_same<TA, __nv_bfloat16>::value ? 0x3F803F80u : 0x3C003C00u;
-                                    v[pp] = row_ok[rr] && ok ? lop_sign(w << P, val) : 0u;
-                                }
-                                const int chunk = 4 * h + qc;  // rows e and e + 128 share the swizzle phase
-                                *reinterpret_cast<uint4 *>(brow + ((chunk ^ (e & 7)) << 4)) =
-                                    make_uint4(v[0], v[1], v[2], v[3]);
+                            for (int pp = 0; pp < 4; ++pp) {
+                                const int P = 4 * qc + pp;  // pair index inside the word
+                                uint32_t val;
+                                if (kS2)
+                                    val = s2w[16 * h + P];
+                                else
+                                    val = std::is_same<TA, __nv_bfloat16>::value ? 0x3F803F80u : 0x3C003C00u;
+                                v[pp] = row_ok && ok ? lop_sign(w << P, val) : 0u;
                             }
+                            const int chunk = 4 * h + qc;
+                            *reinterpret_cast<uint4 *>(brow + ((chunk ^ (e & 7)) << 4)) =
+                                make_uint4(v[0], v[1], v[2], v[3]);
                         }
                     }
                     fence_proxy_async_smem();
@@ -324,7 +324,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3;  // TMEM lanes this warp may access
         const int m = m0 + quarter * 32 + lane;
         const TOut *sc = static_cast<const TOut *>(p.col_scale);
-        for (int c = 0; c < kBN; c += 32) {
+        // kExpWarps / 4 warps share a lane quarter: each drains its own share of the columns
+        constexpr int kColParts = kExpWarps / 4, kColsPer = kBN / kColParts;
+        const int cpart = (warp - 2) / 4;
+        for (int c = cpart * kColsPer; c < (cpart + 1) * kColsPer; c += 32) {
             uint32_t r[32];
             tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, r);
             if (!ok || m >= p.M || n0 + c >= p.N) continue;
