@@ -33,8 +33,11 @@ namespace gemm {
 
 constexpr int BM = 128, BN = 128, BK = 64;
 
-constexpr int kExpWarps = 8;                  // weight expanders (and epilogue warps)
-constexpr int kThreads = 64 + 32 * kExpWarps;  // + the TMA producer and the MMA issuer
+// Weight expanders (and epilogue warps) per CTA: 16 for 256-column tiles, 8 for 128-column
+// tiles (one 32-column word of a row per thread either way); plus the TMA producer and the MMA
+// issuer.
+__host__ __device__ constexpr int exp_warps(int bn) { return bn == 256 ? 16 : 8; }
+__host__ __device__ constexpr int cta_threads(int bn) { return 64 + 32 * exp_warps(bn); }
 constexpr int kTileBytes = 128 * 128;  // 128 rows x 128 bytes (64 16-bit values)
 
 struct Params {
@@ -162,7 +165,7 @@ struct Layout {
 // owns kBN / 128 weight rows).  A 256-wide tile reads the activation tile once per two weight
 // row blocks, which lowers the shared-memory traffic per MMA.
 template <typename TA, typename TOut, bool kS2, bool kTwoA, bool kHiLo, bool kStoreT, int kBN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(cta_threads(kBN), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
                 const __grid_constant__ CUtensorMap map_s2, const Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -170,6 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     using L = Layout<kTwoA, kS2, kBN>;
     constexpr int kStages = L::kStg;
+    constexpr int kExpWarps = exp_warps(kBN);
     uint64_t *full_a = reinterpret_cast<uint64_t *>(smem + L::kBars);
     uint64_t *full_b = full_a + kStages;
     uint64_t *empty = full_b + kStages;
@@ -530,7 +534,7 @@ static int launch_stage(const CUtensorMap &a, const CUtensorMap &a2, const CUten
         attr_set[dev] = true;
     }
     dim3 grid((p.N + kBN - 1) / kBN, (p.M + BM - 1) / BM, p.partial ? splits : 1);
-    kern<<<grid, kThreads, smem, stream>>>(a, a2, s2, p);
+    kern<<<grid, cta_threads(kBN), smem, stream>>>(a, a2, s2, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
     if (p.partial) {
