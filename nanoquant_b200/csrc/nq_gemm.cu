@@ -300,15 +300,16 @@ __global__ void __launch_bounds__(cta_threads(kBN), 1)
                         const int h = h0 + j;  // word of the K step: columns 32 h .. 32 h + 31
 #pragma unroll
                         for (int qc = 0; qc < 4; ++qc) {
-                            uint32_t v[4];
+                            uint32_t v[4], sv[4] = {0u, 0u, 0u, 0u};
+                            if (kS2) {  // the four s2 pairs of this chunk in one 16-byte (broadcast) load
+                                const uint4 s4 = reinterpret_cast<const uint4 *>(s2w)[4 * h + qc];
+                                sv[0] = s4.x, sv[1] = s4.y, sv[2] = s4.z, sv[3] = s4.w;
+                            }
 #pragma unroll
                             for (int pp = 0; pp < 4; ++pp) {
                                 const int P = 4 * qc + pp;  // pair index inside the word
-                                uint32_t val;
-                                if (kS2)
-                                    val = s2w[16 * h + P];
-                                else
-                                    val = std::is_same<TA, __nv_bfloat16>::value ? 0x3F803F80u : 0x3C003C00u;
+                                const uint32_t val =
+                                    kS2 ? sv[pp] : (std::is_same<TA, __nv_bfloat16>::value ? 0x3F803F80u : 0x3C003C00u);
                                 v[pp] = row_ok && ok ? lop_sign(w << P, val) : 0u;
                             }
                             const int chunk = 4 * h + qc;
