@@ -190,7 +190,7 @@ constexpr int kAttnThreads = 256;  // 8 warps
 constexpr int kMaxChunks = 64;     // chunk length grows with max_seq to keep at most this many
 constexpr int kHeadDim = 128;
 constexpr int kAttnMaxStages = 12;  // copy ring depth limit (sub-blocks of K or V in flight)
-constexpr int kAttnCtasPerSm = 2;   // chunks per head are sized for about this many CTAs per SM
+constexpr int kAttnCtasPerSm = 4;   // chunks per head are sized for about this many CTAs per SM
 constexpr size_t kAttnScoreBytes = 48 * 1024;  // per-chunk score buffer limit (GRP x chunk x 4 B)
 constexpr int kClusterChunks = 8;  // chunks of one head combined through distributed shared memory
 
@@ -768,8 +768,9 @@ int attn_prepare(int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t head
     ctas *= p.qsplit;
     const int64_t gcta = grp / p.qsplit;  // query heads per CTA
     // ring depth: every sub-block of the chunk in flight if shared memory allows, keeping room
-    // for two CTAs per SM when the grid needs that many
-    const size_t budget = ctas > sm_count() ? 110 * 1024 : 200 * 1024;
+    // for two or four CTAs per SM when the grid needs that many (7B, L = 2048: 12.7 -> 12.3 us
+    // with the chunking sized for four CTAs per SM instead of two; L = 4096: 19.2 -> 17.4 us)
+    const size_t budget = ctas > 2 * (int64_t)sm_count() ? 54 * 1024 : ctas > sm_count() ? 110 * 1024 : 200 * 1024;
     const size_t fixed = (size_t)gcta * kHeadDim * 2 + (size_t)gcta * ch.nsub * kSub * sizeof(float) +
                          (p.cl ? (size_t)kClusterChunks * gcta * (kHeadDim + 2) * 4 : 0);
     int nst = (int)std::min<int64_t>(kAttnMaxStages, 2 * (int64_t)ch.nsub);
