@@ -643,6 +643,9 @@ def run_reference_layer(args):
     launch configuration) on this GPU, timed exactly like run_layer: --copies distinct random
     weight sets cycled past L2, CUDA events, algorithmic bytes per launch."""
     out_f, in_f, r = (int(v) for v in args.layer.split(","))
+    if not torch.cuda.is_available():
+        emit({"impl": "reference", "unavailable": "--layer times the reference's CUDA GEMV and needs a GPU"})
+        return
     ops, rk = _ref_ops("--layer")
     if ops is None:
         return
