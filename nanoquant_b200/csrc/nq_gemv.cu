@@ -27,8 +27,11 @@
 //  * t[b, :] goes to the (L2-resident) workspace; one bounded grid barrier separates
 //    the stages.  The barrier resets itself, so the workspace stays reusable.
 // Layers too large for the per-CTA shared-memory budget run the same kernel as two
-// ordinary launches (stage 1 then stage 2, one 16-row tile per CTA).
+// ordinary launches (stage 1 then stage 2), each over the fewest whole waves of CTAs whose
+// slabs fit in shared memory.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "nq_common.cuh"
@@ -132,8 +135,13 @@ __device__ unsigned int g_trace_launch;
 #endif
 
 __device__ __forceinline__ void tile_range(int tiles, int c, int G, int &b, int &e) {
-    b = (tiles * c) / G;  // tiles <= 2^16 and G <= 2^10 keep this within 32 bits
-    e = (tiles * (c + 1)) / G;
+    if ((long long)tiles * G < (1LL << 31)) {  // every launch of the decode shapes
+        b = (tiles * c) / G;
+        e = (tiles * (c + 1)) / G;
+    } else {  // split launches of very tall layers (tiles <= 2^16, grid up to the tile count)
+        b = (int)(((long long)tiles * c) / G);
+        e = (int)(((long long)tiles * (c + 1)) / G);
+    }
 }
 
 // Copy `n` 16-bit values into a zero-padded shared row of `npad` values (unaligned inputs).
@@ -1117,6 +1125,16 @@ static size_t layout(Params &p, int tiles1, int tiles2, bool stage1, bool stage2
     return off;
 }
 
+// NQ_GEMV_SPLIT_GRID=tiles gives the two-launch plan one 16-row tile per CTA (its earlier
+// form, kept for A/B timing); unset, the split launches run in whole waves (make_plan).
+static bool split_one_tile() {
+    static const bool v = [] {
+        const char *e = std::getenv("NQ_GEMV_SPLIT_GRID");
+        return e != nullptr && std::strcmp(e, "tiles") == 0;
+    }();
+    return v;
+}
+
 static int make_plan(int dev, const Params &base, Plan &plan) {
     const DeviceInfo &di = device_info(dev);
     const size_t cap = (size_t)di.max_smem_optin - kStaticSmemReserve;
@@ -1139,27 +1157,53 @@ static int make_plan(int dev, const Params &base, Plan &plan) {
             return NQ_OK;
         }
     }
-    // two ordinary launches, one 16-row tile per CTA
-    for (const auto &v : variants) {
-        if (v[1] && p.batch > kFoldMaxBatch) continue;
-        if (p.xmode != kChainPlain && !v[0]) continue;
-        Params q1 = p, q2 = p;
-        q1.mode = kStage1;
-        q2.mode = kStage2;
-        const size_t n1 = layout(q1, 1, 0, true, false, v[0] != 0, v[1] != 0);
-        const size_t n2 = layout(q2, 0, 1, false, true, false, false);
-        if (n1 <= cap && n2 <= cap) {
-            plan.mode = kStage1 | kStage2 | 4;  // marker: split
-            plan.grid1 = p.tiles1;
-            plan.grid2 = p.tiles2;
-            plan.smem1 = n1;
-            plan.smem2 = n2;
-            plan.prm1 = q1;
-            plan.prm2 = q2;
-            return NQ_OK;
+    // Two ordinary launches (stage 1, then stage 2).  Each spreads its tiles over the fewest
+    // whole waves of CTAs (multiples of the SM count; the kernel holds one CTA per SM) whose
+    // slabs fit in shared memory: a CTA copies all its tiles' weights at once, so a large layer
+    // streams its planes in one wave rather than in tiles / SMs waves of one 16-row tile per
+    // CTA, and the per-CTA prologue (x staging, input transform, fold) runs once per CTA, not
+    // once per tile.  Stage 1 takes the first variant that fits at the smallest grid.
+    const bool one_tile = split_one_tile();
+    Params q1{}, q2 = p;
+    size_t n1 = 0, n2 = 0;
+    int g1 = 0, g2 = 0;
+    for (int g = one_tile ? p.tiles1 : std::min(G, p.tiles1); g1 == 0; g = std::min(g + G, p.tiles1)) {
+        const int tpc = (p.tiles1 + g - 1) / g;
+        for (const auto &v : variants) {
+            if (v[1] && p.batch > kFoldMaxBatch) continue;
+            if (p.xmode != kChainPlain && !v[0]) continue;
+            Params q = p;
+            q.mode = kStage1;
+            const size_t n = layout(q, tpc, 0, true, false, v[0] != 0, v[1] != 0);
+            if (n <= cap) {
+                q1 = q;
+                n1 = n;
+                g1 = g;
+                break;
+            }
+        }
+        if (g1 == 0 && g >= p.tiles1) break;
+    }
+    q2.mode = kStage2;
+    for (int g = one_tile ? p.tiles2 : std::min(G, p.tiles2); g2 == 0; g = std::min(g + G, p.tiles2)) {
+        const size_t n = layout(q2, 0, (p.tiles2 + g - 1) / g, false, true, false, false);
+        if (n <= cap) {
+            n2 = n;
+            g2 = g;
+        } else if (g >= p.tiles2) {
+            break;
         }
     }
-    return fail(NQ_ERR_UNSUPPORTED, "layer group too large for the shared-memory budget (in=%d)", p.in_f);
+    if (g1 == 0 || g2 == 0)
+        return fail(NQ_ERR_UNSUPPORTED, "layer group too large for the shared-memory budget (in=%d)", p.in_f);
+    plan.mode = kStage1 | kStage2 | 4;  // marker: split
+    plan.grid1 = g1;
+    plan.grid2 = g2;
+    plan.smem1 = n1;
+    plan.smem2 = n2;
+    plan.prm1 = q1;
+    plan.prm2 = q2;
+    return NQ_OK;
 }
 
 template <typename T>
