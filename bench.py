@@ -234,7 +234,7 @@ def cpu_reference_token_time(cfg, context: int, seconds: float):
 
 def config_block(cfg, args, world, dec=None):
     """The line's config; with the decoder, the tensor-parallel sum it actually runs (the fused
-    exchange falls back to NCCL where a shard's GEMV has no single-launch plan)."""
+    exchange falls back to NCCL where a shard's exchanging GEMV launch cannot run one CTA per SM)."""
     exchange = not getattr(args, "no_exchange", False) if dec is None else dec.tpx is not None
     return {"workload": f"{cfg.name} 0.55bpw batch-{args.batch} greedy decode after a {args.prompt}-token "
                         f"random-id prompt",

@@ -158,12 +158,14 @@ NQ_API int nq_gemv_group_ex(int dtype, const nq_gemv_input *input, int64_t batch
  * nq_allreduce_region_free), exports it with nq_ipc_handle and maps the others with nq_ipc_open
  * (include/nq_decoder.h); `regions` lists every rank's region as mapped in the calling process.
  * Every rank must make the same sequence of calls, PUSH and PULL alternating (nq_tp_pull counts
- * as a PULL); batch <= 8; the GEMV must run as its single cooperative launch; a timed-out wait
- * records NQ_ERR_DEVICE_TIMEOUT in the region's status word (nq_workspace_status).
+ * as a PULL); batch <= 8; the launch that exchanges must run one CTA per SM: the single
+ * cooperative launch, or for a layer group too large for it the stage-1 launch of its two (a
+ * PULL) or the stage-2 launch (a PUSH), not both in one call; a timed-out wait records
+ * NQ_ERR_DEVICE_TIMEOUT in the region's status word (nq_workspace_status).
  * NQ_TP_CHECK added to tp_mode plans the call without launching it (and without reading the
  * regions, which may be NULL): NQ_OK when the exchange can run at these shapes, otherwise the
- * error the launch would return (for instance a layer group whose weight slabs need the
- * two-launch GEMV), so a caller can fall back to a separate all-reduce before it starts.
+ * error the launch would return (for instance a two-launch GEMV whose exchanging launch needs
+ * more CTAs than SMs), so a caller can fall back to a separate all-reduce before it starts.
  * ------------------------------------------------------------------------------- */
 #define NQ_TP_PULL 1
 #define NQ_TP_PUSH 2

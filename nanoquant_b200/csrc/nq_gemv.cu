@@ -1074,7 +1074,10 @@ static inline int padded_stride(int w) {
 }
 
 // Shared-memory layout for a launch whose CTAs own at most `tiles1`/`tiles2` tiles.
-static size_t layout(Params &p, int tiles1, int tiles2, bool stage1, bool stage2, bool x_in_smem, bool fold) {
+// `push_rows`: a stage-2-only launch that PUSHes its rows gets a staging region for them
+// (a launch with stage 1 stages them in its x region).
+static size_t layout(Params &p, int tiles1, int tiles2, bool stage1, bool stage2, bool x_in_smem, bool fold,
+                     bool push_rows = false) {
     size_t off = 128;  // mbarriers
     p.kbu2 = 1;
     for (int l = 0; l < p.nm; ++l) p.kbu2 = std::max(p.kbu2, p.m[l].kb2);
@@ -1113,6 +1116,10 @@ static size_t layout(Params &p, int tiles1, int tiles2, bool stage1, bool stage2
         p.off_v = (uint32_t)off;
         off = align128(off + (size_t)16 * tiles1 * p.wvs * 4 + 16);
     }
+    if (stage2 && !stage1 && push_rows) {
+        p.off_x = (uint32_t)off;
+        off = align128(off + (size_t)16 * tiles2 * p.batch * 2 + 16);
+    }
     p.off_u = (uint32_t)off;
     p.off_s1 = (uint32_t)off;
     if (stage2) {
@@ -1135,7 +1142,8 @@ static bool split_one_tile() {
     return v;
 }
 
-static int make_plan(int dev, const Params &base, Plan &plan) {
+// `push_rows`: the stage-2 launch of a split plan PUSHes its rows (tensor-parallel exchange).
+static int make_plan(int dev, const Params &base, Plan &plan, bool push_rows = false) {
     const DeviceInfo &di = device_info(dev);
     const size_t cap = (size_t)di.max_smem_optin - kStaticSmemReserve;
     const int G = di.sms;
@@ -1186,7 +1194,7 @@ static int make_plan(int dev, const Params &base, Plan &plan) {
     }
     q2.mode = kStage2;
     for (int g = one_tile ? p.tiles2 : std::min(G, p.tiles2); g2 == 0; g = std::min(g + G, p.tiles2)) {
-        const size_t n = layout(q2, 0, (p.tiles2 + g - 1) / g, false, true, false, false);
+        const size_t n = layout(q2, 0, (p.tiles2 + g - 1) / g, false, true, false, false, push_rows);
         if (n <= cap) {
             n2 = n;
             g2 = g;
@@ -1260,16 +1268,22 @@ static int launch(const Plan &plan, cudaStream_t stream, const TpX &tp) {
                                           : cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, false>, plan.prm, tp));
         return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv fused launch");
     }
-    if (tp.mode) return fail(NQ_ERR_UNSUPPORTED, "the tensor-parallel exchange needs the single-launch GEMV");
+    // split: a PULL exchanges in the stage-1 launch (it forms x), a PUSH in the stage-2 launch
+    // (it stores y); group_impl checked that launch's grid
     const TpX none{};
+    TpX pull = none, push = none;
+    if (tp.mode & kTpPull) pull = tp, pull.mode = kTpPull;
+    if (tp.mode & kTpPush) push = tp, push.mode = kTpPush;
     cfg.numAttrs = na;
     cfg.gridDim = dim3(plan.grid1);
     cfg.dynamicSmemBytes = plan.smem1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, false>, plan.prm1, none);
+    cudaError_t e = pull.mode ? cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, true>, plan.prm1, pull)
+                              : cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, false>, plan.prm1, none);
     if (e != cudaSuccess) return cuda_fail(e, "gemv stage-1 launch");
     cfg.gridDim = dim3(plan.grid2);
     cfg.dynamicSmemBytes = plan.smem2;
-    e = cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, false>, plan.prm2, none);
+    e = push.mode ? cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, true>, plan.prm2, push)
+                  : cudaLaunchKernelEx(&cfg, gemv_kernel<T, false, false>, plan.prm2, none);
     return e == cudaSuccess ? NQ_OK : cuda_fail(e, "gemv stage-2 launch");
 }
 
@@ -1397,18 +1411,25 @@ static int group_impl(int dtype, const GroupInput &in, int64_t batch, int64_t in
         for (int l = 0; l < n; ++l)
             p.m[l].y = static_cast<char *>(layers[l].y) + (size_t)b0 * layers[l].out_features * 2;
         Plan plan;
-        int st = make_plan(dev, p, plan);
+        int st = make_plan(dev, p, plan, (tp.mode & kTpPush) != 0);
         if (st) return st;
         if (tp.mode) {
             if (batch > kMaxBatch) return fail(NQ_ERR_UNSUPPORTED, "the exchange supports batch <= %d", kMaxBatch);
-            if (plan.mode != kFused || plan.grid != tp.gprod || ((tp.mode & kTpPull) && !plan.prm.x_in_smem))
-                return fail(NQ_ERR_UNSUPPORTED, "the exchange needs the single-launch GEMV on %d CTAs", tp.gprod);
+            // The launch that forms x (PULL: stage 1) and the one that stores y (PUSH: stage 2) run
+            // one CTA per SM: every launch of a kind advances the epoch counter of each CTA index.
+            // A split plan exchanges in its stage-1 (PULL) or stage-2 (PUSH) launch, not both.
+            const bool fused = plan.mode == kFused;
+            const int gpull = fused ? plan.grid : plan.grid1, gpush = fused ? plan.grid : plan.grid2;
+            const bool xs_ok = fused ? plan.prm.x_in_smem != 0 : plan.prm1.x_in_smem != 0;
+            if (((tp.mode & kTpPull) && (gpull != tp.gprod || !xs_ok)) || ((tp.mode & kTpPush) && gpush != tp.gprod) ||
+                (!fused && tp.mode == (kTpPull | kTpPush)))
+                return fail(NQ_ERR_UNSUPPORTED, "the exchange needs its GEMV launches on %d CTAs", tp.gprod);
             if ((tp.mode & kTpPull) && (p.in_f % 8 || (long long)p.batch * p.in_f > tp.max_elems))
                 return fail(NQ_ERR_UNSUPPORTED, "pull: batch * in_features must fit the exchange buffers");
             if ((tp.mode & kTpPush) && (n != 1 || (long long)p.batch * p.m[0].out_f > tp.max_elems ||
                                          p.m[0].out_f % 8 != 0))
                 return fail(NQ_ERR_UNSUPPORTED, "push: one layer, out_features % 8 == 0, batch * out within the buffers");
-            if ((tp.mode & kTpPush) &&
+            if ((tp.mode & kTpPush) && fused &&
                 (!plan.prm.x_in_smem || (size_t)plan.prm.kb1 * 64 < (size_t)16 * ((p.tiles2 + plan.grid - 1) / plan.grid)))
                 return fail(NQ_ERR_UNSUPPORTED, "push: the rows of a CTA must fit its staged-x region");
         }

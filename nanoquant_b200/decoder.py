@@ -20,8 +20,8 @@ Tensor parallelism (one sum over the ranks per attention block and per MLP block
   columns of its shard (V split by input columns) and the full U; by linearity the ranks'
   outputs s1 * U(smid * V_shard (s2 * x_shard)) sum to the full layer;
 * in decode the sum runs inside the GEMVs (TPExchange: o / down push their rows to every rank
-  over NVLink, the next RMSNorm prologue pulls and sums them) where every exchange launch has
-  its single-launch plan, otherwise through torch.distributed (NCCL), as in prefill.
+  over NVLink, the next RMSNorm prologue pulls and sums them) where every exchanging GEMV
+  launch runs one CTA per SM, otherwise through torch.distributed (NCCL), as in prefill.
 Weights are random (seeded) with the per-layer ranks of the benchmark configs; every rank
 draws the same global planes and keeps its slice, so any TP degree computes the same model.
 """
@@ -327,9 +327,10 @@ class Decoder:
 
     def _exchange_fits(self) -> bool:
         """Whether the four exchange GEMVs of a decoder block (q/k/v and gate/up pulling, o and
-        down pushing) have their single-launch plan at this shard's shapes: planned with
-        NQ_TP_CHECK, nothing launched.  Wide shards (Llama-3-70B at TP2) whose weight slabs need
-        the two-launch GEMV keep the NCCL sums instead."""
+        down pushing) have a plan whose exchanging launch runs one CTA per SM at this shard's
+        shapes: planned with NQ_TP_CHECK, nothing launched.  The two-launch GEMV of a wide shard
+        (Llama-3-70B gate/up at TP2) qualifies when its pulling (stage-1) or pushing (stage-2)
+        launch does; where it does not (70B at TP2 batch 8) the step keeps the NCCL sums."""
         ops, lay, B, dev, dt = torch.ops.nq_b200, self.layers[0], self.batch, self.device, self.dtype
         check, mx = 4, (B * self.cfg.hidden + 7) // 8 * 8
         ex = ([0] * self.tp, self.tp_rank, mx)

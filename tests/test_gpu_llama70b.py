@@ -72,14 +72,16 @@ def test_gemm_llama3_70b_shapes_m2048_sampled_rows(proj):
     assert workspace_status(ws) == 0
 
 
-@pytest.mark.parametrize("tp,fits", [(2, False), (8, True)])
-def test_exchange_plan_check_on_70b_shards(tp, fits):
-    """NQ_TP_CHECK plans the exchange launches without running them (no peers, no regions): every
-    exchange GEMV of a TP8 shard has its single-launch plan; at TP2 some shard's weight slabs need
-    the two-launch GEMV, which the check reports, so the decoder keeps NCCL sums there."""
+@pytest.mark.parametrize("tp,batch,fits", [(2, 1, True), (8, 1, True), (2, 8, False)])
+def test_exchange_plan_check_on_70b_shards(tp, batch, fits):
+    """NQ_TP_CHECK plans the exchange launches without running them (no peers, no regions).  At
+    TP8 every exchange GEMV has its single-launch plan; at TP2 the gate/up shard needs the
+    two-launch GEMV, whose stage-1 launch runs one CTA per SM and pulls; at TP2 batch 8 that
+    launch needs one CTA per tile (436), which the check reports, so the decoder keeps NCCL sums."""
     import dataclasses
 
     from nanoquant_b200.decoder import Decoder
     cfg = dataclasses.replace(LLAMA3_70B, layers=1)
-    dec = Decoder(cfg, max_seq=64, tp_rank=0, tp=tp, tp_exchange=False, dtype=torch.float16, device="cuda")
+    dec = Decoder(cfg, max_seq=64, batch=batch, tp_rank=0, tp=tp, tp_exchange=False, dtype=torch.float16,
+                  device="cuda")
     assert dec._exchange_fits() is fits

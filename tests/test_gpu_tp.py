@@ -1,6 +1,8 @@
 """Tensor-parallel decode on 2 GPUs: the sharded model must produce the same greedy tokens and
 nearly the same logits as the unsharded one, with the per-block sums fused into the GEMVs (the
-default exchange), through NCCL, or through the standalone peer all-reduce.  Skipped with fewer
+default exchange), through NCCL, or through the standalone peer all-reduce.  A one-block model of
+Llama-3-70B width runs the exchange through the two-launch GEMV (its gate/up shard pulls in the
+stage-1 launch; at batch 2 its down shard pushes from the stage-2 launch).  Skipped with fewer
 than 2 GPUs."""
 import os
 import tempfile
@@ -9,12 +11,15 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
+from nanoquant_b200.configs import LLAMA3_70B
 from nanoquant_b200.decoder import Decoder, DecoderConfig
 
 pytestmark = pytest.mark.gpu
 
 CFG = DecoderConfig("tp-small", 1024, 512, 2, 4, 2, 128, 1024,
                     {"q": 160, "k": 96, "v": 96, "o": 160, "gate": 200, "up": 200, "down": 200})
+W70B = DecoderConfig("llama3-70b-1l", 4096, 8192, 1, 64, 8, 128, 28672, dict(LLAMA3_70B.ranks),
+                     rope_theta=LLAMA3_70B.rope_theta)
 
 
 def _rendezvous():
@@ -26,24 +31,24 @@ def _rendezvous():
     return "file://" + path
 
 
-def _run(rank, world, rdzv, prompt, steps, q, mode="exchange"):
+def _run(rank, world, rdzv, prompt, steps, q, mode="exchange", cfg=CFG):
     import datetime
     os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     torch.distributed.init_process_group("nccl", init_method=rdzv, rank=rank, world_size=world,
                                          timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     try:
-        dec = Decoder(CFG, max_seq=128, tp_rank=rank, tp=world, group=torch.distributed.group.WORLD, seed=3,
-                      peer_allreduce=mode == "peer_allreduce", tp_exchange=mode == "exchange",
-                      device=f"cuda:{rank}")
+        dec = Decoder(cfg, max_seq=128, batch=prompt.shape[0], tp_rank=rank, tp=world,
+                      group=torch.distributed.group.WORLD, seed=3, peer_allreduce=mode == "peer_allreduce",
+                      tp_exchange=mode == "exchange", device=f"cuda:{rank}")
         assert (dec.tpx is not None) == (mode == "exchange")
-        first = int(dec.prefill(prompt.cuda())[0])
+        first = dec.prefill(prompt.cuda()).tolist()
         logits = dec.step_logits().float().cpu()
-        dec.tokens.fill_(int(torch.argmax(logits[0])))
+        dec.tokens.copy_(torch.argmax(logits, dim=-1))
         dec.pos.add_(1)
         dec.seq_len.add_(1)
         g = dec.capture(warmup=2)
-        toks = [int(g.replay()[0]) for _ in range(steps)]
+        toks = [g.replay().tolist() for _ in range(steps)]
         g.release()
         status = dec.tpx.status() if dec.tpx is not None else 0
         torch.distributed.barrier(device_ids=[rank])
@@ -54,22 +59,24 @@ def _run(rank, world, rdzv, prompt, steps, q, mode="exchange"):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("mode", ["exchange", "nccl", "peer_allreduce"])
-def test_tp2_matches_tp1(mode):
-    prompt = torch.randint(0, CFG.vocab, (37,), generator=torch.Generator().manual_seed(9))
-    ref = Decoder(CFG, max_seq=128, seed=3, device="cuda:0")
-    first = int(ref.prefill(prompt.cuda())[0])
+@pytest.mark.parametrize("mode,cfg,batch", [("exchange", CFG, 1), ("nccl", CFG, 1), ("peer_allreduce", CFG, 1),
+                                            ("exchange", W70B, 1), ("exchange", W70B, 2)],
+                         ids=["exchange", "nccl", "peer_allreduce", "exchange-70b-width", "exchange-70b-width-b2"])
+def test_tp2_matches_tp1(mode, cfg, batch):
+    prompt = torch.randint(0, cfg.vocab, (batch, 37), generator=torch.Generator().manual_seed(9))
+    ref = Decoder(cfg, max_seq=128, batch=batch, seed=3, device="cuda:0")
+    first = ref.prefill(prompt.cuda()).tolist()
     logits = ref.step_logits().float().cpu()
-    ref.tokens.fill_(int(torch.argmax(logits[0])))
+    ref.tokens.copy_(torch.argmax(logits, dim=-1))
     ref.pos.add_(1)
     ref.seq_len.add_(1)
-    toks = [int(ref.step()[0]) for _ in range(6)]
+    toks = [ref.step().tolist() for _ in range(6)]
     del ref
     torch.cuda.empty_cache()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     rdzv = _rendezvous()
-    procs = [ctx.Process(target=_run, args=(r, 2, rdzv, prompt, 6, q, mode)) for r in range(2)]
+    procs = [ctx.Process(target=_run, args=(r, 2, rdzv, prompt, 6, q, mode, cfg)) for r in range(2)]
     for p in procs:
         p.start()
     outs = sorted([q.get(timeout=240) for _ in range(2)], key=lambda t: t[0])
